@@ -1,0 +1,378 @@
+#!/usr/bin/env python3
+"""Benchmark of the quantised-linear hot path on B200 (one JSON line on rank 0).
+
+Workloads (--workload):
+  gemm   (default) BASELINE config 2: Q4_K prefill tile GEMM, M=2048 tokens, K=4096, N=14336, f16 out; TFLOP/s.
+  gemv   BASELINE config 3 decode GEMV: Q4_K 4096 x 14336 weights, M tokens (--tokens, default 1); HBM GB/s.
+A step is one launch of the kernel over one batch. Inputs are resident in HBM when the timed region starts; the
+step rotates through input copies whose total exceeds L2 (126 MB), so no step reads inputs another step left in
+L2. Timing: W warm-up steps, then exactly K steps between a barrier + device synchronise on both sides, CUDA
+events on the launching stream, max over ranks. `e2e` repeats the metric through the public API with pinned host
+buffers: every step copies its activations host->device and its output device->host inside the timed region.
+
+Multi-GPU (torchrun, one process per GPU): every rank runs the same workload on its own batch (replicas, weak
+scaling; the single GEMM / GEMV has no exchange step). torch.distributed (gloo, CPU tensors) is used only for the
+barrier and the max over ranks.
+
+--impl reference: the reference's CPU path for the same metric (its test-suite oracle: gguf-py
+quants.dequantize -> f16 -> numpy matmul, engine/gpu/loom/tools/gemv_check.py:161-162), on the host cores, rank 0.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+L2_BYTES = 126 * 2 ** 20
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return {"hbm_gbs": d["hbm_gbs"], "tflops": d["bf16_tflops"], "tflops_sustained": d["bf16_tflops_sustained"],
+                "src": "measured"}
+    return {"hbm_gbs": 6650.0, "tflops": 1590.0, "tflops_sustained": 1400.0, "src": "fallback"}
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region (median SM clock, throttle reasons seen)."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.index), "-lms", "100"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [v.strip() for v in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = max(mx, float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_init(n):
+    if n <= 1 or "RANK" not in os.environ:
+        return None
+    import datetime
+
+    import torch.distributed as dist
+    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
+    return dist
+
+
+def barrier(dist):
+    if dist:
+        dist.barrier()
+
+
+def max_over_ranks(dist, v):
+    if not dist:
+        return v
+    import torch
+    t = torch.tensor([v], dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def cpu_cores():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+# ------------------------------------------------------------------------------------------------ workloads
+def gemm_workload(args):
+    return dict(name="q4k_prefill_gemm", fmt=12, M=2048, K=4096, N=14336, out="f16")
+
+
+def gemv_workload(args):
+    return dict(name="q4k_decode_gemv", fmt=12, M=args.tokens, K=14336, N=4096, out="f32")
+
+
+def run_ours(args, dist, rank, local_rank):
+    import __graft_entry__ as ge
+    pkg = ge.load_package()
+    F, ops = pkg.formats, pkg.ops
+    dev = pkg.Device(local_rank)
+    wl = gemm_workload(args) if args.workload == "gemm" else gemv_workload(args)
+    t, M, K, N = wl["fmt"], wl["M"], wl["K"], wl["N"]
+    gemv = args.workload == "gemv"
+    w = F.synth_weights(t, N, K, seed=0)
+    x = F.synth_activations(M, K, seed=1 + rank)
+    wbytes, xbytes = w.nbytes, x.nbytes
+    ydt = 1 if wl["out"] == "f16" else 0
+    ybytes = M * N * (2 if ydt else 4)
+    per_copy = wbytes + xbytes
+    copies = max(2, int(np.ceil(2.2 * L2_BYTES / per_copy)))
+    wd = [dev.upload(w) for _ in range(copies)]
+    xd = [dev.upload(x) for _ in range(copies)]
+    yd = [dev.empty(ybytes) for _ in range(2)]
+    stream = pkg.Stream()
+    s = stream.handle
+    fn = ops.qgemv_ptr if gemv else ops.qgemm_ptr
+
+    def step(i):
+        j = i % copies
+        fn(wd[j].ptr, t, N, K, w.shape[1], 0, xd[j].ptr, M, K, yd[i & 1].ptr, ydt, N, stream=s)
+
+    for i in range(args.warmup):
+        step(i)
+    stream.synchronize()
+    e0, e1 = pkg.Event(), pkg.Event()
+    clocks = Clocks(local_rank)
+    barrier(dist)
+    dev.synchronize()
+    clocks.start()
+    time.sleep(0.05)
+    e0.record(s)
+    for i in range(args.steps):
+        step(i)
+    e1.record(s)
+    e1.synchronize()
+    dev.synchronize()
+    clk = clocks.stop()
+    barrier(dist)
+    ms_local = e0.elapsed_ms(e1)
+    ms = max_over_ranks(dist, ms_local)
+    status = dev.status_word()
+    if status:
+        raise RuntimeError(f"kernel status word {status}")
+
+    # ---------------- e2e: pinned host activations in, output out, every step
+    xh = pkg.PinnedBuffer(xbytes)
+    xh.array(np.float16, x.shape)[...] = x
+    yh = pkg.PinnedBuffer(ybytes)
+    xdev = dev.empty(xbytes)
+
+    def e2e_step(i):
+        pkg.lib().yah_memcpy_h2d(xdev.ptr, xh.ptr, xbytes, s)
+        fn(wd[0].ptr, t, N, K, w.shape[1], 0, xdev.ptr, M, K, yd[0].ptr, ydt, N, stream=s)
+        pkg.lib().yah_memcpy_d2h(yh.ptr, yd[0].ptr, ybytes, s)
+
+    for i in range(max(1, args.warmup)):
+        e2e_step(i)
+    stream.synchronize()
+    barrier(dist)
+    e2 = pkg.Event()
+    e3 = pkg.Event()
+    e2.record(s)
+    for i in range(args.steps):
+        e2e_step(i)
+    e3.record(s)
+    e3.synchronize()
+    ms_e2e = max_over_ranks(dist, e2.elapsed_ms(e3))
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    pk = peaks()
+    per_step_ms = ms / args.steps
+    if gemv:
+        alg_bytes = wbytes + xbytes + ybytes
+        value = world * alg_bytes / (per_step_ms * 1e-3) / 1e9
+        unit, metric = "GB/s", f"Q4_K decode GEMV HBM GB/s (M={M})"
+        achieved = alg_bytes / (ms_local / args.steps * 1e-3) / 1e9
+        roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": None, "peak_src": pk["src"],
+                "algorithmic_bytes_per_launch": alg_bytes}
+        e2e_val = world * alg_bytes / (ms_e2e / args.steps * 1e-3) / 1e9
+    else:
+        flops = 2.0 * M * N * K
+        value = world * flops / (per_step_ms * 1e-3) / 1e12
+        unit, metric = "TFLOP/s", "Q4_K dequant-GEMM prefill TFLOP/s"
+        achieved = flops / (ms_local / args.steps * 1e-3) / 1e12
+        roof = {"bound": "tensor", "achieved": round(achieved, 1), "peak": pk["tflops"], "unit": "TFLOP/s",
+                "frac": round(achieved / pk["tflops"], 4), "traffic": None, "peak_src": pk["src"],
+                "frac_of_sustained": round(achieved / pk["tflops_sustained"], 4),
+                "algorithmic_flops_per_launch": flops}
+        e2e_val = world * flops / (ms_e2e / args.steps * 1e-3) / 1e12
+    traffic = load_traffic(wl["name"])
+    if traffic is not None:
+        roof["traffic"] = traffic
+    line = {
+        "metric": metric, "value": round(value, 2), "unit": unit, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(per_step_ms, 5), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f16 x GGUF-Q4_K -> f32 acc", "data": "synthetic",
+        "config": {"workload": wl["name"], "M_tokens": M, "K": K, "N": N, "weight_format": "Q4_K",
+                   "out_dtype": wl["out"], "parallelism": f"replicas x{world}",
+                   "l2": f"rotating {copies} input copies ({copies * per_copy / 2**20:.0f} MiB > L2)"},
+        "e2e": {"value": round(e2e_val, 2), "unit": unit, "h2d_bytes_per_step": xbytes, "d2h_bytes_per_step": ybytes},
+        "gpu_launches": args.steps,
+        "roofline": roof,
+        "clocks": clk,
+    }
+    return line
+
+
+def load_traffic(name):
+    """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary (profiles/*.json)."""
+    p = os.path.join(ROOT, "profiles", f"{name}.traffic.json")
+    if os.path.exists(p):
+        try:
+            return json.load(open(p))["dram_bytes_per_launch"]
+        except (ValueError, KeyError):
+            return None
+    return None
+
+
+# ------------------------------------------------------------------------------------------------ CPU paths
+def cpu_reference_step(fmt, w, x, K, use_gguf=True):
+    """One dequant-then-GEMM on the host: gguf-py's dequantize (the reference's oracle) -> f16 -> f32 matmul."""
+    N = w.shape[0]
+    if use_gguf:
+        from gguf import GGMLQuantizationType as T
+        from gguf import quants
+        qt = {8: T.Q8_0, 12: T.Q4_K, 14: T.Q6_K}[fmt]
+        wq = quants.dequantize(w, qt).astype(np.float16)
+    else:
+        from oracle import oracle as O
+        wq = O.dequant_f16(fmt, w, N, K)
+    return x.astype(np.float32) @ wq.astype(np.float32).T
+
+
+def cpu_baseline(args, seconds=10.0):
+    """The CPU path timed on a bounded sample (rows of the weight) for the same metric."""
+    wl = gemm_workload(args) if args.workload == "gemm" else gemv_workload(args)
+    import __graft_entry__ as ge
+    F = ge.load_package().formats
+    t, M, K, N = wl["fmt"], wl["M"], wl["K"], wl["N"]
+    rows = min(N, 2048)
+    w = F.synth_weights(t, rows, K, seed=0)
+    x = F.synth_activations(M, K, seed=1)
+    try:
+        import gguf  # noqa: F401
+        use_gguf, kind = True, "reference"
+    except ImportError:
+        use_gguf, kind = False, "port"
+    cpu_reference_step(t, w, x, K, use_gguf)  # warm-up
+    n, t0 = 0, time.perf_counter()
+    while True:
+        cpu_reference_step(t, w, x, K, use_gguf)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= seconds or n >= 50:
+            break
+    per = el / n
+    if args.workload == "gemv":
+        val = (w.nbytes + x.nbytes + M * rows * 4) / per / 1e9
+        unit = "GB/s"
+    else:
+        val = 2.0 * M * rows * K / per / 1e12
+        unit = "TFLOP/s"
+    return {"value": round(val, 5), "unit": unit, "cores": cpu_cores(), "kind": kind,
+            "sample": f"{'gguf-py dequantize' if use_gguf else 'oracle C dequant'} + numpy f32 matmul of {rows} of "
+                      f"{N} weight rows x {M} tokens x K={K}, {n} runs ({per * 1e3:.1f} ms each); "
+                      f"OPENBLAS_NUM_THREADS={os.environ.get('OPENBLAS_NUM_THREADS', 'unset')}"}
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return None
+    wl = gemm_workload(args) if args.workload == "gemm" else gemv_workload(args)
+    import __graft_entry__ as ge
+    F = ge.load_package().formats
+    t, M, K, N = wl["fmt"], wl["M"], wl["K"], wl["N"]
+    rows = min(N, 1024)
+    w = F.synth_weights(t, rows, K, seed=0)
+    x = F.synth_activations(M, K, seed=1)
+    try:
+        import gguf  # noqa: F401
+        use_gguf, kind = True, "reference"
+    except ImportError:
+        use_gguf, kind = False, "port"
+    for _ in range(args.warmup):
+        cpu_reference_step(t, w, x, K, use_gguf)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu_reference_step(t, w, x, K, use_gguf)
+    el = time.perf_counter() - t0
+    per = el / args.steps
+    if args.workload == "gemv":
+        val, unit = (w.nbytes + x.nbytes + M * rows * 4) / per / 1e9, "GB/s"
+        metric = f"Q4_K decode GEMV HBM GB/s (M={M})"
+    else:
+        val, unit = 2.0 * M * rows * K / per / 1e12, "TFLOP/s"
+        metric = "Q4_K dequant-GEMM prefill TFLOP/s"
+    sample = (f"{'gguf-py dequantize' if use_gguf else 'oracle C dequant'} + numpy f32 matmul of {rows} of {N} "
+              f"weight rows x {M} tokens x K={K} per step")
+    return {"impl": "reference", "metric": metric, "value": round(val, 5), "unit": unit,
+            "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(per * 1e3, 3), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f16 weights (dequantised) x f16 -> f32", "data": "synthetic",
+            "config": {"workload": wl["name"], "M_tokens": M, "K": K, "N": N, "weight_format": "Q4_K"},
+            "cpu_baseline": {"value": round(val, 5), "unit": unit, "cores": cpu_cores(), "kind": kind,
+                             "sample": sample},
+            "e2e": {"value": round(val, 5), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="gemm", choices=["gemm", "gemv"])
+    ap.add_argument("--tokens", type=int, default=1, help="gemv tokens (1..32)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        line = run_reference(args, rank)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
+    dist = dist_init(args.gpus)
+    line = run_ours(args, dist, rank, local_rank)
+    if rank == 0:
+        if not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(args)
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

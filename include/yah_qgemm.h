@@ -1,0 +1,150 @@
+/*
+ * yah_qgemm.h - C ABI of the B200 (sm_100a) quantised-linear library libyah_b200.so.
+ *
+ * The reference engine has no C-ABI GEMM: its operator is a compiled Loom kernel dispatched through
+ * LoomDevice::Dispatch / LoomGraph::Dispatch (engine/model/loom_runtime.hpp:276-290, :384-410) with the binding
+ * order weight, input, [gate | resid], ..., output (engine/gpu/loom/tools/gen_gemm_tile.py:319-320) and the
+ * GEMV's weights, x, y (engine/gpu/loom/tools/gen_gemv.py:729). Each entry point below names the reference
+ * interface it replaces. Conventions:
+ *   - plain pointers and sizes only; every function returns a status (YAH_OK = 0) and never throws;
+ *     yah_last_error() returns the calling thread's last message;
+ *   - all tensors are caller-owned device memory; the library writes only the outputs it is given
+ *     (engine/model/loom_prefill.hpp:647-657);
+ *   - `stream` is a cudaStream_t (NULL = the legacy default stream); calls are stream-ordered;
+ *   - shapes are runtime values (the reference bakes them per kernel, gen_gemm_tile.py:347-348);
+ *   - layouts are the engine's: weights are GGUF rows [N][K / block * block bytes] as loaded from the file
+ *     (engine/model/weights.hpp:140-152), activations token-major [M][ldx] f16, outputs token-major [M][ldy]
+ *     (gen_gemm_tile.py:1230-1231);
+ *   - K is a multiple of 256 (Q8_0 is taken 8 blocks at a time, gen_gemm_decode.py:1338-1339); a K window of
+ *     longer rows starts at super-block kb_off of each row (the reference's KWIN, gen_gemm_tile.py:262-264);
+ *     a row range at a full output stride is a weight pointer offset plus ldy (OSTRIDE, gen_gemm_tile.py:246-250).
+ */
+#ifndef YAH_QGEMM_H_
+#define YAH_QGEMM_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* The library is built with hidden visibility; exactly the functions declared here are exported. */
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+/* Status codes (the reference throws LoomError, engine/model/loom_runtime.hpp:25-40). */
+#define YAH_OK 0
+#define YAH_ERR_ARG 1         /* null pointer, bad shape, misaligned pointer or stride */
+#define YAH_ERR_UNSUPPORTED 2 /* format / dtype / epilogue / layout the kernels do not cover */
+#define YAH_ERR_SIZE 3        /* a buffer is smaller than the operation's footprint */
+#define YAH_ERR_CUDA 4        /* a CUDA runtime or driver call failed */
+#define YAH_ERR_DEVICE 5      /* no sm_100 device, or a kernel reported a bounded-wait timeout */
+#define YAH_ERR_NCCL 6        /* a collective failed (tensor-parallel layer) */
+
+/* GGML type ids (engine/core/gguf.hpp GgmlType). */
+#define YAH_Q8_0 8
+#define YAH_Q4_K 12
+#define YAH_Q6_K 14
+
+/* Element types of activations / outputs. */
+#define YAH_F32 0
+#define YAH_F16 1
+
+/* Epilogues: the reference kernel kinds (gen_gemm_tile.py:309-322, gen_gemv.py:16-19). */
+#define YAH_EPI_STORE 0  /* kstore / plain:  y = W x                                  */
+#define YAH_EPI_RESID 1  /* kres / resid:    y = aux + W x   (aux, y f32; y may be aux) */
+#define YAH_EPI_SWIGLU 2 /* swiglu:          y = f16(silu(aux) * W x)   (aux f32 gate)  */
+
+/* ---- library ----------------------------------------------------------------------------------------- */
+const char* yah_version(void);
+/* Message of the calling thread's last failed call ("" if none). */
+const char* yah_last_error(void);
+
+/* ---- format traits (engine/core/gguf.hpp:49-50 BlockElements / BlockBytes, gguf.cpp:27-35) ------------- */
+int yah_block_elements(int ggml_type);
+int yah_block_bytes(int ggml_type);
+/* Bytes of one row of K values; -1 if K is not a whole number of blocks or the type is unsupported. */
+int64_t yah_row_bytes(int ggml_type, int64_t K);
+
+/* ---- device runtime (LoomDevice Allocate / H2D / D2H / Synchronize, loom_runtime.hpp:153-325) -------- */
+int yah_device_count(int* count);
+int yah_set_device(int device);
+int yah_get_device(int* device);
+/* sm count, compute capability and global memory of a device. */
+int yah_device_info(int device, int* sm_count, int* cc_major, int* cc_minor, int64_t* total_mem);
+int yah_malloc(void** ptr, size_t bytes);
+int yah_free(void* ptr);
+/* Page-locked host memory (for host<->device copies that overlap and run at full PCIe rate). */
+int yah_host_alloc(void** ptr, size_t bytes);
+int yah_host_free(void* ptr);
+int yah_memcpy_h2d(void* dst, const void* src, size_t bytes, void* stream);
+int yah_memcpy_d2h(void* dst, const void* src, size_t bytes, void* stream);
+int yah_memcpy_d2d(void* dst, const void* src, size_t bytes, void* stream);
+int yah_memset(void* ptr, int value, size_t bytes, void* stream);
+int yah_stream_create(void** stream);
+int yah_stream_destroy(void* stream);
+int yah_stream_synchronize(void* stream);
+int yah_device_synchronize(void);
+int yah_event_create(void** event);
+int yah_event_destroy(void* event);
+int yah_event_record(void* event, void* stream);
+int yah_event_synchronize(void* event);
+int yah_event_elapsed_ms(void* start, void* end, float* ms);
+/* Read and clear the current device's kernel status word: 0, or the code of a bounded wait that ran out
+ * (1 data wait, 2 free-stage wait, 3 exit drain). A non-zero word means the output of that launch is invalid. */
+int yah_status_word(int* code);
+
+/* ---- kernels ------------------------------------------------------------------------------------------ */
+
+/* Footprints in bytes of the buffers a yah_qgemm / yah_qgemv call touches (the reference's bounds gate,
+ * engine/gpu/loom/tools/footprint_gate.py:57-79 and gen_gemv.py:856-862); callers that know their buffer sizes
+ * refuse a call whose buffer is smaller (as engine/run/hal_run.cc:107-111 does). */
+int yah_qgemm_footprint(int ggml_type, int64_t N, int64_t K, int64_t w_row_stride, int64_t kb_off, int64_t M,
+                        int64_t ldx, int y_dtype, int64_t ldy, int64_t* w_bytes, int64_t* x_bytes, int64_t* y_bytes);
+
+/* Dequantise rows x K values of a GGUF weight to f16 out[rows][ldo] with the tile GEMM's own decode,
+ * bit-identical to the reference dequant (gen_gemm_tile.py kind "dequant", :314-327; checked as
+ * dq_bfp16_check.py:87-92). w: rows at w_row_stride bytes (2-byte aligned), K window from super-block kb_off.
+ * out: 16-byte aligned, ldo a multiple of 8. */
+int yah_dequant(const void* w, int ggml_type, int64_t rows, int64_t K, int64_t w_row_stride, int64_t kb_off,
+                void* out, int64_t ldo, void* stream);
+
+/* Tile GEMM (prefill): y[M][ldy] = epilogue(x[M][ldx] * W[N][K]^T), f32 accumulation.
+ * Replaces the yah_ffn_gemm_<fmt>[_kres|_swiglu] kernels (gen_gemm_tile.py:221-238, :309-322) and their
+ * dispatch sites LoomPrefill::RunKstore / RunResidual / RunSwiglu (engine/model/loom_prefill.hpp:1954-2110).
+ *   w        weight rows, 16-byte aligned, w_row_stride a multiple of 16 bytes (Q6_K: K window rows of a
+ *            multiple of 8 super-blocks, or padded rows);
+ *   x        f16 activations, 16-byte aligned, ldx >= K and a multiple of 8;
+ *   y        output; y_dtype YAH_F32 or YAH_F16 (YAH_EPI_RESID: f32; YAH_EPI_SWIGLU: f16); ldy >= N;
+ *   aux      f32 [M][ldaux] residual (YAH_EPI_RESID) or gate (YAH_EPI_SWIGLU), else NULL. */
+int yah_qgemm(const void* w, int ggml_type, int64_t N, int64_t K, int64_t w_row_stride, int64_t kb_off,
+              const void* x, int64_t M, int64_t ldx, void* y, int y_dtype, int64_t ldy, int epilogue,
+              const void* aux, int64_t ldaux, void* stream);
+
+/* yah_qgemm with an explicit tile choice (the tuner's knob set, engine/tune/tune.py:77):
+ *   bn    tokens per tile: 64, 128 or 256 (0 = default 256);
+ *   grid  persistent CTAs (0 = one per SM). Every legal choice gives identical results. */
+int yah_qgemm_tile(const void* w, int ggml_type, int64_t N, int64_t K, int64_t w_row_stride, int64_t kb_off,
+                   const void* x, int64_t M, int64_t ldx, void* y, int y_dtype, int64_t ldy, int epilogue,
+                   const void* aux, int64_t ldaux, int bn, int grid, void* stream);
+
+/* Decode GEMV, 1 <= M <= 32 tokens (replaces gen_gemv.py's gv_{plain,resid}_<fmt>_<M>_<K> kernels and the
+ * LoomDecoder::Gemv call site, engine/model/loom_decoder.hpp:415-439). Same layouts and alignment rules as
+ * yah_qgemm; epilogue YAH_EPI_STORE or YAH_EPI_RESID. Uses a library-owned per-device split-K workspace
+ * (allocated on first use, grown on demand), so concurrent calls on different streams of one device must not
+ * overlap. */
+int yah_qgemv(const void* w, int ggml_type, int64_t N, int64_t K, int64_t w_row_stride, int64_t kb_off,
+              const void* x, int64_t M, int64_t ldx, void* y, int y_dtype, int64_t ldy, int epilogue,
+              const void* aux, int64_t ldaux, void* stream);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* YAH_QGEMM_H_ */

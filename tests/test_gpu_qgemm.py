@@ -1,0 +1,150 @@
+"""Tile GEMM (tcgen05) vs the oracle's dequant-then-GEMM, through the C ABI.
+
+Tolerances (float64 oracle of f16-dequantised weights @ f16 activations, gemv_check.py:161-162):
+  f32 output:  max-abs <= 2e-2 and relative Frobenius <= 1e-3;
+  f16 output:  max-abs <= 2e-2 + half an f16 ulp of the reference value (the output rounding itself), and
+               relative Frobenius <= 1e-3.
+"""
+import os
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN
+
+pytestmark = pytest.mark.gpu
+FMTS = ["q8_0", "q4_k", "q6_k"]
+MAX_ABS, REL_FRO = 2e-2, 1e-3
+
+
+def check(O, y, ref, f16=False):
+    e = O.errors(y, ref)
+    assert e["finite"], e
+    assert e["rel_fro"] <= REL_FRO, e
+    if f16:
+        bound = MAX_ABS + O.f16_half_ulp(ref)
+        excess = np.abs(y.astype(np.float64) - ref) - bound
+        assert excess.max() <= 0, (e, float(excess.max()))
+    else:
+        assert e["max_abs"] <= MAX_ABS, e
+    return e
+
+
+@pytest.mark.parametrize("name", FMTS)
+def test_golden_gemm(pkg, F, O, dev, name):
+    z = np.load(os.path.join(GOLDEN, f"gemm_{name}.npz"))
+    t = F.type_of(name)
+    w, K, x = z["blocks"], int(z["K"]), z["x"]
+    y = pkg.ops.qgemm(dev, w, t, x, N=w.shape[0], K=K, out_dtype="f32")
+    check(O, y, z["y_f16w"])
+
+
+@pytest.mark.parametrize("name", FMTS)
+@pytest.mark.parametrize("M,N,K", [(1, 128, 256), (7, 320, 1024), (48, 1000, 2048), (300, 256, 4096),
+                                   (513, 384, 512)])
+def test_qgemm_shapes(pkg, F, O, dev, name, M, N, K):
+    t = F.type_of(name)
+    if F.row_bytes(t, K) % 16:
+        K = 2048  # Q6_K rows are 16-byte aligned only at multiples of 8 super-blocks (see test_q6k_unaligned_rows)
+    w = F.synth_weights(t, N, K, seed=M + N + K)
+    x = F.synth_activations(M, K, seed=M)
+    ref = O.gemm_ref(O.dequant_f16(t, w, N, K), x)
+    y = pkg.ops.qgemm(dev, w, t, x, N=N, K=K, out_dtype="f32")
+    check(O, y, ref)
+    y16 = pkg.ops.qgemm(dev, w, t, x, N=N, K=K, out_dtype="f16")
+    check(O, y16, ref, f16=True)
+
+
+@pytest.mark.parametrize("name", FMTS)
+def test_epilogues(pkg, F, O, dev, name):
+    t = F.type_of(name)
+    M, N, K = 40, 384, 1024
+    w = F.synth_weights(t, N, K, seed=5)
+    x = F.synth_activations(M, K, seed=6)
+    acc = O.gemm_ref(O.dequant_f16(t, w, N, K), x)
+    rng = np.random.default_rng(7)
+    resid = rng.standard_normal((M, N)).astype(np.float32) * 10
+    y = pkg.ops.qgemm(dev, w, t, x, N=N, K=K, kind="kres", aux=resid)
+    check(O, y, O.epilogue_ref(acc, 1, resid))
+    gate = rng.standard_normal((M, N)).astype(np.float32) * 3
+    ys = pkg.ops.qgemm(dev, w, t, x, N=N, K=K, kind="swiglu", aux=gate)
+    assert ys.dtype == np.float16
+    check(O, ys, O.epilogue_ref(acc, 2, gate), f16=True)
+
+
+@pytest.mark.parametrize("name", FMTS)
+def test_k_window_and_strides(pkg, F, O, dev, name):
+    """A K window of longer rows (KWIN) and padded activation / output strides (OSTRIDE-style)."""
+    t = F.type_of(name)
+    M, N, K, kb_off = 33, 256, 1024, 8   # Q6_K: 8 super-blocks keep the window 16-byte aligned
+    Kfull = K + 256 * kb_off + 1024
+    w = F.synth_weights(t, N, Kfull, seed=9)
+    x = F.synth_activations(M, K, seed=10)
+    ref = O.gemm_ref(O.dequant_f16(t, w, N, K, kb_off=kb_off), x)
+    y = pkg.ops.qgemm(dev, w, t, x, N=N, K=K, kb_off=kb_off, w_row_stride=w.shape[1])
+    check(O, y, ref)
+    # ldx > K and ldy > N through the raw pointer API
+    ldx, ldy = K + 64, N + 40
+    xp = np.zeros((M, ldx), np.float16)
+    xp[:, :K] = x
+    wd, xd = dev.upload(w), dev.upload(xp)
+    yd = dev.empty(M * ldy * 4).fill(0xFF)   # NaN sentinel: columns past N must stay untouched
+    pkg.ops.qgemm_ptr(wd.ptr, t, N, K, w.shape[1], kb_off, xd.ptr, M, ldx, yd.ptr, "f32", ldy)
+    dev.synchronize()
+    yy = yd.download(np.float32, (M, ldy))
+    check(O, yy[:, :N], ref)
+    assert np.isnan(yy[:, N:]).all()
+
+
+@pytest.mark.parametrize("bn", [64, 128, 256])
+@pytest.mark.parametrize("grid", [0, 1, 5, 37])
+def test_tile_choices_are_identical(pkg, F, O, dev, bn, grid):
+    """Every legal tile gives the same bits (the reference tuner's hash check, engine/tune/tune.py:13)."""
+    t = F.Q4_K
+    M, N, K = 300, 640, 2048
+    w = F.synth_weights(t, N, K, seed=1)
+    x = F.synth_activations(M, K, seed=2)
+    base = pkg.ops.qgemm(dev, w, t, x, N=N, K=K)
+    y = pkg.ops.qgemm(dev, w, t, x, N=N, K=K, bn=bn, grid=grid)
+    assert np.array_equal(y.view(np.uint32), base.view(np.uint32))
+    check(O, y, O.gemm_ref(O.dequant_f16(t, w, N, K), x))
+
+
+def test_row_shards_match_full(pkg, F, dev):
+    """Column-parallel shards (a row range of the GGUF tensor) give exactly the full GEMM's columns."""
+    t = F.Q4_K
+    M, N, K = 64, 768, 1024
+    w = F.synth_weights(t, N, K, seed=3)
+    x = F.synth_activations(M, K, seed=4)
+    full = pkg.ops.qgemm(dev, w, t, x, N=N, K=K)
+    parts = [pkg.ops.qgemm(dev, w[r:r + 192], t, x, N=192, K=K) for r in range(0, N, 192)]
+    assert np.array_equal(np.concatenate(parts, axis=1).view(np.uint32), full.view(np.uint32))
+
+
+@pytest.mark.parametrize("name", ["q4_k"])
+def test_full_size_config2_sampled(pkg, F, O, dev, name):
+    """BASELINE config 2 (Q4_K, M=2048, K=4096, N=14336) on the GPU, checked on a sample of 256 weight rows
+    against the oracle and on the whole output for finiteness."""
+    t = F.type_of(name)
+    M, N, K = 2048, 14336, 4096
+    w = F.synth_weights(t, N, K, seed=0)
+    x = F.synth_activations(M, K, seed=1)
+    y = pkg.ops.qgemm(dev, w, t, x, N=N, K=K, out_dtype="f16")
+    assert np.isfinite(y).all()
+    rows = np.random.default_rng(0).choice(N, 256, replace=False)
+    ref = O.gemm_ref(O.dequant_f16(t, w[rows], len(rows), K), x)
+    check(O, y[:, rows], ref, f16=True)
+
+
+def test_q6k_unaligned_rows_are_refused(pkg, F, dev):
+    """Q6_K rows that are not 16-byte aligned (K = 1280) are refused with YAH_ERR_UNSUPPORTED, not run."""
+    t = F.Q6_K
+    w = F.synth_weights(t, 128, 1280, seed=0)
+    x = F.synth_activations(4, 1280, seed=0)
+    with pytest.raises(pkg.YahError) as ei:
+        pkg.ops.qgemm(dev, w, t, x, N=128, K=1280)
+    assert ei.value.code == 2
+
+
+def test_status_word_clear(pkg, dev):
+    assert dev.status_word() == 0

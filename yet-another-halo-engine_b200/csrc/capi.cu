@@ -1,0 +1,404 @@
+// The C ABI of libyah_b200.so (declared in include/yah_qgemm.h): argument and footprint checks, per-device
+// state (SM count, the kernel status word, the GEMV split-K workspace), and the CUDA runtime wrappers that play
+// the role of the reference's LoomDevice (engine/model/loom_runtime.hpp:153-325). Every entry point returns a
+// status code; nothing throws across the boundary.
+#include <cuda_runtime.h>
+#include <stdarg.h>
+#include <stdio.h>
+
+#include <mutex>
+#include <string>
+
+#include "../../include/yah_qgemm.h"
+#include "kernels.h"
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(YAH_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+}
+
+#define CK(call)                                   \
+  do {                                             \
+    cudaError_t e_ = (call);                       \
+    if (e_ != cudaSuccess) return cuda_fail(e_, #call); \
+  } while (0)
+
+struct DevState {
+  bool ready = false;
+  int sms = 0;
+  int cc_major = 0, cc_minor = 0;
+  int* status = nullptr;  // device status word
+  float* ws = nullptr;    // GEMV split-K partials
+  size_t ws_bytes = 0;
+  int* counters = nullptr;
+  size_t counters_n = 0;
+};
+
+constexpr int kMaxDev = 64;
+DevState g_dev[kMaxDev];
+std::mutex g_mu;
+
+// State of the current device, created on first use (status word allocated and zeroed).
+int dev_state(DevState** out) {
+  int d = 0;
+  CK(cudaGetDevice(&d));
+  if (d < 0 || d >= kMaxDev) return fail(YAH_ERR_DEVICE, "device ordinal %d out of range", d);
+  std::lock_guard<std::mutex> lk(g_mu);
+  DevState& s = g_dev[d];
+  if (!s.ready) {
+    cudaDeviceProp prop;
+    CK(cudaGetDeviceProperties(&prop, d));
+    s.sms = prop.multiProcessorCount;
+    s.cc_major = prop.major;
+    s.cc_minor = prop.minor;
+    if (s.cc_major != 10) return fail(YAH_ERR_DEVICE, "device %d is sm_%d%d; this library is built for sm_100a", d,
+                                      s.cc_major, s.cc_minor);
+    if (!yah::tensor_map_encoder_available())
+      return fail(YAH_ERR_DEVICE, "the driver does not provide cuTensorMapEncodeTiled");
+    CK(cudaMalloc(&s.status, sizeof(int)));
+    CK(cudaMemset(s.status, 0, sizeof(int)));
+    s.ready = true;
+  }
+  *out = &s;
+  return YAH_OK;
+}
+
+int sb_bytes(int type) {
+  switch (type) {
+    case YAH_Q8_0: return 272;
+    case YAH_Q4_K: return 144;
+    case YAH_Q6_K: return 210;
+    default: return 0;
+  }
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+constexpr int64_t kMaxDim = (int64_t)1 << 30;
+
+// Shared checks of yah_qgemm / yah_qgemv.
+int check_linear(const void* w, int type, int64_t N, int64_t K, int64_t w_row_stride, int64_t kb_off, const void* x,
+                 int64_t M, int64_t ldx, const void* y, int y_dtype, int64_t ldy, int epilogue, const void* aux,
+                 int64_t ldaux) {
+  const int sb = sb_bytes(type);
+  if (!sb) return fail(YAH_ERR_UNSUPPORTED, "unsupported GGML type %d (supported: Q8_0=8, Q4_K=12, Q6_K=14)", type);
+  if (!w || !x || !y) return fail(YAH_ERR_ARG, "null weight, input or output pointer");
+  if (N < 1 || M < 1 || K < 256 || N > kMaxDim || M > kMaxDim || K > kMaxDim)
+    return fail(YAH_ERR_ARG, "bad shape N=%lld K=%lld M=%lld", (long long)N, (long long)K, (long long)M);
+  if (K % 256) return fail(YAH_ERR_ARG, "K=%lld is not a multiple of 256", (long long)K);
+  if (kb_off < 0) return fail(YAH_ERR_ARG, "negative kb_off");
+  if (w_row_stride < (kb_off + K / 256) * sb)
+    return fail(YAH_ERR_ARG, "w_row_stride %lld is shorter than the K window (%lld bytes)", (long long)w_row_stride,
+                (long long)((kb_off + K / 256) * sb));
+  if (!aligned16(w) || w_row_stride % 16)
+    return fail(YAH_ERR_UNSUPPORTED,
+                "weight rows must start 16-byte aligned (pointer %p, row stride %lld); Q6_K rows are aligned when "
+                "their super-block count is a multiple of 8",
+                w, (long long)w_row_stride);
+  if (!aligned16(x) || ldx < K || ldx % 8)
+    return fail(YAH_ERR_ARG, "activations must be 16-byte aligned with ldx >= K and ldx %% 8 == 0 (ldx=%lld)",
+                (long long)ldx);
+  if (ldy < N) return fail(YAH_ERR_ARG, "ldy %lld < N %lld", (long long)ldy, (long long)N);
+  if (y_dtype != YAH_F32 && y_dtype != YAH_F16) return fail(YAH_ERR_UNSUPPORTED, "y_dtype %d", y_dtype);
+  if (epilogue == YAH_EPI_RESID) {
+    if (!aux || ldaux < N) return fail(YAH_ERR_ARG, "YAH_EPI_RESID needs aux f32 [M][ldaux >= N]");
+    if (y_dtype != YAH_F32) return fail(YAH_ERR_UNSUPPORTED, "YAH_EPI_RESID writes f32");
+  } else if (epilogue == YAH_EPI_SWIGLU) {
+    if (!aux || ldaux < N) return fail(YAH_ERR_ARG, "YAH_EPI_SWIGLU needs aux f32 gate [M][ldaux >= N]");
+    if (y_dtype != YAH_F16) return fail(YAH_ERR_UNSUPPORTED, "YAH_EPI_SWIGLU writes f16");
+  } else if (epilogue != YAH_EPI_STORE) {
+    return fail(YAH_ERR_UNSUPPORTED, "epilogue %d", epilogue);
+  }
+  return YAH_OK;
+}
+
+int after_launch(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) return cuda_fail(e, what);
+  return YAH_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* yah_version(void) { return "yah_b200 0.1 (sm_100a)"; }
+
+const char* yah_last_error(void) { return g_err.c_str(); }
+
+int yah_block_elements(int t) { return t == YAH_Q8_0 ? 32 : (t == YAH_Q4_K || t == YAH_Q6_K) ? 256 : 0; }
+
+int yah_block_bytes(int t) { return t == YAH_Q8_0 ? 34 : t == YAH_Q4_K ? 144 : t == YAH_Q6_K ? 210 : 0; }
+
+int64_t yah_row_bytes(int t, int64_t K) {
+  const int be = yah_block_elements(t);
+  if (!be || K < 0 || K % be) return -1;
+  return K / be * yah_block_bytes(t);
+}
+
+int yah_device_count(int* count) {
+  if (!count) return fail(YAH_ERR_ARG, "null count");
+  CK(cudaGetDeviceCount(count));
+  return YAH_OK;
+}
+
+int yah_set_device(int device) {
+  CK(cudaSetDevice(device));
+  return YAH_OK;
+}
+
+int yah_get_device(int* device) {
+  if (!device) return fail(YAH_ERR_ARG, "null device");
+  CK(cudaGetDevice(device));
+  return YAH_OK;
+}
+
+int yah_device_info(int device, int* sm_count, int* cc_major, int* cc_minor, int64_t* total_mem) {
+  cudaDeviceProp prop;
+  CK(cudaGetDeviceProperties(&prop, device));
+  if (sm_count) *sm_count = prop.multiProcessorCount;
+  if (cc_major) *cc_major = prop.major;
+  if (cc_minor) *cc_minor = prop.minor;
+  if (total_mem) *total_mem = (int64_t)prop.totalGlobalMem;
+  return YAH_OK;
+}
+
+int yah_malloc(void** ptr, size_t bytes) {
+  if (!ptr) return fail(YAH_ERR_ARG, "null ptr");
+  CK(cudaMalloc(ptr, bytes));
+  return YAH_OK;
+}
+
+int yah_free(void* ptr) {
+  CK(cudaFree(ptr));
+  return YAH_OK;
+}
+
+int yah_host_alloc(void** ptr, size_t bytes) {
+  if (!ptr) return fail(YAH_ERR_ARG, "null ptr");
+  CK(cudaHostAlloc(ptr, bytes, cudaHostAllocDefault));
+  return YAH_OK;
+}
+
+int yah_host_free(void* ptr) {
+  CK(cudaFreeHost(ptr));
+  return YAH_OK;
+}
+
+int yah_memcpy_h2d(void* dst, const void* src, size_t bytes, void* stream) {
+  CK(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, (cudaStream_t)stream));
+  return YAH_OK;
+}
+
+int yah_memcpy_d2h(void* dst, const void* src, size_t bytes, void* stream) {
+  CK(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, (cudaStream_t)stream));
+  return YAH_OK;
+}
+
+int yah_memcpy_d2d(void* dst, const void* src, size_t bytes, void* stream) {
+  CK(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, (cudaStream_t)stream));
+  return YAH_OK;
+}
+
+int yah_memset(void* ptr, int value, size_t bytes, void* stream) {
+  CK(cudaMemsetAsync(ptr, value, bytes, (cudaStream_t)stream));
+  return YAH_OK;
+}
+
+int yah_stream_create(void** stream) {
+  if (!stream) return fail(YAH_ERR_ARG, "null stream");
+  cudaStream_t s;
+  CK(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
+  *stream = s;
+  return YAH_OK;
+}
+
+int yah_stream_destroy(void* stream) {
+  CK(cudaStreamDestroy((cudaStream_t)stream));
+  return YAH_OK;
+}
+
+int yah_stream_synchronize(void* stream) {
+  CK(cudaStreamSynchronize((cudaStream_t)stream));
+  return YAH_OK;
+}
+
+int yah_device_synchronize(void) {
+  CK(cudaDeviceSynchronize());
+  return YAH_OK;
+}
+
+int yah_event_create(void** event) {
+  if (!event) return fail(YAH_ERR_ARG, "null event");
+  cudaEvent_t e;
+  CK(cudaEventCreate(&e));
+  *event = e;
+  return YAH_OK;
+}
+
+int yah_event_destroy(void* event) {
+  CK(cudaEventDestroy((cudaEvent_t)event));
+  return YAH_OK;
+}
+
+int yah_event_record(void* event, void* stream) {
+  CK(cudaEventRecord((cudaEvent_t)event, (cudaStream_t)stream));
+  return YAH_OK;
+}
+
+int yah_event_synchronize(void* event) {
+  CK(cudaEventSynchronize((cudaEvent_t)event));
+  return YAH_OK;
+}
+
+int yah_event_elapsed_ms(void* start, void* end, float* ms) {
+  if (!ms) return fail(YAH_ERR_ARG, "null ms");
+  CK(cudaEventElapsedTime(ms, (cudaEvent_t)start, (cudaEvent_t)end));
+  return YAH_OK;
+}
+
+int yah_status_word(int* code) {
+  if (!code) return fail(YAH_ERR_ARG, "null code");
+  DevState* s;
+  int rc = dev_state(&s);
+  if (rc) return rc;
+  CK(cudaMemcpy(code, s->status, sizeof(int), cudaMemcpyDeviceToHost));
+  if (*code) CK(cudaMemset(s->status, 0, sizeof(int)));
+  return YAH_OK;
+}
+
+int yah_qgemm_footprint(int t, int64_t N, int64_t K, int64_t w_row_stride, int64_t kb_off, int64_t M, int64_t ldx,
+                        int y_dtype, int64_t ldy, int64_t* w_bytes, int64_t* x_bytes, int64_t* y_bytes) {
+  const int sb = sb_bytes(t);
+  if (!sb || K % 256 || N < 1 || M < 1) return fail(YAH_ERR_ARG, "bad footprint query");
+  if (w_bytes) *w_bytes = (N - 1) * w_row_stride + (kb_off + K / 256) * sb;
+  if (x_bytes) *x_bytes = ((M - 1) * ldx + K) * 2;
+  if (y_bytes) *y_bytes = ((M - 1) * ldy + N) * (y_dtype == YAH_F16 ? 2 : 4);
+  return YAH_OK;
+}
+
+int yah_dequant(const void* w, int t, int64_t rows, int64_t K, int64_t w_row_stride, int64_t kb_off, void* out,
+                int64_t ldo, void* stream) {
+  const int sb = sb_bytes(t);
+  if (!sb) return fail(YAH_ERR_UNSUPPORTED, "unsupported GGML type %d", t);
+  if (!w || !out) return fail(YAH_ERR_ARG, "null pointer");
+  if (rows < 1 || K < 256 || K % 256 || kb_off < 0) return fail(YAH_ERR_ARG, "bad shape rows=%lld K=%lld",
+                                                                 (long long)rows, (long long)K);
+  if (w_row_stride < (kb_off + K / 256) * sb) return fail(YAH_ERR_ARG, "w_row_stride shorter than the K window");
+  if ((reinterpret_cast<uintptr_t>(w) & 1) || (w_row_stride & 1))
+    return fail(YAH_ERR_ARG, "weight rows must be 2-byte aligned");
+  if (!aligned16(out) || ldo < K || ldo % 8) return fail(YAH_ERR_ARG, "out must be 16-byte aligned, ldo >= K, %% 8");
+  DevState* s;
+  int rc = dev_state(&s);
+  if (rc) return rc;
+  return after_launch(yah::launch_dequant(w, t, rows, K, w_row_stride, kb_off, static_cast<uint16_t*>(out), ldo,
+                                          s->sms, (cudaStream_t)stream),
+                      "dequant launch");
+}
+
+int yah_qgemm_tile(const void* w, int t, int64_t N, int64_t K, int64_t w_row_stride, int64_t kb_off, const void* x,
+                   int64_t M, int64_t ldx, void* y, int y_dtype, int64_t ldy, int epilogue, const void* aux,
+                   int64_t ldaux, int bn, int grid, void* stream) {
+  int rc = check_linear(w, t, N, K, w_row_stride, kb_off, x, M, ldx, y, y_dtype, ldy, epilogue, aux, ldaux);
+  if (rc) return rc;
+  if (bn == 0) bn = 256;
+  if (bn != 64 && bn != 128 && bn != 256) return fail(YAH_ERR_ARG, "bn must be 64, 128 or 256 (got %d)", bn);
+  if (grid < 0) return fail(YAH_ERR_ARG, "negative grid");
+  DevState* s;
+  rc = dev_state(&s);
+  if (rc) return rc;
+  yah::QGemmArgs a;
+  a.w = w;
+  a.type = t;
+  a.N = N;
+  a.K = K;
+  a.w_row_stride = w_row_stride;
+  a.kb_off = kb_off;
+  a.x = x;
+  a.M = M;
+  a.ldx = ldx;
+  a.y = y;
+  a.y_f16 = y_dtype == YAH_F16;
+  a.ldy = ldy;
+  a.epilogue = epilogue;
+  a.aux = static_cast<const float*>(aux);
+  a.ldaux = ldaux;
+  a.status = s->status;
+  a.num_sms = s->sms;
+  a.grid = grid > s->sms ? s->sms : grid;
+  a.bn = bn;
+  return after_launch(yah::launch_qgemm_tc(a, (cudaStream_t)stream), "qgemm launch");
+}
+
+int yah_qgemm(const void* w, int t, int64_t N, int64_t K, int64_t w_row_stride, int64_t kb_off, const void* x,
+              int64_t M, int64_t ldx, void* y, int y_dtype, int64_t ldy, int epilogue, const void* aux, int64_t ldaux,
+              void* stream) {
+  return yah_qgemm_tile(w, t, N, K, w_row_stride, kb_off, x, M, ldx, y, y_dtype, ldy, epilogue, aux, ldaux, 0, 0,
+                        stream);
+}
+
+int yah_qgemv(const void* w, int t, int64_t N, int64_t K, int64_t w_row_stride, int64_t kb_off, const void* x,
+              int64_t M, int64_t ldx, void* y, int y_dtype, int64_t ldy, int epilogue, const void* aux, int64_t ldaux,
+              void* stream) {
+  int rc = check_linear(w, t, N, K, w_row_stride, kb_off, x, M, ldx, y, y_dtype, ldy, epilogue, aux, ldaux);
+  if (rc) return rc;
+  if (M > 32) return fail(YAH_ERR_ARG, "yah_qgemv takes at most 32 tokens (M=%lld); use yah_qgemm", (long long)M);
+  if (epilogue == YAH_EPI_SWIGLU) return fail(YAH_ERR_UNSUPPORTED, "yah_qgemv: epilogue swiglu not provided");
+  DevState* s;
+  rc = dev_state(&s);
+  if (rc) return rc;
+  const int S = yah::qgemv_splits(N, K, s->sms);
+  if (S > 1) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    const size_t need = (size_t)S * M * N * sizeof(float);
+    const size_t nrb = (size_t)((N + 127) / 128);
+    if (need > s->ws_bytes) {
+      if (s->ws) CK(cudaFree(s->ws));
+      s->ws = nullptr;
+      s->ws_bytes = 0;
+      CK(cudaMalloc(&s->ws, need));
+      s->ws_bytes = need;
+    }
+    if (nrb > s->counters_n) {
+      if (s->counters) CK(cudaFree(s->counters));
+      s->counters = nullptr;
+      s->counters_n = 0;
+      CK(cudaMalloc(&s->counters, nrb * sizeof(int)));
+      CK(cudaMemset(s->counters, 0, nrb * sizeof(int)));
+      s->counters_n = nrb;
+    }
+  }
+  yah::QGemvArgs a;
+  a.w = w;
+  a.type = t;
+  a.N = N;
+  a.K = K;
+  a.w_row_stride = w_row_stride;
+  a.kb_off = kb_off;
+  a.x = x;
+  a.M = M;
+  a.ldx = ldx;
+  a.y = y;
+  a.y_f16 = y_dtype == YAH_F16;
+  a.ldy = ldy;
+  a.epilogue = epilogue;
+  a.aux = static_cast<const float*>(aux);
+  a.ldaux = ldaux;
+  a.status = s->status;
+  a.num_sms = s->sms;
+  return after_launch(yah::launch_qgemv_ws(a, s->ws, s->counters, S, (cudaStream_t)stream), "qgemv launch");
+}
+
+}  // extern "C"

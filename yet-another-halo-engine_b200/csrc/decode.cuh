@@ -1,0 +1,272 @@
+// Bit-exact decode of one 64-value K block of a GGUF super-block into 32 packed f16 pairs.
+//
+// Output convention (shared by every caller): out[c], c = 0..31, holds the values at K offsets 2c (low half) and
+// 2c + 1 (high half) of the 64-value block. This is also the TMEM layout of an A-operand stage for
+// tcgen05.mma kind::f16: one 32-bit column holds two consecutive K elements of a row.
+//
+// Arithmetic (reference: engine/gpu/loom/tools/gen_gemm_decode.py; every value is the f32 value of the
+// reference dequant rounded once to f16, bit-identical to gguf-py dequantize(...).astype(float16)):
+//   Q8_0 (:1338-1378)  w = f16(d * q). d * q is exact (11 x 8 bits), so one f16 multiply (mul.rn.f16x2) of the
+//                      exact f16 integer q gives the same single rounding.
+//   Q4_K (:837-1069)   w = f16(fma(d*sc, q, -dmin*m)). d*sc and dmin*m are exact in f32, d*sc*q is exact, so
+//                      the f32 fma rounds once and the f16 conversion once, exactly as gguf-py's d*q - dm.
+//                      q comes from a "magic float": (nibble << s) | 0x4B000000 is the float 2^23 + q*2^s, and
+//                      subtracting 2^23 leaves q*2^s exactly; the matching scale d*sc*2^-s is exact too.
+//   Q6_K (:1243-1335)  w = f16((d*sc) * (code - 32)). sc*(code - 32) is an integer of magnitude <= 1024, exact in
+//                      f16; fma.rn.f16x2(1024 + code, sc, -1056*sc) produces it exactly (1056*sc is an exact f16),
+//                      then one mul.rn.f16x2 by d rounds the exact product d*sc*(code-32) once.
+#pragma once
+#include "ptx.cuh"
+
+namespace yah {
+
+constexpr float kMagic23 = 8388608.0f;  // 2^23
+
+__device__ __forceinline__ float magic_q(uint32_t bits) { return __uint_as_float(bits | 0x4B000000u) - kMagic23; }
+
+__device__ __forceinline__ float h2f_bits(uint32_t h) { return __half2float(__ushort_as_half((unsigned short)h)); }
+
+// ------------------------------------------------------------------------------------------------ Q4_K
+// hdr: the 16-byte block header (d | dmin << 16, scales[0..11]); qs: the 32 qs bytes of K block j (qs[32j..32j+31]).
+__device__ __forceinline__ void q4k_scales(const uint4& hdr, int j, float& dsa, float& dma, float& dsb, float& dmb) {
+  const float d = h2f_bits(hdr.x & 0xFFFFu);
+  const float dmin = h2f_bits(hdr.x >> 16);
+  // groups 2j (low nibbles) and 2j + 1 (high nibbles); s = scales bytes, w1 = s0..3, w2 = s4..7, w3 = s8..11
+  int sc[2], m[2];
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const int g = 2 * j + u;
+    const int gg = g & 3;
+    const uint32_t b1 = (hdr.y >> (8 * gg)) & 0xFFu;
+    const uint32_t b2 = (hdr.z >> (8 * gg)) & 0xFFu;
+    const uint32_t b3 = (hdr.w >> (8 * gg)) & 0xFFu;
+    if (g < 4) {
+      sc[u] = b1 & 63;
+      m[u] = b2 & 63;
+    } else {
+      sc[u] = (b3 & 15) | ((b1 >> 6) << 4);
+      m[u] = (b3 >> 4) | ((b2 >> 6) << 4);
+    }
+  }
+  dsa = d * (float)sc[0];
+  dma = dmin * (float)m[0];
+  dsb = d * (float)sc[1];
+  dmb = dmin * (float)m[1];
+}
+
+__device__ __forceinline__ void q4k_decode_kblock(const uint4& hdr, const uint32_t (&qs)[8], int j,
+                                                  uint32_t (&out)[32]) {
+  float dsa, dma, dsb, dmb;
+  q4k_scales(hdr, j, dsa, dma, dsb, dmb);
+  const float a0 = dsa, a8 = dsa * 0.00390625f;        // group 2j scales for nibbles at bit 0 / bit 8
+  const float b4 = dsb * 0.0625f, b12 = dsb * 2.44140625e-4f;  // group 2j+1 scales for bit 4 / bit 12
+  const float na = -dma, nb = -dmb;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint32_t w = qs[i];
+    const uint32_t v = w >> 16;
+    // low nibbles (group 2j): bytes 0,1 -> column 2i; bytes 2,3 -> column 2i+1
+    const float l0 = __fmaf_rn(a0, magic_q(w & 0xFu), na);
+    const float l1 = __fmaf_rn(a8, magic_q(w & 0xF00u), na);
+    const float l2 = __fmaf_rn(a0, magic_q(v & 0xFu), na);
+    const float l3 = __fmaf_rn(a8, magic_q(v & 0xF00u), na);
+    // high nibbles (group 2j+1)
+    const float h0 = __fmaf_rn(b4, magic_q(w & 0xF0u), nb);
+    const float h1 = __fmaf_rn(b12, magic_q(w & 0xF000u), nb);
+    const float h2 = __fmaf_rn(b4, magic_q(v & 0xF0u), nb);
+    const float h3 = __fmaf_rn(b12, magic_q(v & 0xF000u), nb);
+    out[2 * i] = pack_f16x2_rn(l0, l1);
+    out[2 * i + 1] = pack_f16x2_rn(l2, l3);
+    out[16 + 2 * i] = pack_f16x2_rn(h0, h1);
+    out[16 + 2 * i + 1] = pack_f16x2_rn(h2, h3);
+  }
+}
+
+// ------------------------------------------------------------------------------------------------ Q8_0
+// W[0..16]: the 68 bytes of K block j (blocks 2j and 2j+1 of the 272-byte super-block), starting 4-byte aligned.
+__device__ __forceinline__ void q80_decode_kblock(const uint32_t (&W)[17], uint32_t (&out)[32]) {
+  const uint32_t dA = W[0] & 0xFFFFu;
+  const uint32_t dB = W[8] >> 16;
+  const uint32_t dA2 = dA | (dA << 16), dB2 = dB | (dB << 16);
+  constexpr uint32_t kBias = 0x64806480u;  // f16 (1152, 1152)
+#pragma unroll
+  for (int c = 0; c < 16; ++c) {
+    // block A value pair (2c, 2c+1) at region bytes 2 + 2c
+    const int wa = (1 + c) >> 1;
+    const uint32_t sela = (c & 1) ? 0x4140u : 0x4342u;
+    const uint32_t pa = prmt(W[wa] ^ 0x80808080u, 0x64646464u, sela);
+    out[c] = hmul2_u32(hsub2_u32(pa, kBias), dA2);
+    // block B value pair at region bytes 36 + 2c
+    const int wb = 9 + (c >> 1);
+    const uint32_t selb = (c & 1) ? 0x4342u : 0x4140u;
+    const uint32_t pb = prmt(W[wb] ^ 0x80808080u, 0x64646464u, selb);
+    out[16 + c] = hmul2_u32(hsub2_u32(pb, kBias), dB2);
+  }
+}
+
+// ------------------------------------------------------------------------------------------------ Q6_K
+// QL: ql bytes [64h, 64h+64); QH: qh bytes [32h, 32h+32); SC: the 4 int8 scales sc[8h + 4(j&1) ...]; dbits: d.
+// j = 2h + (j&1) is the K block within the super-block.
+// Arithmetic in f32, as the reference: ds = d * sc (exact), q = code - 32 (exact), w = f16(ds * q) with the
+// product exact (<= 23 bits) and IEEE zero signs identical to gguf-py's (d * scales) * q. The code byte is moved
+// to bits 16..21 of the magic float 2^23 (one prmt); subtracting 2^23 + 32 * 2^16 leaves (code - 32) * 2^16, and
+// the matching scale ds * 2^-16 is exact.
+__device__ __forceinline__ void q6k_decode_kblock(const uint32_t (&QL)[16], const uint32_t (&QH)[8], uint32_t SC,
+                                                  uint32_t dbits, int jodd, uint32_t (&out)[32]) {
+  const float d = h2f_bits(dbits & 0xFFFFu);
+  float ds[4];
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int s = (int)(int8_t)((SC >> (8 * u)) & 0xFFu);
+    ds[u] = (d * (float)s) * 1.52587890625e-05f;  // * 2^-16, exact
+  }
+  constexpr float kOff = 10485760.0f;  // 2^23 + 32 * 2^16
+  const int lsh = 4 * jodd;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const uint32_t lo4 = (QL[i] >> lsh) & 0x0F0F0F0Fu;
+    const uint32_t hi2 = (QH[i & 7] >> (lsh + 2 * (i >> 3))) & 0x03030303u;
+    const uint32_t code = lo4 | (hi2 << 4);
+    const float s = ds[i >> 2];
+    const float v0 = __fmul_rn(s, __uint_as_float(prmt(code, 0x4B000000u, 0x7044u)) - kOff);
+    const float v1 = __fmul_rn(s, __uint_as_float(prmt(code, 0x4B000000u, 0x7144u)) - kOff);
+    const float v2 = __fmul_rn(s, __uint_as_float(prmt(code, 0x4B000000u, 0x7244u)) - kOff);
+    const float v3 = __fmul_rn(s, __uint_as_float(prmt(code, 0x4B000000u, 0x7344u)) - kOff);
+    out[2 * i] = pack_f16x2_rn(v0, v1);
+    out[2 * i + 1] = pack_f16x2_rn(v2, v3);
+  }
+}
+
+// ------------------------------------------------------------------------------------------------ shared-memory
+// Readers of one weight row of a staged super-block (the tile GEMM's TMA weight stage). `rb` is the shared address
+// of the row's first staged byte (16-byte aligned).
+
+__device__ __forceinline__ void q4k_decode_smem(uint32_t rb, int j, uint32_t (&out)[32]) {
+  const uint4 hdr = lds128(rb);
+  const uint4 a = lds128(rb + 16 + 32 * j);
+  const uint4 b = lds128(rb + 32 + 32 * j);
+  const uint32_t qs[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+  q4k_decode_kblock(hdr, qs, j, out);
+}
+
+template <int J>
+__device__ __forceinline__ void q80_decode_smem_j(uint32_t rb, uint32_t (&out)[32]) {
+  uint32_t L[20];
+#pragma unroll
+  for (int c = 0; c < 5; ++c) {
+    const uint4 v = lds128(rb + 64 * J + 16 * c);
+    L[4 * c] = v.x;
+    L[4 * c + 1] = v.y;
+    L[4 * c + 2] = v.z;
+    L[4 * c + 3] = v.w;
+  }
+  uint32_t W[17];
+#pragma unroll
+  for (int i = 0; i < 17; ++i) W[i] = L[i + J];
+  q80_decode_kblock(W, out);
+}
+
+__device__ __forceinline__ void q80_decode_smem(uint32_t rb, int j, uint32_t (&out)[32]) {
+  switch (j) {
+    case 0: q80_decode_smem_j<0>(rb, out); break;
+    case 1: q80_decode_smem_j<1>(rb, out); break;
+    case 2: q80_decode_smem_j<2>(rb, out); break;
+    default: q80_decode_smem_j<3>(rb, out); break;
+  }
+}
+
+// Q6_K rows are staged as a 224-byte window starting at the 16-byte boundary at or below the super-block, which
+// then begins at byte o = 4*OW + 2*odd2 of the window (o even, 0..14). The row's stage slot is followed by at least
+// 16 readable bytes (the stage is padded), so the one-word over-read at the window's end stays in shared memory.
+template <int OW>
+__device__ __forceinline__ void q6k_decode_smem_o(uint32_t rb, int j, uint32_t sel, uint32_t (&out)[32]) {
+  const int h = j >> 1, jodd = j & 1;
+  uint32_t L[20];
+#pragma unroll
+  for (int c = 0; c < 5; ++c) {
+    const uint4 v = lds128(rb + 64 * h + 16 * c);
+    L[4 * c] = v.x;
+    L[4 * c + 1] = v.y;
+    L[4 * c + 2] = v.z;
+    L[4 * c + 3] = v.w;
+  }
+  uint32_t QL[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) QL[i] = prmt(L[OW + i], L[OW + i + 1], sel);
+  uint32_t M[12];
+#pragma unroll
+  for (int c = 0; c < 3; ++c) {
+    const uint4 v = lds128(rb + 128 + 32 * h + 16 * c);
+    M[4 * c] = v.x;
+    M[4 * c + 1] = v.y;
+    M[4 * c + 2] = v.z;
+    M[4 * c + 3] = v.w;
+  }
+  uint32_t QH[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) QH[i] = prmt(M[OW + i], M[OW + i + 1], sel);
+  const int ws = OW + 2 * h + jodd;  // word of the 4 scales, relative to byte 192
+  const uint32_t SC = prmt(lds32(rb + 192 + 4 * ws), lds32(rb + 196 + 4 * ws), sel);
+  const uint32_t D = prmt(lds32(rb + 208 + 4 * OW), lds32(rb + 212 + 4 * OW), sel);
+  q6k_decode_kblock(QL, QH, SC, D, jodd, out);
+}
+
+__device__ __forceinline__ void q6k_decode_smem(uint32_t rb, int j, int o, uint32_t (&out)[32]) {
+  const uint32_t sel = (o & 2) ? 0x5432u : 0x3210u;
+  switch (o >> 2) {
+    case 0: q6k_decode_smem_o<0>(rb, j, sel, out); break;
+    case 1: q6k_decode_smem_o<1>(rb, j, sel, out); break;
+    case 2: q6k_decode_smem_o<2>(rb, j, sel, out); break;
+    default: q6k_decode_smem_o<3>(rb, j, sel, out); break;
+  }
+}
+
+// ------------------------------------------------------------------------------------------------ global memory
+// A 32-bit little-endian word at a 2-byte aligned global address (read-only path).
+__device__ __forceinline__ uint32_t ldg_word2(const uint8_t* p) {
+  const unsigned short lo = __ldg(reinterpret_cast<const unsigned short*>(p));
+  const unsigned short hi = __ldg(reinterpret_cast<const unsigned short*>(p + 2));
+  return (uint32_t)lo | ((uint32_t)hi << 16);
+}
+
+// Decode K block j of the super-block at `sb` (global, 2-byte aligned) of format T.
+template <int T>
+__device__ __forceinline__ void decode_global(const uint8_t* sb, int j, uint32_t (&out)[32]);
+
+template <>
+__device__ __forceinline__ void decode_global<12>(const uint8_t* sb, int j, uint32_t (&out)[32]) {
+  uint4 hdr;
+  hdr.x = ldg_word2(sb);
+  hdr.y = ldg_word2(sb + 4);
+  hdr.z = ldg_word2(sb + 8);
+  hdr.w = ldg_word2(sb + 12);
+  uint32_t qs[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) qs[i] = ldg_word2(sb + 16 + 32 * j + 4 * i);
+  q4k_decode_kblock(hdr, qs, j, out);
+}
+
+template <>
+__device__ __forceinline__ void decode_global<8>(const uint8_t* sb, int j, uint32_t (&out)[32]) {
+  uint32_t W[17];
+#pragma unroll
+  for (int i = 0; i < 17; ++i) W[i] = ldg_word2(sb + 68 * j + 4 * i);
+  q80_decode_kblock(W, out);
+}
+
+template <>
+__device__ __forceinline__ void decode_global<14>(const uint8_t* sb, int j, uint32_t (&out)[32]) {
+  const int h = j >> 1, jodd = j & 1;
+  uint32_t QL[16], QH[8];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) QL[i] = ldg_word2(sb + 64 * h + 4 * i);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) QH[i] = ldg_word2(sb + 128 + 32 * h + 4 * i);
+  const uint32_t SC = ldg_word2(sb + 192 + 8 * h + 4 * jodd);
+  const uint32_t D = __ldg(reinterpret_cast<const unsigned short*>(sb + 208));
+  q6k_decode_kblock(QL, QH, SC, D, jodd, out);
+}
+
+__host__ __device__ constexpr int superblock_bytes(int T) { return T == 8 ? 272 : (T == 12 ? 144 : 210); }
+
+}  // namespace yah

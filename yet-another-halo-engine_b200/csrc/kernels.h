@@ -1,0 +1,63 @@
+// Internal launch interface between the C ABI (capi.cu) and the kernel translation units. Host-only types.
+// Every launcher assumes its arguments were validated by the C ABI and returns a cudaError_t.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace yah {
+
+enum Epilogue : int { kEpiStore = 0, kEpiResid = 1, kEpiSwiglu = 2 };
+
+// Tile-GEMM problem (token-major): y[M][ldy] (+)= x[M][ldx] (f16) * W[N][K]^T, W in GGUF rows.
+struct QGemmArgs {
+  const void* w;        // weight rows (GGUF block layout)
+  int type;             // GGML type id (8, 12, 14)
+  int64_t N, K;         // weight rows, reduction length (K window length)
+  int64_t w_row_stride; // bytes between weight rows
+  int64_t kb_off;       // first 256-element super-block of the K window within each row
+  const void* x;        // f16 activations [M][ldx]
+  int64_t M, ldx;
+  void* y;              // output [M][ldy], f32 or f16
+  int y_f16;            // 1: f16 output, 0: f32
+  int64_t ldy;
+  int epilogue;         // kEpiStore / kEpiResid / kEpiSwiglu
+  const float* aux;     // resid (kres) or gate (swiglu), f32 [M][ldaux]
+  int64_t ldaux;
+  int* status;          // device status word (bounded-wait failures)
+  int num_sms;          // SMs of the device
+  int grid;             // persistent CTAs (0: one per SM)
+  int bn;               // max tokens per tile (64, 128, 256)
+};
+
+cudaError_t launch_qgemm_tc(const QGemmArgs& a, cudaStream_t stream);
+
+// Standalone dequant: out[rows][ldo] f16 = decode(W).
+cudaError_t launch_dequant(const void* w, int type, int64_t rows, int64_t K, int64_t row_stride, int64_t kb_off,
+                           uint16_t* out, int64_t ldo, int num_sms, cudaStream_t stream);
+
+// Decode GEMV (M <= 32 tokens).
+struct QGemvArgs {
+  const void* w;
+  int type;
+  int64_t N, K, w_row_stride, kb_off;
+  const void* x;   // f16 [M][ldx]
+  int64_t M, ldx;
+  void* y;         // [M][ldy], f32 or f16
+  int y_f16;
+  int64_t ldy;
+  int epilogue;    // kEpiStore / kEpiResid
+  const float* aux;
+  int64_t ldaux;
+  int* status;
+  int num_sms;
+};
+
+// Split-K factor of a GEMV launch and the launcher (ws: [S][M][N] f32 partials, counters: one zeroed int per
+// 128-row block; both unused when S == 1).
+int qgemv_splits(int64_t N, int64_t K, int num_sms);
+cudaError_t launch_qgemv_ws(const QGemvArgs& a, float* ws, int* counters, int S, cudaStream_t stream);
+
+// Tensor-map encoder resolved from the driver at first use (no libcuda link dependency).
+bool tensor_map_encoder_available();
+
+}  // namespace yah

@@ -1,0 +1,415 @@
+// Quantised tile GEMM for sm_100a: GGUF Q8_0 / Q4_K / Q6_K weights x f16 activations, f32 accumulation in TMEM.
+//
+// Reference: engine/gpu/loom/tools/gen_gemm_tile.py (the tile GEMM, kinds kstore / kres / swiglu :309-322, store
+// :1229-1245) with the decoders of engine/gpu/loom/tools/gen_gemm_decode.py. Like the reference, the weight tile
+// is decoded inside the K loop to exactly the f16 values of the reference dequant, multiplied in f16 with f32
+// accumulation, and written token-major: out[t][r] at t * ldy + r (gen_gemm_tile.py:1230-1231).
+//
+// B200 design (one persistent CTA per SM, 14 warps):
+//   warp 0      TMA producer: raw super-blocks of 128 weight rows (one 256-K super-block per stage) and 64-K
+//               activation tiles (BN tokens x 128 B, 128-byte swizzle) into shared-memory rings.
+//   warp 1      MMA issuer (one thread): tcgen05.mma.cta_group::1.kind::f16, A (weights) from TMEM, B
+//               (activations) from shared memory, D (128 rows x up to 256 tokens, f32) in TMEM columns 0..255.
+//   warps 2-9   two dequant warpgroups (even / odd 64-K blocks). Thread = weight row (= TMEM lane). A thread
+//               decodes its row's 64 values to f16 pairs in registers and tcgen05.st's them into one of 8 A
+//               stages (TMEM columns 256..511): the dequantised tile never touches shared memory.
+//   warps 10-13 epilogue: tcgen05.ld of the accumulator, kstore / kres / swiglu, token-major global stores.
+// Tiles are 128 weight rows x up to BN tokens. The persistent schedule splits the (row tile, 16-token unit) space
+// into equal contiguous ranges per CTA, so every SM gets the same MMA work (no wave-quantisation tail).
+// Every mbarrier wait is bounded (ptx.cuh mbar_wait); on a timeout the kernel records a status code, drains its
+// own in-flight TMA copies and MMAs, frees TMEM and returns.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <mutex>
+
+#include "decode.cuh"
+#include "kernels.h"
+#include "ptx.cuh"
+
+namespace yah {
+namespace {
+
+constexpr int kThreads = 448;
+constexpr int kBM = 128;      // weight rows per tile = TMEM lanes
+constexpr int kNA = 8;        // A stages in TMEM
+constexpr int kAccCols = 256; // accumulator columns
+constexpr int kACol0 = 256;   // first A-stage column
+constexpr int kNSW = 2;       // weight super-block stages
+
+template <int T>
+struct Fmt;
+template <>
+struct Fmt<8> {  // Q8_0: 8 blocks of 34 B as one 272-B super-block
+  static constexpr int kSB = 272, kBox = 272;
+};
+template <>
+struct Fmt<12> {  // Q4_K
+  static constexpr int kSB = 144, kBox = 144;
+};
+template <>
+struct Fmt<14> {  // Q6_K: a 224-B window from the 16-B boundary at or below the super-block
+  static constexpr int kSB = 210, kBox = 224;
+};
+
+template <int BN>
+struct XCfg {
+  static constexpr int kNSX = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
+  static constexpr int kStage = BN * 128;  // BN rows x 64 f16
+};
+
+struct KParams {
+  int N, K, M, kb_off;
+  void* y;
+  int64_t ldy;
+  const float* aux;
+  int64_t ldaux;
+  int* status;
+  int64_t total_units;  // row tiles x 16-token units
+  int upr;              // 16-token units per row tile
+};
+
+template <int T, int BN>
+struct Smem {
+  static constexpr int kWStage = ((kBM * Fmt<T>::kBox + 16) + 127) / 128 * 128;
+  static constexpr int kXBytes = XCfg<BN>::kNSX * XCfg<BN>::kStage;
+  static constexpr int kWOff = kXBytes;
+  static constexpr int kBarOff = kWOff + kNSW * kWStage;
+  // barriers: xfull, xempty [NSX]; wfull, wempty [NSW]; afull, aempty [NA]; accfull, accempty; drain
+  static constexpr int kNumBars = 2 * XCfg<BN>::kNSX + 2 * kNSW + 2 * kNA + 3;
+  static constexpr int kTmemSlotOff = kBarOff + kNumBars * 8;
+  static constexpr int kBytes = kTmemSlotOff + 16;
+  static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-byte alignment of the base
+};
+
+// The persistent schedule: CTA b owns units [b * total / G, (b + 1) * total / G) of the (row tile, 16-token unit)
+// space, walked row tile by row tile, at most BN / 16 units per tile.
+template <int BN>
+struct Sched {
+  int64_t u, end;
+  int upr, M;
+  __device__ Sched(const KParams& p) : upr(p.upr), M(p.M) {
+    const int64_t G = gridDim.x, b = blockIdx.x;
+    u = b * p.total_units / G;
+    end = (b + 1) * p.total_units / G;
+  }
+  __device__ bool next(int& rt, int& t0, int& nt) {
+    if (u >= end) return false;
+    rt = (int)(u / upr);
+    const int tu = (int)(u % upr);
+    int nu = min(BN / 16, upr - tu);
+    if ((int64_t)nu > end - u) nu = (int)(end - u);
+    t0 = tu * 16;
+    nt = min(nu * 16, M - t0);
+    u += nu;
+    return true;
+  }
+};
+
+__device__ __forceinline__ float silu_f(float g) { return g / (1.0f + __expf(-g)); }
+
+template <int T, int BN, int EPI, bool OUT_F16>
+__global__ void __launch_bounds__(kThreads, 1)
+    qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
+                    const KParams p) {
+  using S = Smem<T, BN>;
+  constexpr int NSX = XCfg<BN>::kNSX;
+  constexpr int XST = XCfg<BN>::kStage;
+  constexpr int WBOX = Fmt<T>::kBox;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::kBarOff);
+  uint64_t* xfull = bars;
+  uint64_t* xempty = xfull + NSX;
+  uint64_t* wfull = xempty + NSX;
+  uint64_t* wempty = wfull + kNSW;
+  uint64_t* afull = wempty + kNSW;
+  uint64_t* aempty = afull + kNA;
+  uint64_t* accfull = aempty + kNA;
+  uint64_t* accempty = accfull + 1;
+  uint64_t* drain = accempty + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::kTmemSlotOff);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nkb = p.K / 64;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NSX; ++i) {
+      mbar_init(&xfull[i], 1);
+      mbar_init(&xempty[i], 1);
+    }
+    for (int i = 0; i < kNSW; ++i) {
+      mbar_init(&wfull[i], 1);
+      mbar_init(&wempty[i], 8);  // 4 warps x 2 dequant warpgroups
+    }
+    for (int i = 0; i < kNA; ++i) {
+      mbar_init(&afull[i], 4);
+      mbar_init(&aempty[i], 1);
+    }
+    mbar_init(accfull, 1);
+    mbar_init(accempty, 4);
+    mbar_init(drain, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmap_w);
+    tma_prefetch_desc(&tmap_x);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      Sched<BN> sc(p);
+      int rt, t0, nt;
+      uint32_t c = 0, cw = 0;  // activation / weight stages issued
+      bool ok = true;
+      while (ok && sc.next(rt, t0, nt)) {
+        for (int kb = 0; kb < nkb; ++kb, ++c) {
+          if ((kb & 3) == 0) {
+            const uint32_t sbc = c >> 2, ws = sbc % kNSW, wph = (sbc / kNSW) & 1;
+            if (!mbar_wait(&wempty[ws], wph ^ 1, p.status, kStatusTimeoutEmpty)) { ok = false; break; }
+            mbar_arrive_expect_tx(&wfull[ws], kBM * WBOX);
+            ++cw;
+            const int64_t sbg = (int64_t)p.kb_off + (kb >> 2);
+            int xw;
+            if (T == 14) xw = (int)(((sbg * 210) & ~int64_t(15)) >> 1);
+            else xw = (int)(sbg * (Fmt<T>::kSB / 2));
+            tma_load_2d(smem + S::kWOff + ws * S::kWStage, &tmap_w, &wfull[ws], xw, rt * kBM);
+          }
+          const uint32_t xs = c % NSX, xph = (c / NSX) & 1;
+          if (!mbar_wait(&xempty[xs], xph ^ 1, p.status, kStatusTimeoutEmpty)) { ok = false; break; }
+          mbar_arrive_expect_tx(&xfull[xs], XST);
+          tma_load_2d(smem + xs * XST, &tmap_x, &xfull[xs], kb * 64, t0);
+        }
+      }
+      // Drain: wait for the copies this thread issued last on every stage (no-ops on the normal path).
+      for (uint32_t i = (c > (uint32_t)NSX ? c - NSX : 0); i < c; ++i)
+        mbar_wait(&xfull[i % NSX], (i / NSX) & 1, p.status, kStatusTimeoutDrain, false);
+      for (uint32_t i = (cw > (uint32_t)kNSW ? cw - kNSW : 0); i < cw; ++i)
+        mbar_wait(&wfull[i % kNSW], (i / kNSW) & 1, p.status, kStatusTimeoutDrain, false);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      Sched<BN> sc(p);
+      int rt, t0, nt;
+      uint32_t c = 0, tcount = 0;
+      bool ok = true;
+      const uint32_t xbase = smem_u32(smem);
+      while (ok && sc.next(rt, t0, nt)) {
+        if (!mbar_wait(accempty, (tcount & 1) ^ 1, p.status, kStatusTimeoutEmpty)) break;
+        tc_fence_after();
+        const int nmma = (nt + 15) & ~15;
+        const uint32_t idesc = idesc_f16_f32(kBM, nmma);
+        for (int kb = 0; kb < nkb; ++kb, ++c) {
+          const uint32_t as = c % kNA, aph = (c / kNA) & 1;
+          const uint32_t xs = c % NSX, xph = (c / NSX) & 1;
+          if (!mbar_wait(&afull[as], aph, p.status, kStatusTimeoutFull)) { ok = false; break; }
+          if (!mbar_wait(&xfull[xs], xph, p.status, kStatusTimeoutFull)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t xa = xbase + xs * XST;
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks)
+            mma_f16_ts(tmem, tmem + kACol0 + as * 32 + ks * 8, sdesc_sw128(xa + ks * 32), idesc,
+                       (kb | ks) != 0);
+          mma_commit(&aempty[as]);
+          mma_commit(&xempty[xs]);
+        }
+        if (!ok) break;
+        mma_commit(accfull);
+        ++tcount;
+      }
+      // Drain: every MMA issued by this thread completes before TMEM is released.
+      mma_commit(drain);
+      mbar_wait(drain, 0, p.status, kStatusTimeoutDrain, false);
+    }
+  } else if (warp < 10) {
+    // ------------------------------------------------------------------ dequant warpgroups
+    const uint32_t wg = (warp - 2) >> 2;  // 0: even K blocks, 1: odd
+    const int q = warp & 3;               // TMEM lane quarter
+    const int r = q * 32 + lane;          // row within the tile
+    Sched<BN> sc(p);
+    int rt, t0, nt;
+    uint32_t c = 0;
+    bool ok = true;
+    const uint32_t wbase = smem_u32(smem + S::kWOff);
+    const uint32_t tl = tmem + ((uint32_t)(q * 32) << 16) + kACol0;
+    while (ok && sc.next(rt, t0, nt)) {
+      for (int kb = 0; kb < nkb; ++kb, ++c) {
+        if ((c & 1) != wg) continue;
+        const uint32_t sbc = c >> 2, ws = sbc % kNSW, wph = (sbc / kNSW) & 1;
+        const uint32_t as = c % kNA, aph = (c / kNA) & 1;
+        if (!mbar_wait(&wfull[ws], wph, p.status, kStatusTimeoutFull)) { ok = false; break; }
+        if (!mbar_wait(&aempty[as], aph ^ 1, p.status, kStatusTimeoutEmpty)) { ok = false; break; }
+        const int j = kb & 3;
+        const uint32_t rb = wbase + ws * S::kWStage + r * WBOX;
+        uint32_t v[32];
+        if (T == 12) {
+          q4k_decode_smem(rb, j, v);
+        } else if (T == 8) {
+          q80_decode_smem(rb, j, v);
+        } else {
+          const int o = (int)((((int64_t)p.kb_off + (kb >> 2)) * 210) & 15);
+          q6k_decode_smem(rb, j, o, v);
+        }
+        if (j >= 2) {  // this warpgroup's last read of the weight stage
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&wempty[ws]);
+        }
+        tmem_st32(tl + as * 32, v);
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&afull[as]);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue
+    const int q = warp & 3;
+    Sched<BN> sc(p);
+    int rt, t0, nt;
+    uint32_t tcount = 0;
+    const uint32_t tl = tmem + ((uint32_t)(q * 32) << 16);
+    while (sc.next(rt, t0, nt)) {
+      if (!mbar_wait(accfull, tcount & 1, p.status, kStatusTimeoutFull)) break;
+      tc_fence_after();
+      const int row = rt * kBM + q * 32 + lane;
+      const bool row_ok = row < p.N;
+      for (int j0 = 0; j0 < nt; j0 += 32) {
+        uint32_t v[32];
+        tmem_ld32(tl + j0, v);
+        tmem_wait_ld();
+        if (row_ok) {
+          const int jn = min(32, nt - j0);
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj) {
+            if (jj >= jn) break;
+            const int64_t t = t0 + j0 + jj;
+            float acc = __uint_as_float(v[jj]);
+            if (EPI == kEpiResid) acc += __ldg(p.aux + t * p.ldaux + row);
+            if (EPI == kEpiSwiglu) acc = silu_f(__ldg(p.aux + t * p.ldaux + row)) * acc;
+            if (OUT_F16)
+              reinterpret_cast<__half*>(p.y)[t * p.ldy + row] = __float2half_rn(acc);
+            else
+              reinterpret_cast<float*>(p.y)[t * p.ldy + row] = acc;
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(accempty);
+      ++tcount;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ------------------------------------------------------------------------------------------------ host side
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encoder() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+template <int T, int BN, int EPI, bool OUT_F16>
+cudaError_t launch_t(const QGemmArgs& a, cudaStream_t stream) {
+  using S = Smem<T, BN>;
+  EncodeTiledFn enc = encoder();
+  if (!enc) return cudaErrorNotSupported;
+  CUtensorMap mw, mx;
+  {
+    const int64_t window_bytes = (a.kb_off + a.K / 256) * Fmt<T>::kSB;
+    cuuint64_t dims[2] = {(cuuint64_t)((window_bytes + 1) / 2), (cuuint64_t)a.N};
+    cuuint64_t strides[1] = {(cuuint64_t)a.w_row_stride};
+    cuuint32_t box[2] = {(cuuint32_t)(Fmt<T>::kBox / 2), (cuuint32_t)kBM};
+    cuuint32_t es[2] = {1, 1};
+    if (enc(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(a.w), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return cudaErrorInvalidValue;
+  }
+  {
+    cuuint64_t dims[2] = {(cuuint64_t)a.K, (cuuint64_t)a.M};
+    cuuint64_t strides[1] = {(cuuint64_t)a.ldx * 2};
+    cuuint32_t box[2] = {64, (cuuint32_t)BN};
+    cuuint32_t es[2] = {1, 1};
+    if (enc(&mx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(a.x), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return cudaErrorInvalidValue;
+  }
+  KParams p;
+  p.N = (int)a.N;
+  p.K = (int)a.K;
+  p.M = (int)a.M;
+  p.kb_off = (int)a.kb_off;
+  p.y = a.y;
+  p.ldy = a.ldy;
+  p.aux = a.aux;
+  p.ldaux = a.ldaux;
+  p.status = a.status;
+  p.upr = (int)((a.M + 15) / 16);
+  const int64_t rtiles = (a.N + kBM - 1) / kBM;
+  p.total_units = rtiles * p.upr;
+  int grid = a.grid > 0 ? a.grid : a.num_sms;
+  if (grid > p.total_units) grid = (int)p.total_units;
+  auto kern = qgemm_tc_kernel<T, BN, EPI, OUT_F16>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kAlloc);
+  if (e != cudaSuccess) return e;
+  kern<<<grid, kThreads, S::kAlloc, stream>>>(mw, mx, p);
+  return cudaGetLastError();
+}
+
+template <int T, int BN>
+cudaError_t launch_bn(const QGemmArgs& a, cudaStream_t s) {
+  if (a.epilogue == kEpiResid) return launch_t<T, BN, kEpiResid, false>(a, s);
+  if (a.epilogue == kEpiSwiglu) return launch_t<T, BN, kEpiSwiglu, true>(a, s);
+  return a.y_f16 ? launch_t<T, BN, kEpiStore, true>(a, s) : launch_t<T, BN, kEpiStore, false>(a, s);
+}
+
+template <int T>
+cudaError_t launch_fmt(const QGemmArgs& a, cudaStream_t s) {
+  if (a.bn == 128) return launch_bn<T, 128>(a, s);
+  if (a.bn == 64) return launch_bn<T, 64>(a, s);
+  return launch_bn<T, 256>(a, s);
+}
+
+}  // namespace
+
+bool tensor_map_encoder_available() { return encoder() != nullptr; }
+
+cudaError_t launch_qgemm_tc(const QGemmArgs& a, cudaStream_t stream) {
+  switch (a.type) {
+    case 8: return launch_fmt<8>(a, stream);
+    case 12: return launch_fmt<12>(a, stream);
+    case 14: return launch_fmt<14>(a, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace yah

@@ -1,0 +1,138 @@
+"""The quantised-linear operator, host side: the reference's kernel kinds over the C ABI.
+
+Reference interface mirrored here:
+  * tile GEMM kinds kstore / kres / swiglu (engine/gpu/loom/tools/gen_gemm_tile.py:309-322) dispatched by
+    LoomPrefill::RunKstore / RunResidual / RunSwiglu (engine/model/loom_prefill.hpp:1954-2110): qgemm();
+  * decode GEMV kinds plain / resid (engine/gpu/loom/tools/gen_gemv.py:16-19, LoomDecoder::Gemv
+    engine/model/loom_decoder.hpp:415-439): qgemv();
+  * the dequant kind (gen_gemm_tile.py:314-327): dequant().
+Layouts: weights are GGUF rows [N][row bytes]; activations x f16 [M][K]; outputs token-major [M][N].
+Arguments are checked twice: the footprint rule here refuses buffers smaller than the call touches (the
+reference's hal_run refuses small bindings, engine/run/hal_run.cc:107-111), and the C ABI checks shapes,
+alignment and kinds. Every call runs on the GPU; a missing library raises.
+
+Two calling forms:
+  *_ptr(...)  raw device pointers (the form the tensor-parallel layer, the tuner and bench.py use);
+  qgemm(dev, w, fmt, x, ...) numpy in / numpy out convenience (uploads, runs, downloads, synchronises).
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+
+from . import formats as F
+from ._lib import EPI_RESID, EPI_STORE, EPI_SWIGLU, F16, F32, check, lib
+from .device import Device, DeviceBuffer
+
+KINDS = {"kstore": EPI_STORE, "store": EPI_STORE, "plain": EPI_STORE, "kres": EPI_RESID, "resid": EPI_RESID,
+         "swiglu": EPI_SWIGLU}
+DTYPES = {"f32": F32, "float32": F32, "f16": F16, "float16": F16}
+
+
+def _epi(kind) -> int:
+    if isinstance(kind, int):
+        return kind
+    if kind not in KINDS:
+        raise ValueError(f"unknown kind {kind!r} (kstore, kres, swiglu)")
+    return KINDS[kind]
+
+
+def _dt(dtype) -> int:
+    if isinstance(dtype, int):
+        return dtype
+    return DTYPES[str(np.dtype(dtype)) if not isinstance(dtype, str) else dtype]
+
+
+def footprint(fmt, N, K, w_row_stride, kb_off, M, ldx, y_dtype, ldy):
+    """(weight, input, output) bytes a call touches (yah_qgemm_footprint)."""
+    wb, xb, yb = ctypes.c_int64(), ctypes.c_int64(), ctypes.c_int64()
+    check(lib().yah_qgemm_footprint(F.type_of(fmt), N, K, w_row_stride, kb_off, M, ldx, _dt(y_dtype), ldy,
+                                    ctypes.byref(wb), ctypes.byref(xb), ctypes.byref(yb)))
+    return wb.value, xb.value, yb.value
+
+
+# ----------------------------------------------------------------------------------------------- raw pointers
+def qgemm_ptr(w, fmt, N, K, w_row_stride, kb_off, x, M, ldx, y, y_dtype, ldy, kind="kstore", aux=None, ldaux=0,
+              stream=None, bn=0, grid=0):
+    check(lib().yah_qgemm_tile(w, F.type_of(fmt), N, K, w_row_stride, kb_off, x, M, ldx, y, _dt(y_dtype), ldy,
+                               _epi(kind), aux, ldaux, bn, grid, stream))
+
+
+def qgemv_ptr(w, fmt, N, K, w_row_stride, kb_off, x, M, ldx, y, y_dtype, ldy, kind="plain", aux=None, ldaux=0,
+              stream=None):
+    check(lib().yah_qgemv(w, F.type_of(fmt), N, K, w_row_stride, kb_off, x, M, ldx, y, _dt(y_dtype), ldy, _epi(kind),
+                          aux, ldaux, stream))
+
+
+def dequant_ptr(w, fmt, rows, K, w_row_stride, kb_off, out, ldo, stream=None):
+    check(lib().yah_dequant(w, F.type_of(fmt), rows, K, w_row_stride, kb_off, out, ldo, stream))
+
+
+# ----------------------------------------------------------------------------------------------- numpy helpers
+def _as_dev(dev: Device, a):
+    if isinstance(a, DeviceBuffer):
+        return a
+    return dev.upload(np.ascontiguousarray(a))
+
+
+def _check_size(buf: DeviceBuffer, need: int, what: str):
+    if buf.nbytes < need:
+        raise ValueError(f"{what} buffer has {buf.nbytes} bytes, the call touches {need}")
+
+
+def qgemm(dev: Device, w, fmt, x, N=None, K=None, kind="kstore", out_dtype="f32", aux=None, kb_off=0,
+          w_row_stride=None, bn=0, grid=0, gemv=False):
+    """y[M][N] = kind(x @ W^T) on the GPU; w: uint8 GGUF rows (numpy or DeviceBuffer), x: f16 [M][K] numpy."""
+    t = F.type_of(fmt)
+    x = np.ascontiguousarray(x, dtype=np.float16)
+    M = x.shape[0]
+    K = K if K is not None else x.shape[1]
+    if w_row_stride is None:
+        w_row_stride = (w.shape[1] if isinstance(w, np.ndarray) else F.row_bytes(t, K + 256 * kb_off))
+    N = N if N is not None else (w.shape[0] if isinstance(w, np.ndarray) else None)
+    ep = _epi(kind)
+    if ep == EPI_SWIGLU:
+        out_dtype = "f16"
+    if ep == EPI_RESID:
+        out_dtype = "f32"
+    ydt = _dt(out_dtype)
+    wb, xb, yb = footprint(t, N, K, w_row_stride, kb_off, M, x.shape[1], ydt, N)
+    wd = _as_dev(dev, w)
+    _check_size(wd, wb, "weight")
+    xd = dev.upload(x)
+    yd = dev.empty(yb)
+    auxd = None
+    if ep != EPI_STORE:
+        auxd = dev.upload(np.ascontiguousarray(aux, dtype=np.float32))
+        _check_size(auxd, M * N * 4, "aux")
+    fn = qgemv_ptr if gemv else qgemm_ptr
+    kw = {} if gemv else {"bn": bn, "grid": grid}
+    fn(wd.ptr, t, N, K, w_row_stride, kb_off, xd.ptr, M, x.shape[1], yd.ptr, ydt, N, ep,
+       auxd.ptr if auxd else None, N if auxd else 0, **kw)
+    dev.synchronize()
+    y = yd.download(np.float16 if ydt == F16 else np.float32, (M, N))
+    code = dev.status_word()
+    if code:
+        raise RuntimeError(f"kernel reported bounded-wait failure code {code}")
+    return y
+
+
+def qgemv(dev: Device, w, fmt, x, N=None, K=None, kind="plain", out_dtype="f32", aux=None, kb_off=0,
+          w_row_stride=None):
+    """Decode GEMV for M <= 32 tokens: same arguments as qgemm (kinds plain / resid)."""
+    return qgemm(dev, w, fmt, x, N=N, K=K, kind=kind, out_dtype=out_dtype, aux=aux, kb_off=kb_off,
+                 w_row_stride=w_row_stride, gemv=True)
+
+
+def dequant(dev: Device, w, fmt, N=None, K=None, kb_off=0, w_row_stride=None) -> np.ndarray:
+    """f16 [N][K] of GGUF rows w with the GEMM's decode (bit-exact to the reference dequant)."""
+    t = F.type_of(fmt)
+    if w_row_stride is None:
+        w_row_stride = w.shape[1]
+    N = N if N is not None else w.shape[0]
+    wd = _as_dev(dev, w)
+    out = dev.empty(N * K * 2)
+    dequant_ptr(wd.ptr, t, N, K, w_row_stride, kb_off, out.ptr, K)
+    dev.synchronize()
+    return out.download(np.float16, (N, K))
