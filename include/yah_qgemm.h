@@ -124,11 +124,16 @@ int yah_qgemm(const void* w, int ggml_type, int64_t N, int64_t K, int64_t w_row_
               const void* aux, int64_t ldaux, void* stream);
 
 /* yah_qgemm with an explicit tile choice (the tuner's knob set, engine/tune/tune.py:77):
- *   bn    tokens per tile: 64, 128 or 256 (0 = default 256);
- *   grid  persistent CTAs (0 = one per SM). Every legal choice gives identical results. */
+ *   bn      tokens per tile: 64, 128 or 192 (0 = default 192);
+ *   grid    persistent CTAs (0 = one per SM);
+ *   kchunk  K per f32 accumulation chunk, a multiple of 64 (0 = auto: 2048 when K > 4096, else all of K;
+ *           -1 = never chunk). Chunk results are summed in f32 round-to-nearest; see the accuracy note in
+ *           csrc/qgemm_tc.cu. Chunking uses a library-owned per-device scratch buffer (grid * bn * 512 bytes),
+ *           so chunked calls on different streams of one device must not overlap.
+ * Every (bn, grid) choice gives identical results for a given kchunk. */
 int yah_qgemm_tile(const void* w, int ggml_type, int64_t N, int64_t K, int64_t w_row_stride, int64_t kb_off,
                    const void* x, int64_t M, int64_t ldx, void* y, int y_dtype, int64_t ldy, int epilogue,
-                   const void* aux, int64_t ldaux, int bn, int grid, void* stream);
+                   const void* aux, int64_t ldaux, int bn, int grid, int64_t kchunk, void* stream);
 
 /* Decode GEMV, 1 <= M <= 32 tokens (replaces gen_gemv.py's gv_{plain,resid}_<fmt>_<M>_<K> kernels and the
  * LoomDecoder::Gemv call site, engine/model/loom_decoder.hpp:415-439). Same layouts and alignment rules as

@@ -35,6 +35,10 @@ def test_golden_gemm(pkg, F, O, dev, name):
     z = np.load(os.path.join(GOLDEN, f"gemm_{name}.npz"))
     t = F.type_of(name)
     w, K, x = z["blocks"], int(z["K"]), z["x"]
+    if w.shape[1] % 16:  # Q6_K at K=512: pad the rows to a 16-byte stride (same bytes, aligned view)
+        wp = np.zeros((w.shape[0], (w.shape[1] + 15) // 16 * 16), np.uint8)
+        wp[:, :w.shape[1]] = w
+        w = wp
     y = pkg.ops.qgemm(dev, w, t, x, N=w.shape[0], K=K, out_dtype="f32")
     check(O, y, z["y_f16w"])
 
@@ -58,7 +62,7 @@ def test_qgemm_shapes(pkg, F, O, dev, name, M, N, K):
 @pytest.mark.parametrize("name", FMTS)
 def test_epilogues(pkg, F, O, dev, name):
     t = F.type_of(name)
-    M, N, K = 40, 384, 1024
+    M, N, K = 40, 384, 2048
     w = F.synth_weights(t, N, K, seed=5)
     x = F.synth_activations(M, K, seed=6)
     acc = O.gemm_ref(O.dequant_f16(t, w, N, K), x)
@@ -96,18 +100,34 @@ def test_k_window_and_strides(pkg, F, O, dev, name):
     assert np.isnan(yy[:, N:]).all()
 
 
-@pytest.mark.parametrize("bn", [64, 128, 256])
+@pytest.mark.parametrize("bn", [64, 128, 192])
 @pytest.mark.parametrize("grid", [0, 1, 5, 37])
-def test_tile_choices_are_identical(pkg, F, O, dev, bn, grid):
-    """Every legal tile gives the same bits (the reference tuner's hash check, engine/tune/tune.py:13)."""
+@pytest.mark.parametrize("kchunk", [-1, 512])
+def test_tile_choices_are_identical(pkg, F, O, dev, bn, grid, kchunk):
+    """Every legal tile gives the same bits for a given accumulation chunk (the reference tuner's hash check,
+    engine/tune/tune.py:13)."""
     t = F.Q4_K
     M, N, K = 300, 640, 2048
     w = F.synth_weights(t, N, K, seed=1)
     x = F.synth_activations(M, K, seed=2)
-    base = pkg.ops.qgemm(dev, w, t, x, N=N, K=K)
-    y = pkg.ops.qgemm(dev, w, t, x, N=N, K=K, bn=bn, grid=grid)
+    base = pkg.ops.qgemm(dev, w, t, x, N=N, K=K, kchunk=kchunk)
+    y = pkg.ops.qgemm(dev, w, t, x, N=N, K=K, bn=bn, grid=grid, kchunk=kchunk)
     assert np.array_equal(y.view(np.uint32), base.view(np.uint32))
     check(O, y, O.gemm_ref(O.dequant_f16(t, w, N, K), x))
+
+
+@pytest.mark.parametrize("kchunk", [64, 256, 1088, 2048])
+def test_chunked_accumulation(pkg, F, O, dev, kchunk):
+    """Chunked accumulation (chunk sums added in f32 round-to-nearest) matches the oracle for any chunk length,
+    including chunks that do not divide K, with every epilogue."""
+    t = F.Q4_K
+    M, N, K = 200, 384, 4096
+    w = F.synth_weights(t, N, K, seed=8)
+    x = F.synth_activations(M, K, seed=9)
+    acc = O.gemm_ref(O.dequant_f16(t, w, N, K), x)
+    check(O, pkg.ops.qgemm(dev, w, t, x, N=N, K=K, kchunk=kchunk), acc)
+    resid = np.random.default_rng(1).standard_normal((M, N)).astype(np.float32)
+    check(O, pkg.ops.qgemm(dev, w, t, x, N=N, K=K, kind="kres", aux=resid, kchunk=kchunk), acc + resid)
 
 
 def test_row_shards_match_full(pkg, F, dev):
@@ -119,6 +139,20 @@ def test_row_shards_match_full(pkg, F, dev):
     full = pkg.ops.qgemm(dev, w, t, x, N=N, K=K)
     parts = [pkg.ops.qgemm(dev, w[r:r + 192], t, x, N=192, K=K) for r in range(0, N, 192)]
     assert np.array_equal(np.concatenate(parts, axis=1).view(np.uint32), full.view(np.uint32))
+
+
+@pytest.mark.parametrize("name", FMTS)
+def test_config3_k_sampled(pkg, F, O, dev, name):
+    """The config 3 reduction length (K = 14336, N = 4096, M = 2048) on a sample of 128 weight rows: the longest
+    f32 accumulation of the benchmark configurations stays within the bar."""
+    t = F.type_of(name)
+    M, N, K = 2048, 4096, 14336
+    w = F.synth_weights(t, N, K, seed=2)
+    x = F.synth_activations(M, K, seed=3)
+    y = pkg.ops.qgemm(dev, w, t, x, N=N, K=K)
+    rows = np.random.default_rng(1).choice(N, 128, replace=False)
+    e = check(O, y[:, rows], O.gemm_ref(O.dequant_f16(t, w[rows], len(rows), K), x))
+    print(f"config3 {name}: {e}")
 
 
 @pytest.mark.parametrize("name", ["q4_k"])

@@ -50,7 +50,7 @@ SYMBOLS = {
     "yah_qgemm": (c_int, [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_int, c_i64, c_int,
                           c_vp, c_i64, c_vp]),
     "yah_qgemm_tile": (c_int, [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_int, c_i64,
-                               c_int, c_vp, c_i64, c_int, c_int, c_vp]),
+                               c_int, c_vp, c_i64, c_int, c_int, c_i64, c_vp]),
     "yah_qgemv": (c_int, [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_int, c_i64, c_int,
                           c_vp, c_i64, c_vp]),
 }

@@ -45,7 +45,21 @@ struct DevState {
   size_t ws_bytes = 0;
   int* counters = nullptr;
   size_t counters_n = 0;
+  float* gemm_scratch = nullptr;  // chunked-accumulation sums of the tile GEMM
+  size_t gemm_scratch_bytes = 0;
 };
+
+// Grow a per-device buffer to at least `need` bytes (cudaFree synchronises the device, so no launch still uses
+// the old one).
+int grow(void** buf, size_t* have, size_t need) {
+  if (need <= *have) return YAH_OK;
+  if (*buf) CK(cudaFree(*buf));
+  *buf = nullptr;
+  *have = 0;
+  CK(cudaMalloc(buf, need));
+  *have = need;
+  return YAH_OK;
+}
 
 constexpr int kMaxDev = 64;
 DevState g_dev[kMaxDev];
@@ -310,12 +324,15 @@ int yah_dequant(const void* w, int t, int64_t rows, int64_t K, int64_t w_row_str
 
 int yah_qgemm_tile(const void* w, int t, int64_t N, int64_t K, int64_t w_row_stride, int64_t kb_off, const void* x,
                    int64_t M, int64_t ldx, void* y, int y_dtype, int64_t ldy, int epilogue, const void* aux,
-                   int64_t ldaux, int bn, int grid, void* stream) {
+                   int64_t ldaux, int bn, int grid, int64_t kchunk, void* stream) {
   int rc = check_linear(w, t, N, K, w_row_stride, kb_off, x, M, ldx, y, y_dtype, ldy, epilogue, aux, ldaux);
   if (rc) return rc;
-  if (bn == 0) bn = 256;
-  if (bn != 64 && bn != 128 && bn != 256) return fail(YAH_ERR_ARG, "bn must be 64, 128 or 256 (got %d)", bn);
+  if (bn == 0) bn = 192;
+  if (bn != 64 && bn != 128 && bn != 192) return fail(YAH_ERR_ARG, "bn must be 64, 128 or 192 (got %d)", bn);
   if (grid < 0) return fail(YAH_ERR_ARG, "negative grid");
+  if (kchunk == 0) kchunk = K > 4096 ? 2048 : K;  // see the accuracy note in qgemm_tc.cu
+  if (kchunk < 0 || kchunk >= K) kchunk = K;
+  if (kchunk % 64) return fail(YAH_ERR_ARG, "kchunk %lld is not a multiple of 64", (long long)kchunk);
   DevState* s;
   rc = dev_state(&s);
   if (rc) return rc;
@@ -339,13 +356,22 @@ int yah_qgemm_tile(const void* w, int t, int64_t N, int64_t K, int64_t w_row_str
   a.num_sms = s->sms;
   a.grid = grid > s->sms ? s->sms : grid;
   a.bn = bn;
+  a.kchunk = kchunk;
+  a.scratch = nullptr;
+  if (kchunk < K) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    const size_t need = (size_t)yah::qgemm_grid(a) * bn * 128 * sizeof(float);
+    rc = grow(reinterpret_cast<void**>(&s->gemm_scratch), &s->gemm_scratch_bytes, need);
+    if (rc) return rc;
+    a.scratch = s->gemm_scratch;
+  }
   return after_launch(yah::launch_qgemm_tc(a, (cudaStream_t)stream), "qgemm launch");
 }
 
 int yah_qgemm(const void* w, int t, int64_t N, int64_t K, int64_t w_row_stride, int64_t kb_off, const void* x,
               int64_t M, int64_t ldx, void* y, int y_dtype, int64_t ldy, int epilogue, const void* aux, int64_t ldaux,
               void* stream) {
-  return yah_qgemm_tile(w, t, N, K, w_row_stride, kb_off, x, M, ldx, y, y_dtype, ldy, epilogue, aux, ldaux, 0, 0,
+  return yah_qgemm_tile(w, t, N, K, w_row_stride, kb_off, x, M, ldx, y, y_dtype, ldy, epilogue, aux, ldaux, 0, 0, 0,
                         stream);
 }
 
@@ -362,20 +388,13 @@ int yah_qgemv(const void* w, int t, int64_t N, int64_t K, int64_t w_row_stride, 
   const int S = yah::qgemv_splits(N, K, s->sms);
   if (S > 1) {
     std::lock_guard<std::mutex> lk(g_mu);
-    const size_t need = (size_t)S * M * N * sizeof(float);
     const size_t nrb = (size_t)((N + 127) / 128);
-    if (need > s->ws_bytes) {
-      if (s->ws) CK(cudaFree(s->ws));
-      s->ws = nullptr;
-      s->ws_bytes = 0;
-      CK(cudaMalloc(&s->ws, need));
-      s->ws_bytes = need;
-    }
+    rc = grow(reinterpret_cast<void**>(&s->ws), &s->ws_bytes, (size_t)S * M * N * sizeof(float));
+    if (rc) return rc;
     if (nrb > s->counters_n) {
-      if (s->counters) CK(cudaFree(s->counters));
-      s->counters = nullptr;
-      s->counters_n = 0;
-      CK(cudaMalloc(&s->counters, nrb * sizeof(int)));
+      size_t have = s->counters_n * sizeof(int);
+      rc = grow(reinterpret_cast<void**>(&s->counters), &have, nrb * sizeof(int));
+      if (rc) return rc;
       CK(cudaMemset(s->counters, 0, nrb * sizeof(int)));
       s->counters_n = nrb;
     }

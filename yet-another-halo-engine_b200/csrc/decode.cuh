@@ -12,9 +12,10 @@
 //                      the f32 fma rounds once and the f16 conversion once, exactly as gguf-py's d*q - dm.
 //                      q comes from a "magic float": (nibble << s) | 0x4B000000 is the float 2^23 + q*2^s, and
 //                      subtracting 2^23 leaves q*2^s exactly; the matching scale d*sc*2^-s is exact too.
-//   Q6_K (:1243-1335)  w = f16((d*sc) * (code - 32)). sc*(code - 32) is an integer of magnitude <= 1024, exact in
-//                      f16; fma.rn.f16x2(1024 + code, sc, -1056*sc) produces it exactly (1056*sc is an exact f16),
-//                      then one mul.rn.f16x2 by d rounds the exact product d*sc*(code-32) once.
+//   Q6_K (:1243-1335)  w = f16((d*sc) * (code - 32)) with d*sc and the product exact in f32 (int8 scales make
+//                      sc*(code - 32) too wide for exact f16 arithmetic, so this one stays in f32).
+// Pairs of f32 values go through the sm_100 packed-FP32 instructions (fma/add/mul .rn.f32x2): the same IEEE
+// operations, two per instruction.
 #pragma once
 #include "ptx.cuh"
 
@@ -54,31 +55,60 @@ __device__ __forceinline__ void q4k_scales(const uint4& hdr, int j, float& dsa, 
   dmb = dmin * (float)m[1];
 }
 
+// Two f32 lanes at once (sm_100 packed FP32): d = a * b + c and d = a + b on register pairs.
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 A, B, C, D;\n\tmov.b64 A, {%2, %3};\n\tmov.b64 B, {%4, %5};\n\tmov.b64 C, {%6, %7};\n\t"
+      "fma.rn.f32x2 D, A, B, C;\n\tmov.b64 {%0, %1}, D;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 A, B, D;\n\tmov.b64 A, {%2, %3};\n\tmov.b64 B, {%4, %5};\n\t"
+      "add.rn.f32x2 D, A, B;\n\tmov.b64 {%0, %1}, D;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 A, B, D;\n\tmov.b64 A, {%2, %3};\n\tmov.b64 B, {%4, %5};\n\t"
+      "mul.rn.f32x2 D, A, B;\n\tmov.b64 {%0, %1}, D;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
+// Two nibble-magic floats: (bits & m) | 0x4B000000 for two masks, minus 2^23 each (exact).
+__device__ __forceinline__ float2 magic_pair(uint32_t w, uint32_t m0, uint32_t m1) {
+  const float2 f = make_float2(__uint_as_float(lop_and_or(w, m0, 0x4B000000u)),
+                               __uint_as_float(lop_and_or(w, m1, 0x4B000000u)));
+  return fadd2(f, make_float2(-kMagic23, -kMagic23));
+}
+
+__device__ __forceinline__ uint32_t pack2(float2 v) { return pack_f16x2_rn(v.x, v.y); }
+
 __device__ __forceinline__ void q4k_decode_kblock(const uint4& hdr, const uint32_t (&qs)[8], int j,
                                                   uint32_t (&out)[32]) {
   float dsa, dma, dsb, dmb;
   q4k_scales(hdr, j, dsa, dma, dsb, dmb);
-  const float a0 = dsa, a8 = dsa * 0.00390625f;        // group 2j scales for nibbles at bit 0 / bit 8
-  const float b4 = dsb * 0.0625f, b12 = dsb * 2.44140625e-4f;  // group 2j+1 scales for bit 4 / bit 12
-  const float na = -dma, nb = -dmb;
+  // group 2j (low nibbles at bits 0 / 8 of a half-word) and 2j+1 (high nibbles at bits 4 / 12)
+  const float2 sa = make_float2(dsa, dsa * 0.00390625f);
+  const float2 sb = make_float2(dsb * 0.0625f, dsb * 2.44140625e-4f);
+  const float2 na = make_float2(-dma, -dma), nb = make_float2(-dmb, -dmb);
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const uint32_t w = qs[i];
     const uint32_t v = w >> 16;
-    // low nibbles (group 2j): bytes 0,1 -> column 2i; bytes 2,3 -> column 2i+1
-    const float l0 = __fmaf_rn(a0, magic_q(w & 0xFu), na);
-    const float l1 = __fmaf_rn(a8, magic_q(w & 0xF00u), na);
-    const float l2 = __fmaf_rn(a0, magic_q(v & 0xFu), na);
-    const float l3 = __fmaf_rn(a8, magic_q(v & 0xF00u), na);
-    // high nibbles (group 2j+1)
-    const float h0 = __fmaf_rn(b4, magic_q(w & 0xF0u), nb);
-    const float h1 = __fmaf_rn(b12, magic_q(w & 0xF000u), nb);
-    const float h2 = __fmaf_rn(b4, magic_q(v & 0xF0u), nb);
-    const float h3 = __fmaf_rn(b12, magic_q(v & 0xF000u), nb);
-    out[2 * i] = pack_f16x2_rn(l0, l1);
-    out[2 * i + 1] = pack_f16x2_rn(l2, l3);
-    out[16 + 2 * i] = pack_f16x2_rn(h0, h1);
-    out[16 + 2 * i + 1] = pack_f16x2_rn(h2, h3);
+    // low nibbles: bytes 0,1 -> column 2i; bytes 2,3 -> column 2i+1; high nibbles -> columns 16+2i, 17+2i
+    out[2 * i] = pack2(ffma2(sa, magic_pair(w, 0xFu, 0xF00u), na));
+    out[2 * i + 1] = pack2(ffma2(sa, magic_pair(v, 0xFu, 0xF00u), na));
+    out[16 + 2 * i] = pack2(ffma2(sb, magic_pair(w, 0xF0u, 0xF000u), nb));
+    out[16 + 2 * i + 1] = pack2(ffma2(sb, magic_pair(v, 0xF0u, 0xF000u), nb));
   }
 }
 
@@ -121,19 +151,20 @@ __device__ __forceinline__ void q6k_decode_kblock(const uint32_t (&QL)[16], cons
     ds[u] = (d * (float)s) * 1.52587890625e-05f;  // * 2^-16, exact
   }
   constexpr float kOff = 10485760.0f;  // 2^23 + 32 * 2^16
+  const float2 off = make_float2(-kOff, -kOff);
   const int lsh = 4 * jodd;
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
     const uint32_t lo4 = (QL[i] >> lsh) & 0x0F0F0F0Fu;
     const uint32_t hi2 = (QH[i & 7] >> (lsh + 2 * (i >> 3))) & 0x03030303u;
     const uint32_t code = lo4 | (hi2 << 4);
-    const float s = ds[i >> 2];
-    const float v0 = __fmul_rn(s, __uint_as_float(prmt(code, 0x4B000000u, 0x7044u)) - kOff);
-    const float v1 = __fmul_rn(s, __uint_as_float(prmt(code, 0x4B000000u, 0x7144u)) - kOff);
-    const float v2 = __fmul_rn(s, __uint_as_float(prmt(code, 0x4B000000u, 0x7244u)) - kOff);
-    const float v3 = __fmul_rn(s, __uint_as_float(prmt(code, 0x4B000000u, 0x7344u)) - kOff);
-    out[2 * i] = pack_f16x2_rn(v0, v1);
-    out[2 * i + 1] = pack_f16x2_rn(v2, v3);
+    const float2 s2 = make_float2(ds[i >> 2], ds[i >> 2]);
+    const float2 c01 = fadd2(make_float2(__uint_as_float(prmt(code, 0x4B000000u, 0x7044u)),
+                                         __uint_as_float(prmt(code, 0x4B000000u, 0x7144u))), off);
+    const float2 c23 = fadd2(make_float2(__uint_as_float(prmt(code, 0x4B000000u, 0x7244u)),
+                                         __uint_as_float(prmt(code, 0x4B000000u, 0x7344u))), off);
+    out[2 * i] = pack2(fmul2(s2, c01));
+    out[2 * i + 1] = pack2(fmul2(s2, c23));
   }
 }
 

@@ -26,8 +26,13 @@ struct QGemmArgs {
   int* status;          // device status word (bounded-wait failures)
   int num_sms;          // SMs of the device
   int grid;             // persistent CTAs (0: one per SM)
-  int bn;               // max tokens per tile (64, 128, 256)
+  int bn;               // max tokens per tile (64, 128, 192)
+  int64_t kchunk;       // K per accumulation chunk (multiple of 64; 0: the whole K in one chunk)
+  float* scratch;       // grid * bn * 128 f32 chunk sums when kchunk < K, else unused
 };
+
+// Largest persistent grid and the chunk scratch a launch needs.
+int qgemm_grid(const QGemmArgs& a);
 
 cudaError_t launch_qgemm_tc(const QGemmArgs& a, cudaStream_t stream);
 

@@ -5,15 +5,21 @@
 // is decoded inside the K loop to exactly the f16 values of the reference dequant, multiplied in f16 with f32
 // accumulation, and written token-major: out[t][r] at t * ldy + r (gen_gemm_tile.py:1230-1231).
 //
-// B200 design (one persistent CTA per SM, 14 warps):
-//   warp 0      TMA producer: raw super-blocks of 128 weight rows (one 256-K super-block per stage) and 64-K
-//               activation tiles (BN tokens x 128 B, 128-byte swizzle) into shared-memory rings.
+// B200 design (one persistent CTA per SM, 15 warps):
+//   warp 0      activation producer: TMA loads of 64-K activation tiles (BN tokens x 128 B, 128-byte swizzle).
+//   warp 14     weight producer: TMA loads of the raw super-blocks of 128 weight rows (one 256-K super-block per
+//               stage, 3-4 stages), decoupled from the activation ring so weights stream ahead on their own.
 //   warp 1      MMA issuer (one thread): tcgen05.mma.cta_group::1.kind::f16, A (weights) from TMEM, B
-//               (activations) from shared memory, D (128 rows x up to 256 tokens, f32) in TMEM columns 0..255.
+//               (activations) from shared memory, D (128 rows x BN tokens, f32) in one of two TMEM accumulator
+//               regions, used alternately, so the epilogue of one accumulation overlaps the MMAs of the next.
 //   warps 2-9   two dequant warpgroups (even / odd 64-K blocks). Thread = weight row (= TMEM lane). A thread
-//               decodes its row's 64 values to f16 pairs in registers and tcgen05.st's them into one of 8 A
-//               stages (TMEM columns 256..511): the dequantised tile never touches shared memory.
+//               decodes its row's 64 values to f16 pairs in registers and tcgen05.st's them into an A stage in
+//               TMEM (after the two accumulators): the dequantised tile never touches shared memory.
 //   warps 10-13 epilogue: tcgen05.ld of the accumulator, kstore / kres / swiglu, token-major global stores.
+// Accuracy: the tensor core's f32 accumulation truncates (round toward zero), which at K = 14336 costs ~0.04
+// absolute on |y| ~ 2000. For K above 4096 each tile is accumulated in chunks of `kcb` 64-K blocks, each chunk
+// starting from zero in the free accumulator region; the epilogue sums the chunk results in f32 round-to-nearest
+// in a per-CTA scratch buffer (L2-resident) while the MMA fills the other region.
 // Tiles are 128 weight rows x up to BN tokens. The persistent schedule splits the (row tile, 16-token unit) space
 // into equal contiguous ranges per CTA, so every SM gets the same MMA work (no wave-quantisation tail).
 // Every mbarrier wait is bounded (ptx.cuh mbar_wait); on a timeout the kernel records a status code, drains its
@@ -30,40 +36,41 @@
 namespace yah {
 namespace {
 
-constexpr int kThreads = 448;
-constexpr int kBM = 128;      // weight rows per tile = TMEM lanes
-constexpr int kNA = 8;        // A stages in TMEM
-constexpr int kAccCols = 256; // accumulator columns
-constexpr int kACol0 = 256;   // first A-stage column
-constexpr int kNSW = 2;       // weight super-block stages
+constexpr int kThreads = 480;
+constexpr int kBM = 128;  // weight rows per tile = TMEM lanes
+constexpr int kWarpX = 0, kWarpMma = 1, kWarpDq0 = 2, kWarpEpi0 = 10, kWarpW = 14;
 
 template <int T>
 struct Fmt;
 template <>
 struct Fmt<8> {  // Q8_0: 8 blocks of 34 B as one 272-B super-block
-  static constexpr int kSB = 272, kBox = 272;
+  static constexpr int kSB = 272, kBox = 272, kNSW = 3;
 };
 template <>
 struct Fmt<12> {  // Q4_K
-  static constexpr int kSB = 144, kBox = 144;
+  static constexpr int kSB = 144, kBox = 144, kNSW = 4;
 };
 template <>
 struct Fmt<14> {  // Q6_K: a 224-B window from the 16-B boundary at or below the super-block
-  static constexpr int kSB = 210, kBox = 224;
+  static constexpr int kSB = 210, kBox = 224, kNSW = 4;
 };
 
 template <int BN>
 struct XCfg {
-  static constexpr int kNSX = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
-  static constexpr int kStage = BN * 128;  // BN rows x 64 f16
+  static constexpr int kNSX = BN == 192 ? 4 : (BN == 128 ? 6 : 8);
+  static constexpr int kStage = BN * 128;                       // BN rows x 64 f16
+  static constexpr int kACol0 = 2 * BN;                         // A stages follow the two accumulators
+  static constexpr int kNA = (512 - 2 * BN) / 32 > 8 ? 8 : (512 - 2 * BN) / 32;
 };
 
 struct KParams {
   int N, K, M, kb_off;
+  int kcb;  // 64-K blocks per accumulation chunk (>= K / 64: one chunk)
   void* y;
   int64_t ldy;
   const float* aux;
   int64_t ldaux;
+  float* scratch;       // [grid][BN][128] f32 chunk sums (chunked accumulation only)
   int* status;
   int64_t total_units;  // row tiles x 16-token units
   int upr;              // 16-token units per row tile
@@ -74,9 +81,9 @@ struct Smem {
   static constexpr int kWStage = ((kBM * Fmt<T>::kBox + 16) + 127) / 128 * 128;
   static constexpr int kXBytes = XCfg<BN>::kNSX * XCfg<BN>::kStage;
   static constexpr int kWOff = kXBytes;
-  static constexpr int kBarOff = kWOff + kNSW * kWStage;
-  // barriers: xfull, xempty [NSX]; wfull, wempty [NSW]; afull, aempty [NA]; accfull, accempty; drain
-  static constexpr int kNumBars = 2 * XCfg<BN>::kNSX + 2 * kNSW + 2 * kNA + 3;
+  static constexpr int kBarOff = kWOff + Fmt<T>::kNSW * kWStage;
+  // barriers: xfull, xempty [NSX]; wfull, wempty [NSW]; afull, aempty [NA]; accfull, accempty [2]; drain
+  static constexpr int kNumBars = 2 * XCfg<BN>::kNSX + 2 * Fmt<T>::kNSW + 2 * XCfg<BN>::kNA + 5;
   static constexpr int kTmemSlotOff = kBarOff + kNumBars * 8;
   static constexpr int kBytes = kTmemSlotOff + 16;
   static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-byte alignment of the base
@@ -115,6 +122,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   using S = Smem<T, BN>;
   constexpr int NSX = XCfg<BN>::kNSX;
   constexpr int XST = XCfg<BN>::kStage;
+  constexpr int NA = XCfg<BN>::kNA;
+  constexpr int ACOL = XCfg<BN>::kACol0;
+  constexpr int NSW = Fmt<T>::kNSW;
   constexpr int WBOX = Fmt<T>::kBox;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -122,40 +132,39 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* xfull = bars;
   uint64_t* xempty = xfull + NSX;
   uint64_t* wfull = xempty + NSX;
-  uint64_t* wempty = wfull + kNSW;
-  uint64_t* afull = wempty + kNSW;
-  uint64_t* aempty = afull + kNA;
-  uint64_t* accfull = aempty + kNA;
-  uint64_t* accempty = accfull + 1;
-  uint64_t* drain = accempty + 1;
+  uint64_t* wempty = wfull + NSW;
+  uint64_t* afull = wempty + NSW;
+  uint64_t* aempty = afull + NA;
+  uint64_t* accfull = aempty + NA;  // [2]
+  uint64_t* accempty = accfull + 2; // [2]
+  uint64_t* drain = accempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::kTmemSlotOff);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nkb = p.K / 64;
+  const int nch = (nkb + p.kcb - 1) / p.kcb;  // accumulation chunks per tile
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < NSX; ++i) {
       mbar_init(&xfull[i], 1);
       mbar_init(&xempty[i], 1);
     }
-    for (int i = 0; i < kNSW; ++i) {
+    for (int i = 0; i < NSW; ++i) {
       mbar_init(&wfull[i], 1);
       mbar_init(&wempty[i], 8);  // 4 warps x 2 dequant warpgroups
     }
-    for (int i = 0; i < kNA; ++i) {
+    for (int i = 0; i < NA; ++i) {
       mbar_init(&afull[i], 4);
       mbar_init(&aempty[i], 1);
     }
-    mbar_init(accfull, 1);
-    mbar_init(accempty, 4);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&accfull[i], 1);
+      mbar_init(&accempty[i], 4);
+    }
     mbar_init(drain, 1);
     fence_barrier_init();
   }
-  if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&tmap_w);
-    tma_prefetch_desc(&tmap_x);
-  }
-  if (warp == 1) {
+  if (warp == kWarpMma) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
@@ -164,89 +173,102 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
-    // ------------------------------------------------------------------ TMA producer
+  if (warp == kWarpX) {
+    // ------------------------------------------------------------------ activation producer
     if (lane == 0) {
+      tma_prefetch_desc(&tmap_x);
       Sched<BN> sc(p);
       int rt, t0, nt;
-      uint32_t c = 0, cw = 0;  // activation / weight stages issued
+      uint32_t c = 0;
       bool ok = true;
       while (ok && sc.next(rt, t0, nt)) {
         for (int kb = 0; kb < nkb; ++kb, ++c) {
-          if ((kb & 3) == 0) {
-            const uint32_t sbc = c >> 2, ws = sbc % kNSW, wph = (sbc / kNSW) & 1;
-            if (!mbar_wait(&wempty[ws], wph ^ 1, p.status, kStatusTimeoutEmpty)) { ok = false; break; }
-            mbar_arrive_expect_tx(&wfull[ws], kBM * WBOX);
-            ++cw;
-            const int64_t sbg = (int64_t)p.kb_off + (kb >> 2);
-            int xw;
-            if (T == 14) xw = (int)(((sbg * 210) & ~int64_t(15)) >> 1);
-            else xw = (int)(sbg * (Fmt<T>::kSB / 2));
-            tma_load_2d(smem + S::kWOff + ws * S::kWStage, &tmap_w, &wfull[ws], xw, rt * kBM);
-          }
           const uint32_t xs = c % NSX, xph = (c / NSX) & 1;
           if (!mbar_wait(&xempty[xs], xph ^ 1, p.status, kStatusTimeoutEmpty)) { ok = false; break; }
           mbar_arrive_expect_tx(&xfull[xs], XST);
           tma_load_2d(smem + xs * XST, &tmap_x, &xfull[xs], kb * 64, t0);
         }
       }
-      // Drain: wait for the copies this thread issued last on every stage (no-ops on the normal path).
       for (uint32_t i = (c > (uint32_t)NSX ? c - NSX : 0); i < c; ++i)
         mbar_wait(&xfull[i % NSX], (i / NSX) & 1, p.status, kStatusTimeoutDrain, false);
-      for (uint32_t i = (cw > (uint32_t)kNSW ? cw - kNSW : 0); i < cw; ++i)
-        mbar_wait(&wfull[i % kNSW], (i / kNSW) & 1, p.status, kStatusTimeoutDrain, false);
     }
-  } else if (warp == 1) {
+  } else if (warp == kWarpW) {
+    // ------------------------------------------------------------------ weight producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmap_w);
+      Sched<BN> sc(p);
+      int rt, t0, nt;
+      uint32_t s = 0;
+      bool ok = true;
+      while (ok && sc.next(rt, t0, nt)) {
+        for (int sb = 0; sb < nkb / 4; ++sb, ++s) {
+          const uint32_t ws = s % NSW, wph = (s / NSW) & 1;
+          if (!mbar_wait(&wempty[ws], wph ^ 1, p.status, kStatusTimeoutEmpty)) { ok = false; break; }
+          mbar_arrive_expect_tx(&wfull[ws], kBM * WBOX);
+          const int64_t sbg = (int64_t)p.kb_off + sb;
+          int xw;
+          if (T == 14) xw = (int)(((sbg * 210) & ~int64_t(15)) >> 1);
+          else xw = (int)(sbg * (Fmt<T>::kSB / 2));
+          tma_load_2d(smem + S::kWOff + ws * S::kWStage, &tmap_w, &wfull[ws], xw, rt * kBM);
+        }
+      }
+      for (uint32_t i = (s > (uint32_t)NSW ? s - NSW : 0); i < s; ++i)
+        mbar_wait(&wfull[i % NSW], (i / NSW) & 1, p.status, kStatusTimeoutDrain, false);
+    }
+  } else if (warp == kWarpMma) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       Sched<BN> sc(p);
       int rt, t0, nt;
-      uint32_t c = 0, tcount = 0;
+      uint32_t c = 0, u = 0;  // k-block and accumulation-unit counters
       bool ok = true;
       const uint32_t xbase = smem_u32(smem);
       while (ok && sc.next(rt, t0, nt)) {
-        if (!mbar_wait(accempty, (tcount & 1) ^ 1, p.status, kStatusTimeoutEmpty)) break;
-        tc_fence_after();
-        const int nmma = (nt + 15) & ~15;
-        const uint32_t idesc = idesc_f16_f32(kBM, nmma);
-        for (int kb = 0; kb < nkb; ++kb, ++c) {
-          const uint32_t as = c % kNA, aph = (c / kNA) & 1;
-          const uint32_t xs = c % NSX, xph = (c / NSX) & 1;
-          if (!mbar_wait(&afull[as], aph, p.status, kStatusTimeoutFull)) { ok = false; break; }
-          if (!mbar_wait(&xfull[xs], xph, p.status, kStatusTimeoutFull)) { ok = false; break; }
+        const uint32_t idesc = idesc_f16_f32(kBM, (nt + 15) & ~15);
+        for (int ch = 0; ok && ch < nch; ++ch, ++u) {
+          const uint32_t r = u & 1;
+          if (!mbar_wait(&accempty[r], ((u >> 1) & 1) ^ 1, p.status, kStatusTimeoutEmpty)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t xa = xbase + xs * XST;
+          const uint32_t dt = tmem + r * BN;
+          const int kb0 = ch * p.kcb, kb1 = min(nkb, kb0 + p.kcb);
+          for (int kb = kb0; kb < kb1; ++kb, ++c) {
+            const uint32_t as = c % NA, aph = (c / NA) & 1;
+            const uint32_t xs = c % NSX, xph = (c / NSX) & 1;
+            if (!mbar_wait(&afull[as], aph, p.status, kStatusTimeoutFull)) { ok = false; break; }
+            if (!mbar_wait(&xfull[xs], xph, p.status, kStatusTimeoutFull)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t xa = xbase + xs * XST;
 #pragma unroll
-          for (int ks = 0; ks < 4; ++ks)
-            mma_f16_ts(tmem, tmem + kACol0 + as * 32 + ks * 8, sdesc_sw128(xa + ks * 32), idesc,
-                       (kb | ks) != 0);
-          mma_commit(&aempty[as]);
-          mma_commit(&xempty[xs]);
+            for (int ks = 0; ks < 4; ++ks)
+              mma_f16_ts(dt, tmem + ACOL + as * 32 + ks * 8, sdesc_sw128(xa + ks * 32), idesc,
+                         (kb > kb0 || ks > 0) ? 1u : 0u);
+            mma_commit(&aempty[as]);
+            mma_commit(&xempty[xs]);
+          }
+          if (!ok) break;
+          mma_commit(&accfull[r]);
         }
-        if (!ok) break;
-        mma_commit(accfull);
-        ++tcount;
       }
       // Drain: every MMA issued by this thread completes before TMEM is released.
       mma_commit(drain);
       mbar_wait(drain, 0, p.status, kStatusTimeoutDrain, false);
     }
-  } else if (warp < 10) {
+  } else if (warp < kWarpEpi0) {
     // ------------------------------------------------------------------ dequant warpgroups
-    const uint32_t wg = (warp - 2) >> 2;  // 0: even K blocks, 1: odd
-    const int q = warp & 3;               // TMEM lane quarter
-    const int r = q * 32 + lane;          // row within the tile
+    const uint32_t wg = (warp - kWarpDq0) >> 2;  // 0: even K blocks, 1: odd
+    const int q = warp & 3;                      // TMEM lane quarter
+    const int r = q * 32 + lane;                 // row within the tile
     Sched<BN> sc(p);
     int rt, t0, nt;
     uint32_t c = 0;
     bool ok = true;
     const uint32_t wbase = smem_u32(smem + S::kWOff);
-    const uint32_t tl = tmem + ((uint32_t)(q * 32) << 16) + kACol0;
+    const uint32_t tl = tmem + ((uint32_t)(q * 32) << 16) + ACOL;
     while (ok && sc.next(rt, t0, nt)) {
       for (int kb = 0; kb < nkb; ++kb, ++c) {
         if ((c & 1) != wg) continue;
-        const uint32_t sbc = c >> 2, ws = sbc % kNSW, wph = (sbc / kNSW) & 1;
-        const uint32_t as = c % kNA, aph = (c / kNA) & 1;
+        const uint32_t sbc = c >> 2, ws = sbc % NSW, wph = (sbc / NSW) & 1;
+        const uint32_t as = c % NA, aph = (c / NA) & 1;
         if (!mbar_wait(&wfull[ws], wph, p.status, kStatusTimeoutFull)) { ok = false; break; }
         if (!mbar_wait(&aempty[as], aph ^ 1, p.status, kStatusTimeoutEmpty)) { ok = false; break; }
         const int j = kb & 3;
@@ -271,29 +293,42 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) mbar_arrive(&afull[as]);
       }
     }
-  } else {
+  } else if (warp < kWarpW) {
     // ------------------------------------------------------------------ epilogue
     const int q = warp & 3;
+    const int rloc = q * 32 + lane;
     Sched<BN> sc(p);
     int rt, t0, nt;
-    uint32_t tcount = 0;
+    uint32_t u = 0;
+    bool ok = true;
     const uint32_t tl = tmem + ((uint32_t)(q * 32) << 16);
-    while (sc.next(rt, t0, nt)) {
-      if (!mbar_wait(accfull, tcount & 1, p.status, kStatusTimeoutFull)) break;
-      tc_fence_after();
-      const int row = rt * kBM + q * 32 + lane;
+    float* part = p.scratch ? p.scratch + (size_t)blockIdx.x * BN * kBM + rloc : nullptr;
+    while (ok && sc.next(rt, t0, nt)) {
+      const int row = rt * kBM + rloc;
       const bool row_ok = row < p.N;
-      for (int j0 = 0; j0 < nt; j0 += 32) {
-        uint32_t v[32];
-        tmem_ld32(tl + j0, v);
-        tmem_wait_ld();
-        if (row_ok) {
+      for (int ch = 0; ch < nch; ++ch, ++u) {
+        const uint32_t r = u & 1;
+        if (!mbar_wait(&accfull[r], (u >> 1) & 1, p.status, kStatusTimeoutFull)) { ok = false; break; }
+        tc_fence_after();
+        const bool first = ch == 0, last = ch == nch - 1;
+        for (int j0 = 0; j0 < nt; j0 += 32) {
+          uint32_t v[32];
+          tmem_ld32(tl + r * BN + j0, v);
+          tmem_wait_ld();
+          if (!row_ok) continue;
           const int jn = min(32, nt - j0);
 #pragma unroll
           for (int jj = 0; jj < 32; ++jj) {
             if (jj >= jn) break;
-            const int64_t t = t0 + j0 + jj;
+            const int col = j0 + jj;
             float acc = __uint_as_float(v[jj]);
+            if (!last) {
+              float* cell = part + (size_t)col * kBM;
+              *cell = first ? acc : *cell + acc;
+              continue;
+            }
+            if (!first) acc = part[(size_t)col * kBM] + acc;
+            const int64_t t = t0 + col;
             if (EPI == kEpiResid) acc += __ldg(p.aux + t * p.ldaux + row);
             if (EPI == kEpiSwiglu) acc = silu_f(__ldg(p.aux + t * p.ldaux + row)) * acc;
             if (OUT_F16)
@@ -302,17 +337,16 @@ __global__ void __launch_bounds__(kThreads, 1)
               reinterpret_cast<float*>(p.y)[t * p.ldy + row] = acc;
           }
         }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&accempty[r]);
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(accempty);
-      ++tcount;
     }
   }
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == kWarpMma) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -368,6 +402,8 @@ cudaError_t launch_t(const QGemmArgs& a, cudaStream_t stream) {
   p.K = (int)a.K;
   p.M = (int)a.M;
   p.kb_off = (int)a.kb_off;
+  p.kcb = (a.kchunk > 0 && a.kchunk < a.K) ? (int)(a.kchunk / 64) : (int)(a.K / 64);
+  p.scratch = a.scratch;
   p.y = a.y;
   p.ldy = a.ldy;
   p.aux = a.aux;
@@ -376,8 +412,7 @@ cudaError_t launch_t(const QGemmArgs& a, cudaStream_t stream) {
   p.upr = (int)((a.M + 15) / 16);
   const int64_t rtiles = (a.N + kBM - 1) / kBM;
   p.total_units = rtiles * p.upr;
-  int grid = a.grid > 0 ? a.grid : a.num_sms;
-  if (grid > p.total_units) grid = (int)p.total_units;
+  const int grid = qgemm_grid(a);
   auto kern = qgemm_tc_kernel<T, BN, EPI, OUT_F16>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kAlloc);
   if (e != cudaSuccess) return e;
@@ -396,12 +431,19 @@ template <int T>
 cudaError_t launch_fmt(const QGemmArgs& a, cudaStream_t s) {
   if (a.bn == 128) return launch_bn<T, 128>(a, s);
   if (a.bn == 64) return launch_bn<T, 64>(a, s);
-  return launch_bn<T, 256>(a, s);
+  return launch_bn<T, 192>(a, s);
 }
 
 }  // namespace
 
 bool tensor_map_encoder_available() { return encoder() != nullptr; }
+
+int qgemm_grid(const QGemmArgs& a) {
+  const int64_t units = (a.N + kBM - 1) / kBM * ((a.M + 15) / 16);
+  int64_t grid = a.grid > 0 ? a.grid : a.num_sms;
+  if (grid > units) grid = units;
+  return (int)grid;
+}
 
 cudaError_t launch_qgemm_tc(const QGemmArgs& a, cudaStream_t stream) {
   switch (a.type) {
