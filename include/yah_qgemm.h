@@ -126,7 +126,7 @@ int yah_qgemm(const void* w, int ggml_type, int64_t N, int64_t K, int64_t w_row_
 /* yah_qgemm with an explicit tile choice (the tuner's knob set, engine/tune/tune.py:77):
  *   bn      tokens per tile: 64, 128 or 192 (0 = default 192);
  *   grid    persistent CTAs (0 = one per SM);
- *   kchunk  K per f32 accumulation chunk, a multiple of 64 (0 = auto: 2048 when K > 4096, else all of K;
+ *   kchunk  K per f32 accumulation chunk, a multiple of 128 (0 = auto: 2048 when K > 4096, else all of K;
  *           -1 = never chunk). Chunk results are summed in f32 round-to-nearest; see the accuracy note in
  *           csrc/qgemm_tc.cu. Chunking uses a library-owned per-device scratch buffer (grid * bn * 512 bytes),
  *           so chunked calls on different streams of one device must not overlap.

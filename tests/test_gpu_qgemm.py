@@ -116,7 +116,7 @@ def test_tile_choices_are_identical(pkg, F, O, dev, bn, grid, kchunk):
     check(O, y, O.gemm_ref(O.dequant_f16(t, w, N, K), x))
 
 
-@pytest.mark.parametrize("kchunk", [64, 256, 1088, 2048])
+@pytest.mark.parametrize("kchunk", [128, 256, 1152, 2048])
 def test_chunked_accumulation(pkg, F, O, dev, kchunk):
     """Chunked accumulation (chunk sums added in f32 round-to-nearest) matches the oracle for any chunk length,
     including chunks that do not divide K, with every epilogue."""

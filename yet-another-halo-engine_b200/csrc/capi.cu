@@ -332,7 +332,7 @@ int yah_qgemm_tile(const void* w, int t, int64_t N, int64_t K, int64_t w_row_str
   if (grid < 0) return fail(YAH_ERR_ARG, "negative grid");
   if (kchunk == 0) kchunk = K > 4096 ? 2048 : K;  // see the accuracy note in qgemm_tc.cu
   if (kchunk < 0 || kchunk >= K) kchunk = K;
-  if (kchunk % 64) return fail(YAH_ERR_ARG, "kchunk %lld is not a multiple of 64", (long long)kchunk);
+  if (kchunk % 128) return fail(YAH_ERR_ARG, "kchunk %lld is not a multiple of 128", (long long)kchunk);
   DevState* s;
   rc = dev_state(&s);
   if (rc) return rc;

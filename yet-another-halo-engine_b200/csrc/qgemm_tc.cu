@@ -5,16 +5,22 @@
 // is decoded inside the K loop to exactly the f16 values of the reference dequant, multiplied in f16 with f32
 // accumulation, and written token-major: out[t][r] at t * ldy + r (gen_gemm_tile.py:1230-1231).
 //
-// B200 design (one persistent CTA per SM, 15 warps):
-//   warp 0      activation producer: TMA loads of 64-K activation tiles (BN tokens x 128 B, 128-byte swizzle).
+// B200 design (one persistent CTA per SM, 15 warps). The K loop advances in stages of 128 K (two 64-K blocks):
+//   warp 0      activation producer: per stage two TMA loads of 64-K activation tiles (BN tokens x 128 B,
+//               128-byte swizzle) into one of 3 shared-memory slots.
 //   warp 14     weight producer: TMA loads of the raw super-blocks of 128 weight rows (one 256-K super-block per
-//               stage, 3-4 stages), decoupled from the activation ring so weights stream ahead on their own.
-//   warp 1      MMA issuer (one thread): tcgen05.mma.cta_group::1.kind::f16, A (weights) from TMEM, B
-//               (activations) from shared memory, D (128 rows x BN tokens, f32) in one of two TMEM accumulator
-//               regions, used alternately, so the epilogue of one accumulation overlaps the MMAs of the next.
-//   warps 2-9   two dequant warpgroups (even / odd 64-K blocks). Thread = weight row (= TMEM lane). A thread
-//               decodes its row's 64 values to f16 pairs in registers and tcgen05.st's them into an A stage in
-//               TMEM (after the two accumulators): the dequantised tile never touches shared memory.
+//               slot), decoupled from the activation ring so weights stream ahead on their own.
+//   warp 1      MMA issuer (one thread): per stage one barrier wait, one fence, 8 x tcgen05.mma.cta_group::1
+//               .kind::f16 (A = weights from TMEM, B = activations from shared memory, D = 128 rows x BN tokens
+//               f32 in one of two TMEM accumulator regions, used alternately so an epilogue overlaps the next
+//               accumulation) and one commit. tcgen05.mma issue is serialised with everything else the issuing
+//               thread executes, so its instruction stream is kept to that minimum: descriptors precomputed,
+//               stage slots compile-time, the activation-ready check folded into the A-stage barrier.
+//   warps 2-9   two dequant warpgroups (first / second 64-K block of a stage). Thread = weight row (= TMEM
+//               lane): it decodes its row's 64 values to f16 pairs in registers and tcgen05.st's them into the
+//               A stage in TMEM (after the two accumulators), so the dequantised tile never touches shared
+//               memory. Before marking the A stage full it also waits for the stage's activation tile, and it
+//               releases activation slots on the MMA's behalf once the MMA has finished with them.
 //   warps 10-13 epilogue: tcgen05.ld of the accumulator, kstore / kres / swiglu, token-major global stores.
 // Accuracy: the tensor core's f32 accumulation truncates (round toward zero), which at K = 14336 costs ~0.04
 // absolute on |y| ~ 2000. For K above 4096 each tile is accumulated in chunks of `kcb` 64-K blocks, each chunk
@@ -44,23 +50,26 @@ template <int T>
 struct Fmt;
 template <>
 struct Fmt<8> {  // Q8_0: 8 blocks of 34 B as one 272-B super-block
-  static constexpr int kSB = 272, kBox = 272, kNSW = 3;
+  static constexpr int kSB = 272, kBox = 272, kNSW = 2;
 };
 template <>
 struct Fmt<12> {  // Q4_K
-  static constexpr int kSB = 144, kBox = 144, kNSW = 4;
+  static constexpr int kSB = 144, kBox = 144, kNSW = 3;
 };
 template <>
 struct Fmt<14> {  // Q6_K: a 224-B window from the 16-B boundary at or below the super-block
-  static constexpr int kSB = 210, kBox = 224, kNSW = 4;
+  static constexpr int kSB = 210, kBox = 224, kNSW = 2;
 };
+
+constexpr int kNSX = 3;  // activation slots (stages of 128 K)
+constexpr int kNA = 2;   // A stages in TMEM (128 K = 64 columns each)
 
 template <int BN>
 struct XCfg {
-  static constexpr int kNSX = BN == 192 ? 4 : (BN == 128 ? 6 : 8);
-  static constexpr int kStage = BN * 128;                       // BN rows x 64 f16
-  static constexpr int kACol0 = 2 * BN;                         // A stages follow the two accumulators
-  static constexpr int kNA = (512 - 2 * BN) / 32 > 8 ? 8 : (512 - 2 * BN) / 32;
+  static constexpr int kSub = BN * 128;     // one 64-K activation tile: BN rows x 64 f16
+  static constexpr int kStage = 2 * kSub;   // a stage holds two
+  static constexpr int kACol0 = 2 * BN;     // A stages follow the two accumulator regions
+  static_assert(2 * BN + kNA * 64 <= 512, "TMEM columns");
 };
 
 struct KParams {
@@ -79,11 +88,11 @@ struct KParams {
 template <int T, int BN>
 struct Smem {
   static constexpr int kWStage = ((kBM * Fmt<T>::kBox + 16) + 127) / 128 * 128;
-  static constexpr int kXBytes = XCfg<BN>::kNSX * XCfg<BN>::kStage;
+  static constexpr int kXBytes = kNSX * XCfg<BN>::kStage;
   static constexpr int kWOff = kXBytes;
   static constexpr int kBarOff = kWOff + Fmt<T>::kNSW * kWStage;
   // barriers: xfull, xempty [NSX]; wfull, wempty [NSW]; afull, aempty [NA]; accfull, accempty [2]; drain
-  static constexpr int kNumBars = 2 * XCfg<BN>::kNSX + 2 * Fmt<T>::kNSW + 2 * XCfg<BN>::kNA + 5;
+  static constexpr int kNumBars = 2 * kNSX + 2 * Fmt<T>::kNSW + 2 * kNA + 5;
   static constexpr int kTmemSlotOff = kBarOff + kNumBars * 8;
   static constexpr int kBytes = kTmemSlotOff + 16;
   static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-byte alignment of the base
@@ -120,9 +129,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                     const KParams p) {
   using S = Smem<T, BN>;
-  constexpr int NSX = XCfg<BN>::kNSX;
+  constexpr int XSUB = XCfg<BN>::kSub;
   constexpr int XST = XCfg<BN>::kStage;
-  constexpr int NA = XCfg<BN>::kNA;
   constexpr int ACOL = XCfg<BN>::kACol0;
   constexpr int NSW = Fmt<T>::kNSW;
   constexpr int WBOX = Fmt<T>::kBox;
@@ -130,22 +138,23 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::kBarOff);
   uint64_t* xfull = bars;
-  uint64_t* xempty = xfull + NSX;
-  uint64_t* wfull = xempty + NSX;
+  uint64_t* xempty = xfull + kNSX;
+  uint64_t* wfull = xempty + kNSX;
   uint64_t* wempty = wfull + NSW;
   uint64_t* afull = wempty + NSW;
-  uint64_t* aempty = afull + NA;
-  uint64_t* accfull = aempty + NA;  // [2]
-  uint64_t* accempty = accfull + 2; // [2]
+  uint64_t* aempty = afull + kNA;
+  uint64_t* accfull = aempty + kNA;  // [2]
+  uint64_t* accempty = accfull + 2;  // [2]
   uint64_t* drain = accempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::kTmemSlotOff);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nkb = p.K / 64;
-  const int nch = (nkb + p.kcb - 1) / p.kcb;  // accumulation chunks per tile
+  const int nst = p.K / 128;                  // 128-K stages per tile
+  const int sch = p.kcb / 2;                  // stages per accumulation chunk
+  const int nch = (nst + sch - 1) / sch;      // accumulation chunks per tile
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < NSX; ++i) {
+    for (int i = 0; i < kNSX; ++i) {
       mbar_init(&xfull[i], 1);
       mbar_init(&xempty[i], 1);
     }
@@ -153,8 +162,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&wfull[i], 1);
       mbar_init(&wempty[i], 8);  // 4 warps x 2 dequant warpgroups
     }
-    for (int i = 0; i < NA; ++i) {
-      mbar_init(&afull[i], 4);
+    for (int i = 0; i < kNA; ++i) {
+      mbar_init(&afull[i], 8);   // every dequant warp (each also saw the activation tile land)
       mbar_init(&aempty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -179,18 +188,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_prefetch_desc(&tmap_x);
       Sched<BN> sc(p);
       int rt, t0, nt;
-      uint32_t c = 0;
+      uint32_t s = 0;  // stages issued
       bool ok = true;
       while (ok && sc.next(rt, t0, nt)) {
-        for (int kb = 0; kb < nkb; ++kb, ++c) {
-          const uint32_t xs = c % NSX, xph = (c / NSX) & 1;
+        for (int st = 0; st < nst; ++st, ++s) {
+          const uint32_t xs = s % kNSX, xph = (s / kNSX) & 1;
           if (!mbar_wait(&xempty[xs], xph ^ 1, p.status, kStatusTimeoutEmpty)) { ok = false; break; }
           mbar_arrive_expect_tx(&xfull[xs], XST);
-          tma_load_2d(smem + xs * XST, &tmap_x, &xfull[xs], kb * 64, t0);
+          tma_load_2d(smem + xs * XST, &tmap_x, &xfull[xs], st * 128, t0);
+          tma_load_2d(smem + xs * XST + XSUB, &tmap_x, &xfull[xs], st * 128 + 64, t0);
         }
       }
-      for (uint32_t i = (c > (uint32_t)NSX ? c - NSX : 0); i < c; ++i)
-        mbar_wait(&xfull[i % NSX], (i / NSX) & 1, p.status, kStatusTimeoutDrain, false);
+      for (uint32_t i = (s > (uint32_t)kNSX ? s - kNSX : 0); i < s; ++i)
+        mbar_wait(&xfull[i % kNSX], (i / kNSX) & 1, p.status, kStatusTimeoutDrain, false);
     }
   } else if (warp == kWarpW) {
     // ------------------------------------------------------------------ weight producer
@@ -201,7 +211,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t s = 0;
       bool ok = true;
       while (ok && sc.next(rt, t0, nt)) {
-        for (int sb = 0; sb < nkb / 4; ++sb, ++s) {
+        for (int sb = 0; sb < p.K / 256; ++sb, ++s) {
           const uint32_t ws = s % NSW, wph = (s / NSW) & 1;
           if (!mbar_wait(&wempty[ws], wph ^ 1, p.status, kStatusTimeoutEmpty)) { ok = false; break; }
           mbar_arrive_expect_tx(&wfull[ws], kBM * WBOX);
@@ -220,9 +230,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       Sched<BN> sc(p);
       int rt, t0, nt;
-      uint32_t c = 0, u = 0;  // k-block and accumulation-unit counters
+      uint32_t s = 0, u = 0;  // stage and accumulation-unit counters
       bool ok = true;
-      const uint32_t xbase = smem_u32(smem);
+      // B descriptors of the 3 activation slots (second 64-K tile: + XSUB bytes) and the 2 A-stage columns
+      const uint64_t bd0 = sdesc_sw128(smem_u32(smem));
+      const uint64_t bstep = (uint64_t)(XST >> 4), bsub = (uint64_t)(XSUB >> 4);
+      const uint32_t a0 = tmem + ACOL;
       while (ok && sc.next(rt, t0, nt)) {
         const uint32_t idesc = idesc_f16_f32(kBM, (nt + 15) & ~15);
         for (int ch = 0; ok && ch < nch; ++ch, ++u) {
@@ -230,20 +243,23 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!mbar_wait(&accempty[r], ((u >> 1) & 1) ^ 1, p.status, kStatusTimeoutEmpty)) { ok = false; break; }
           tc_fence_after();
           const uint32_t dt = tmem + r * BN;
-          const int kb0 = ch * p.kcb, kb1 = min(nkb, kb0 + p.kcb);
-          for (int kb = kb0; kb < kb1; ++kb, ++c) {
-            const uint32_t as = c % NA, aph = (c / NA) & 1;
-            const uint32_t xs = c % NSX, xph = (c / NSX) & 1;
-            if (!mbar_wait(&afull[as], aph, p.status, kStatusTimeoutFull)) { ok = false; break; }
-            if (!mbar_wait(&xfull[xs], xph, p.status, kStatusTimeoutFull)) { ok = false; break; }
+          const int st1 = min(nst, (ch + 1) * sch);
+          for (int st = ch * sch; st < st1; ++st, ++s) {
+            const uint32_t as = s & 1, xs = s % kNSX;
+            if (!mbar_wait(&afull[as], (s >> 1) & 1, p.status, kStatusTimeoutFull)) { ok = false; break; }
             tc_fence_after();
-            const uint32_t xa = xbase + xs * XST;
-#pragma unroll
-            for (int ks = 0; ks < 4; ++ks)
-              mma_f16_ts(dt, tmem + ACOL + as * 32 + ks * 8, sdesc_sw128(xa + ks * 32), idesc,
-                         (kb > kb0 || ks > 0) ? 1u : 0u);
+            const uint32_t a = a0 + as * 64;
+            const uint64_t b = bd0 + xs * bstep;
+            const bool fresh = st == ch * sch;
+            mma_f16_ts(dt, a, b, idesc, fresh ? 0u : 1u);
+            mma_f16_ts(dt, a + 8, b + 2, idesc, 1u);
+            mma_f16_ts(dt, a + 16, b + 4, idesc, 1u);
+            mma_f16_ts(dt, a + 24, b + 6, idesc, 1u);
+            mma_f16_ts(dt, a + 32, b + bsub, idesc, 1u);
+            mma_f16_ts(dt, a + 40, b + bsub + 2, idesc, 1u);
+            mma_f16_ts(dt, a + 48, b + bsub + 4, idesc, 1u);
+            mma_f16_ts(dt, a + 56, b + bsub + 6, idesc, 1u);
             mma_commit(&aempty[as]);
-            mma_commit(&xempty[xs]);
           }
           if (!ok) break;
           mma_commit(&accfull[r]);
@@ -255,22 +271,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp < kWarpEpi0) {
     // ------------------------------------------------------------------ dequant warpgroups
-    const uint32_t wg = (warp - kWarpDq0) >> 2;  // 0: even K blocks, 1: odd
-    const int q = warp & 3;                      // TMEM lane quarter
-    const int r = q * 32 + lane;                 // row within the tile
+    const int half = (warp - kWarpDq0) >> 2;  // 0: first 64-K block of each stage, 1: second
+    const int q = warp & 3;                   // TMEM lane quarter
+    const int r = q * 32 + lane;              // row within the tile
+    const bool releaser = (warp == kWarpDq0) && lane == 0;  // frees activation slots for the MMA
     Sched<BN> sc(p);
     int rt, t0, nt;
-    uint32_t c = 0;
+    uint32_t s = 0;
     bool ok = true;
     const uint32_t wbase = smem_u32(smem + S::kWOff);
-    const uint32_t tl = tmem + ((uint32_t)(q * 32) << 16) + ACOL;
+    const uint32_t tl = tmem + ((uint32_t)(q * 32) << 16) + ACOL + 32 * half;
     while (ok && sc.next(rt, t0, nt)) {
-      for (int kb = 0; kb < nkb; ++kb, ++c) {
-        if ((c & 1) != wg) continue;
-        const uint32_t sbc = c >> 2, ws = sbc % NSW, wph = (sbc / NSW) & 1;
-        const uint32_t as = c % NA, aph = (c / NA) & 1;
+      for (int st = 0; st < nst; ++st, ++s) {
+        const int kb = 2 * st + half;              // 64-K block within the tile
+        const uint32_t sbc = (s >> 1), ws = sbc % NSW, wph = (sbc / NSW) & 1;  // super-block = 2 stages
+        const uint32_t as = s & 1, aph = (s >> 1) & 1;
         if (!mbar_wait(&wfull[ws], wph, p.status, kStatusTimeoutFull)) { ok = false; break; }
         if (!mbar_wait(&aempty[as], aph ^ 1, p.status, kStatusTimeoutEmpty)) { ok = false; break; }
+        // The MMA has finished stage s - 2, so its activation slot can be refilled.
+        if (releaser && s >= 2) mbar_arrive(&xempty[(s - 2) % kNSX]);
         const int j = kb & 3;
         const uint32_t rb = wbase + ws * S::kWStage + r * WBOX;
         uint32_t v[32];
@@ -286,9 +305,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(&wempty[ws]);
         }
-        tmem_st32(tl + as * 32, v);
+        tmem_st32(tl + as * 64, v);
         tmem_wait_st();
         tc_fence_before();
+        if (!mbar_wait(&xfull[s % kNSX], (s / kNSX) & 1, p.status, kStatusTimeoutFull)) { ok = false; break; }
         __syncwarp();
         if (lane == 0) mbar_arrive(&afull[as]);
       }
@@ -317,17 +337,21 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_wait_ld();
           if (!row_ok) continue;
           const int jn = min(32, nt - j0);
+          float prev[32];
+          if (!first) {  // all partial-sum loads first: one L2 round trip per 32 columns
+#pragma unroll
+            for (int jj = 0; jj < 32; ++jj) prev[jj] = jj < jn ? __ldcg(part + (size_t)(j0 + jj) * kBM) : 0.f;
+          }
 #pragma unroll
           for (int jj = 0; jj < 32; ++jj) {
             if (jj >= jn) break;
             const int col = j0 + jj;
             float acc = __uint_as_float(v[jj]);
+            if (!first) acc = prev[jj] + acc;
             if (!last) {
-              float* cell = part + (size_t)col * kBM;
-              *cell = first ? acc : *cell + acc;
+              __stcg(part + (size_t)col * kBM, acc);
               continue;
             }
-            if (!first) acc = part[(size_t)col * kBM] + acc;
             const int64_t t = t0 + col;
             if (EPI == kEpiResid) acc += __ldg(p.aux + t * p.ldaux + row);
             if (EPI == kEpiSwiglu) acc = silu_f(__ldg(p.aux + t * p.ldaux + row)) * acc;
@@ -390,7 +414,7 @@ cudaError_t launch_t(const QGemmArgs& a, cudaStream_t stream) {
   {
     cuuint64_t dims[2] = {(cuuint64_t)a.K, (cuuint64_t)a.M};
     cuuint64_t strides[1] = {(cuuint64_t)a.ldx * 2};
-    cuuint32_t box[2] = {64, (cuuint32_t)BN};
+    cuuint32_t box[2] = {64, (cuuint32_t)BN};  // one 64-K tile; a stage loads two
     cuuint32_t es[2] = {1, 1};
     if (enc(&mx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(a.x), dims, strides, box, es,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -402,7 +426,7 @@ cudaError_t launch_t(const QGemmArgs& a, cudaStream_t stream) {
   p.K = (int)a.K;
   p.M = (int)a.M;
   p.kb_off = (int)a.kb_off;
-  p.kcb = (a.kchunk > 0 && a.kchunk < a.K) ? (int)(a.kchunk / 64) : (int)(a.K / 64);
+  p.kcb = (a.kchunk > 0 && a.kchunk < a.K) ? (int)(a.kchunk / 64) : (int)(a.K / 64);  // even: whole stages
   p.scratch = a.scratch;
   p.y = a.y;
   p.ldy = a.ldy;
