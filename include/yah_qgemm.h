@@ -104,6 +104,10 @@ int yah_status_word(int* code);
 int yah_qgemm_footprint(int ggml_type, int64_t N, int64_t K, int64_t w_row_stride, int64_t kb_off, int64_t M,
                         int64_t ldx, int y_dtype, int64_t ldy, int64_t* w_bytes, int64_t* x_bytes, int64_t* y_bytes);
 
+/* Launch limits of the tile GEMM on the current device: SMs, and the 2-CTA clusters that can be resident at
+ * once (0 when the device offers no clusters; the tuner's search space, engine/tune/tune.py:77). */
+int yah_qgemm_limits(int* sm_count, int* max_pairs);
+
 /* Dequantise rows x K values of a GGUF weight to f16 out[rows][ldo] with the tile GEMM's own decode,
  * bit-identical to the reference dequant (gen_gemm_tile.py kind "dequant", :314-327; checked as
  * dq_bfp16_check.py:87-92). w: rows at w_row_stride bytes (2-byte aligned), K window from super-block kb_off.
@@ -124,16 +128,19 @@ int yah_qgemm(const void* w, int ggml_type, int64_t N, int64_t K, int64_t w_row_
               const void* aux, int64_t ldaux, void* stream);
 
 /* yah_qgemm with an explicit tile choice (the tuner's knob set, engine/tune/tune.py:77):
- *   bn      tokens per tile: 64, 128 or 192 (0 = default 192);
+ *   bn      tokens per tile: 256, 160 or 128 for 2-SM pairs, 192, 128 or 64 for single CTAs (0 = auto:
+ *           256, or 160 when accumulating in chunks, for pairs; 192 for single CTAs);
  *   grid    persistent CTAs (0 = one per SM);
  *   kchunk  K per f32 accumulation chunk, a multiple of 128 (0 = auto: 2048 when K > 4096, else all of K;
  *           -1 = never chunk). Chunk results are summed in f32 round-to-nearest; see the accuracy note in
  *           csrc/qgemm_tc.cu. Chunking uses a library-owned per-device scratch buffer (grid * bn * 512 bytes),
- *           so chunked calls on different streams of one device must not overlap.
- * Every (bn, grid) choice gives identical results for a given kchunk. */
+ *           so chunked calls on different streams of one device must not overlap;
+ *   cta_pair  1: 2-SM pairs (256 weight rows per tile, tcgen05 cta_group::2 over clusters of 2 CTAs),
+ *           0: one CTA per 128-row tile, -1: auto (pairs where the device supports clusters).
+ * Every (bn, grid, cta_pair) choice gives identical results for a given kchunk. */
 int yah_qgemm_tile(const void* w, int ggml_type, int64_t N, int64_t K, int64_t w_row_stride, int64_t kb_off,
                    const void* x, int64_t M, int64_t ldx, void* y, int y_dtype, int64_t ldy, int epilogue,
-                   const void* aux, int64_t ldaux, int bn, int grid, int64_t kchunk, void* stream);
+                   const void* aux, int64_t ldaux, int bn, int grid, int64_t kchunk, int cta_pair, void* stream);
 
 /* Decode GEMV, 1 <= M <= 32 tokens (replaces gen_gemv.py's gv_{plain,resid}_<fmt>_<M>_<K> kernels and the
  * LoomDecoder::Gemv call site, engine/model/loom_decoder.hpp:415-439). Same layouts and alignment rules as

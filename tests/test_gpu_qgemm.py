@@ -45,7 +45,7 @@ def test_golden_gemm(pkg, F, O, dev, name):
 
 @pytest.mark.parametrize("name", FMTS)
 @pytest.mark.parametrize("M,N,K", [(1, 128, 256), (7, 320, 1024), (48, 1000, 2048), (300, 256, 4096),
-                                   (513, 384, 512)])
+                                   (513, 384, 512), (33, 130, 768)])
 def test_qgemm_shapes(pkg, F, O, dev, name, M, N, K):
     t = F.type_of(name)
     if F.row_bytes(t, K) % 16:
@@ -100,34 +100,44 @@ def test_k_window_and_strides(pkg, F, O, dev, name):
     assert np.isnan(yy[:, N:]).all()
 
 
-@pytest.mark.parametrize("bn", [64, 128, 192])
-@pytest.mark.parametrize("grid", [0, 1, 5, 37])
+@pytest.mark.parametrize("pair,bn", [(0, 64), (0, 128), (0, 192), (1, 128), (1, 160), (1, 256)])
+@pytest.mark.parametrize("grid", [0, 2, 6, 38])
 @pytest.mark.parametrize("kchunk", [-1, 512])
-def test_tile_choices_are_identical(pkg, F, O, dev, bn, grid, kchunk):
-    """Every legal tile gives the same bits for a given accumulation chunk (the reference tuner's hash check,
-    engine/tune/tune.py:13)."""
+def test_tile_choices_are_identical(pkg, F, O, dev, bn, grid, kchunk, pair):
+    """Every legal tile (width, persistent grid, single CTA or 2-SM pair) gives the same bits for a given
+    accumulation chunk (the reference tuner's hash check, engine/tune/tune.py:13)."""
     t = F.Q4_K
     M, N, K = 300, 640, 2048
     w = F.synth_weights(t, N, K, seed=1)
     x = F.synth_activations(M, K, seed=2)
-    base = pkg.ops.qgemm(dev, w, t, x, N=N, K=K, kchunk=kchunk)
-    y = pkg.ops.qgemm(dev, w, t, x, N=N, K=K, bn=bn, grid=grid, kchunk=kchunk)
+    base = pkg.ops.qgemm(dev, w, t, x, N=N, K=K, kchunk=kchunk, pair=0)
+    y = pkg.ops.qgemm(dev, w, t, x, N=N, K=K, bn=bn, grid=grid, kchunk=kchunk, pair=pair)
     assert np.array_equal(y.view(np.uint32), base.view(np.uint32))
     check(O, y, O.gemm_ref(O.dequant_f16(t, w, N, K), x))
 
 
 @pytest.mark.parametrize("kchunk", [128, 256, 1152, 2048])
-def test_chunked_accumulation(pkg, F, O, dev, kchunk):
+@pytest.mark.parametrize("pair,bn", [(0, 0), (1, 0), (1, 256)])
+def test_chunked_accumulation(pkg, F, O, dev, kchunk, pair, bn):
     """Chunked accumulation (chunk sums added in f32 round-to-nearest) matches the oracle for any chunk length,
-    including chunks that do not divide K, with every epilogue."""
+    including chunks that do not divide K, with every epilogue, also with a single accumulator region."""
     t = F.Q4_K
     M, N, K = 200, 384, 4096
     w = F.synth_weights(t, N, K, seed=8)
     x = F.synth_activations(M, K, seed=9)
     acc = O.gemm_ref(O.dequant_f16(t, w, N, K), x)
-    check(O, pkg.ops.qgemm(dev, w, t, x, N=N, K=K, kchunk=kchunk), acc)
+    check(O, pkg.ops.qgemm(dev, w, t, x, N=N, K=K, kchunk=kchunk, pair=pair, bn=bn), acc)
     resid = np.random.default_rng(1).standard_normal((M, N)).astype(np.float32)
-    check(O, pkg.ops.qgemm(dev, w, t, x, N=N, K=K, kind="kres", aux=resid, kchunk=kchunk), acc + resid)
+    check(O, pkg.ops.qgemm(dev, w, t, x, N=N, K=K, kind="kres", aux=resid, kchunk=kchunk, pair=pair, bn=bn),
+          acc + resid)
+
+
+def test_invalid_tile_is_refused(pkg, F, dev):
+    t = F.Q4_K
+    w = F.synth_weights(t, 128, 256, seed=0)
+    x = F.synth_activations(4, 256, seed=0)
+    with pytest.raises(pkg.YahError):
+        pkg.ops.qgemm(dev, w, t, x, N=128, K=256, bn=256, pair=0)
 
 
 def test_row_shards_match_full(pkg, F, dev):

@@ -46,11 +46,12 @@ SYMBOLS = {
     "yah_status_word": (c_int, [P(c_int)]),
     "yah_qgemm_footprint": (c_int, [c_int, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_int, c_i64,
                                     P(c_i64), P(c_i64), P(c_i64)]),
+    "yah_qgemm_limits": (c_int, [P(c_int), P(c_int)]),
     "yah_dequant": (c_int, [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_vp, c_i64, c_vp]),
     "yah_qgemm": (c_int, [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_int, c_i64, c_int,
                           c_vp, c_i64, c_vp]),
     "yah_qgemm_tile": (c_int, [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_int, c_i64,
-                               c_int, c_vp, c_i64, c_int, c_int, c_i64, c_vp]),
+                               c_int, c_vp, c_i64, c_int, c_int, c_i64, c_int, c_vp]),
     "yah_qgemv": (c_int, [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_int, c_i64, c_int,
                           c_vp, c_i64, c_vp]),
 }

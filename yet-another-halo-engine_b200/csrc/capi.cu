@@ -47,6 +47,7 @@ struct DevState {
   size_t counters_n = 0;
   float* gemm_scratch = nullptr;  // chunked-accumulation sums of the tile GEMM
   size_t gemm_scratch_bytes = 0;
+  int max_pairs = -1;             // resident 2-CTA clusters of the tile GEMM (-1: not queried yet)
 };
 
 // Grow a per-device buffer to at least `need` bytes (cudaFree synchronises the device, so no launch still uses
@@ -293,6 +294,19 @@ int yah_status_word(int* code) {
   return YAH_OK;
 }
 
+int yah_qgemm_limits(int* sm_count, int* max_pairs) {
+  DevState* s;
+  int rc = dev_state(&s);
+  if (rc) return rc;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (s->max_pairs < 0) s->max_pairs = yah::qgemm_max_pairs(YAH_Q4_K, 192);
+  }
+  if (sm_count) *sm_count = s->sms;
+  if (max_pairs) *max_pairs = s->max_pairs;
+  return YAH_OK;
+}
+
 int yah_qgemm_footprint(int t, int64_t N, int64_t K, int64_t w_row_stride, int64_t kb_off, int64_t M, int64_t ldx,
                         int y_dtype, int64_t ldy, int64_t* w_bytes, int64_t* x_bytes, int64_t* y_bytes) {
   const int sb = sb_bytes(t);
@@ -324,11 +338,9 @@ int yah_dequant(const void* w, int t, int64_t rows, int64_t K, int64_t w_row_str
 
 int yah_qgemm_tile(const void* w, int t, int64_t N, int64_t K, int64_t w_row_stride, int64_t kb_off, const void* x,
                    int64_t M, int64_t ldx, void* y, int y_dtype, int64_t ldy, int epilogue, const void* aux,
-                   int64_t ldaux, int bn, int grid, int64_t kchunk, void* stream) {
+                   int64_t ldaux, int bn, int grid, int64_t kchunk, int cta_pair, void* stream) {
   int rc = check_linear(w, t, N, K, w_row_stride, kb_off, x, M, ldx, y, y_dtype, ldy, epilogue, aux, ldaux);
   if (rc) return rc;
-  if (bn == 0) bn = 192;
-  if (bn != 64 && bn != 128 && bn != 192) return fail(YAH_ERR_ARG, "bn must be 64, 128 or 192 (got %d)", bn);
   if (grid < 0) return fail(YAH_ERR_ARG, "negative grid");
   if (kchunk == 0) kchunk = K > 4096 ? 2048 : K;  // see the accuracy note in qgemm_tc.cu
   if (kchunk < 0 || kchunk >= K) kchunk = K;
@@ -355,9 +367,20 @@ int yah_qgemm_tile(const void* w, int t, int64_t N, int64_t K, int64_t w_row_str
   a.status = s->status;
   a.num_sms = s->sms;
   a.grid = grid > s->sms ? s->sms : grid;
-  a.bn = bn;
   a.kchunk = kchunk;
   a.scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (s->max_pairs < 0) s->max_pairs = yah::qgemm_max_pairs(t, bn);
+  }
+  a.max_pairs = s->max_pairs;
+  a.pair = (cta_pair != 0 && a.max_pairs > 0) ? 1 : 0;
+  if (cta_pair == 1 && !a.pair) return fail(YAH_ERR_UNSUPPORTED, "2-CTA clusters are not available on this device");
+  if (bn == 0) bn = a.pair ? (kchunk < K ? 160 : 256) : 192;
+  if (a.pair ? (bn != 256 && bn != 160 && bn != 128) : (bn != 192 && bn != 128 && bn != 64))
+    return fail(YAH_ERR_ARG, "bn %d is not a %s tile width (pairs: 256, 160, 128; single CTAs: 192, 128, 64)", bn,
+                a.pair ? "2-SM pair" : "single-CTA");
+  a.bn = bn;
   if (kchunk < K) {
     std::lock_guard<std::mutex> lk(g_mu);
     const size_t need = (size_t)yah::qgemm_grid(a) * bn * 128 * sizeof(float);
@@ -372,7 +395,7 @@ int yah_qgemm(const void* w, int t, int64_t N, int64_t K, int64_t w_row_stride, 
               int64_t M, int64_t ldx, void* y, int y_dtype, int64_t ldy, int epilogue, const void* aux, int64_t ldaux,
               void* stream) {
   return yah_qgemm_tile(w, t, N, K, w_row_stride, kb_off, x, M, ldx, y, y_dtype, ldy, epilogue, aux, ldaux, 0, 0, 0,
-                        stream);
+                        -1, stream);
 }
 
 int yah_qgemv(const void* w, int t, int64_t N, int64_t K, int64_t w_row_stride, int64_t kb_off, const void* x,

@@ -29,7 +29,12 @@ struct QGemmArgs {
   int bn;               // max tokens per tile (64, 128, 192)
   int64_t kchunk;       // K per accumulation chunk (multiple of 64; 0: the whole K in one chunk)
   float* scratch;       // grid * bn * 128 f32 chunk sums when kchunk < K, else unused
+  int pair;             // 1: 2-SM pairs (tcgen05 cta_group::2, clusters of 2), 0: one CTA per tile
+  int max_pairs;        // resident 2-CTA clusters the device holds (pair mode)
 };
+
+// Resident 2-CTA clusters of the tile-GEMM kernel on the current device (0 if clusters are unavailable).
+int qgemm_max_pairs(int type, int bn);
 
 // Largest persistent grid and the chunk scratch a launch needs.
 int qgemm_grid(const QGemmArgs& a);

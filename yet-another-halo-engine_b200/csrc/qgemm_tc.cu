@@ -10,17 +10,21 @@
 //               128-byte swizzle) into one of 3 shared-memory slots.
 //   warp 14     weight producer: TMA loads of the raw super-blocks of 128 weight rows (one 256-K super-block per
 //               slot), decoupled from the activation ring so weights stream ahead on their own.
-//   warp 1      MMA issuer (one thread): per stage one barrier wait, one fence, 8 x tcgen05.mma.cta_group::1
-//               .kind::f16 (A = weights from TMEM, B = activations from shared memory, D = 128 rows x BN tokens
-//               f32 in one of two TMEM accumulator regions, used alternately so an epilogue overlaps the next
-//               accumulation) and one commit. tcgen05.mma issue is serialised with everything else the issuing
-//               thread executes, so its instruction stream is kept to that minimum: descriptors precomputed,
-//               stage slots compile-time, the activation-ready check folded into the A-stage barrier.
+//   warp 1      MMA issuer (one thread): per stage one barrier wait, one fence, 8 x tcgen05.mma.kind::f16
+//               (A = weights from TMEM, B = activations from shared memory, D = f32 in TMEM) and the commits
+//               that free the stage. tcgen05.mma issue is serialised with everything else the issuing thread
+//               executes, so its instruction stream is kept to that minimum: descriptors precomputed, the
+//               activation-ready check folded into the A-stage barrier.
+// 2-SM pairs (default): a cluster of 2 CTAs runs tcgen05.mma.cta_group::2 with M = 256: each CTA decodes its
+// own 128 weight rows into its TMEM and stages half of the tile's tokens, so each SM's shared memory carries half
+// of the activation traffic; the first CTA issues the MMAs and commits to both CTAs' barriers.
+// TMEM layout: NACC accumulator regions of BN columns (2 for BN <= 192, so an epilogue overlaps the next
+// accumulation; 1 for BN = 256) and then the A stages of 128 K (64 columns each, up to 4).
 //   warps 2-9   two dequant warpgroups (first / second 64-K block of a stage). Thread = weight row (= TMEM
 //               lane): it decodes its row's 64 values to f16 pairs in registers and tcgen05.st's them into the
 //               A stage in TMEM (after the two accumulators), so the dequantised tile never touches shared
-//               memory. Before marking the A stage full it also waits for the stage's activation tile, and it
-//               releases activation slots on the MMA's behalf once the MMA has finished with them.
+//               memory. Before marking the A stage full it also waits for the stage's activation tile, so the
+//               MMA issuer waits on one barrier per stage.
 //   warps 10-13 epilogue: tcgen05.ld of the accumulator, kstore / kres / swiglu, token-major global stores.
 // Accuracy: the tensor core's f32 accumulation truncates (round toward zero), which at K = 14336 costs ~0.04
 // absolute on |y| ~ 2000. For K above 4096 each tile is accumulated in chunks of `kcb` 64-K blocks, each chunk
@@ -61,15 +65,22 @@ struct Fmt<14> {  // Q6_K: a 224-B window from the 16-B boundary at or below the
   static constexpr int kSB = 210, kBox = 224, kNSW = 2;
 };
 
-constexpr int kNSX = 3;  // activation slots (stages of 128 K)
-constexpr int kNA = 2;   // A stages in TMEM (128 K = 64 columns each)
+// TMEM (512 columns) holds NACC accumulator regions of BN columns, then NA A stages of 128 K (64 columns).
+// NACC = 2 overlaps an epilogue with the next accumulation and is needed for chunked accumulation; NACC = 1
+// (BN = 256) trades that for four A stages.
+template <int BN, int NACC>
+struct TCfg {
+  static constexpr int kACol0 = NACC * BN;
+  static constexpr int kNA = (512 - NACC * BN) / 64 > 4 ? 4 : (512 - NACC * BN) / 64;
+  static_assert(kNA >= 2, "TMEM columns");
+};
 
-template <int BN>
+// Activation slots of 128 K: a CTA stages XR token rows (all of the tile's, or half in a pair).
+template <int XR>
 struct XCfg {
-  static constexpr int kSub = BN * 128;     // one 64-K activation tile: BN rows x 64 f16
+  static constexpr int kSub = XR * 128;     // one 64-K tile: XR rows x 64 f16
   static constexpr int kStage = 2 * kSub;   // a stage holds two
-  static constexpr int kACol0 = 2 * BN;     // A stages follow the two accumulator regions
-  static_assert(2 * BN + kNA * 64 <= 512, "TMEM columns");
+  static constexpr int kNSX = XR <= 128 ? 4 : 3;
 };
 
 struct KParams {
@@ -81,18 +92,19 @@ struct KParams {
   int64_t ldaux;
   float* scratch;       // [grid][BN][128] f32 chunk sums (chunked accumulation only)
   int* status;
-  int64_t total_units;  // row tiles x 16-token units
+  int64_t total_units;  // row tiles (of 128 rows, or 256 for a pair) x 16-token units
   int upr;              // 16-token units per row tile
+  int ncta;             // CTAs per tile: 1, or 2 for a 2-SM pair
 };
 
-template <int T, int BN>
+template <int T, int XR>  // XR: activation rows a CTA stages (the tile's tokens, or half of them in a pair)
 struct Smem {
   static constexpr int kWStage = ((kBM * Fmt<T>::kBox + 16) + 127) / 128 * 128;
-  static constexpr int kXBytes = kNSX * XCfg<BN>::kStage;
+  static constexpr int kXBytes = XCfg<XR>::kNSX * XCfg<XR>::kStage;
   static constexpr int kWOff = kXBytes;
   static constexpr int kBarOff = kWOff + Fmt<T>::kNSW * kWStage;
-  // barriers: xfull, xempty [NSX]; wfull, wempty [NSW]; afull, aempty [NA]; accfull, accempty [2]; drain
-  static constexpr int kNumBars = 2 * kNSX + 2 * Fmt<T>::kNSW + 2 * kNA + 5;
+  // barriers: xfull, xempty [NSX]; wfull, wempty [NSW]; afull, aempty [4]; accfull, accempty [2]; drain
+  static constexpr int kNumBars = 2 * XCfg<XR>::kNSX + 2 * Fmt<T>::kNSW + 2 * 4 + 5;
   static constexpr int kTmemSlotOff = kBarOff + kNumBars * 8;
   static constexpr int kBytes = kTmemSlotOff + 16;
   static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-byte alignment of the base
@@ -105,7 +117,7 @@ struct Sched {
   int64_t u, end;
   int upr, M;
   __device__ Sched(const KParams& p) : upr(p.upr), M(p.M) {
-    const int64_t G = gridDim.x, b = blockIdx.x;
+    const int64_t G = gridDim.x / p.ncta, b = blockIdx.x / p.ncta;  // a pair shares one range
     u = b * p.total_units / G;
     end = (b + 1) * p.total_units / G;
   }
@@ -124,16 +136,20 @@ struct Sched {
 
 __device__ __forceinline__ float silu_f(float g) { return g / (1.0f + __expf(-g)); }
 
-template <int T, int BN, int EPI, bool OUT_F16>
+template <int T, int BN, int NACC, int EPI, bool OUT_F16, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                     const KParams p) {
-  using S = Smem<T, BN>;
-  constexpr int XSUB = XCfg<BN>::kSub;
-  constexpr int XST = XCfg<BN>::kStage;
-  constexpr int ACOL = XCfg<BN>::kACol0;
+  constexpr int XROWS = PAIR ? BN / 2 : BN;  // a CTA of a pair stages half of the tokens
+  using S = Smem<T, XROWS>;
+  constexpr int XSUB = XCfg<XROWS>::kSub;
+  constexpr int XST = XCfg<XROWS>::kStage;
+  constexpr int kNSX = XCfg<XROWS>::kNSX;
+  constexpr int kNA = TCfg<BN, NACC>::kNA;
+  constexpr int ACOL = TCfg<BN, NACC>::kACol0;
   constexpr int NSW = Fmt<T>::kNSW;
   constexpr int WBOX = Fmt<T>::kBox;
+  constexpr int NCTA = PAIR ? 2 : 1;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::kBarOff);
@@ -141,14 +157,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* xempty = xfull + kNSX;
   uint64_t* wfull = xempty + kNSX;
   uint64_t* wempty = wfull + NSW;
-  uint64_t* afull = wempty + NSW;
-  uint64_t* aempty = afull + kNA;
-  uint64_t* accfull = aempty + kNA;  // [2]
-  uint64_t* accempty = accfull + 2;  // [2]
+  uint64_t* afull = wempty + NSW;    // the pair's first CTA counts both CTAs' dequant warps
+  uint64_t* aempty = afull + 4;
+  uint64_t* accfull = aempty + 4;    // [2]
+  uint64_t* accempty = accfull + 2;  // [2], counts both CTAs' epilogue warps
   uint64_t* drain = accempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::kTmemSlotOff);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = PAIR ? cluster_rank() : 0;  // 0 issues the pair's MMAs
   const int nst = p.K / 128;                  // 128-K stages per tile
   const int sch = p.kcb / 2;                  // stages per accumulation chunk
   const int nch = (nst + sch - 1) / sch;      // accumulation chunks per tile
@@ -162,25 +179,33 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&wfull[i], 1);
       mbar_init(&wempty[i], 8);  // 4 warps x 2 dequant warpgroups
     }
-    for (int i = 0; i < kNA; ++i) {
-      mbar_init(&afull[i], 8);   // every dequant warp (each also saw the activation tile land)
+    for (int i = 0; i < 4; ++i) {
+      mbar_init(&afull[i], 8 * NCTA);   // every dequant warp (each also saw its activation tile land)
       mbar_init(&aempty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&accfull[i], 1);
-      mbar_init(&accempty[i], 4);
+      mbar_init(&accempty[i], 4 * NCTA);
     }
     mbar_init(drain, 1);
     fence_barrier_init();
   }
   if (warp == kWarpMma) {
-    tmem_alloc(tmem_slot, 512);
-    tmem_relinquish();
+    if (PAIR) {
+      tmem_alloc_pair(tmem_slot, 512);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, 512);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if (PAIR) cluster_sync(); else __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // Barriers the pair's first CTA owns, as addresses the second CTA can arrive on.
+  const uint32_t afull_lead = PAIR ? mapa_shared(smem_u32(afull), 0) : smem_u32(afull);
+  const uint32_t accempty_lead = PAIR ? mapa_shared(smem_u32(accempty), 0) : smem_u32(accempty);
 
   if (warp == kWarpX) {
     // ------------------------------------------------------------------ activation producer
@@ -191,12 +216,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t s = 0;  // stages issued
       bool ok = true;
       while (ok && sc.next(rt, t0, nt)) {
+        // a pair splits the tile's tokens: CTA r holds columns [r * n / 2, (r + 1) * n / 2) of the MMA's N
+        const int ty = PAIR ? t0 + (int)rank * (((nt + 31) & ~31) / 2) : t0;
         for (int st = 0; st < nst; ++st, ++s) {
           const uint32_t xs = s % kNSX, xph = (s / kNSX) & 1;
           if (!mbar_wait(&xempty[xs], xph ^ 1, p.status, kStatusTimeoutEmpty)) { ok = false; break; }
           mbar_arrive_expect_tx(&xfull[xs], XST);
-          tma_load_2d(smem + xs * XST, &tmap_x, &xfull[xs], st * 128, t0);
-          tma_load_2d(smem + xs * XST + XSUB, &tmap_x, &xfull[xs], st * 128 + 64, t0);
+          tma_load_2d(smem + xs * XST, &tmap_x, &xfull[xs], st * 128, ty);
+          tma_load_2d(smem + xs * XST + XSUB, &tmap_x, &xfull[xs], st * 128 + 64, ty);
         }
       }
       for (uint32_t i = (s > (uint32_t)kNSX ? s - kNSX : 0); i < s; ++i)
@@ -211,6 +238,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t s = 0;
       bool ok = true;
       while (ok && sc.next(rt, t0, nt)) {
+        const int row0 = (rt * NCTA + (int)rank) * kBM;
         for (int sb = 0; sb < p.K / 256; ++sb, ++s) {
           const uint32_t ws = s % NSW, wph = (s / NSW) & 1;
           if (!mbar_wait(&wempty[ws], wph ^ 1, p.status, kStatusTimeoutEmpty)) { ok = false; break; }
@@ -219,62 +247,76 @@ __global__ void __launch_bounds__(kThreads, 1)
           int xw;
           if (T == 14) xw = (int)(((sbg * 210) & ~int64_t(15)) >> 1);
           else xw = (int)(sbg * (Fmt<T>::kSB / 2));
-          tma_load_2d(smem + S::kWOff + ws * S::kWStage, &tmap_w, &wfull[ws], xw, rt * kBM);
+          tma_load_2d(smem + S::kWOff + ws * S::kWStage, &tmap_w, &wfull[ws], xw, row0);
         }
       }
       for (uint32_t i = (s > (uint32_t)NSW ? s - NSW : 0); i < s; ++i)
         mbar_wait(&wfull[i % NSW], (i / NSW) & 1, p.status, kStatusTimeoutDrain, false);
     }
   } else if (warp == kWarpMma) {
-    // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    // ------------------------------------------------------------------ MMA issuer (pair: first CTA only)
+    if (lane == 0 && rank == 0) {
       Sched<BN> sc(p);
       int rt, t0, nt;
       uint32_t s = 0, u = 0;  // stage and accumulation-unit counters
       bool ok = true;
-      // B descriptors of the 3 activation slots (second 64-K tile: + XSUB bytes) and the 2 A-stage columns
       const uint64_t bd0 = sdesc_sw128(smem_u32(smem));
       const uint64_t bstep = (uint64_t)(XST >> 4), bsub = (uint64_t)(XSUB >> 4);
       const uint32_t a0 = tmem + ACOL;
       while (ok && sc.next(rt, t0, nt)) {
-        const uint32_t idesc = idesc_f16_f32(kBM, (nt + 15) & ~15);
+        const uint32_t idesc = PAIR ? idesc_f16_f32(2 * kBM, (nt + 31) & ~31) : idesc_f16_f32(kBM, (nt + 15) & ~15);
         for (int ch = 0; ok && ch < nch; ++ch, ++u) {
-          const uint32_t r = u & 1;
-          if (!mbar_wait(&accempty[r], ((u >> 1) & 1) ^ 1, p.status, kStatusTimeoutEmpty)) { ok = false; break; }
+          const uint32_t r = u % NACC, rph = (u / NACC) & 1;
+          const bool acc_free = mbar_wait(&accempty[r], rph ^ 1, p.status, kStatusTimeoutEmpty);
+          if (!acc_free) { ok = false; break; }
           tc_fence_after();
           const uint32_t dt = tmem + r * BN;
           const int st1 = min(nst, (ch + 1) * sch);
           for (int st = ch * sch; st < st1; ++st, ++s) {
-            const uint32_t as = s & 1, xs = s % kNSX;
-            if (!mbar_wait(&afull[as], (s >> 1) & 1, p.status, kStatusTimeoutFull)) { ok = false; break; }
+            const uint32_t as = s % kNA, xs = s % kNSX;
+            const bool ready = mbar_wait(&afull[as], (s / kNA) & 1, p.status, kStatusTimeoutFull);
+            if (!ready) { ok = false; break; }
             tc_fence_after();
             const uint32_t a = a0 + as * 64;
             const uint64_t b = bd0 + xs * bstep;
-            const bool fresh = st == ch * sch;
-            mma_f16_ts(dt, a, b, idesc, fresh ? 0u : 1u);
-            mma_f16_ts(dt, a + 8, b + 2, idesc, 1u);
-            mma_f16_ts(dt, a + 16, b + 4, idesc, 1u);
-            mma_f16_ts(dt, a + 24, b + 6, idesc, 1u);
-            mma_f16_ts(dt, a + 32, b + bsub, idesc, 1u);
-            mma_f16_ts(dt, a + 40, b + bsub + 2, idesc, 1u);
-            mma_f16_ts(dt, a + 48, b + bsub + 4, idesc, 1u);
-            mma_f16_ts(dt, a + 56, b + bsub + 6, idesc, 1u);
-            mma_commit(&aempty[as]);
+            const uint32_t acc0 = st == ch * sch ? 0u : 1u;
+            if (PAIR) {
+              mma_f16_ts_pair(dt, a, b, idesc, acc0);
+              mma_f16_ts_pair(dt, a + 8, b + 2, idesc, 1u);
+              mma_f16_ts_pair(dt, a + 16, b + 4, idesc, 1u);
+              mma_f16_ts_pair(dt, a + 24, b + 6, idesc, 1u);
+              mma_f16_ts_pair(dt, a + 32, b + bsub, idesc, 1u);
+              mma_f16_ts_pair(dt, a + 40, b + bsub + 2, idesc, 1u);
+              mma_f16_ts_pair(dt, a + 48, b + bsub + 4, idesc, 1u);
+              mma_f16_ts_pair(dt, a + 56, b + bsub + 6, idesc, 1u);
+              mma_commit_pair(&aempty[as], 3);
+              mma_commit_pair(&xempty[xs], 3);
+            } else {
+              mma_f16_ts(dt, a, b, idesc, acc0);
+              mma_f16_ts(dt, a + 8, b + 2, idesc, 1u);
+              mma_f16_ts(dt, a + 16, b + 4, idesc, 1u);
+              mma_f16_ts(dt, a + 24, b + 6, idesc, 1u);
+              mma_f16_ts(dt, a + 32, b + bsub, idesc, 1u);
+              mma_f16_ts(dt, a + 40, b + bsub + 2, idesc, 1u);
+              mma_f16_ts(dt, a + 48, b + bsub + 4, idesc, 1u);
+              mma_f16_ts(dt, a + 56, b + bsub + 6, idesc, 1u);
+              mma_commit(&aempty[as]);
+              mma_commit(&xempty[xs]);
+            }
           }
           if (!ok) break;
-          mma_commit(&accfull[r]);
+          if (PAIR) mma_commit_pair(&accfull[r], 3); else mma_commit(&accfull[r]);
         }
       }
       // Drain: every MMA issued by this thread completes before TMEM is released.
-      mma_commit(drain);
+      if (PAIR) mma_commit_pair(drain, 1); else mma_commit(drain);
       mbar_wait(drain, 0, p.status, kStatusTimeoutDrain, false);
     }
   } else if (warp < kWarpEpi0) {
     // ------------------------------------------------------------------ dequant warpgroups
     const int half = (warp - kWarpDq0) >> 2;  // 0: first 64-K block of each stage, 1: second
     const int q = warp & 3;                   // TMEM lane quarter
-    const int r = q * 32 + lane;              // row within the tile
-    const bool releaser = (warp == kWarpDq0) && lane == 0;  // frees activation slots for the MMA
+    const int r = q * 32 + lane;              // row within the CTA's 128 rows
     Sched<BN> sc(p);
     int rt, t0, nt;
     uint32_t s = 0;
@@ -285,11 +327,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int st = 0; st < nst; ++st, ++s) {
         const int kb = 2 * st + half;              // 64-K block within the tile
         const uint32_t sbc = (s >> 1), ws = sbc % NSW, wph = (sbc / NSW) & 1;  // super-block = 2 stages
-        const uint32_t as = s & 1, aph = (s >> 1) & 1;
+        const uint32_t as = s % kNA, aph = (s / kNA) & 1;
         if (!mbar_wait(&wfull[ws], wph, p.status, kStatusTimeoutFull)) { ok = false; break; }
         if (!mbar_wait(&aempty[as], aph ^ 1, p.status, kStatusTimeoutEmpty)) { ok = false; break; }
-        // The MMA has finished stage s - 2, so its activation slot can be refilled.
-        if (releaser && s >= 2) mbar_arrive(&xempty[(s - 2) % kNSX]);
         const int j = kb & 3;
         const uint32_t rb = wbase + ws * S::kWStage + r * WBOX;
         uint32_t v[32];
@@ -310,7 +350,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_before();
         if (!mbar_wait(&xfull[s % kNSX], (s / kNSX) & 1, p.status, kStatusTimeoutFull)) { ok = false; break; }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&afull[as]);
+        if (lane == 0) {
+          if (PAIR) mbar_arrive_cluster(afull_lead + as * 8);
+          else mbar_arrive(&afull[as]);
+        }
       }
     }
   } else if (warp < kWarpW) {
@@ -324,11 +367,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tl = tmem + ((uint32_t)(q * 32) << 16);
     float* part = p.scratch ? p.scratch + (size_t)blockIdx.x * BN * kBM + rloc : nullptr;
     while (ok && sc.next(rt, t0, nt)) {
-      const int row = rt * kBM + rloc;
+      const int row = (rt * NCTA + (int)rank) * kBM + rloc;
       const bool row_ok = row < p.N;
       for (int ch = 0; ch < nch; ++ch, ++u) {
-        const uint32_t r = u & 1;
-        if (!mbar_wait(&accfull[r], (u >> 1) & 1, p.status, kStatusTimeoutFull)) { ok = false; break; }
+        const uint32_t r = u % NACC;
+        if (!mbar_wait(&accfull[r], (u / NACC) & 1, p.status, kStatusTimeoutFull)) { ok = false; break; }
         tc_fence_after();
         const bool first = ch == 0, last = ch == nch - 1;
         for (int j0 = 0; j0 < nt; j0 += 32) {
@@ -363,16 +406,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&accempty[r]);
+        if (lane == 0) {
+          if (PAIR) mbar_arrive_cluster(accempty_lead + r * 8);
+          else mbar_arrive(&accempty[r]);
+        }
       }
     }
   }
 
   tc_fence_before();
-  __syncthreads();
+  if (PAIR) cluster_sync(); else __syncthreads();
   if (warp == kWarpMma) {
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    if (PAIR) tmem_dealloc_pair(tmem, 512); else tmem_dealloc(tmem, 512);
   }
 }
 
@@ -394,9 +440,13 @@ EncodeTiledFn encoder() {
   return fn;
 }
 
-template <int T, int BN, int EPI, bool OUT_F16>
+// Dynamic shared memory is at least this much, so that one CTA (which owns all 512 TMEM columns) fills an SM.
+constexpr int kMinSmem = 120 * 1024;
+
+template <int T, int BN, int NACC, int EPI, bool OUT_F16, bool PAIR>
 cudaError_t launch_t(const QGemmArgs& a, cudaStream_t stream) {
-  using S = Smem<T, BN>;
+  constexpr int XROWS = PAIR ? BN / 2 : BN;
+  using S = Smem<T, XROWS>;
   EncodeTiledFn enc = encoder();
   if (!enc) return cudaErrorNotSupported;
   CUtensorMap mw, mx;
@@ -414,7 +464,7 @@ cudaError_t launch_t(const QGemmArgs& a, cudaStream_t stream) {
   {
     cuuint64_t dims[2] = {(cuuint64_t)a.K, (cuuint64_t)a.M};
     cuuint64_t strides[1] = {(cuuint64_t)a.ldx * 2};
-    cuuint32_t box[2] = {64, (cuuint32_t)BN};  // one 64-K tile; a stage loads two
+    cuuint32_t box[2] = {64, (cuuint32_t)XROWS};  // one 64-K tile of this CTA's tokens; a stage loads two
     cuuint32_t es[2] = {1, 1};
     if (enc(&mx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(a.x), dims, strides, box, es,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -434,28 +484,55 @@ cudaError_t launch_t(const QGemmArgs& a, cudaStream_t stream) {
   p.ldaux = a.ldaux;
   p.status = a.status;
   p.upr = (int)((a.M + 15) / 16);
-  const int64_t rtiles = (a.N + kBM - 1) / kBM;
+  p.ncta = PAIR ? 2 : 1;
+  const int64_t rtiles = (a.N + kBM * p.ncta - 1) / (kBM * p.ncta);
   p.total_units = rtiles * p.upr;
   const int grid = qgemm_grid(a);
-  auto kern = qgemm_tc_kernel<T, BN, EPI, OUT_F16>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kAlloc);
+  auto kern = qgemm_tc_kernel<T, BN, NACC, EPI, OUT_F16, PAIR>;
+  const int smem_bytes = S::kAlloc > kMinSmem ? S::kAlloc : kMinSmem;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
   if (e != cudaSuccess) return e;
-  kern<<<grid, kThreads, S::kAlloc, stream>>>(mw, mx, p);
-  return cudaGetLastError();
+  if (!PAIR) {
+    kern<<<grid, kThreads, smem_bytes, stream>>>(mw, mx, p);
+    return cudaGetLastError();
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem_bytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, mw, mx, p);
 }
 
-template <int T, int BN>
-cudaError_t launch_bn(const QGemmArgs& a, cudaStream_t s) {
-  if (a.epilogue == kEpiResid) return launch_t<T, BN, kEpiResid, false>(a, s);
-  if (a.epilogue == kEpiSwiglu) return launch_t<T, BN, kEpiSwiglu, true>(a, s);
-  return a.y_f16 ? launch_t<T, BN, kEpiStore, true>(a, s) : launch_t<T, BN, kEpiStore, false>(a, s);
+template <int T, int BN, int NACC, bool PAIR>
+cudaError_t launch_epi(const QGemmArgs& a, cudaStream_t s) {
+  if (a.epilogue == kEpiResid) return launch_t<T, BN, NACC, kEpiResid, false, PAIR>(a, s);
+  if (a.epilogue == kEpiSwiglu) return launch_t<T, BN, NACC, kEpiSwiglu, true, PAIR>(a, s);
+  return a.y_f16 ? launch_t<T, BN, NACC, kEpiStore, true, PAIR>(a, s)
+                 : launch_t<T, BN, NACC, kEpiStore, false, PAIR>(a, s);
 }
 
+// Instantiated tiles: pairs at BN 256 (one accumulator region, 4 A stages), 160 and 128 (two regions); single
+// CTAs at BN 192, 128 and 64 (two regions). The C ABI only passes these combinations.
 template <int T>
 cudaError_t launch_fmt(const QGemmArgs& a, cudaStream_t s) {
-  if (a.bn == 128) return launch_bn<T, 128>(a, s);
-  if (a.bn == 64) return launch_bn<T, 64>(a, s);
-  return launch_bn<T, 192>(a, s);
+  if (a.pair) {
+    if (a.bn == 256) return launch_epi<T, 256, 1, true>(a, s);
+    if (a.bn == 160) return launch_epi<T, 160, 2, true>(a, s);
+    if (a.bn == 128) return launch_epi<T, 128, 2, true>(a, s);
+    return cudaErrorInvalidValue;
+  }
+  if (a.bn == 192) return launch_epi<T, 192, 2, false>(a, s);
+  if (a.bn == 128) return launch_epi<T, 128, 2, false>(a, s);
+  if (a.bn == 64) return launch_epi<T, 64, 2, false>(a, s);
+  return cudaErrorInvalidValue;
 }
 
 }  // namespace
@@ -463,10 +540,39 @@ cudaError_t launch_fmt(const QGemmArgs& a, cudaStream_t s) {
 bool tensor_map_encoder_available() { return encoder() != nullptr; }
 
 int qgemm_grid(const QGemmArgs& a) {
-  const int64_t units = (a.N + kBM - 1) / kBM * ((a.M + 15) / 16);
+  const int ncta = a.pair ? 2 : 1;
+  const int64_t units = (a.N + kBM * ncta - 1) / (kBM * ncta) * ((a.M + 15) / 16);
   int64_t grid = a.grid > 0 ? a.grid : a.num_sms;
+  if (a.pair) {
+    grid = grid / 2 < a.max_pairs ? grid / 2 : a.max_pairs;  // pairs that can be resident at once
+    if (grid > units) grid = units;
+    if (grid < 1) grid = 1;
+    return (int)(2 * grid);
+  }
   if (grid > units) grid = units;
   return (int)grid;
+}
+
+int qgemm_max_pairs(int type, int bn) {
+  // Clusters of 2 that the device can hold at once with this kernel's resources (one CTA per SM).
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = kMinSmem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  const void* k = (const void*)qgemm_tc_kernel<12, 256, 1, kEpiStore, true, true>;
+  (void)type;
+  (void)bn;
+  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kMinSmem) != cudaSuccess) return 0;
+  if (cudaOccupancyMaxActiveClusters(&n, k, &cfg) != cudaSuccess) return 0;
+  return n;
 }
 
 cudaError_t launch_qgemm_tc(const QGemmArgs& a, cudaStream_t stream) {

@@ -54,9 +54,9 @@ def footprint(fmt, N, K, w_row_stride, kb_off, M, ldx, y_dtype, ldy):
 
 # ----------------------------------------------------------------------------------------------- raw pointers
 def qgemm_ptr(w, fmt, N, K, w_row_stride, kb_off, x, M, ldx, y, y_dtype, ldy, kind="kstore", aux=None, ldaux=0,
-              stream=None, bn=0, grid=0, kchunk=0):
+              stream=None, bn=0, grid=0, kchunk=0, pair=-1):
     check(lib().yah_qgemm_tile(w, F.type_of(fmt), N, K, w_row_stride, kb_off, x, M, ldx, y, _dt(y_dtype), ldy,
-                               _epi(kind), aux, ldaux, bn, grid, kchunk, stream))
+                               _epi(kind), aux, ldaux, bn, grid, kchunk, pair, stream))
 
 
 def qgemv_ptr(w, fmt, N, K, w_row_stride, kb_off, x, M, ldx, y, y_dtype, ldy, kind="plain", aux=None, ldaux=0,
@@ -82,7 +82,7 @@ def _check_size(buf: DeviceBuffer, need: int, what: str):
 
 
 def qgemm(dev: Device, w, fmt, x, N=None, K=None, kind="kstore", out_dtype="f32", aux=None, kb_off=0,
-          w_row_stride=None, bn=0, grid=0, kchunk=0, gemv=False):
+          w_row_stride=None, bn=0, grid=0, kchunk=0, pair=-1, gemv=False):
     """y[M][N] = kind(x @ W^T) on the GPU; w: uint8 GGUF rows (numpy or DeviceBuffer), x: f16 [M][K] numpy."""
     t = F.type_of(fmt)
     x = np.ascontiguousarray(x, dtype=np.float16)
@@ -107,7 +107,7 @@ def qgemm(dev: Device, w, fmt, x, N=None, K=None, kind="kstore", out_dtype="f32"
         auxd = dev.upload(np.ascontiguousarray(aux, dtype=np.float32))
         _check_size(auxd, M * N * 4, "aux")
     fn = qgemv_ptr if gemv else qgemm_ptr
-    kw = {} if gemv else {"bn": bn, "grid": grid, "kchunk": kchunk}
+    kw = {} if gemv else {"bn": bn, "grid": grid, "kchunk": kchunk, "pair": pair}
     fn(wd.ptr, t, N, K, w_row_stride, kb_off, xd.ptr, M, x.shape[1], yd.ptr, ydt, N, ep,
        auxd.ptr if auxd else None, N if auxd else 0, **kw)
     dev.synchronize()
