@@ -5,10 +5,10 @@
 // is decoded inside the K loop to exactly the f16 values of the reference dequant, multiplied in f16 with f32
 // accumulation, and written token-major: out[t][r] at t * ldy + r (gen_gemm_tile.py:1230-1231).
 //
-// B200 design (one persistent CTA per SM, 15 warps). The K loop advances in stages of 128 K (two 64-K blocks):
+// B200 design (one persistent CTA per SM, 23 warps). The K loop advances in stages of 128 K (two 64-K blocks):
 //   warp 0      activation producer: per stage two TMA loads of 64-K activation tiles (BN tokens x 128 B,
 //               128-byte swizzle) into one of 3 shared-memory slots.
-//   warp 14     weight producer: TMA loads of the raw super-blocks of 128 weight rows (one 256-K super-block per
+//   warp 22     weight producer: TMA loads of the raw super-blocks of 128 weight rows (one 256-K super-block per
 //               slot), decoupled from the activation ring so weights stream ahead on their own.
 //   warp 1      MMA issuer (one thread): per stage one barrier wait, one fence, 8 x tcgen05.mma.kind::f16
 //               (A = weights from TMEM, B = activations from shared memory, D = f32 in TMEM) and the commits
@@ -20,12 +20,13 @@
 // of the activation traffic; the first CTA issues the MMAs and commits to both CTAs' barriers.
 // TMEM layout: NACC accumulator regions of BN columns (2 for BN <= 192, so an epilogue overlaps the next
 // accumulation; 1 for BN = 256) and then the A stages of 128 K (64 columns each, up to 4).
-//   warps 2-9   two dequant warpgroups (first / second 64-K block of a stage). Thread = weight row (= TMEM
-//               lane): it decodes its row's 64 values to f16 pairs in registers and tcgen05.st's them into the
-//               A stage in TMEM (after the two accumulators), so the dequantised tile never touches shared
-//               memory. Before marking the A stage full it also waits for the stage's activation tile, so the
-//               MMA issuer waits on one barrier per stage.
-//   warps 10-13 epilogue: tcgen05.ld of the accumulator, kstore / kres / swiglu, token-major global stores.
+//   warps 2-17  four dequant warpgroups: (first / second 64-K block of a stage) x (even / odd stages), so each
+//               warp has two stages of MMA time for its decode. Thread = weight row (= TMEM lane): it decodes its
+//               row's 64 values to f16 pairs in registers and tcgen05.st's them into the A stage in TMEM (after
+//               the accumulators), so the dequantised tile never touches shared memory. Before marking the A
+//               stage full it also waits for the stage's activation tile, so the MMA issuer waits on one
+//               barrier per stage.
+//   warps 18-21 epilogue: tcgen05.ld of the accumulator, kstore / kres / swiglu, token-major global stores.
 // Accuracy: the tensor core's f32 accumulation truncates (round toward zero), which at K = 14336 costs ~0.04
 // absolute on |y| ~ 2000. For K above 4096 each tile is accumulated in chunks of `kcb` 64-K blocks, each chunk
 // starting from zero in the free accumulator region; the epilogue sums the chunk results in f32 round-to-nearest
@@ -46,9 +47,10 @@
 namespace yah {
 namespace {
 
-constexpr int kThreads = 480;
+constexpr int kThreads = 736;
 constexpr int kBM = 128;  // weight rows per tile = TMEM lanes
-constexpr int kWarpX = 0, kWarpMma = 1, kWarpDq0 = 2, kWarpEpi0 = 10, kWarpW = 14;
+constexpr int kDqGroups = 4;  // dequant warpgroups: (64-K block of the stage) x (stage parity)
+constexpr int kWarpX = 0, kWarpMma = 1, kWarpDq0 = 2, kWarpEpi0 = 2 + 4 * kDqGroups, kWarpW = kWarpEpi0 + 4;
 
 template <int T>
 struct Fmt;
@@ -95,6 +97,7 @@ struct KParams {
   int64_t total_units;  // row tiles (of 128 rows, or 256 for a pair) x 16-token units
   int upr;              // 16-token units per row tile
   int ncta;             // CTAs per tile: 1, or 2 for a 2-SM pair
+  int tma_store;        // 1: the output is written with TMA stores through shared memory (tmap_y is valid)
 };
 
 template <int T, int XR>  // XR: activation rows a CTA stages (the tile's tokens, or half of them in a pair)
@@ -102,7 +105,9 @@ struct Smem {
   static constexpr int kWStage = ((kBM * Fmt<T>::kBox + 16) + 127) / 128 * 128;
   static constexpr int kXBytes = XCfg<XR>::kNSX * XCfg<XR>::kStage;
   static constexpr int kWOff = kXBytes;
-  static constexpr int kBarOff = kWOff + Fmt<T>::kNSW * kWStage;
+  static constexpr int kOutOff = kWOff + Fmt<T>::kNSW * kWStage;  // 2 output staging buffers (TMA stores)
+  static constexpr int kOutBuf = 4096;                            // 128 rows x 16 f16 or 8 f32 tokens
+  static constexpr int kBarOff = kOutOff + 2 * kOutBuf;
   // barriers: xfull, xempty [NSX]; wfull, wempty [NSW]; afull, aempty [4]; accfull, accempty [2]; drain
   static constexpr int kNumBars = 2 * XCfg<XR>::kNSX + 2 * Fmt<T>::kNSW + 2 * 4 + 5;
   static constexpr int kTmemSlotOff = kBarOff + kNumBars * 8;
@@ -139,7 +144,7 @@ __device__ __forceinline__ float silu_f(float g) { return g / (1.0f + __expf(-g)
 template <int T, int BN, int NACC, int EPI, bool OUT_F16, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
-                    const KParams p) {
+                    const __grid_constant__ CUtensorMap tmap_y, const KParams p) {
   constexpr int XROWS = PAIR ? BN / 2 : BN;  // a CTA of a pair stages half of the tokens
   using S = Smem<T, XROWS>;
   constexpr int XSUB = XCfg<XROWS>::kSub;
@@ -177,7 +182,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < NSW; ++i) {
       mbar_init(&wfull[i], 1);
-      mbar_init(&wempty[i], 8);  // 4 warps x 2 dequant warpgroups
+      mbar_init(&wempty[i], 4 * kDqGroups);  // every dequant warp reads one 64-K block of each super-block
     }
     for (int i = 0; i < 4; ++i) {
       mbar_init(&afull[i], 8 * NCTA);   // every dequant warp (each also saw its activation tile land)
@@ -314,7 +319,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp < kWarpEpi0) {
     // ------------------------------------------------------------------ dequant warpgroups
-    const int half = (warp - kWarpDq0) >> 2;  // 0: first 64-K block of each stage, 1: second
+    const int g = (warp - kWarpDq0) >> 2;
+    const int half = g & 1;                   // 0: first 64-K block of the stage, 1: second
+    const uint32_t parity = (uint32_t)(g >> 1);  // stages this warpgroup handles: s % 2 == parity
     const int q = warp & 3;                   // TMEM lane quarter
     const int r = q * 32 + lane;              // row within the CTA's 128 rows
     Sched<BN> sc(p);
@@ -325,6 +332,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tl = tmem + ((uint32_t)(q * 32) << 16) + ACOL + 32 * half;
     while (ok && sc.next(rt, t0, nt)) {
       for (int st = 0; st < nst; ++st, ++s) {
+        if ((s & 1) != parity) continue;
         const int kb = 2 * st + half;              // 64-K block within the tile
         const uint32_t sbc = (s >> 1), ws = sbc % NSW, wph = (sbc / NSW) & 1;  // super-block = 2 stages
         const uint32_t as = s % kNA, aph = (s / kNA) & 1;
@@ -341,10 +349,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int o = (int)((((int64_t)p.kb_off + (kb >> 2)) * 210) & 15);
           q6k_decode_smem(rb, j, o, v);
         }
-        if (j >= 2) {  // this warpgroup's last read of the weight stage
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&wempty[ws]);
-        }
+        __syncwarp();  // the warp's only read of this weight slot is done
+        if (lane == 0) mbar_arrive(&wempty[ws]);
         tmem_st32(tl + as * 64, v);
         tmem_wait_st();
         tc_fence_before();
@@ -358,51 +364,92 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp < kWarpW) {
     // ------------------------------------------------------------------ epilogue
+    // Accumulator columns are drained CH at a time (CH = 16 f16 / 8 f32 tokens); the final values go to a
+    // [CH tokens][128 rows] shared-memory buffer (double-buffered) written out by one TMA store, or, when the
+    // output layout does not allow TMA, by direct stores.
+    constexpr int CH = OUT_F16 ? 16 : 8;
+    constexpr int ES = OUT_F16 ? 2 : 4;
     const int q = warp & 3;
     const int rloc = q * 32 + lane;
+    const bool leader = warp == kWarpEpi0 && lane == 0;  // issues the TMA stores
     Sched<BN> sc(p);
     int rt, t0, nt;
-    uint32_t u = 0;
+    uint32_t u = 0, nbuf = 0;
     bool ok = true;
     const uint32_t tl = tmem + ((uint32_t)(q * 32) << 16);
     float* part = p.scratch ? p.scratch + (size_t)blockIdx.x * BN * kBM + rloc : nullptr;
+    uint8_t* obuf = smem + S::kOutOff;
     while (ok && sc.next(rt, t0, nt)) {
-      const int row = (rt * NCTA + (int)rank) * kBM + rloc;
+      const int row0 = (rt * NCTA + (int)rank) * kBM;
+      const int row = row0 + rloc;
       const bool row_ok = row < p.N;
       for (int ch = 0; ch < nch; ++ch, ++u) {
         const uint32_t r = u % NACC;
         if (!mbar_wait(&accfull[r], (u / NACC) & 1, p.status, kStatusTimeoutFull)) { ok = false; break; }
         tc_fence_after();
         const bool first = ch == 0, last = ch == nch - 1;
-        for (int j0 = 0; j0 < nt; j0 += 32) {
-          uint32_t v[32];
-          tmem_ld32(tl + r * BN + j0, v);
+        for (int j0 = 0; j0 < nt; j0 += CH) {
+          uint32_t v[CH];
+          if constexpr (CH == 16) tmem_ld16(tl + r * BN + j0, v); else tmem_ld8(tl + r * BN + j0, v);
           tmem_wait_ld();
-          if (!row_ok) continue;
-          const int jn = min(32, nt - j0);
-          float prev[32];
-          if (!first) {  // all partial-sum loads first: one L2 round trip per 32 columns
+          const int jn = min(CH, nt - j0);
+          float val[CH];
+          float prev[CH];
+          if (!first && row_ok) {  // all partial-sum loads first: one L2 round trip per chunk
 #pragma unroll
-            for (int jj = 0; jj < 32; ++jj) prev[jj] = jj < jn ? __ldcg(part + (size_t)(j0 + jj) * kBM) : 0.f;
+            for (int jj = 0; jj < CH; ++jj) prev[jj] = jj < jn ? __ldcg(part + (size_t)(j0 + jj) * kBM) : 0.f;
           }
 #pragma unroll
-          for (int jj = 0; jj < 32; ++jj) {
-            if (jj >= jn) break;
-            const int col = j0 + jj;
+          for (int jj = 0; jj < CH; ++jj) {
             float acc = __uint_as_float(v[jj]);
-            if (!first) acc = prev[jj] + acc;
-            if (!last) {
-              __stcg(part + (size_t)col * kBM, acc);
-              continue;
-            }
-            const int64_t t = t0 + col;
-            if (EPI == kEpiResid) acc += __ldg(p.aux + t * p.ldaux + row);
-            if (EPI == kEpiSwiglu) acc = silu_f(__ldg(p.aux + t * p.ldaux + row)) * acc;
-            if (OUT_F16)
-              reinterpret_cast<__half*>(p.y)[t * p.ldy + row] = __float2half_rn(acc);
-            else
-              reinterpret_cast<float*>(p.y)[t * p.ldy + row] = acc;
+            if (!first && row_ok) acc = prev[jj] + acc;
+            val[jj] = acc;
           }
+          if (!last) {
+            if (row_ok) {
+#pragma unroll
+              for (int jj = 0; jj < CH; ++jj)
+                if (jj < jn) __stcg(part + (size_t)(j0 + jj) * kBM, val[jj]);
+            }
+            continue;
+          }
+          if (EPI != kEpiStore && row_ok) {
+            float ax[CH];
+#pragma unroll
+            for (int jj = 0; jj < CH; ++jj) ax[jj] = jj < jn ? __ldg(p.aux + (int64_t)(t0 + j0 + jj) * p.ldaux + row) : 0.f;
+#pragma unroll
+            for (int jj = 0; jj < CH; ++jj) val[jj] = EPI == kEpiResid ? ax[jj] + val[jj] : silu_f(ax[jj]) * val[jj];
+          }
+          if (p.tma_store) {
+            uint8_t* buf = obuf + (nbuf & 1) * S::kOutBuf;
+            if (leader) bulk_wait_read<1>();  // the store that last used this buffer has read it
+            named_bar(1, 128);
+#pragma unroll
+            for (int jj = 0; jj < CH; ++jj) {
+              if (OUT_F16)
+                reinterpret_cast<__half*>(buf)[jj * kBM + rloc] = __float2half_rn(val[jj]);
+              else
+                reinterpret_cast<float*>(buf)[jj * kBM + rloc] = val[jj];
+            }
+            fence_proxy_async();
+            named_bar(1, 128);
+            if (leader) {
+              tma_store_2d(&tmap_y, buf, row0, t0 + j0);
+              bulk_commit();
+            }
+            ++nbuf;
+          } else if (row_ok) {
+#pragma unroll
+            for (int jj = 0; jj < CH; ++jj) {
+              if (jj >= jn) break;
+              const int64_t t = t0 + j0 + jj;
+              if (OUT_F16)
+                reinterpret_cast<__half*>(p.y)[t * p.ldy + row] = __float2half_rn(val[jj]);
+              else
+                reinterpret_cast<float*>(p.y)[t * p.ldy + row] = val[jj];
+            }
+          }
+          (void)ES;
         }
         tc_fence_before();
         __syncwarp();
@@ -412,6 +459,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
+    if (leader) bulk_wait_all();  // stores complete before the CTA (and its shared memory) goes away
   }
 
   tc_fence_before();
@@ -471,7 +519,23 @@ cudaError_t launch_t(const QGemmArgs& a, cudaStream_t stream) {
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return cudaErrorInvalidValue;
   }
+  CUtensorMap my;
+  const int esz = a.y_f16 ? 2 : 4;
+  const bool tma_store = (reinterpret_cast<uintptr_t>(a.y) & 15) == 0 && (a.ldy * esz) % 16 == 0;
+  if (tma_store) {
+    cuuint64_t dims[2] = {(cuuint64_t)a.N, (cuuint64_t)a.M};
+    cuuint64_t strides[1] = {(cuuint64_t)(a.ldy * esz)};
+    cuuint32_t box[2] = {(cuuint32_t)kBM, (cuuint32_t)(a.y_f16 ? 16 : 8)};
+    cuuint32_t es[2] = {1, 1};
+    if (enc(&my, a.y_f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, a.y, dims, strides,
+            box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return cudaErrorInvalidValue;
+  } else {
+    my = mx;  // unused
+  }
   KParams p;
+  p.tma_store = tma_store ? 1 : 0;
   p.N = (int)a.N;
   p.K = (int)a.K;
   p.M = (int)a.M;
@@ -493,7 +557,7 @@ cudaError_t launch_t(const QGemmArgs& a, cudaStream_t stream) {
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
   if (e != cudaSuccess) return e;
   if (!PAIR) {
-    kern<<<grid, kThreads, smem_bytes, stream>>>(mw, mx, p);
+    kern<<<grid, kThreads, smem_bytes, stream>>>(mw, mx, my, p);
     return cudaGetLastError();
   }
   cudaLaunchConfig_t cfg = {};
@@ -508,7 +572,7 @@ cudaError_t launch_t(const QGemmArgs& a, cudaStream_t stream) {
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, mw, mx, p);
+  return cudaLaunchKernelEx(&cfg, kern, mw, mx, my, p);
 }
 
 template <int T, int BN, int NACC, bool PAIR>
