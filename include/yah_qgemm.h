@@ -151,6 +151,24 @@ int yah_qgemv(const void* w, int ggml_type, int64_t N, int64_t K, int64_t w_row_
               const void* x, int64_t M, int64_t ldx, void* y, int y_dtype, int64_t ldy, int epilogue,
               const void* aux, int64_t ldaux, void* stream);
 
+/* Decode GEMV that allocates nothing. This entry point has no counterpart in the reference engine.
+ * For callers that cannot call cudaMalloc when they run the GEMV: code inside a CUDA-graph capture region, a
+ * decode loop with a fixed device-memory budget, or a host process whose device allocator belongs to another
+ * framework. Same arguments, layouts and results as yah_qgemv; the difference is where the split-K scratch
+ * lives: a fixed 4 MiB + 16 KiB device array inside this library (every GPU that loads the library holds it
+ * until the process exits), holding the partial sums (at most 2^20 floats: splits x tokens x rows), one split
+ * counter per 128-row block (N <= 524288) and the variant's own status word. A call whose split-K scratch would
+ * exceed that is refused with YAH_ERR_SIZE (with the GEMV's split rule, 1..32 tokens always fit on a 148-SM B200).
+ * The first call on a device looks up the array's device address (cudaGetSymbolAddress, with that device
+ * current); make that first call before any stream capture. Every call shares the one array and leaves the last
+ * call's contents in it (each call clears the counters it uses first), so calls whose executions overlap on the
+ * GPU (different streams, or different host threads on one device) race: serialise them. */
+int yah_qgemv_noalloc(const void* w, int ggml_type, int64_t N, int64_t K, int64_t w_row_stride, int64_t kb_off,
+                      const void* x, int64_t M, int64_t ldx, void* y, int y_dtype, int64_t ldy, int epilogue,
+                      const void* aux, int64_t ldaux, void* stream);
+/* Read and clear the status word of yah_qgemv_noalloc on the current device (same codes as yah_status_word). */
+int yah_qgemv_noalloc_status(int* code);
+
 #if defined(__GNUC__)
 #pragma GCC visibility pop
 #endif

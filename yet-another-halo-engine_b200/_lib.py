@@ -54,6 +54,9 @@ SYMBOLS = {
                                c_int, c_vp, c_i64, c_int, c_int, c_i64, c_int, c_vp]),
     "yah_qgemv": (c_int, [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_int, c_i64, c_int,
                           c_vp, c_i64, c_vp]),
+    "yah_qgemv_noalloc": (c_int, [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_int, c_i64,
+                                  c_int, c_vp, c_i64, c_vp]),
+    "yah_qgemv_noalloc_status": (c_int, [P(c_int)]),
 }
 
 # status codes (include/yah_qgemm.h)

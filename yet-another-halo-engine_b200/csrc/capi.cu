@@ -443,4 +443,59 @@ int yah_qgemv(const void* w, int t, int64_t N, int64_t K, int64_t w_row_stride, 
   return after_launch(yah::launch_qgemv_ws(a, s->ws, s->counters, S, (cudaStream_t)stream), "qgemv launch");
 }
 
+int yah_qgemv_noalloc(const void* w, int t, int64_t N, int64_t K, int64_t w_row_stride, int64_t kb_off,
+                      const void* x, int64_t M, int64_t ldx, void* y, int y_dtype, int64_t ldy, int epilogue,
+                      const void* aux, int64_t ldaux, void* stream) {
+  int rc = check_linear(w, t, N, K, w_row_stride, kb_off, x, M, ldx, y, y_dtype, ldy, epilogue, aux, ldaux);
+  if (rc) return rc;
+  if (M > 32) return fail(YAH_ERR_ARG, "yah_qgemv_noalloc takes at most 32 tokens (M=%lld)", (long long)M);
+  if (epilogue == YAH_EPI_SWIGLU) return fail(YAH_ERR_UNSUPPORTED, "yah_qgemv_noalloc: epilogue swiglu not provided");
+  // No call below allocates: device attributes, the driver's tensor-map encoder and the static scratch address.
+  int dev = 0, sms = 0, major = 0;
+  CK(cudaGetDevice(&dev));
+  CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  CK(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev));
+  if (major != 10) return fail(YAH_ERR_DEVICE, "device %d is not an sm_100 device", dev);
+  if (!yah::tensor_map_encoder_available())
+    return fail(YAH_ERR_DEVICE, "the driver does not provide cuTensorMapEncodeTiled");
+  const int S = yah::qgemv_splits(N, K, sms);
+  const size_t nrb = (size_t)((N + 127) / 128);
+  if (S > 1 && ((size_t)S * (size_t)M * (size_t)N > yah::qgemv_static_partials() || nrb > yah::qgemv_static_counters()))
+    return fail(YAH_ERR_SIZE,
+                "yah_qgemv_noalloc: split-K scratch of %lld floats (%d splits x %lld tokens x %lld rows) exceeds the "
+                "static %zu-float scratch; call yah_qgemv instead",
+                (long long)S * M * N, S, (long long)M, (long long)N, yah::qgemv_static_partials());
+  void* base = nullptr;
+  CK(yah::qgemv_static_setup(dev, &base));
+  yah::QGemvArgs a;
+  a.w = w;
+  a.type = t;
+  a.N = N;
+  a.K = K;
+  a.w_row_stride = w_row_stride;
+  a.kb_off = kb_off;
+  a.x = x;
+  a.M = M;
+  a.ldx = ldx;
+  a.y = y;
+  a.y_f16 = y_dtype == YAH_F16;
+  a.ldy = ldy;
+  a.epilogue = epilogue;
+  a.aux = static_cast<const float*>(aux);
+  a.ldaux = ldaux;
+  a.status = nullptr;  // set by the launcher: the variant's own status word
+  a.num_sms = sms;
+  return after_launch(yah::launch_qgemv_static(a, base, S, (cudaStream_t)stream), "qgemv_noalloc launch");
+}
+
+int yah_qgemv_noalloc_status(int* code) {
+  if (!code) return fail(YAH_ERR_ARG, "null code");
+  int dev = 0;
+  CK(cudaGetDevice(&dev));
+  void* base = nullptr;
+  CK(yah::qgemv_static_setup(dev, &base));
+  CK(yah::qgemv_static_status(base, code, true));
+  return YAH_OK;
+}
+
 }  // extern "C"

@@ -67,6 +67,15 @@ struct QGemvArgs {
 int qgemv_splits(int64_t N, int64_t K, int num_sms);
 cudaError_t launch_qgemv_ws(const QGemvArgs& a, float* ws, int* counters, int S, cudaStream_t stream);
 
+// The allocation-free GEMV: its scratch is a file-scope device array in qgemv.cu. setup looks up its address on
+// `device` (which must be current) once and caches it; the launcher clears the split counters it needs and runs
+// the GEMV on that scratch; status reads (and optionally clears) the variant's own status word.
+size_t qgemv_static_partials();
+size_t qgemv_static_counters();
+cudaError_t qgemv_static_setup(int device, void** base);
+cudaError_t launch_qgemv_static(const QGemvArgs& a, void* base, int S, cudaStream_t stream);
+cudaError_t qgemv_static_status(void* base, int* code, bool clear);
+
 // Tensor-map encoder resolved from the driver at first use (no libcuda link dependency).
 bool tensor_map_encoder_available();
 

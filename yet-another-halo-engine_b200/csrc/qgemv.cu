@@ -15,6 +15,8 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <mutex>
+
 #include "decode.cuh"
 #include "kernels.h"
 #include "ptx.cuh"
@@ -376,6 +378,70 @@ cudaError_t launch_qgemv_ws(const QGemvArgs& a, float* ws, int* counters, int S,
     case 14: return gv_fmt<14>(a, ws, counters, S, stream);
     default: return cudaErrorInvalidValue;
   }
+}
+
+}  // namespace yah
+
+// ------------------------------------------------------------------------------------------------ static scratch
+// A variant of the decode GEMV for callers that cannot allocate device memory at call time: code that runs
+// where cudaMalloc is not available or not allowed (inside a CUDA-graph capture region, in a real-time decode loop
+// with a fixed memory budget, or in a host process whose allocator is owned by someone else). Its split-K
+// workspace, split counters and status word live in one file-scope device array that every GPU loading this
+// library holds until the process exits. Host code cannot use the array's name as a device address, so the
+// first call on each device looks the address up with cudaGetSymbolAddress (with that device current) and keeps
+// it; later calls reuse it.
+namespace yah {
+namespace {
+
+constexpr size_t kStaticStatusBytes = 256;                 // status word (padded)
+constexpr size_t kStaticCounters = 4096;                   // one per 128-row block: N <= 524288
+constexpr size_t kStaticPartials = (size_t)1 << 20;        // split-K partial sums: S * M * N <= 1M floats
+constexpr size_t kStaticBytes = kStaticStatusBytes + kStaticCounters * sizeof(int) + kStaticPartials * sizeof(float);
+
+static __device__ __align__(256) unsigned char g_qgemv_static[kStaticBytes];
+
+constexpr int kStaticMaxDev = 64;
+void* g_static_addr[kStaticMaxDev] = {};
+std::mutex g_static_mu;
+
+}  // namespace
+
+size_t qgemv_static_partials() { return kStaticPartials; }
+size_t qgemv_static_counters() { return kStaticCounters; }
+
+cudaError_t qgemv_static_setup(int device, void** base) {
+  if (device < 0 || device >= kStaticMaxDev) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lk(g_static_mu);
+  if (!g_static_addr[device]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_qgemv_static);
+    if (e != cudaSuccess) return e;
+    g_static_addr[device] = p;
+  }
+  *base = g_static_addr[device];
+  return cudaSuccess;
+}
+
+cudaError_t launch_qgemv_static(const QGemvArgs& a_in, void* base, int S, cudaStream_t stream) {
+  QGemvArgs a = a_in;
+  unsigned char* b = static_cast<unsigned char*>(base);
+  int* status = reinterpret_cast<int*>(b);
+  int* counters = reinterpret_cast<int*>(b + kStaticStatusBytes);
+  float* partials = reinterpret_cast<float*>(b + kStaticStatusBytes + kStaticCounters * sizeof(int));
+  a.status = status;
+  if (S > 1) {
+    // The counters must start at zero; a previous call leaves them at zero unless it was interrupted.
+    const size_t nrb = (size_t)((a.N + 127) / 128);
+    const cudaError_t e = cudaMemsetAsync(counters, 0, nrb * sizeof(int), stream);
+    if (e != cudaSuccess) return e;
+  }
+  return launch_qgemv_ws(a, partials, counters, S, stream);
+}
+
+cudaError_t qgemv_static_status(void* base, int* code, bool clear) {
+  cudaError_t e = cudaMemcpy(code, base, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess && clear && *code) e = cudaMemset(base, 0, sizeof(int));
+  return e;
 }
 
 }  // namespace yah
