@@ -144,9 +144,11 @@ int yah_qgemm_tile(const void* w, int ggml_type, int64_t N, int64_t K, int64_t w
 
 /* Decode GEMV, 1 <= M <= 32 tokens (replaces gen_gemv.py's gv_{plain,resid}_<fmt>_<M>_<K> kernels and the
  * LoomDecoder::Gemv call site, engine/model/loom_decoder.hpp:415-439). Same layouts and alignment rules as
- * yah_qgemm; epilogue YAH_EPI_STORE or YAH_EPI_RESID. Uses a library-owned per-device split-K workspace
+ * yah_qgemm; epilogue YAH_EPI_STORE or YAH_EPI_RESID. Computes with the f32 weight values of the GGUF dequant,
+ * as the reference GEMV does (no f16 rounding of weights). One persistent CTA per SM streams an equal share of
+ * the weight bytes; row blocks shared by two CTAs are summed through a library-owned per-device workspace
  * (allocated on first use, grown on demand), so concurrent calls on different streams of one device must not
- * overlap. */
+ * overlap. Results are deterministic. */
 int yah_qgemv(const void* w, int ggml_type, int64_t N, int64_t K, int64_t w_row_stride, int64_t kb_off,
               const void* x, int64_t M, int64_t ldx, void* y, int y_dtype, int64_t ldy, int epilogue,
               const void* aux, int64_t ldaux, void* stream);
@@ -155,10 +157,10 @@ int yah_qgemv(const void* w, int ggml_type, int64_t N, int64_t K, int64_t w_row_
  * For callers that cannot call cudaMalloc when they run the GEMV: code inside a CUDA-graph capture region, a
  * decode loop with a fixed device-memory budget, or a host process whose device allocator belongs to another
  * framework. Same arguments, layouts and results as yah_qgemv; the difference is where the split-K scratch
- * lives: a fixed 4 MiB + 16 KiB device array inside this library (every GPU that loads the library holds it
- * until the process exits), holding the partial sums (at most 2^20 floats: splits x tokens x rows), one split
- * counter per 128-row block (N <= 524288) and the variant's own status word. A call whose split-K scratch would
- * exceed that is refused with YAH_ERR_SIZE (with the GEMV's split rule, 1..32 tokens always fit on a 148-SM B200).
+ * lives: a fixed 8 MiB + 128 KiB device array inside this library (every GPU that loads the library holds it
+ * until the process exits), holding the partial sums (at most 2^21 floats: 2 x tokens x 128 per CTA), eight
+ * counters per 128-row block (N <= 524288) and the variant's own status word. A call whose scratch would exceed
+ * that is refused with YAH_ERR_SIZE (1..32 tokens always fit on devices of up to 256 SMs).
  * The first call on a device looks up the array's device address (cudaGetSymbolAddress, with that device
  * current); make that first call before any stream capture. Every call shares the one array and leaves the last
  * call's contents in it (each call clears the counters it uses first), so calls whose executions overlap on the

@@ -408,18 +408,17 @@ int yah_qgemv(const void* w, int t, int64_t N, int64_t K, int64_t w_row_stride, 
   DevState* s;
   rc = dev_state(&s);
   if (rc) return rc;
-  const int S = yah::qgemv_splits(N, K, s->sms);
-  if (S > 1) {
+  const yah::GemvPlan plan = yah::qgemv_plan(t, N, K, M, s->sms);
+  if (plan.ws_floats > 0) {
     std::lock_guard<std::mutex> lk(g_mu);
-    const size_t nrb = (size_t)((N + 127) / 128);
-    rc = grow(reinterpret_cast<void**>(&s->ws), &s->ws_bytes, (size_t)S * M * N * sizeof(float));
+    rc = grow(reinterpret_cast<void**>(&s->ws), &s->ws_bytes, (size_t)plan.ws_floats * sizeof(float));
     if (rc) return rc;
-    if (nrb > s->counters_n) {
+    if ((size_t)plan.counters > s->counters_n) {
       size_t have = s->counters_n * sizeof(int);
-      rc = grow(reinterpret_cast<void**>(&s->counters), &have, nrb * sizeof(int));
+      rc = grow(reinterpret_cast<void**>(&s->counters), &have, (size_t)plan.counters * sizeof(int));
       if (rc) return rc;
-      CK(cudaMemset(s->counters, 0, nrb * sizeof(int)));
-      s->counters_n = nrb;
+      CK(cudaMemset(s->counters, 0, (size_t)plan.counters * sizeof(int)));
+      s->counters_n = (size_t)plan.counters;
     }
   }
   yah::QGemvArgs a;
@@ -440,7 +439,7 @@ int yah_qgemv(const void* w, int t, int64_t N, int64_t K, int64_t w_row_stride, 
   a.ldaux = ldaux;
   a.status = s->status;
   a.num_sms = s->sms;
-  return after_launch(yah::launch_qgemv_ws(a, s->ws, s->counters, S, (cudaStream_t)stream), "qgemv launch");
+  return after_launch(yah::launch_qgemv_ws(a, plan, s->ws, s->counters, (cudaStream_t)stream), "qgemv launch");
 }
 
 int yah_qgemv_noalloc(const void* w, int t, int64_t N, int64_t K, int64_t w_row_stride, int64_t kb_off,
@@ -458,13 +457,12 @@ int yah_qgemv_noalloc(const void* w, int t, int64_t N, int64_t K, int64_t w_row_
   if (major != 10) return fail(YAH_ERR_DEVICE, "device %d is not an sm_100 device", dev);
   if (!yah::tensor_map_encoder_available())
     return fail(YAH_ERR_DEVICE, "the driver does not provide cuTensorMapEncodeTiled");
-  const int S = yah::qgemv_splits(N, K, sms);
-  const size_t nrb = (size_t)((N + 127) / 128);
-  if (S > 1 && ((size_t)S * (size_t)M * (size_t)N > yah::qgemv_static_partials() || nrb > yah::qgemv_static_counters()))
+  const yah::GemvPlan plan = yah::qgemv_plan(t, N, K, M, sms);
+  if ((size_t)plan.ws_floats > yah::qgemv_static_partials() || (size_t)plan.counters > yah::qgemv_static_counters())
     return fail(YAH_ERR_SIZE,
-                "yah_qgemv_noalloc: split-K scratch of %lld floats (%d splits x %lld tokens x %lld rows) exceeds the "
+                "yah_qgemv_noalloc: partial sums of %lld floats (%lld tokens, %lld rows, %d CTAs) exceed the "
                 "static %zu-float scratch; call yah_qgemv instead",
-                (long long)S * M * N, S, (long long)M, (long long)N, yah::qgemv_static_partials());
+                (long long)plan.ws_floats, (long long)M, (long long)N, plan.grid, yah::qgemv_static_partials());
   void* base = nullptr;
   CK(yah::qgemv_static_setup(dev, &base));
   yah::QGemvArgs a;
@@ -485,7 +483,7 @@ int yah_qgemv_noalloc(const void* w, int t, int64_t N, int64_t K, int64_t w_row_
   a.ldaux = ldaux;
   a.status = nullptr;  // set by the launcher: the variant's own status word
   a.num_sms = sms;
-  return after_launch(yah::launch_qgemv_static(a, base, S, (cudaStream_t)stream), "qgemv_noalloc launch");
+  return after_launch(yah::launch_qgemv_static(a, plan, base, (cudaStream_t)stream), "qgemv_noalloc launch");
 }
 
 int yah_qgemv_noalloc_status(int* code) {

@@ -62,10 +62,21 @@ struct QGemvArgs {
   int num_sms;
 };
 
-// Split-K factor of a GEMV launch and the launcher (ws: [S][M][N] f32 partials, counters: one zeroed int per
-// 128-row block; both unused when S == 1).
-int qgemv_splits(int64_t N, int64_t K, int num_sms);
-cudaError_t launch_qgemv_ws(const QGemvArgs& a, float* ws, int* counters, int S, cudaStream_t stream);
+// Work split and shared-memory layout of a GEMV launch. Stream-K launches whose row blocks are split between CTAs
+// need `ws_floats` floats of partial sums and `counters` zeroed ints (both 0 otherwise).
+struct GemvPlan {
+  int mode;    // 0: each CTA owns a row range (no scratch); 1: stream-K over 128-row blocks (scratch when split)
+  int grid;
+  int rb, rgp, slots, tsplit, ntw, cw;  // stage rows, row groups, super-block slots, token split, tiles per warp
+  int sst, ringst;                      // super-blocks per stage (divides slots), stages per ring
+  int P, ops, opw;                      // super-blocks per weight copy, copies per stage, copy row width
+  int wreg, xoff, sumoff, stage_bytes, stages, redoff, baroff, smem;
+  int xres, resoff, ressum;             // activations resident for the whole launch (small M * K)
+  int64_t ws_floats, counters;
+};
+GemvPlan qgemv_plan(int type, int64_t N, int64_t K, int64_t M, int num_sms);
+cudaError_t launch_qgemv_ws(const QGemvArgs& a, const GemvPlan& plan, float* ws, int* counters,
+                            cudaStream_t stream);
 
 // The allocation-free GEMV: its scratch is a file-scope device array in qgemv.cu. setup looks up its address on
 // `device` (which must be current) once and caches it; the launcher clears the split counters it needs and runs
@@ -73,7 +84,7 @@ cudaError_t launch_qgemv_ws(const QGemvArgs& a, float* ws, int* counters, int S,
 size_t qgemv_static_partials();
 size_t qgemv_static_counters();
 cudaError_t qgemv_static_setup(int device, void** base);
-cudaError_t launch_qgemv_static(const QGemvArgs& a, void* base, int S, cudaStream_t stream);
+cudaError_t launch_qgemv_static(const QGemvArgs& a, const GemvPlan& plan, void* base, cudaStream_t stream);
 cudaError_t qgemv_static_status(void* base, int* code, bool clear);
 
 // Tensor-map encoder resolved from the driver at first use (no libcuda link dependency).

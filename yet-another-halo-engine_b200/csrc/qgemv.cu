@@ -1,17 +1,28 @@
 // Decode GEMV for M <= 32 tokens: y[t][n] (+)= sum_k W[n][k] x[t][k], GGUF weights, f16 activations.
 //
-// Reference: engine/gpu/loom/tools/gen_gemv.py (kinds plain / resid :96-754, the per-row decode :365-526, the
-// butterfly reduction :679-690) and its call site engine/model/loom_decoder.hpp:415-439. The reference GEMV is
-// judged purely on bandwidth; so is this one. Its weights are the f16 values of the tile GEMM's decode (the
-// reference dequant, bit-exact), so decode and prefill compute the same products.
+// Reference: engine/gpu/loom/tools/gen_gemv.py (kinds plain / resid, :96-754). Like the reference GEMV, this
+// kernel never rounds a dequantised weight: it computes with the f32 weight values of the reference dequant
+// (gguf-py dequantize, the reference GEMV's oracle, gemv_check.py:112, 161) through the algebra
+// `scale * dot(q, x) - offset * sum(x)` (gen_gemv.py:7-9), with small integers on the tensor cores:
+//   Q4_K  w = d*sc*q - dmin*m. A nibble masked in place is an exact f16 subnormal (q * 2^-24 or q * 2^-20);
+//         per 32-value group the MMA gives sum(q x), scaled back together with d * sc in one f32 FMA; the min
+//         term - dmin * sum_g m_g X_g is one more MMA, X_g (the group's activation sum) in two f16 parts.
+//   Q6_K  w = (d*sc)*(code - 32): one MMA per 16-value sub-block on the exact integers code - 32, then
+//         y += (d*sc) * acc.
+//   Q8_0  w = d*q: two MMAs per 32-value block on the exact int8 q, then y += d * acc.
+// The reference GEMV is judged on bandwidth; so is this one.
 //
-// B200 design. A CTA owns 128 weight rows and a contiguous range of K super-blocks (split-K over CTAs when there
-// are fewer row blocks than SMs). Warp 16 streams the range with TMA: per stage one 256-K super-block of the 128
-// rows plus the matching 4 x 64-K activation tiles (tokens x 128 B, 128-byte swizzle), 4 stages in flight.
-// Warps 0-15 each own 8 rows: lane t decodes 16 values of row t/4 (quarter t%4 of every 64-K block) into f16 pairs,
-// which are exactly the B fragment of mma.sync.m16n8k16 (tokens = M side, rows = N side) under a K permutation
-// that the activation fragments follow. Split-K partials go to a workspace; the last CTA of a row block to finish
-// (atomic counter) sums them in split order, so results are deterministic.
+// B200 design. mma.sync.m16n8k16 with the weights as A (16 rows per warp; a lane applies the scales of its rows
+// g and g + 8) and the tokens as B. A stage holds RB weight rows x S super-blocks (one TMA copy per <= P
+// super-blocks) plus the matching activations (one 3-D TMA copy: 4S 64-K chunks x M token rows, 128-byte
+// swizzle); a TMA warp keeps up to 8 stages in flight. Compute warp w works on row group w % rgp (16 rows) and
+// super-block slot (w / rgp) % S of every stage, and on its share of the tokens. For Q4_K a helper warp permutes
+// each stage's activations to the order the nibble pairs come in ((x0, x2), (x1, x3)) and forms the group sums.
+// Two ways to split the work over the GPU:
+//   row ranges (N >= 4 * #SMs): CTA b owns a contiguous range of ~N / #SMs rows (4-row granularity) and all of
+//     K; the slots of a row group are added through shared memory. No scratch, balanced within 4 rows per SM.
+//   stream-K (small N): 128-row blocks x super-blocks, cut into equal ranges per CTA; a row block shared by
+//     several CTAs is summed through a workspace by the last CTA to arrive, in CTA order (deterministic).
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -24,122 +35,60 @@
 namespace yah {
 namespace {
 
-constexpr int kGvWarps = 16;
-constexpr int kGvThreads = (kGvWarps + 1) * 32;
-constexpr int kGvRows = 128;
-constexpr int kGvStages = 4;
+constexpr int kGvBlock = 128;    // stream-K row block
+constexpr int kGvMaxStages = 16;
+constexpr int kGvSmemBudget = 210 * 1024;
 
-template <int T>
-struct GvFmt;
-template <>
-struct GvFmt<8> { static constexpr int kSB = 272, kBox = 272; };
-template <>
-struct GvFmt<12> { static constexpr int kSB = 144, kBox = 144; };
-template <>
-struct GvFmt<14> { static constexpr int kSB = 210, kBox = 224; };
+// Bytes per super-block and the most super-blocks one TMA copy of a row holds (box width <= 256 elements:
+// u64 elements for Q4_K / Q8_0, u16 for Q6_K, whose super-blocks are not 8-byte aligned).
+__host__ __device__ constexpr int gv_sb_bytes(int t) { return t == 8 ? 272 : t == 12 ? 144 : 210; }
+__host__ __device__ constexpr int gv_pmax(int t) { return t == 8 ? 4 : t == 12 ? 8 : 2; }
+// Shared-memory row width of one W copy of P super-blocks (Q6_K: a 16-byte aligned window around them).
+__host__ __device__ constexpr int gv_opw(int t, int P) {
+  return t == 14 ? ((P * 210 + 14 + 15) / 16) * 16 : P * gv_sb_bytes(t);
+}
 
-template <int T, int MT>
-struct GvSmem {
-  static constexpr int kTP = 16 * MT;                  // token rows per activation tile
-  static constexpr int kXTile = kTP * 128;             // one 64-K activation tile
-  static constexpr int kW = ((kGvRows * GvFmt<T>::kBox + 16) + 1023) / 1024 * 1024;
-  static constexpr int kStage = kW + 4 * kXTile;
-  static constexpr int kBarOff = kGvStages * kStage;
-  static constexpr int kBytes = kBarOff + 2 * kGvStages * 8 + 16;
-  static constexpr int kAlloc = kBytes + 1024;
+template <int T, int CW>
+struct GvRoles {
+  static constexpr int kThreads = (CW + (T == 12 ? 2 : 1)) * 32;  // compute warps + TMA warp (+ Q4_K helper)
 };
 
 struct GvParams {
-  int N, K, M, kb_off, nsb, S;
+  int N, M, kb_off, nsb;
+  int mode;                  // 0 row ranges, 1 stream-K
+  int rb, rgp, slots, tsplit, sst, P, ops, opw;  // sst: super-blocks per stage (a divisor of slots)
+  int turns, ringst, ringlog;  // stage rings: stage k of a segment goes to ring k % turns (ringst = 2^ringlog)
+  int wreg, xoff, sumoff, stage_bytes, stages, redoff, baroff;
+  int xres, resoff, ressum;  // activations resident for the whole launch (row ranges, small M * K)
+  const __half* x;
+  int64_t ldx;
+  int K;
+  int64_t units;             // row ranges: ceil(N / 4)
+  int64_t items;             // stream-K: row blocks x super-blocks
   void* y;
   int64_t ldy;
   int y_f16, epi;
   const float* aux;
   int64_t ldaux;
-  float* ws;      // [S][M][N] split-K partials (S > 1)
-  int* counters;  // one per row block, zero between launches
+  float* ws;                 // stream-K: [G][2][M][128] partial sums
+  int* counters;             // stream-K: [row blocks][8], zero between launches
   int* status;
 };
 
-// 4 words at an even byte offset `off` of a shared-memory row (reads 5 aligned words).
-__device__ __forceinline__ void lds_words4(uint32_t rb, int off, uint32_t (&w)[4]) {
-  const uint32_t a = rb + (off & ~3);
-  const uint32_t sel = (off & 2) ? 0x5432u : 0x3210u;
-  uint32_t L[5];
-#pragma unroll
-  for (int i = 0; i < 5; ++i) L[i] = lds32(a + 4 * i);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) w[i] = prmt(L[i], L[i + 1], sel);
+// ------------------------------------------------------------------------------------------------ small helpers
+__device__ __forceinline__ uint32_t lds_word(uint32_t addr) {  // 4 bytes at an even byte address
+  const uint32_t a = addr & ~3u;
+  return prmt(lds32(a), lds32(a + 4), (addr & 2) ? 0x5432u : 0x3210u);
 }
 
-__device__ __forceinline__ uint32_t lds_u16(uint32_t rb, int off) {
-  return (lds32(rb + (off & ~3)) >> (8 * (off & 3))) & 0xFFFFu;
+__device__ __forceinline__ uint32_t lds_u16(uint32_t addr) {
+  return (lds32(addr & ~3u) >> (8 * (addr & 3))) & 0xFFFFu;
 }
 
-// Decode 16 values (quarter c of 64-K block j) of a staged row into 8 f16 pairs: out[i] = values (2i, 2i + 1)
-// of the quarter. Same arithmetic as decode.cuh's 64-value decoders.
-template <int T>
-__device__ __forceinline__ void decode16(uint32_t rb, int j, int c, int o, uint32_t (&out)[8]);
-
-template <>
-__device__ __forceinline__ void decode16<12>(uint32_t rb, int j, int c, int, uint32_t (&out)[8]) {
-  const uint4 hdr = lds128(rb);
-  const uint4 q = lds128(rb + 16 + 32 * j + 16 * (c & 1));
-  const int hi = c >> 1;  // quarters 2, 3: group 2j + 1, high nibbles
-  float dsa, dma, dsb, dmb;
-  q4k_scales(hdr, j, dsa, dma, dsb, dmb);
-  const float ds = hi ? dsb : dsa;
-  const float nd = hi ? -dmb : -dma;
-  const int sh = 4 * hi;
-  const float s0 = hi ? ds * 0.0625f : ds;                      // nibble at bit sh
-  const float s8 = hi ? ds * 2.44140625e-4f : ds * 0.00390625f;  // nibble at bit 8 + sh
-  const uint32_t m0 = 0xFu << sh, m8 = 0xF00u << sh;
-  const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const uint32_t w = qw[i], v = w >> 16;
-    out[2 * i] = pack_f16x2_rn(__fmaf_rn(s0, magic_q(w & m0), nd), __fmaf_rn(s8, magic_q(w & m8), nd));
-    out[2 * i + 1] = pack_f16x2_rn(__fmaf_rn(s0, magic_q(v & m0), nd), __fmaf_rn(s8, magic_q(v & m8), nd));
-  }
-}
-
-template <>
-__device__ __forceinline__ void decode16<8>(uint32_t rb, int j, int c, int, uint32_t (&out)[8]) {
-  const int b = 2 * j + (c >> 1);
-  uint32_t W[4];
-  lds_words4(rb, 34 * b + 2 + 16 * (c & 1), W);
-  const uint32_t d = lds_u16(rb, 34 * b);
-  const uint32_t d2 = d | (d << 16);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const uint32_t x = W[i] ^ 0x80808080u;
-    out[2 * i] = hmul2_u32(hsub2_u32(prmt(x, 0x64646464u, 0x4140u), 0x64806480u), d2);
-    out[2 * i + 1] = hmul2_u32(hsub2_u32(prmt(x, 0x64646464u, 0x4342u), 0x64806480u), d2);
-  }
-}
-
-template <>
-__device__ __forceinline__ void decode16<14>(uint32_t rb, int j, int c, int o, uint32_t (&out)[8]) {
-  const int h = j >> 1, jodd = j & 1;
-  uint32_t QL[4], QH[4];
-  lds_words4(rb, o + 64 * h + 16 * c, QL);
-  lds_words4(rb, o + 128 + 32 * h + 16 * (c & 1), QH);
-  const int sy = o + 192 + 8 * h + 4 * jodd + c;
-  const int s = (int)(int8_t)((lds32(rb + (sy & ~3)) >> (8 * (sy & 3))) & 0xFFu);
-  const float d = h2f_bits(lds_u16(rb, o + 208));
-  const float ds = (d * (float)s) * 1.52587890625e-05f;
-  const int lsh = 4 * jodd, hsh = 4 * jodd + 2 * (c >> 1);
-  constexpr float kOff = 10485760.0f;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const uint32_t code = ((QL[i] >> lsh) & 0x0F0F0F0Fu) | (((QH[i] >> hsh) & 0x03030303u) << 4);
-    const float v0 = __fmul_rn(ds, __uint_as_float(prmt(code, 0x4B000000u, 0x7044u)) - kOff);
-    const float v1 = __fmul_rn(ds, __uint_as_float(prmt(code, 0x4B000000u, 0x7144u)) - kOff);
-    const float v2 = __fmul_rn(ds, __uint_as_float(prmt(code, 0x4B000000u, 0x7244u)) - kOff);
-    const float v3 = __fmul_rn(ds, __uint_as_float(prmt(code, 0x4B000000u, 0x7344u)) - kOff);
-    out[2 * i] = pack_f16x2_rn(v0, v1);
-    out[2 * i + 1] = pack_f16x2_rn(v2, v3);
-  }
+__device__ __forceinline__ uint2 lds64(uint32_t addr) {
+  uint2 v;
+  asm volatile("ld.shared.v2.b32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
+  return v;
 }
 
 __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
@@ -151,141 +100,629 @@ __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-__device__ __forceinline__ uint2 lds64(uint32_t addr) {
-  uint2 v;
-  asm volatile("ld.shared.v2.b32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
-  return v;
+// Activations of a stage: 128-byte rows, row = chunk * rows_per_chunk + token, the 16-byte pieces of a row
+// swizzled by (row mod 8) (TMA 128-byte swizzle; the stage's activation region is 1024-byte aligned).
+// Address of 16-byte piece q of row `row`:
+__device__ __forceinline__ uint32_t xpiece(uint32_t xs, int row, int q) {
+  return xs + row * 128 + ((q ^ (row & 7)) << 4);
 }
 
-template <int T, int MT>
-__global__ void __launch_bounds__(kGvThreads, 1)
+// 4-byte word at an even offset, as f32 2^23 + byte (for the scale bytes of Q4_K)
+__device__ __forceinline__ float magic_byte(uint32_t word, int byte) {
+  return __uint_as_float(prmt(word, 0x4B000000u, (uint32_t)byte | 0x7650u));
+}
+
+// ------------------------------------------------------------------------------------------------ one super-block
+// A warp's 16 weight rows x one 256-K super-block, accumulated into y (rows g / g + 8, tokens tok0 + 8n + 2c + e).
+// w0 / w1: shared addresses of the super-block in rows g and g + 8; xs: the stage's activations (xrows token
+// rows per 64-K chunk, this super-block's first chunk c0); sums: this super-block's Q4_K group sums
+// ([hi, lo][xrows tokens][8] f16). Tokens >= M are zero and are not read.
+template <int T, int NTW>
+__device__ __forceinline__ void gv_superblock(uint32_t w0, uint32_t w1, uint32_t xs, int xrows, int c0, int tok0,
+                                              int M, uint32_t sums, float (&y)[NTW][4], int g, int c) {
+  bool tok[NTW];
+#pragma unroll
+  for (int n = 0; n < NTW; ++n) tok[n] = tok0 + 8 * n + g < M;
+  if (T == 12) {
+    const uint4 h0 = lds128(w0), h1 = lds128(w1);
+    // 6-bit scales of groups 0-3 / 4-7 and mins of groups 0-3 / 4-7, one per byte
+    const uint32_t sc0a = h0.y & 0x3F3F3F3Fu, sc0b = (h0.w & 0x0F0F0F0Fu) | ((h0.y >> 2) & 0x30303030u);
+    const uint32_t sc1a = h1.y & 0x3F3F3F3Fu, sc1b = (h1.w & 0x0F0F0F0Fu) | ((h1.y >> 2) & 0x30303030u);
+    const uint32_t m0a = h0.z & 0x3F3F3F3Fu, m0b = ((h0.w >> 4) & 0x0F0F0F0Fu) | ((h0.z >> 2) & 0x30303030u);
+    const uint32_t m1a = h1.z & 0x3F3F3F3Fu, m1b = ((h1.w >> 4) & 0x0F0F0F0Fu) | ((h1.z >> 2) & 0x30303030u);
+    // Low nibble q masked in place reads as q * 2^-24, high nibble as q * 2^-20 (exact f16 subnormals). The group
+    // factor F = (2^23 + sc) * D - 2^23 * D = sc * D (one rounding) with D = d * 2^24 or d * 2^20 undoes that.
+    const float d0 = h2f_bits(h0.x & 0xFFFFu), d1 = h2f_bits(h1.x & 0xFFFFu);
+    const float dl0 = d0 * 16777216.0f, dh0 = d0 * 1048576.0f, dl1 = d1 * 16777216.0f, dh1 = d1 * 1048576.0f;
+    const float bl0 = dl0 * -8388608.0f, bh0 = dh0 * -8388608.0f, bl1 = dl1 * -8388608.0f, bh1 = dh1 * -8388608.0f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      // lane bytes 8c .. 8c + 7 of the 64-K block: low nibbles at positions 8c + (0..7) (group 2j), high nibbles
+      // at 32 + 8c + (0..7) (group 2j + 1)
+      const uint2 q0 = lds64(w0 + 16 + 32 * j + 8 * c), q1 = lds64(w1 + 16 + 32 * j + 8 * c);
+      const uint32_t s0 = j < 2 ? sc0a : sc0b, s1 = j < 2 ? sc1a : sc1b;
+      const float fl0 = __fmaf_rn(magic_byte(s0, (2 * j) & 3), dl0, bl0);
+      const float fh0 = __fmaf_rn(magic_byte(s0, (2 * j + 1) & 3), dh0, bh0);
+      const float fl1 = __fmaf_rn(magic_byte(s1, (2 * j) & 3), dl1, bl1);
+      const float fh1 = __fmaf_rn(magic_byte(s1, (2 * j + 1) & 3), dh1, bh1);
+      // A registers: word wi, bytes (0, 2) and (1, 3) of rows g and g + 8, low / high nibbles
+      uint32_t lo[2][4], hi[2][4];
+#pragma unroll
+      for (int wi = 0; wi < 2; ++wi) {
+        const uint32_t u0 = wi ? q0.y : q0.x, u1 = wi ? q1.y : q1.x;
+        const uint32_t v0 = u0 >> 8, v1 = u1 >> 8;
+        lo[wi][0] = u0 & 0x000F000Fu, lo[wi][1] = u1 & 0x000F000Fu, lo[wi][2] = v0 & 0x000F000Fu,
+        lo[wi][3] = v1 & 0x000F000Fu;
+        hi[wi][0] = u0 & 0x00F000F0u, hi[wi][1] = u1 & 0x00F000F0u, hi[wi][2] = v0 & 0x00F000F0u,
+        hi[wi][3] = v1 & 0x00F000F0u;
+      }
+#pragma unroll
+      for (int n = 0; n < NTW; ++n) {
+        // permuted activations: 16-byte piece c = units 2c, 2c + 1 (low nibbles), piece 4 + c (high nibbles)
+        const int row = (c0 + j) * xrows + tok0 + 8 * n + g;
+        const uint32_t al = xpiece(xs, row, c);  // piece 4 + c: the same row, 16-byte index bit 2 flipped
+        const uint4 xl = tok[n] ? lds128(al) : make_uint4(0u, 0u, 0u, 0u);
+        const uint4 xh = tok[n] ? lds128(al ^ 64u) : make_uint4(0u, 0u, 0u, 0u);
+        float alo[4] = {0.f, 0.f, 0.f, 0.f}, ahi[4] = {0.f, 0.f, 0.f, 0.f};
+        mma16816(alo, lo[0][0], lo[0][1], lo[0][2], lo[0][3], xl.x, xl.y);
+        mma16816(ahi, hi[0][0], hi[0][1], hi[0][2], hi[0][3], xh.x, xh.y);
+        mma16816(alo, lo[1][0], lo[1][1], lo[1][2], lo[1][3], xl.z, xl.w);
+        mma16816(ahi, hi[1][0], hi[1][1], hi[1][2], hi[1][3], xh.z, xh.w);
+        y[n][0] = __fmaf_rn(fh0, ahi[0], __fmaf_rn(fl0, alo[0], y[n][0]));
+        y[n][1] = __fmaf_rn(fh0, ahi[1], __fmaf_rn(fl0, alo[1], y[n][1]));
+        y[n][2] = __fmaf_rn(fh1, ahi[2], __fmaf_rn(fl1, alo[2], y[n][2]));
+        y[n][3] = __fmaf_rn(fh1, ahi[3], __fmaf_rn(fl1, alo[3], y[n][3]));
+      }
+    }
+    // - dmin * sum_g m_g X_g: A row g / g + 8 = mins of groups 2c, 2c + 1 (repeated at k + 8), B = X hi / lo
+    const int mb = (2 * c) & 3;
+    const uint32_t msel = (uint32_t)mb | 0x40u | ((uint32_t)(mb + 1) << 8) | 0x4000u;
+    const uint32_t am0 = hsub2_u32(prmt(c < 2 ? m0a : m0b, 0x64646464u, msel), 0x64006400u);
+    const uint32_t am1 = hsub2_u32(prmt(c < 2 ? m1a : m1b, 0x64646464u, msel), 0x64006400u);
+    const float n0 = -h2f_bits(h0.x >> 16), n1 = -h2f_bits(h1.x >> 16);
+#pragma unroll
+    for (int n = 0; n < NTW; ++n) {
+      const int tau = tok0 + 8 * n + g;
+      const uint32_t bh = tok[n] ? lds32(sums + (tau * 8 + 2 * c) * 2) : 0u;
+      const uint32_t bl = tok[n] ? lds32(sums + (xrows * 8 + tau * 8 + 2 * c) * 2) : 0u;
+      float acc2[4] = {0.f, 0.f, 0.f, 0.f};
+      mma16816(acc2, am0, am1, am0, am1, bh, bl);
+      y[n][0] = __fmaf_rn(n0, acc2[0], y[n][0]);
+      y[n][1] = __fmaf_rn(n0, acc2[1], y[n][1]);
+      y[n][2] = __fmaf_rn(n1, acc2[2], y[n][2]);
+      y[n][3] = __fmaf_rn(n1, acc2[3], y[n][3]);
+    }
+  } else if (T == 14) {
+    // ql[128], qh[64], int8 scales[16], d; x in natural order: unit 4u + c of a 64-K chunk = 16-byte piece
+    // 2u + (c >> 1), half c & 1
+    const float dd0 = h2f_bits(lds_u16(w0 + 208)), dd1 = h2f_bits(lds_u16(w1 + 208));
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int h = j >> 1, jo = j & 1;  // 128-value half, which 64 of it
+      const uint32_t scw0 = lds_word(w0 + 192 + 8 * h + 4 * jo), scw1 = lds_word(w1 + 192 + 8 * h + 4 * jo);
+      const uint32_t qh0[2] = {lds_word(w0 + 128 + 32 * h + 4 * c), lds_word(w0 + 144 + 32 * h + 4 * c)};
+      const uint32_t qh1[2] = {lds_word(w1 + 128 + 32 * h + 4 * c), lds_word(w1 + 144 + 32 * h + 4 * c)};
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {  // 16-value sub-block u of the 64-K block (scale index 8h + 4jo + u)
+        const uint32_t ql0 = lds_word(w0 + 64 * h + 16 * u + 4 * c), ql1 = lds_word(w1 + 64 * h + 16 * u + 4 * c);
+        const int hs = 4 * jo + 2 * (u >> 1);
+        const uint32_t c0w = ((ql0 >> (4 * jo)) & 0x0F0F0F0Fu) | (((qh0[u & 1] >> hs) & 0x03030303u) << 4);
+        const uint32_t c1w = ((ql1 >> (4 * jo)) & 0x0F0F0F0Fu) | (((qh1[u & 1] >> hs) & 0x03030303u) << 4);
+        constexpr uint32_t kB = 0x64206420u;  // f16 (1056, 1056) = 1024 + 32
+        const uint32_t a0 = hsub2_u32(prmt(c0w, 0x64646464u, 0x4140u), kB);
+        const uint32_t a2 = hsub2_u32(prmt(c0w, 0x64646464u, 0x4342u), kB);
+        const uint32_t a1 = hsub2_u32(prmt(c1w, 0x64646464u, 0x4140u), kB);
+        const uint32_t a3 = hsub2_u32(prmt(c1w, 0x64646464u, 0x4342u), kB);
+        const float f0 = dd0 * (float)(int)(int8_t)((scw0 >> (8 * u)) & 0xFFu);
+        const float f1 = dd1 * (float)(int)(int8_t)((scw1 >> (8 * u)) & 0xFFu);
+#pragma unroll
+        for (int n = 0; n < NTW; ++n) {
+          const int row = (c0 + j) * xrows + tok0 + 8 * n + g;
+          const uint2 b = tok[n] ? lds64(xpiece(xs, row, 2 * u + (c >> 1)) + 8 * (c & 1)) : make_uint2(0u, 0u);
+          float t4[4] = {0.f, 0.f, 0.f, 0.f};
+          mma16816(t4, a0, a1, a2, a3, b.x, b.y);
+          y[n][0] = __fmaf_rn(f0, t4[0], y[n][0]);
+          y[n][1] = __fmaf_rn(f0, t4[1], y[n][1]);
+          y[n][2] = __fmaf_rn(f1, t4[2], y[n][2]);
+          y[n][3] = __fmaf_rn(f1, t4[3], y[n][3]);
+        }
+      }
+    }
+  } else {  // Q8_0: eight 34-byte blocks (d f16, 32 int8); unit 8(bk & 1) + 4hb + c of chunk bk >> 1
+#pragma unroll
+    for (int bk = 0; bk < 8; ++bk) {
+      const float d0 = h2f_bits(lds_u16(w0 + 34 * bk)), d1 = h2f_bits(lds_u16(w1 + 34 * bk));
+      float t4[NTW][4];
+#pragma unroll
+      for (int n = 0; n < NTW; ++n) t4[n][0] = t4[n][1] = t4[n][2] = t4[n][3] = 0.f;
+#pragma unroll
+      for (int hb = 0; hb < 2; ++hb) {
+        const uint32_t q0 = lds_word(w0 + 34 * bk + 2 + 16 * hb + 4 * c) ^ 0x80808080u;
+        const uint32_t q1 = lds_word(w1 + 34 * bk + 2 + 16 * hb + 4 * c) ^ 0x80808080u;
+        constexpr uint32_t kB = 0x64806480u;  // f16 (1152, 1152) = 1024 + 128
+        const uint32_t a0 = hsub2_u32(prmt(q0, 0x64646464u, 0x4140u), kB);
+        const uint32_t a2 = hsub2_u32(prmt(q0, 0x64646464u, 0x4342u), kB);
+        const uint32_t a1 = hsub2_u32(prmt(q1, 0x64646464u, 0x4140u), kB);
+        const uint32_t a3 = hsub2_u32(prmt(q1, 0x64646464u, 0x4342u), kB);
+#pragma unroll
+        for (int n = 0; n < NTW; ++n) {
+          const int row = (c0 + (bk >> 1)) * xrows + tok0 + 8 * n + g;
+          const int v = 8 * (bk & 1) + 4 * hb + c;
+          const uint2 b = tok[n] ? lds64(xpiece(xs, row, v >> 1) + 8 * (v & 1)) : make_uint2(0u, 0u);
+          mma16816(t4[n], a0, a1, a2, a3, b.x, b.y);
+        }
+      }
+#pragma unroll
+      for (int n = 0; n < NTW; ++n) {
+        y[n][0] = __fmaf_rn(d0, t4[n][0], y[n][0]);
+        y[n][1] = __fmaf_rn(d0, t4[n][1], y[n][1]);
+        y[n][2] = __fmaf_rn(d1, t4[n][2], y[n][2]);
+        y[n][3] = __fmaf_rn(d1, t4[n][3], y[n][3]);
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------------ Q4_K helper
+__device__ __forceinline__ void gv_store_sum(uint32_t ss, int M, int t, int grp, float v) {
+  const __half hv = __float2half_rn(v);
+  const __half lv = __float2half_rn(v - __half2float(hv));
+  asm volatile("st.shared.b16 [%0], %1;" ::"r"(ss + (t * 8 + grp) * 2), "h"(__half_as_ushort(hv)) : "memory");
+  asm volatile("st.shared.b16 [%0], %1;" ::"r"(ss + (M * 8 + t * 8 + grp) * 2), "h"(__half_as_ushort(lv)) : "memory");
+}
+
+// One stage's activation prep for Q4_K, by one warp: (1) the group sums X_g (hi, lo f16) of each slot's
+// super-block; (2) every 4 activations (x0, x1, x2, x3) become (x0, x2, x1, x3), the order in which a weight
+// word yields its nibble pairs (bytes 0, 2 and 1, 3).
+// Sums for up to 4 tokens: lane l adds the 8 values at positions 8l .. 8l + 7 of the super-block in f32 and
+// two shuffles finish group l / 4. For more tokens: MMAs D[group][token] += Sel[group][k] * x[k][token] over the
+// 16 k16 slices of a super-block, Sel = 1 where slice k lies in the group (lane row g: ones on slices 2g, 2g + 1).
+__device__ __forceinline__ void gv_prep_q4k(uint32_t xs, int slots, int M, uint32_t sums, int lane) {
+  const int g = lane >> 2, c = lane & 3;
+  if (M <= 4) {
+    for (int s = 0; s < slots; ++s) {
+      const uint32_t ss = sums + s * 32 * M;
+      for (int t = 0; t < M; ++t) {
+        const uint4 q = lds128(xpiece(xs, (4 * s + (lane >> 3)) * M + t, lane & 7));
+        const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&q.x));
+        const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&q.y));
+        const float2 e = __half22float2(*reinterpret_cast<const __half2*>(&q.z));
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&q.w));
+        float v = ((a.x + a.y) + (b.x + b.y)) + ((e.x + e.y) + (f.x + f.y));
+        v += __shfl_xor_sync(0xffffffffu, v, 1);
+        v += __shfl_xor_sync(0xffffffffu, v, 2);
+        if (c == 0) gv_store_sum(ss, M, t, g, v);
+      }
+    }
+  } else {
+    const int ntiles = (M + 7) >> 3;
+    for (int s = 0; s < slots; ++s) {
+      const uint32_t ss = sums + s * 32 * M;
+      for (int nt = 0; nt < ntiles; ++nt) {
+        const int tau = 8 * nt + g;
+        float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int ch = 0; ch < 16; ch += 2) {
+          const uint32_t a = (g == (ch >> 1)) ? 0x3C003C00u : 0u;
+          uint2 b0 = make_uint2(0u, 0u), b1 = make_uint2(0u, 0u);
+          if (tau < M) {
+            const int v0 = 4 * (ch & 3) + c, v1 = 4 * ((ch + 1) & 3) + c;
+            b0 = lds64(xpiece(xs, (4 * s + (ch >> 2)) * M + tau, v0 >> 1) + 8 * (v0 & 1));
+            b1 = lds64(xpiece(xs, (4 * s + ((ch + 1) >> 2)) * M + tau, v1 >> 1) + 8 * (v1 & 1));
+          }
+          mma16816(d0, a, 0u, a, 0u, b0.x, b0.y);
+          mma16816(d1, a, 0u, a, 0u, b1.x, b1.y);
+        }
+        // d[0], d[1]: group g, tokens 8nt + 2c, 8nt + 2c + 1
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int t = 8 * nt + 2 * c + e;
+          if (t < M) gv_store_sum(ss, M, t, g, d0[e] + d1[e]);
+        }
+      }
+    }
+  }
+  __syncwarp();
+  const int units = 4 * slots * M * 16;
+  for (int u = lane; u < units; u += 32) {
+    const int row = u >> 4, v = u & 15;
+    const uint32_t a = xpiece(xs, row, v >> 1) + 8 * (v & 1);
+    const uint2 q = lds64(a);
+    asm volatile("st.shared.v2.b32 [%0], {%1, %2};" ::"r"(a), "r"(prmt(q.x, q.y, 0x5410u)), "r"(prmt(q.x, q.y, 0x7632u))
+                 : "memory");
+  }
+}
+
+// ------------------------------------------------------------------------------------------------ outputs
+__device__ __forceinline__ void gv_store(const GvParams& p, int t, int row, float v) {
+  if (p.epi == kEpiResid) v += p.aux[(int64_t)t * p.ldaux + row];
+  if (p.y_f16) reinterpret_cast<__half*>(p.y)[(int64_t)t * p.ldy + row] = __float2half_rn(v);
+  else reinterpret_cast<float*>(p.y)[(int64_t)t * p.ldy + row] = v;
+}
+
+// ------------------------------------------------------------------------------------------------ stream-K split
+// First item of CTA b: floor(b * items / G).
+__device__ __forceinline__ int64_t gv_lo(int b, int64_t items, int G) { return (int64_t)b * items / G; }
+
+// The CTA whose range holds `item`.
+__device__ __forceinline__ int gv_owner(int64_t item, int64_t items, int G) {
+  int b = (int)(item * G / items);
+  while (b + 1 < G && gv_lo(b + 1, items, G) <= item) ++b;
+  while (b > 0 && gv_lo(b, items, G) > item) --b;
+  return b;
+}
+
+// A CTA's item range [lo, hi) in processing order: the partial row block it starts in (head), then the partial
+// row block it ends in (tail, when that differs), then the whole row blocks between. Both partial blocks are
+// exchanged with the neighbouring CTAs early, behind the stream.
+struct GvRange {
+  int64_t lo, hi, head_end, tail_start;
+  int n_head, n_tail;
+};
+
+__device__ __forceinline__ GvRange gv_range(int b, const GvParams& p) {
+  GvRange r;
+  r.lo = gv_lo(b, p.items, gridDim.x);
+  r.hi = gv_lo(b + 1, p.items, gridDim.x);
+  const int64_t block_end = (r.lo / p.nsb + 1) * p.nsb;
+  r.head_end = block_end < r.hi ? block_end : r.hi;
+  r.n_head = (int)(r.head_end - r.lo);
+  const int64_t ts = ((r.hi - 1) / p.nsb) * p.nsb;
+  const bool tail = (r.hi % p.nsb) != 0 && ts >= r.head_end;
+  r.tail_start = tail ? ts : r.hi;
+  r.n_tail = tail ? (int)(r.hi - ts) : 0;
+  return r;
+}
+
+// A CTA's work as segments: weight rows [row0, row0 + rows) x super-blocks [sb_begin, sb_end), flushed at the
+// end. Row ranges: one segment per chunk of rb rows, all of K. Stream-K: head, tail, then the whole row blocks.
+struct GvSeg {
+  int64_t row0;
+  int sb_begin, sb_end;
+};
+
+struct GvWork {
+  int64_t rs, re;  // row ranges: this CTA's rows
+  GvRange r;       // stream-K
+  int nseg;
+};
+
+template <bool RANGES>
+__device__ __forceinline__ GvWork gv_work(const GvParams& p) {
+  GvWork w;
+  const int G = gridDim.x;
+  if (RANGES) {
+    w.rs = 4 * ((int64_t)blockIdx.x * p.units / G);
+    w.re = 4 * ((int64_t)(blockIdx.x + 1) * p.units / G);
+    if (w.re > p.N) w.re = p.N;
+    w.nseg = (int)((w.re - w.rs + p.rb - 1) / p.rb);
+  } else {
+    w.rs = w.re = 0;
+    w.r = gv_range(blockIdx.x, p);
+    w.nseg = (w.r.n_head > 0 ? 1 : 0) + (w.r.n_tail > 0 ? 1 : 0) +
+             (int)(((w.r.tail_start < w.r.hi ? w.r.tail_start : w.r.hi) - w.r.head_end) / p.nsb);
+  }
+  return w;
+}
+
+template <bool RANGES>
+__device__ __forceinline__ GvSeg gv_seg(const GvParams& p, const GvWork& w, int si) {
+  GvSeg s;
+  if (RANGES) {
+    s.row0 = w.rs + (int64_t)si * p.rb;
+    s.sb_begin = 0;
+    s.sb_end = p.nsb;
+    return s;
+  }
+  int64_t first, last;  // items
+  if (si == 0) {
+    first = w.r.lo;
+    last = w.r.head_end;
+  } else if (si == 1 && w.r.n_tail > 0) {
+    first = w.r.tail_start;
+    last = w.r.hi;
+  } else {
+    first = w.r.head_end + (int64_t)(si - 1 - (w.r.n_tail > 0 ? 1 : 0)) * p.nsb;
+    last = first + p.nsb;
+  }
+  const int64_t rb = first / p.nsb;
+  s.row0 = rb * kGvBlock;
+  s.sb_begin = (int)(first - rb * p.nsb);
+  s.sb_end = (int)(last - rb * p.nsb);
+  return s;
+}
+
+// Stream-K: a warp's 16 x (8 * NT) results for row block rb. Stored directly when the CTA covered the whole block,
+// otherwise parked in the CTA's workspace slot (2b for the row block CTA b starts in, 2b + 1 for the one it ends
+// in); the last of the block's CTAs to arrive adds the slots in CTA order, so the sum is deterministic.
+template <int NT>
+__device__ __forceinline__ void gv_flush_streamk(const GvParams& p, const GvRange& r, float (&y)[NT][4], int rb,
+                                                 int warp, int lane) {
+  const int g = lane >> 2, c = lane & 3;
+  const int G = gridDim.x;
+  const int64_t first = (int64_t)rb * p.nsb;
+  const int bf = gv_owner(first, p.items, G), bl = gv_owner(first + p.nsb - 1, p.items, G);
+  const int rloc = warp * 16 + g;
+  if (bl > bf) {
+    const int64_t slot = (int64_t)blockIdx.x * 2 + (rb == (int)(r.lo / p.nsb) ? 0 : 1);
+    float* wsb = p.ws + slot * p.M * kGvBlock + rloc;
+#pragma unroll
+    for (int n = 0; n < NT; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int t = 8 * n + 2 * c + (e & 1);
+        if (t < p.M) __stcg(wsb + (int64_t)t * kGvBlock + 8 * (e >> 1), y[n][e]);
+      }
+    // Release the warp's stores and count this CTA in (the last arrival acquires everyone's).
+    __syncwarp();
+    int prev = 0;
+    if (lane == 0)
+      asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;"
+                   : "=r"(prev)
+                   : "l"(p.counters + (int64_t)rb * 8 + warp)
+                   : "memory");
+    prev = __shfl_sync(0xffffffffu, prev, 0);
+    if (prev != bl - bf) return;
+    __syncwarp();
+    // CTA bf's slot is 2bf + 1 when its range started before this row block; every later CTA starts inside it.
+    const int64_t lo_bf = gv_lo(bf, p.items, G);
+    constexpr int kBatch = NT == 1 ? 8 : (NT == 2 ? 4 : 2);
+#pragma unroll
+    for (int n = 0; n < NT; ++n) y[n][0] = y[n][1] = y[n][2] = y[n][3] = 0.f;
+    for (int b0 = bf; b0 <= bl; b0 += kBatch) {
+      float part[kBatch][NT][4];
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        const int b = b0 + u;
+        const int64_t sl = (int64_t)b * 2 + ((b == bf && lo_bf < first) ? 1 : 0);
+        const float* src = p.ws + sl * p.M * kGvBlock + rloc;
+#pragma unroll
+        for (int n = 0; n < NT; ++n)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int t = 8 * n + 2 * c + (e & 1);
+            part[u][n][e] = (b <= bl && t < p.M) ? __ldcg(src + (int64_t)t * kGvBlock + 8 * (e >> 1)) : 0.f;
+          }
+      }
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u)
+#pragma unroll
+        for (int n = 0; n < NT; ++n)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) y[n][e] += part[u][n][e];
+    }
+    if (lane == 0) p.counters[(int64_t)rb * 8 + warp] = 0;
+  }
+#pragma unroll
+  for (int n = 0; n < NT; ++n)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int t = 8 * n + 2 * c + (e & 1), row = rb * kGvBlock + rloc + 8 * (e >> 1);
+      if (t < p.M && row < p.N) gv_store(p, t, row, y[n][e]);
+    }
+}
+
+__device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int x, int y,
+                                            int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], "
+      "[%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+
+// Row ranges: the slots of each row group are added in slot order through shared memory (red[warp][lane][...]),
+// then the slot-0 warps store. rfull: all compute warps have parked their sums; rdone: the readers are done,
+// so the next chunk may overwrite red. Returns false when a bounded wait ran out.
+template <int NTW, int CW>
+__device__ __forceinline__ bool gv_flush_rows(const GvParams& p, float (&y)[NTW][4], float* red, uint64_t* rfull,
+                                              uint64_t* rdone, int chunk, int64_t row0, int64_t row_end, int rgi,
+                                              int slot, int tp, int warp, int lane) {
+  const int g = lane >> 2, c = lane & 3, tok0 = tp * NTW * 8;
+  if (p.slots > 1) {
+    if (chunk > 0 && !mbar_wait(rdone, (chunk - 1) & 1, p.status, kStatusTimeoutFull)) return false;
+    float* mine = red + (warp * 32 + lane) * NTW * 4;
+#pragma unroll
+    for (int n = 0; n < NTW; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) mine[n * 4 + e] = y[n][e];
+    mbar_arrive(rfull);
+    if (slot != 0) return true;
+    if (!mbar_wait(rfull, chunk & 1, p.status, kStatusTimeoutFull)) return false;
+    for (int s = 1; s < p.slots; ++s) {
+      const float* other = red + ((rgi + p.rgp * (s + p.slots * tp)) * 32 + lane) * NTW * 4;
+#pragma unroll
+      for (int n = 0; n < NTW; ++n)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) y[n][e] += other[n * 4 + e];
+    }
+  }
+#pragma unroll
+  for (int n = 0; n < NTW; ++n)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int t = tok0 + 8 * n + 2 * c + (e & 1);
+      const int64_t row = row0 + rgi * 16 + g + 8 * (e >> 1);
+      if (t < p.M && row < row_end) gv_store(p, t, (int)row, y[n][e]);
+    }
+  if (p.slots > 1) mbar_arrive(rdone);
+  return true;
+}
+
+// Resident activations (row ranges with small M * K): the compute warps copy all of x into shared memory once,
+// in the stage layout (row = 64-K chunk * M + token, swizzled), Q4_K already permuted, with the Q4_K group sums
+// ([super-block][hi, lo][token][8] f16). A thread takes one 16-byte piece (8 values); four consecutive pieces
+// are one group, added in f32 by two shuffles.
+template <int T>
+__device__ __forceinline__ void gv_prep_resident(const GvParams& p, uint32_t res, uint32_t ressum, int tid,
+                                                 int nthreads) {
+  const int kp_total = p.K / 8;  // pieces per token, a multiple of 32
+  const int total = p.M * kp_total;
+  for (int L = tid; L < total; L += nthreads) {
+    const int t = L / kp_total, kp = L - t * kp_total;
+    uint4 v = __ldg(reinterpret_cast<const uint4*>(p.x + (int64_t)t * p.ldx + (int64_t)kp * 8));
+    if (T == 12) {
+      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&v.x));
+      const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&v.y));
+      const float2 e = __half22float2(*reinterpret_cast<const __half2*>(&v.z));
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&v.w));
+      float sum = ((a.x + a.y) + (b.x + b.y)) + ((e.x + e.y) + (f.x + f.y));
+      sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+      sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+      if ((kp & 3) == 0) {
+        const int group = kp >> 2;
+        gv_store_sum(ressum + (group >> 3) * 32 * p.M, p.M, t, group & 7, sum);
+      }
+      v = make_uint4(prmt(v.x, v.y, 0x5410u), prmt(v.x, v.y, 0x7632u), prmt(v.z, v.w, 0x5410u),
+                     prmt(v.z, v.w, 0x7632u));
+    }
+    const uint32_t a = xpiece(res, (kp >> 3) * p.M + t, kp & 7);
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                 : "memory");
+  }
+}
+
+template <int T, int NTW, int CW, bool RANGES>
+__global__ void __launch_bounds__(GvRoles<T, CW>::kThreads, (CW == 8 && NTW == 1) ? 2 : 1)
     qgemv_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                  const GvParams p) {
-  using S = GvSmem<T, MT>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kBarOff);
-  uint64_t* empty = full + kGvStages;
-  __shared__ int s_last;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.baroff);
+  uint64_t* empty = full + kGvMaxStages;
+  uint64_t* sready = empty + kGvMaxStages;
+  uint64_t* rfull = sready + kGvMaxStages;
+  uint64_t* rdone = rfull + 1;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
+  constexpr bool ranges = RANGES;
 
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int rb = blockIdx.x / p.S, split = blockIdx.x % p.S;
-  const int sb0 = (int)((int64_t)split * p.nsb / p.S), sb1 = (int)((int64_t)(split + 1) * p.nsb / p.S);
+  const GvWork W = gv_work<RANGES>(p);
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kGvStages; ++i) {
+    for (int i = 0; i < p.turns * p.ringst; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], kGvWarps);
+      mbar_init(&empty[i], CW / p.turns + (T == 12 && !p.xres ? 1 : 0));
+      mbar_init(&sready[i], 32);
     }
+    mbar_init(rfull, CW * 32);
+    mbar_init(rdone, p.rgp * p.tsplit * 32);
     fence_barrier_init();
   }
   __syncthreads();
 
-  float acc[MT][4];
-#pragma unroll
-  for (int m = 0; m < MT; ++m) acc[m][0] = acc[m][1] = acc[m][2] = acc[m][3] = 0.f;
-
-  if (warp == kGvWarps) {
-    if (lane == 0) {
-      tma_prefetch_desc(&tmap_w);
-      tma_prefetch_desc(&tmap_x);
-      int i = 0;
-      for (int sb = sb0; sb < sb1; ++sb, ++i) {
-        const int st = i % kGvStages, ph = (i / kGvStages) & 1;
-        if (!mbar_wait(&empty[st], ph ^ 1, p.status, kStatusTimeoutEmpty)) break;
-        uint8_t* base = smem + st * S::kStage;
-        mbar_arrive_expect_tx(&full[st], kGvRows * GvFmt<T>::kBox + 4 * S::kXTile);
-        const int64_t sbg = (int64_t)p.kb_off + sb;
-        const int xw = (T == 14) ? (int)(((sbg * 210) & ~int64_t(15)) >> 1) : (int)(sbg * (GvFmt<T>::kSB / 2));
-        tma_load_2d(base, &tmap_w, &full[st], xw, rb * kGvRows);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) tma_load_2d(base + S::kW + j * S::kXTile, &tmap_x, &full[st], sb * 256 + 64 * j, 0);
+  if (warp == CW) {
+    // ---------------------------------------------------------------- TMA producer
+    if (lane != 0) return;
+    tma_prefetch_desc(&tmap_w);
+    tma_prefetch_desc(&tmap_x);
+    const uint32_t bytes = (uint32_t)(p.ops * p.rb * p.opw + (p.xres ? 0 : 4 * p.sst * p.M * 128));
+    int cnt[8] = {0, 0, 0, 0, 0, 0, 0, 0};  // stages issued per ring
+    const int mask = p.ringst - 1;
+    bool ok = true;
+    for (int si = 0; si < W.nseg && ok; ++si) {
+      const GvSeg sg = gv_seg<RANGES>(p, W, si);
+      const int64_t row0 = sg.row0;
+      int r = 0;
+      for (int sb0 = sg.sb_begin; sb0 < sg.sb_end; sb0 += p.sst) {
+      const int q = cnt[r]++;
+      const int st = r * p.ringst + (q & mask), ph = (q >> p.ringlog) & 1;
+      if (++r == p.turns) r = 0;
+      if (!mbar_wait(&empty[st], ph ^ 1, p.status, kStatusTimeoutEmpty)) { ok = false; break; }
+      uint8_t* base = smem + st * p.stage_bytes;
+      mbar_arrive_expect_tx(&full[st], bytes);
+      for (int op = 0; op < p.ops; ++op) {
+        const int64_t sbg = (int64_t)p.kb_off + sb0 + op * p.P;
+        const int xw = T == 14 ? (int)(((sbg * 210) & ~int64_t(15)) >> 1) : (int)(sbg * (gv_sb_bytes(T) / 8));
+        tma_load_2d(base + op * p.wreg, &tmap_w, &full[st], xw, (int)row0);
       }
-      // drain the last copies
-      const int n = sb1 - sb0;
-      for (int k = (n > kGvStages ? n - kGvStages : 0); k < i; ++k)
-        mbar_wait(&full[k % kGvStages], (k / kGvStages) & 1, p.status, kStatusTimeoutDrain, false);
+      if (!p.xres) tma_load_3d(base + p.xoff, &tmap_x, &full[st], 0, 0, 4 * sb0);
+      }
     }
-  } else {
-    const int g = lane >> 2, c = lane & 3;
-    const int row_local = warp * 8 + g;
-    int i = 0;
-    for (int sb = sb0; sb < sb1; ++sb, ++i) {
-      const int st = i % kGvStages, ph = (i / kGvStages) & 1;
-      if (!mbar_wait(&full[st], ph, p.status, kStatusTimeoutFull)) break;
-      const uint32_t base = smem_u32(smem + st * S::kStage);
-      const uint32_t rbase = base + row_local * GvFmt<T>::kBox;
-      const int o = (T == 14) ? (int)((((int64_t)p.kb_off + sb) * 210) & 15) : 0;
-#pragma unroll 1
-      for (int j = 0; j < 4; ++j) {
-        uint32_t b[8];
-        decode16<T>(rbase, j, c, o, b);
-        const uint32_t xb = base + S::kW + j * S::kXTile;
+    for (int r = 0; r < p.turns; ++r)
+      for (int q = (cnt[r] > p.ringst ? cnt[r] - p.ringst : 0); q < cnt[r]; ++q)
+        mbar_wait(&full[r * p.ringst + (q & mask)], (q >> p.ringlog) & 1, p.status, kStatusTimeoutDrain, false);
+    return;
+  }
+
+  if (warp == CW + 1) {
+    // ---------------------------------------------------------------- Q4_K activation prep
+    if (p.xres) return;
+    int cnt[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    const int mask = p.ringst - 1;
+    bool ok = true;
+    for (int si = 0; si < W.nseg && ok; ++si) {
+      const GvSeg sg = gv_seg<RANGES>(p, W, si);
+      int r = 0;
+      for (int sb0 = sg.sb_begin; sb0 < sg.sb_end; sb0 += p.sst) {
+      const int q = cnt[r]++;
+      const int st = r * p.ringst + (q & mask), ph = (q >> p.ringlog) & 1;
+      if (++r == p.turns) r = 0;
+      if (!mbar_wait(&full[st], ph, p.status, kStatusTimeoutFull)) { ok = false; break; }
+      const uint32_t base = smem_u32(smem + st * p.stage_bytes);
+      gv_prep_q4k(base + p.xoff, p.sst, p.M, base + p.sumoff, lane);
+      fence_proxy_async();  // the permuted activations are overwritten by a later copy into this stage
+      __syncwarp();
+      mbar_arrive(&sready[st]);
+      if (lane == 0) mbar_arrive(&empty[st]);
+      }
+    }
+    return;
+  }
+
+  // ------------------------------------------------------------------ compute warps
+  const int rgi = warp % p.rgp, rest = warp / p.rgp, slot = rest % p.slots, tp = rest / p.slots;
+  const int tok0 = tp * NTW * 8;
+  // Stage k of a segment holds super-blocks k * sst .. + sst - 1; this warp takes super-block slot (mod slots),
+  // i.e. position slot % sst of the stages k with k % (slots / sst) == slot / sst.
+  const int pos = slot % p.sst, turn = slot / p.sst;
+  const int op = pos / p.P, within = pos % p.P;
+  const bool has_rows = rgi * 16 < p.rb;
+  float* red = reinterpret_cast<float*>(smem + p.redoff);
+  const uint32_t res = smem_u32(smem + p.resoff), ressum = smem_u32(smem + p.ressum);
+  if (p.xres) {
+    gv_prep_resident<T>(p, res, ressum, threadIdx.x, CW * 32);
+    named_bar(1, CW * 32);
+  }
+  float y[NTW][4];
 #pragma unroll
-        for (int m = 0; m < MT; ++m) {
-          const int t0 = 16 * m + g, t1 = t0 + 8;
-#pragma unroll
-          for (int s = 0; s < 4; ++s) {
-            const int ch = 2 * c + (s >> 1), lo8 = 8 * (s & 1);
-            const uint2 x0 = lds64(xb + t0 * 128 + ((ch ^ (t0 & 7)) << 4) + lo8);
-            const uint2 x1 = lds64(xb + t1 * 128 + ((ch ^ (t1 & 7)) << 4) + lo8);
-            mma16816(acc[m], x0.x, x1.x, x0.y, x1.y, b[2 * s], b[2 * s + 1]);
-          }
-        }
+  for (int n = 0; n < NTW; ++n) y[n][0] = y[n][1] = y[n][2] = y[n][3] = 0.f;
+  int lc = 0;  // this warp's ring: stages consumed so far
+  for (int si = 0; si < W.nseg; ++si) {
+    const GvSeg sg = gv_seg<RANGES>(p, W, si);
+    bool ok = true;
+    for (int sb0 = sg.sb_begin + turn * p.sst; sb0 < sg.sb_end; sb0 += p.slots) {
+      const int st = turn * p.ringst + (lc & (p.ringst - 1)), ph = (lc >> p.ringlog) & 1;
+      ++lc;
+      if (!mbar_wait(&full[st], ph, p.status, kStatusTimeoutFull) ||
+          (T == 12 && !p.xres && !mbar_wait(&sready[st], ph, p.status, kStatusTimeoutFull))) {
+        ok = false;
+        break;
+      }
+      if (has_rows && sb0 + pos < sg.sb_end) {
+        const uint32_t base = smem_u32(smem + st * p.stage_bytes);
+        uint32_t off = (uint32_t)(within * gv_sb_bytes(T));
+        if (T == 14) off = (uint32_t)((((int64_t)p.kb_off + sb0 + op * p.P) * 210) & 15) + within * 210;
+        const uint32_t w0 = base + op * p.wreg + (rgi * 16 + g) * p.opw + off;
+        if (p.xres)
+          gv_superblock<T, NTW>(w0, w0 + 8 * p.opw, res, p.M, 4 * (sb0 + pos), tok0, p.M,
+                                ressum + (sb0 + pos) * 32 * p.M, y, g, c);
+        else
+          gv_superblock<T, NTW>(w0, w0 + 8 * p.opw, base + p.xoff, p.M, 4 * pos, tok0, p.M,
+                                base + p.sumoff + pos * 32 * p.M, y, g, c);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[st]);
     }
-  }
-
-  // ---------------------------------------------------------------- results
-  const bool compute = warp < kGvWarps;
-  const int g = lane >> 2, c = lane & 3;
-  const int row0 = rb * kGvRows + warp * 8 + 2 * c;
-  if (p.S == 1) {
-    if (compute) {
-#pragma unroll
-      for (int m = 0; m < MT; ++m)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int t = 16 * m + g + 8 * (e >> 1), n = row0 + (e & 1);
-          if (t < p.M && n < p.N) {
-            float v = acc[m][e];
-            if (p.epi == kEpiResid) v += p.aux[(int64_t)t * p.ldaux + n];
-            if (p.y_f16) reinterpret_cast<__half*>(p.y)[(int64_t)t * p.ldy + n] = __float2half_rn(v);
-            else reinterpret_cast<float*>(p.y)[(int64_t)t * p.ldy + n] = v;
-          }
-        }
+    if (!ok) break;
+    if constexpr (ranges) {
+      const int64_t row_end = sg.row0 + p.rb < W.re ? sg.row0 + p.rb : W.re;
+      if (!gv_flush_rows<NTW, CW>(p, y, red, rfull, rdone, si, sg.row0, row_end, rgi, slot, tp, warp, lane)) break;
+    } else {
+      gv_flush_streamk<NTW>(p, W.r, y, (int)(sg.row0 / kGvBlock), warp, lane);
     }
-    return;
-  }
-  if (compute) {
 #pragma unroll
-    for (int m = 0; m < MT; ++m)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int t = 16 * m + g + 8 * (e >> 1), n = row0 + (e & 1);
-        if (t < p.M && n < p.N) p.ws[((int64_t)split * p.M + t) * p.N + n] = acc[m][e];
-      }
+    for (int n = 0; n < NTW; ++n) y[n][0] = y[n][1] = y[n][2] = y[n][3] = 0.f;
   }
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) s_last = (atomicAdd(&p.counters[rb], 1) == p.S - 1);
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  const int rows = min(kGvRows, p.N - rb * kGvRows);
-  for (int idx = threadIdx.x; idx < p.M * kGvRows; idx += blockDim.x) {
-    const int t = idx / kGvRows, r = idx % kGvRows;
-    if (r >= rows) continue;
-    const int n = rb * kGvRows + r;
-    float v = 0.f;
-    for (int s = 0; s < p.S; ++s) v += __ldcg(p.ws + ((int64_t)s * p.M + t) * p.N + n);
-    if (p.epi == kEpiResid) v += p.aux[(int64_t)t * p.ldaux + n];
-    if (p.y_f16) reinterpret_cast<__half*>(p.y)[(int64_t)t * p.ldy + n] = __float2half_rn(v);
-    else reinterpret_cast<float*>(p.y)[(int64_t)t * p.ldy + n] = v;
-  }
-  if (threadIdx.x == 0) p.counters[rb] = 0;
 }
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -304,40 +741,74 @@ EncodeTiledFn gv_encoder() {
   return fn;
 }
 
-template <int T, int MT>
-cudaError_t gv_launch(const QGemvArgs& a, float* ws, int* counters, int S, cudaStream_t stream) {
-  using SM = GvSmem<T, MT>;
+int pow2_ceil(int v) {
+  int r = 1;
+  while (r < v) r <<= 1;
+  return r;
+}
+
+template <int T, int NTW, int CW, bool RANGES>
+cudaError_t gv_launch(const QGemvArgs& a, const GemvPlan& pl, float* ws, int* counters, cudaStream_t stream) {
   EncodeTiledFn enc = gv_encoder();
   if (!enc) return cudaErrorNotSupported;
   CUtensorMap mw, mx;
   {
-    const int64_t window_bytes = (a.kb_off + a.K / 256) * GvFmt<T>::kSB;
-    cuuint64_t dims[2] = {(cuuint64_t)((window_bytes + 1) / 2), (cuuint64_t)a.N};
+    // weights: u64 elements for Q4_K / Q8_0 (whole super-blocks), u16 for Q6_K (a 16-byte aligned window)
+    const int64_t window_bytes = (a.kb_off + a.K / 256) * gv_sb_bytes(T);
+    const int es = T == 14 ? 2 : 8;
+    cuuint64_t dims[2] = {(cuuint64_t)((window_bytes + es - 1) / es), (cuuint64_t)a.N};
     cuuint64_t strides[1] = {(cuuint64_t)a.w_row_stride};
-    cuuint32_t box[2] = {(cuuint32_t)(GvFmt<T>::kBox / 2), (cuuint32_t)kGvRows};
-    cuuint32_t es[2] = {1, 1};
-    if (enc(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(a.w), dims, strides, box, es,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    cuuint32_t box[2] = {(cuuint32_t)(pl.opw / es), (cuuint32_t)pl.rb};
+    cuuint32_t ones[2] = {1, 1};
+    if (enc(&mw, T == 14 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void*>(a.w),
+            dims, strides, box, ones, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return cudaErrorInvalidValue;
   }
   {
-    cuuint64_t dims[2] = {(cuuint64_t)a.K, (cuuint64_t)a.M};
-    cuuint64_t strides[1] = {(cuuint64_t)a.ldx * 2};
-    cuuint32_t box[2] = {64, (cuuint32_t)SM::kTP};
-    cuuint32_t es[2] = {1, 1};
-    if (enc(&mx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(a.x), dims, strides, box, es,
+    // activations as [K / 64][M][64]: one copy brings the 4 * sst 64-K chunks of a stage, all M tokens
+    cuuint64_t dims[3] = {64, (cuuint64_t)a.M, (cuuint64_t)(a.K / 64)};
+    cuuint64_t strides[2] = {(cuuint64_t)a.ldx * 2, 128};
+    cuuint32_t box[3] = {64, (cuuint32_t)a.M, (cuuint32_t)(4 * pl.sst)};
+    cuuint32_t ones[3] = {1, 1, 1};
+    if (enc(&mx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(a.x), dims, strides, box, ones,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return cudaErrorInvalidValue;
   }
   GvParams p;
   p.N = (int)a.N;
-  p.K = (int)a.K;
   p.M = (int)a.M;
   p.kb_off = (int)a.kb_off;
   p.nsb = (int)(a.K / 256);
-  p.S = S;
+  p.mode = pl.mode;
+  p.rb = pl.rb;
+  p.rgp = pl.rgp;
+  p.slots = pl.slots;
+  p.sst = pl.sst;
+  p.turns = pl.slots / pl.sst;
+  p.ringst = pl.ringst;
+  p.ringlog = 0;
+  while ((1 << p.ringlog) < pl.ringst) ++p.ringlog;
+  p.tsplit = pl.tsplit;
+  p.P = pl.P;
+  p.ops = pl.ops;
+  p.opw = pl.opw;
+  p.wreg = pl.wreg;
+  p.xoff = pl.xoff;
+  p.sumoff = pl.sumoff;
+  p.stage_bytes = pl.stage_bytes;
+  p.stages = pl.stages;
+  p.redoff = pl.redoff;
+  p.baroff = pl.baroff;
+  p.xres = pl.xres;
+  p.resoff = pl.resoff;
+  p.ressum = pl.ressum;
+  p.x = static_cast<const __half*>(a.x);
+  p.ldx = a.ldx;
+  p.K = (int)a.K;
+  p.units = (a.N + 3) / 4;
+  p.items = ((a.N + kGvBlock - 1) / kGvBlock) * (a.K / 256);
   p.y = a.y;
   p.ldy = a.ldy;
   p.y_f16 = a.y_f16;
@@ -347,35 +818,107 @@ cudaError_t gv_launch(const QGemvArgs& a, float* ws, int* counters, int S, cudaS
   p.ws = ws;
   p.counters = counters;
   p.status = a.status;
-  const int rblocks = (int)((a.N + kGvRows - 1) / kGvRows);
-  auto kern = qgemv_kernel<T, MT>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SM::kAlloc);
+  auto kern = qgemv_kernel<T, NTW, CW, RANGES>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, pl.smem);
   if (e != cudaSuccess) return e;
-  kern<<<rblocks * S, kGvThreads, SM::kAlloc, stream>>>(mw, mx, p);
+  kern<<<pl.grid, GvRoles<T, CW>::kThreads, pl.smem, stream>>>(mw, mx, p);
   return cudaGetLastError();
 }
 
 template <int T>
-cudaError_t gv_fmt(const QGemvArgs& a, float* ws, int* counters, int S, cudaStream_t s) {
-  return a.M <= 16 ? gv_launch<T, 1>(a, ws, counters, S, s) : gv_launch<T, 2>(a, ws, counters, S, s);
+cudaError_t gv_fmt(const QGemvArgs& a, const GemvPlan& pl, float* ws, int* counters, cudaStream_t s) {
+  if (pl.mode == 0) {
+    if (pl.cw == 16) return gv_launch<T, 1, 16, true>(a, pl, ws, counters, s);
+    if (pl.ntw == 1) return gv_launch<T, 1, 8, true>(a, pl, ws, counters, s);
+    if (pl.ntw == 2) return gv_launch<T, 2, 8, true>(a, pl, ws, counters, s);
+    return gv_launch<T, 4, 8, true>(a, pl, ws, counters, s);
+  }
+  if (pl.ntw == 1) return gv_launch<T, 1, 8, false>(a, pl, ws, counters, s);
+  if (pl.ntw == 2) return gv_launch<T, 2, 8, false>(a, pl, ws, counters, s);
+  return gv_launch<T, 4, 8, false>(a, pl, ws, counters, s);
 }
 
 }  // namespace
 
-// Split-K factor and workspace need of a GEMV launch (host helpers for the C ABI).
-int qgemv_splits(int64_t N, int64_t K, int num_sms) {
-  const int64_t rblocks = (N + kGvRows - 1) / kGvRows;
-  int64_t S = num_sms / rblocks;
-  if (S < 1) S = 1;
-  if (S > K / 256) S = K / 256;
-  return (int)S;
+GemvPlan qgemv_plan(int type, int64_t N, int64_t K, int64_t M, int num_sms) {
+  GemvPlan pl{};
+  const int nt = pow2_ceil((int)((M + 7) / 8));  // token tiles of 8: 1, 2 or 4
+  const int64_t units = (N + 3) / 4, nsb = K / 256;
+  const bool ranges = units >= 4 * (int64_t)num_sms;  // at least 16 rows per CTA
+  pl.mode = ranges ? 0 : 1;
+  if (ranges) {
+    pl.grid = num_sms;
+    const int64_t per_cta = (units + pl.grid - 1) / pl.grid;
+    pl.rb = (int)(4 * per_cta < 128 ? 4 * per_cta : 128);
+    pl.rgp = pow2_ceil((pl.rb + 15) / 16);
+    pl.cw = nt == 1 ? 16 : 8;
+    const int room = pl.cw / pl.rgp;
+    pl.tsplit = nt > 1 ? (nt / 2 < room ? nt / 2 : room) : 1;
+    if (pl.tsplit < 1) pl.tsplit = 1;
+    pl.ntw = nt / pl.tsplit;
+    pl.slots = room / pl.tsplit;
+  } else {
+    pl.rb = kGvBlock;
+    pl.rgp = 8;
+    pl.cw = 8;
+    pl.tsplit = 1;
+    pl.ntw = nt;
+    pl.slots = 1;
+  }
+  pl.xres = ranges && M * K * 2 <= 32 * 1024;  // all activations fit beside the weight stages
+  const int red_bytes = (ranges && pl.slots > 1) ? pl.cw * 32 * pl.ntw * 4 * 4 : 0;
+  const int bar_bytes = (3 * kGvMaxStages + 2) * 8;
+  const bool two_per_sm = !ranges && pl.ntw == 1;
+  const int res_bytes = pl.xres ? (int)((M * K * 2 + 1023) / 1024 * 1024) : 0;
+  const int ressum_bytes = pl.xres && type == 12 ? (int)(((K / 256) * 32 * M + 1023) / 1024 * 1024) : 0;
+  const int budget = (two_per_sm ? 104 * 1024 : kGvSmemBudget) - red_bytes - bar_bytes - res_bytes - ressum_bytes;
+  // Stages of ~8 KB of weights, so every CTA's first data arrives early; the warps of one super-block turn
+  // (slots / sst turns) consume a ring of their own, of a power-of-two number of stages >= 2.
+  pl.sst = 1;
+  while (pl.sst < pl.slots && 2 * pl.sst * pl.rb * gv_sb_bytes(type) <= 8 * 1024) pl.sst *= 2;
+  for (;;) {
+    pl.P = pl.sst < gv_pmax(type) ? pl.sst : gv_pmax(type);
+    pl.ops = pl.sst / pl.P;
+    pl.opw = gv_opw(type, pl.P);
+    pl.wreg = ((pl.rgp * 16 * pl.opw) + 127) / 128 * 128;
+    pl.xoff = (pl.ops * pl.wreg + 1023) / 1024 * 1024;
+    pl.sumoff = pl.xoff + (pl.xres ? 0 : 4 * pl.sst * (int)M * 128);
+    const int sum_bytes = type == 12 && !pl.xres ? pl.sst * 32 * (int)M : 0;
+    pl.stage_bytes = (pl.sumoff + sum_bytes + 1023) / 1024 * 1024;
+    const int turns = pl.slots / pl.sst;
+    int fit = budget / pl.stage_bytes;
+    if (fit > kGvMaxStages) fit = kGvMaxStages;
+    pl.ringst = 1;
+    while (2 * pl.ringst * turns <= fit) pl.ringst *= 2;
+    if (pl.ringst >= 2 || pl.sst == pl.slots) break;
+    pl.sst *= 2;
+  }
+  pl.stages = (pl.slots / pl.sst) * pl.ringst;
+  pl.resoff = pl.stages * pl.stage_bytes;
+  pl.ressum = pl.resoff + res_bytes;
+  pl.redoff = pl.ressum + ressum_bytes;
+  pl.baroff = (pl.redoff + red_bytes + 7) / 8 * 8;
+  pl.smem = pl.baroff + bar_bytes + 1024;  // + alignment of the dynamic shared memory base
+  if (!ranges) {
+    const int64_t items = ((N + kGvBlock - 1) / kGvBlock) * nsb;
+    const int64_t ctas = (int64_t)num_sms * (two_per_sm ? 2 : 1);
+    pl.grid = (int)(items < ctas ? items : ctas);
+    if (pl.grid < 1) pl.grid = 1;
+    bool split = false;  // does any CTA range start inside a row block?
+    for (int b = 1; b < pl.grid && !split; ++b) split = ((int64_t)b * items / pl.grid) % nsb != 0;
+    pl.ws_floats = split ? (int64_t)pl.grid * 2 * M * kGvBlock : 0;
+    pl.counters = split ? ((N + kGvBlock - 1) / kGvBlock) * 8 : 0;
+  }
+  return pl;
 }
 
-cudaError_t launch_qgemv_ws(const QGemvArgs& a, float* ws, int* counters, int S, cudaStream_t stream) {
+cudaError_t launch_qgemv_ws(const QGemvArgs& a, const GemvPlan& plan, float* ws, int* counters,
+                            cudaStream_t stream) {
+  if (plan.ringst < 2) return cudaErrorInvalidConfiguration;
   switch (a.type) {
-    case 8: return gv_fmt<8>(a, ws, counters, S, stream);
-    case 12: return gv_fmt<12>(a, ws, counters, S, stream);
-    case 14: return gv_fmt<14>(a, ws, counters, S, stream);
+    case 8: return gv_fmt<8>(a, plan, ws, counters, stream);
+    case 12: return gv_fmt<12>(a, plan, ws, counters, stream);
+    case 14: return gv_fmt<14>(a, plan, ws, counters, stream);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -394,8 +937,8 @@ namespace yah {
 namespace {
 
 constexpr size_t kStaticStatusBytes = 256;                 // status word (padded)
-constexpr size_t kStaticCounters = 4096;                   // one per 128-row block: N <= 524288
-constexpr size_t kStaticPartials = (size_t)1 << 20;        // split-K partial sums: S * M * N <= 1M floats
+constexpr size_t kStaticCounters = 32768;                  // 8 per 128-row block: N <= 524288
+constexpr size_t kStaticPartials = (size_t)1 << 21;        // partial sums: 2 x 32 x 128 floats per CTA, 256 CTAs
 constexpr size_t kStaticBytes = kStaticStatusBytes + kStaticCounters * sizeof(int) + kStaticPartials * sizeof(float);
 
 static __device__ __align__(256) unsigned char g_qgemv_static[kStaticBytes];
@@ -422,20 +965,19 @@ cudaError_t qgemv_static_setup(int device, void** base) {
   return cudaSuccess;
 }
 
-cudaError_t launch_qgemv_static(const QGemvArgs& a_in, void* base, int S, cudaStream_t stream) {
+cudaError_t launch_qgemv_static(const QGemvArgs& a_in, const GemvPlan& plan, void* base, cudaStream_t stream) {
   QGemvArgs a = a_in;
   unsigned char* b = static_cast<unsigned char*>(base);
   int* status = reinterpret_cast<int*>(b);
   int* counters = reinterpret_cast<int*>(b + kStaticStatusBytes);
   float* partials = reinterpret_cast<float*>(b + kStaticStatusBytes + kStaticCounters * sizeof(int));
   a.status = status;
-  if (S > 1) {
+  if (plan.counters > 0) {
     // The counters must start at zero; a previous call leaves them at zero unless it was interrupted.
-    const size_t nrb = (size_t)((a.N + 127) / 128);
-    const cudaError_t e = cudaMemsetAsync(counters, 0, nrb * sizeof(int), stream);
+    const cudaError_t e = cudaMemsetAsync(counters, 0, (size_t)plan.counters * sizeof(int), stream);
     if (e != cudaSuccess) return e;
   }
-  return launch_qgemv_ws(a, partials, counters, S, stream);
+  return launch_qgemv_ws(a, plan, partials, counters, stream);
 }
 
 cudaError_t qgemv_static_status(void* base, int* code, bool clear) {
