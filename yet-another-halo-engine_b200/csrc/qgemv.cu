@@ -19,9 +19,10 @@
 // super-block slot (w / rgp) % S of every stage, and on its share of the tokens. For Q4_K a helper warp permutes
 // each stage's activations to the order the nibble pairs come in ((x0, x2), (x1, x3)) and forms the group sums.
 // Two ways to split the work over the GPU:
-//   row ranges (N >= 4 * #SMs): CTA b owns a contiguous range of ~N / #SMs rows (4-row granularity) and all of
-//     K; the slots of a row group are added through shared memory. No scratch, balanced within 4 rows per SM.
-//   stream-K (small N): 128-row blocks x super-blocks, cut into equal ranges per CTA; a row block shared by
+//   row ranges (N >= 16 * #SMs and M * K small enough that all activations stay in shared memory): CTA b owns a
+//     contiguous range of ~N / #SMs rows (4-row granularity) and all of K; the slots of a row group are added
+//     through shared memory. No scratch, balanced within 4 rows per SM.
+//   stream-K (otherwise): 128-row blocks x super-blocks, cut into equal ranges per CTA; a row block shared by
 //     several CTAs is summed through a workspace by the last CTA to arrive, in CTA order (deterministic).
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -107,6 +108,14 @@ __device__ __forceinline__ uint32_t xpiece(uint32_t xs, int row, int q) {
   return xs + row * 128 + ((q ^ (row & 7)) << 4);
 }
 
+// u >> 8 as the high word of u * 2^24: a multiply, so it issues on the FMA pipe and leaves the integer/logic
+// pipe (the busiest one in the Q4_K decode) to the nibble masks.
+__device__ __forceinline__ uint32_t shr8_fma(uint32_t u) {
+  uint32_t r;
+  asm("mul.hi.u32 %0, %1, 16777216;" : "=r"(r) : "r"(u));
+  return r;
+}
+
 // 4-byte word at an even offset, as f32 2^23 + byte (for the scale bytes of Q4_K)
 __device__ __forceinline__ float magic_byte(uint32_t word, int byte) {
   return __uint_as_float(prmt(word, 0x4B000000u, (uint32_t)byte | 0x7650u));
@@ -150,7 +159,7 @@ __device__ __forceinline__ void gv_superblock(uint32_t w0, uint32_t w1, uint32_t
 #pragma unroll
       for (int wi = 0; wi < 2; ++wi) {
         const uint32_t u0 = wi ? q0.y : q0.x, u1 = wi ? q1.y : q1.x;
-        const uint32_t v0 = u0 >> 8, v1 = u1 >> 8;
+        const uint32_t v0 = shr8_fma(u0), v1 = shr8_fma(u1);
         lo[wi][0] = u0 & 0x000F000Fu, lo[wi][1] = u1 & 0x000F000Fu, lo[wi][2] = v0 & 0x000F000Fu,
         lo[wi][3] = v1 & 0x000F000Fu;
         hi[wi][0] = u0 & 0x00F000F0u, hi[wi][1] = u1 & 0x00F000F0u, hi[wi][2] = v0 & 0x00F000F0u,
@@ -558,9 +567,19 @@ __device__ __forceinline__ void gv_prep_resident(const GvParams& p, uint32_t res
                                                  int nthreads) {
   const int kp_total = p.K / 8;  // pieces per token, a multiple of 32
   const int total = p.M * kp_total;
-  for (int L = tid; L < total; L += nthreads) {
-    const int t = L / kp_total, kp = L - t * kp_total;
-    uint4 v = __ldg(reinterpret_cast<const uint4*>(p.x + (int64_t)t * p.ldx + (int64_t)kp * 8));
+  // four loads in flight per thread before any is used: the prep costs one L2 round trip, not one per piece
+  for (int L0 = tid; L0 < total; L0 += 4 * nthreads) {
+    uint4 vv[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int L = L0 + u * nthreads, t = L / kp_total, kp = L - t * kp_total;
+      if (L < total) vv[u] = __ldg(reinterpret_cast<const uint4*>(p.x + (int64_t)t * p.ldx + (int64_t)kp * 8));
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+    const int L = L0 + u * nthreads, t = L / kp_total, kp = L - t * kp_total;
+    if (L >= total) break;  // uniform across a warp: total and nthreads are multiples of 32
+    uint4 v = vv[u];
     if (T == 12) {
       const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&v.x));
       const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&v.y));
@@ -579,6 +598,7 @@ __device__ __forceinline__ void gv_prep_resident(const GvParams& p, uint32_t res
     const uint32_t a = xpiece(res, (kp >> 3) * p.M + t, kp & 7);
     asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
                  : "memory");
+    }
   }
 }
 
@@ -844,7 +864,10 @@ GemvPlan qgemv_plan(int type, int64_t N, int64_t K, int64_t M, int num_sms) {
   GemvPlan pl{};
   const int nt = pow2_ceil((int)((M + 7) / 8));  // token tiles of 8: 1, 2 or 4
   const int64_t units = (N + 3) / 4, nsb = K / 256;
-  const bool ranges = units >= 4 * (int64_t)num_sms;  // at least 16 rows per CTA
+  // Row ranges need >= 16 rows per CTA and pay off when the activations stay resident (no per-stage activation
+  // copies, permutes and group sums); otherwise stream-K over 128-row blocks shares each stage's activations
+  // among 128 rows.
+  const bool ranges = units >= 4 * (int64_t)num_sms && M * K * 2 <= 32 * 1024;
   pl.mode = ranges ? 0 : 1;
   if (ranges) {
     pl.grid = num_sms;
