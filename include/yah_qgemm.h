@@ -171,6 +171,41 @@ int yah_qgemv_noalloc(const void* w, int ggml_type, int64_t N, int64_t K, int64_
 /* Read and clear the status word of yah_qgemv_noalloc on the current device (same codes as yah_status_word). */
 int yah_qgemv_noalloc_status(int* code);
 
+/* ------------------------------------------------------------------ tensor-parallel layer (NCCL over NVLink)
+ * The reference engine runs on one GPU and has no counterpart; this is the sharding layer the B200 build adds for
+ * the Llama-shaped stack (one process per GPU). Column-parallel linears (QKV, gate, up) use a row range of the GGUF
+ * tensor and need no collective; row-parallel linears (o_proj, down) use a K window of whole super-blocks and end
+ * in one ncclAllReduce(sum) of f32 partials. NCCL is loaded at run time (libnccl.so.2). */
+#define YAH_TP_ID_BYTES 128
+typedef struct yah_tp_comm yah_tp_comm;
+
+/* 1 when NCCL could be loaded, else 0. */
+int yah_tp_available(void);
+/* A new NCCL unique id (YAH_TP_ID_BYTES bytes) for yah_tp_init; create it on one rank and share it. */
+int yah_tp_unique_id(void* id);
+/* Join a communicator of nranks processes as `rank`, on the current device. */
+int yah_tp_init(yah_tp_comm** comm, int nranks, int rank, const void* id);
+int yah_tp_destroy(yah_tp_comm* comm);
+int yah_tp_rank(const yah_tp_comm* comm, int* rank, int* nranks);
+/* In-place sum of an f32 device buffer over the ranks, on `stream`. */
+int yah_tp_allreduce_f32(yah_tp_comm* comm, float* buf, int64_t count, void* stream);
+/* Column-parallel linear: y[M][N_local] = x W_shard^T for this rank's row range (w_shard points at its first row);
+ * same arguments as yah_qgemm (yah_qgemv for M <= 32). No collective. */
+int yah_tp_linear_col(yah_tp_comm* comm, const void* w_shard, int ggml_type, int64_t N_local, int64_t K,
+                      int64_t w_row_stride, const void* x, int64_t M, int64_t ldx, void* y, int y_dtype,
+                      int64_t ldy, int epilogue, const void* aux, int64_t ldaux, void* stream);
+/* Row-parallel linear: this rank's K window (K_local values from super-block kb_off of rows of w_row_stride bytes)
+ * times its x slice [M][K_local]; y (f32, contiguous [M][N]) becomes resid + sum over ranks of the partials,
+ * on every rank (rank 0 adds resid in its GEMM epilogue; resid may be y; NULL adds nothing). */
+int yah_tp_linear_row(yah_tp_comm* comm, const void* w_shard, int ggml_type, int64_t N, int64_t K_local,
+                      int64_t w_row_stride, int64_t kb_off, const void* x, int64_t M, int64_t ldx, float* y,
+                      const float* resid, void* stream);
+/* RMSNorm of the f32 residual stream into f16: out[m][i] = h[m][i] * gain / sqrt(mean_i h[m][i]^2 + eps). The
+ * layer stack's norm before QKV and gate/up (the reference normalises every layer input, docs/architecture.md:68);
+ * weightless, with one gain (H and strides multiples of 4, h 16-byte and out 8-byte aligned). */
+int yah_rmsnorm(const float* h, int64_t ldh, int64_t M, int64_t H, float eps, float gain, void* out, int64_t ldo,
+                void* stream);
+
 #if defined(__GNUC__)
 #pragma GCC visibility pop
 #endif

@@ -1,0 +1,88 @@
+"""Tensor-parallel layer (yah_tp_*, yah_rmsnorm) on the GPU vs the oracle.
+
+One GPU: a one-rank NCCL communicator exercises the row-parallel linear (GEMM + allreduce, with the residual added
+by rank 0's epilogue), the K-window form, the RMSNorm and a small two-layer stack. Two or more GPUs: the same stack
+sharded over two ranks (one process per GPU) must match the float64 reference on every rank.
+"""
+import ctypes
+import multiprocessing as mp
+
+import numpy as np
+import pytest
+
+import _tp_work as W
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def comm(pkg, dev):
+    assert pkg.lib().yah_tp_available(), "NCCL (libnccl.so.2) must load on the GPU box"
+    c = pkg.tp.Comm(1, 0)
+    yield c
+    c.close()
+
+
+def test_rmsnorm(pkg, dev):
+    M, H = 37, 4096
+    h = (np.random.default_rng(60).standard_normal((M, H)) * 50).astype(np.float32)
+    hd, out = dev.upload(h), dev.empty(M * H * 2)
+    pkg._lib.check(pkg.lib().yah_rmsnorm(hd.ptr, H, M, H, ctypes.c_float(1e-6), ctypes.c_float(1 / 64), out.ptr, H,
+                                         None))
+    dev.synchronize()
+    got = out.download(np.float16, (M, H)).astype(np.float64)
+    ref64 = h.astype(np.float64) / 64 / np.sqrt((h.astype(np.float64) ** 2).mean(1, keepdims=True) + 1e-6)
+    ulp = np.spacing(np.abs(ref64).astype(np.float16)).astype(np.float64)
+    assert (np.abs(got - ref64) <= ulp).all()
+
+
+@pytest.mark.parametrize("M", [64, 4])
+@pytest.mark.parametrize("window", [False, True])
+def test_linear_row_one_rank(pkg, F, O, dev, comm, M, window):
+    """y = resid + x W^T over the rank's K window (GEMM path for 64 tokens, GEMV path for 4), allreduce of 1."""
+    t, N, K = F.Q4_K, 256, 2048
+    w = F.synth_weights(t, N, K, seed=61)
+    x = F.synth_activations(M, K, seed=62)
+    resid = np.random.default_rng(63).standard_normal((M, N)).astype(np.float32)
+    kb_off, kl = (2, 1024) if window else (0, K)
+    xs = np.ascontiguousarray(x[:, 256 * kb_off:256 * kb_off + kl])
+    wd, xd, yd = dev.upload(w), dev.upload(xs), dev.upload(resid)
+    pkg._lib.check(pkg.lib().yah_tp_linear_row(comm.handle, wd.ptr, t, N, kl, w.shape[1], kb_off, xd.ptr, M, kl,
+                                               yd.ptr, yd.ptr, None))
+    dev.synchronize()
+    y = yd.download(np.float32, (M, N))
+    deq = (O.dequant_f16 if M > 32 else O.dequant_f32)(t, w, N, kl, kb_off=kb_off)
+    e = O.errors(y, resid.astype(np.float64) + O.gemm_ref(deq, xs))
+    assert e["finite"] and e["max_abs"] <= 2e-2 and e["rel_fro"] <= 1e-3, e
+
+
+def test_small_stack_one_rank(pkg, O, dev, comm):
+    tp = pkg.tp
+    shape = tp.StackShape(layers=2, hidden=512, n_q=4, n_kv=2, head_dim=128, ff=1024)
+    M = 64
+    full = [tp.layer_weights(shape, i) for i in range(shape.layers)]
+    stack = tp.LlamaStack(dev, comm, shape, [tp.shard_layer(shape, f, 1, 0) for f in full], M)
+    h0 = np.random.default_rng(72).standard_normal((M, shape.hidden)).astype(np.float32)
+    h = dev.upload(h0)
+    stack.forward(h)
+    got = h.download(np.float32, (M, shape.hidden))
+    e = O.errors(got, W.stack_ref(O, shape, full, h0, tp.NORM_GAIN, tp.NORM_EPS))
+    stack.close()
+    assert e["finite"] and e["rel_fro"] <= 2e-3, e
+    assert dev.status_word() == 0
+
+
+def test_small_stack_two_ranks(pkg):
+    """The same stack over two GPUs (column shards + two allreduces per layer) matches the reference."""
+    if pkg.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    ctx = mp.get_context("spawn")
+    id_q, out_q = ctx.Queue(), ctx.Queue()
+    procs = [ctx.Process(target=W.gpu_stack_worker, args=(r, 2, id_q, out_q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [out_q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, rel_fro, finite, status in res:
+        assert finite and rel_fro <= 2e-3 and status == 0, (rank, rel_fro, finite, status)

@@ -5,8 +5,9 @@ Modules:
   _lib     ctypes binding of libyah_b200.so (include/yah_qgemm.h)
   device   device memory, streams, events (the reference's LoomDevice role)
   ops      qgemm / qgemv / dequant: the reference's kernel kinds over the C ABI
+  tp       tensor-parallel layer stack: shard planning, NCCL communicator, Llama-shaped linear stack
 """
 from . import formats  # noqa: F401
 from ._lib import YahError, lib  # noqa: F401
-from . import device, ops  # noqa: F401
+from . import device, ops, tp  # noqa: F401
 from .device import Device, DeviceBuffer, Event, PinnedBuffer, Stream, device_count  # noqa: F401

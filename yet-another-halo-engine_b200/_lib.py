@@ -57,7 +57,19 @@ SYMBOLS = {
     "yah_qgemv_noalloc": (c_int, [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_int, c_i64,
                                   c_int, c_vp, c_i64, c_vp]),
     "yah_qgemv_noalloc_status": (c_int, [P(c_int)]),
+    "yah_tp_available": (c_int, []),
+    "yah_tp_unique_id": (c_int, [c_vp]),
+    "yah_tp_init": (c_int, [P(c_vp), c_int, c_int, c_vp]),
+    "yah_tp_destroy": (c_int, [c_vp]),
+    "yah_tp_rank": (c_int, [c_vp, P(c_int), P(c_int)]),
+    "yah_tp_allreduce_f32": (c_int, [c_vp, c_vp, c_i64, c_vp]),
+    "yah_tp_linear_col": (c_int, [c_vp, c_vp, c_int, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_int, c_i64,
+                                  c_int, c_vp, c_i64, c_vp]),
+    "yah_tp_linear_row": (c_int, [c_vp, c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_vp,
+                                  c_vp]),
+    "yah_rmsnorm": (c_int, [c_vp, c_i64, c_i64, c_i64, c_f, c_f, c_vp, c_i64, c_vp]),
 }
+TP_ID_BYTES = 128
 
 # status codes (include/yah_qgemm.h)
 OK, ERR_ARG, ERR_UNSUPPORTED, ERR_SIZE, ERR_CUDA, ERR_DEVICE, ERR_NCCL = range(7)

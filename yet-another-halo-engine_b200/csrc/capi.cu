@@ -147,6 +147,17 @@ int after_launch(cudaError_t e, const char* what) {
 
 }  // namespace
 
+namespace yah {
+int set_error(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  return fail(code, "%s", buf);
+}
+}  // namespace yah
+
 extern "C" {
 
 const char* yah_version(void) { return "yah_b200 0.1 (sm_100a)"; }

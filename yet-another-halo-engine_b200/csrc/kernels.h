@@ -87,6 +87,9 @@ cudaError_t qgemv_static_setup(int device, void** base);
 cudaError_t launch_qgemv_static(const QGemvArgs& a, const GemvPlan& plan, void* base, cudaStream_t stream);
 cudaError_t qgemv_static_status(void* base, int* code, bool clear);
 
+// Records an error for yah_last_error() and returns `code` (shared by the C ABI translation units).
+int set_error(int code, const char* fmt, ...);
+
 // Tensor-map encoder resolved from the driver at first use (no libcuda link dependency).
 bool tensor_map_encoder_available();
 

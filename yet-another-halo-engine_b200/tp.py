@@ -1,0 +1,206 @@
+"""Tensor-parallel layer stack over the C ABI (yah_tp_*): shard planning, the NCCL communicator, and the
+Llama-shaped linear stack of the benchmark's layer configuration.
+
+The reference engine runs on one GPU; this is the sharding layer the B200 build adds. Megatron split over the
+GPUs of one box, one process per GPU:
+  * column-parallel QKV, gate, up: a rank holds a row range of the GGUF tensor (no re-quantisation; QKV in whole
+    head groups, so the rank's query heads stay together) and writes its slice of the outputs, no collective;
+  * row-parallel o_proj, down: a rank holds a K window of every row (whole super-blocks; the precedent is the
+    reference's K-window GEMM form, gen_gemm_tile.py:262-264) and one ncclAllReduce(sum) of f32 partials gives the
+    result; rank 0 adds the residual in its GEMM epilogue.
+Per layer (attention replaced by identity, so the o_proj input is the rank's query slice of the QKV output):
+
+    xn  = rmsnorm(h)                      f16, weightless, gain 1/64
+    qkv = xn Wqkv_r^T                     f16 [M][qkv_r]
+    h   = h + allreduce(qkv[:, :q_r] Wo_r^T)
+    xn  = rmsnorm(h)
+    g   = xn Wg_r^T                       f32 [M][ff_r]
+    a   = silu(g) * (xn Wu_r^T)           f16 (the GEMM's swiglu epilogue)
+    h   = h + allreduce(a Wd_r^T)
+
+The residual stream h is f32 [M][hidden] on every rank. The reference normalises every layer input
+(docs/architecture.md:68); the fixed gain keeps silu(gate) * up inside the f16 range with the synthetic weights.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import numpy as np
+
+from . import formats as F
+from ._lib import EPI_RESID, EPI_STORE, EPI_SWIGLU, F16, F32, TP_ID_BYTES, check, lib  # noqa: F401
+from .device import Device, DeviceBuffer
+
+NORM_GAIN = 1.0 / 64.0
+NORM_EPS = 1e-6
+
+
+# ----------------------------------------------------------------------------------------------- shard planning
+def even_range(n: int, parts: int, part: int, align: int = 1) -> tuple:
+    """[lo, hi) of part `part` when n (a multiple of align) is cut into `parts` near-equal aligned pieces."""
+    if n % align:
+        raise ValueError(f"{n} is not a multiple of {align}")
+    units = n // align
+    lo = part * units // parts
+    hi = (part + 1) * units // parts
+    return lo * align, hi * align
+
+
+def qkv_rows(n_q: int, n_kv: int, head_dim: int, parts: int, part: int) -> list:
+    """Row ranges of the fused [q | k | v] projection held by `part`: its query heads, then its key and value heads
+    (whole head groups: n_q and n_kv must divide by parts)."""
+    if n_q % parts or n_kv % parts:
+        raise ValueError(f"{n_q} query / {n_kv} kv heads do not split over {parts} ranks")
+    q0, q1 = even_range(n_q, parts, part)
+    k0, k1 = even_range(n_kv, parts, part)
+    kv_base = n_q * head_dim
+    return [(q0 * head_dim, q1 * head_dim), (kv_base + k0 * head_dim, kv_base + k1 * head_dim),
+            (kv_base + (n_kv + k0) * head_dim, kv_base + (n_kv + k1) * head_dim)]
+
+
+def k_window(K: int, parts: int, part: int) -> tuple:
+    """(k0, k1) of the row-parallel K window of `part`, in whole 256-value super-blocks."""
+    return even_range(K, parts, part, align=256)
+
+
+def take_rows(w: np.ndarray, ranges: list) -> np.ndarray:
+    """The rank's contiguous weight shard: the listed row ranges of GGUF rows w, stacked."""
+    return np.ascontiguousarray(np.concatenate([w[a:b] for a, b in ranges], axis=0))
+
+
+def take_k_window(w: np.ndarray, fmt: int, k0: int, k1: int) -> np.ndarray:
+    """Compact GGUF rows of the K window [k0, k1) (whole blocks; super-block = 256 values)."""
+    sb = F.SUPERBLOCK_BYTES[fmt]
+    return np.ascontiguousarray(w[:, (k0 // 256) * sb:(k1 // 256) * sb])
+
+
+@dataclass(frozen=True)
+class StackShape:
+    """The Llama-shaped stack of the layer configuration (defaults: 32 layers, hidden 4096, 32 query heads and
+    8 kv heads of 128, feed-forward 14336)."""
+    layers: int = 32
+    hidden: int = 4096
+    n_q: int = 32
+    n_kv: int = 8
+    head_dim: int = 128
+    ff: int = 14336
+    fmt: int = F.Q4_K
+
+    @property
+    def qkv(self) -> int:
+        return (self.n_q + 2 * self.n_kv) * self.head_dim
+
+    def flops(self, M: int) -> float:
+        """Algorithmic FLOPs of one forward pass over M tokens (linears only)."""
+        H = self.hidden
+        return 2.0 * M * self.layers * (H * self.qkv + H * self.n_q * self.head_dim + 2 * H * self.ff + self.ff * H)
+
+
+def layer_weights(shape: StackShape, layer: int, seed: int = 4000) -> dict:
+    """Full GGUF tensors of one layer (seeded synthetic, per formats.synth_weights)."""
+    H, s = shape.hidden, seed + 16 * layer
+    return {
+        "qkv": F.synth_weights(shape.fmt, shape.qkv, H, seed=s),
+        "o": F.synth_weights(shape.fmt, H, shape.n_q * shape.head_dim, seed=s + 1),
+        "gate": F.synth_weights(shape.fmt, shape.ff, H, seed=s + 2),
+        "up": F.synth_weights(shape.fmt, shape.ff, H, seed=s + 3),
+        "down": F.synth_weights(shape.fmt, H, shape.ff, seed=s + 4),
+    }
+
+
+def shard_layer(shape: StackShape, full: dict, parts: int, part: int) -> dict:
+    """This rank's shards of one layer's tensors (host arrays)."""
+    q0, q1 = (r * shape.head_dim for r in even_range(shape.n_q, parts, part))
+    f0, f1 = even_range(shape.ff, parts, part)
+    return {
+        "qkv": take_rows(full["qkv"], qkv_rows(shape.n_q, shape.n_kv, shape.head_dim, parts, part)),
+        "o": take_k_window(full["o"], shape.fmt, q0, q1),
+        "gate": take_rows(full["gate"], [(f0, f1)]),
+        "up": take_rows(full["up"], [(f0, f1)]),
+        "down": take_k_window(full["down"], shape.fmt, f0, f1),
+    }
+
+
+# ----------------------------------------------------------------------------------------------- communicator
+class Comm:
+    """An NCCL communicator of `nranks` processes, one per GPU (yah_tp_init on the current device).
+
+    `exchange(id_bytes_or_None) -> bytes` shares rank 0's unique id with every rank (for example a broadcast over
+    torch.distributed or a file); rank 0 passes its id, the others pass None."""
+
+    def __init__(self, nranks: int, rank: int, exchange=None):
+        if not lib().yah_tp_available():
+            raise RuntimeError("NCCL (libnccl.so.2) is not available")
+        uid = None
+        if rank == 0:
+            buf = ctypes.create_string_buffer(TP_ID_BYTES)
+            check(lib().yah_tp_unique_id(buf))
+            uid = buf.raw
+        if nranks > 1:
+            if exchange is None:
+                raise ValueError("exchange is required for more than one rank")
+            uid = exchange(uid)
+        if uid is None or len(uid) != TP_ID_BYTES:
+            raise ValueError("bad unique id")
+        self.rank, self.nranks = rank, nranks
+        h = ctypes.c_void_p()
+        check(lib().yah_tp_init(ctypes.byref(h), nranks, rank, ctypes.create_string_buffer(uid, TP_ID_BYTES)))
+        self.handle = h.value
+
+    def allreduce_f32(self, ptr: int, count: int, stream=None):
+        check(lib().yah_tp_allreduce_f32(self.handle, ptr, count, stream))
+
+    def close(self):
+        if self.handle:
+            check(lib().yah_tp_destroy(self.handle))
+            self.handle = None
+
+
+# ----------------------------------------------------------------------------------------------- the stack
+class LlamaStack:
+    """One rank's part of the linear layer stack: its weight shards on the device and the forward pass."""
+
+    def __init__(self, dev: Device, comm: Comm, shape: StackShape, shards: list, M: int):
+        self.dev, self.comm, self.shape, self.M = dev, comm, shape, M
+        p = comm.nranks
+        self.q_r = shape.n_q * shape.head_dim // p
+        self.qkv_r = shape.qkv // p
+        self.ff_r = shape.ff // p
+        self.w = [{k: dev.upload(v) for k, v in s.items()} for s in shards]
+        self.row_bytes = {k: v.shape[1] for k, v in shards[0].items()}
+        H = shape.hidden
+        self.xn = dev.empty(M * H * 2)
+        self.qkv = dev.empty(M * self.qkv_r * 2)
+        self.g = dev.empty(M * self.ff_r * 4)
+        self.act = dev.empty(M * self.ff_r * 2)
+
+    @property
+    def launches_per_forward(self) -> int:
+        """Library kernel launches per forward pass (2 norms + 5 linears per layer)."""
+        return 7 * self.shape.layers
+
+    def forward(self, h: DeviceBuffer, stream=None):
+        """h (f32 [M][hidden], the residual stream, identical on every rank) is updated in place."""
+        L, s, M, H, fmt = lib(), self.shape, self.M, self.shape.hidden, self.shape.fmt
+        c = self.comm.handle
+        for w in self.w:
+            check(L.yah_rmsnorm(h.ptr, H, M, H, NORM_EPS, NORM_GAIN, self.xn.ptr, H, stream))
+            check(L.yah_tp_linear_col(c, w["qkv"].ptr, fmt, self.qkv_r, H, self.row_bytes["qkv"], self.xn.ptr, M, H,
+                                      self.qkv.ptr, F16, self.qkv_r, EPI_STORE, None, 0, stream))
+            check(L.yah_tp_linear_row(c, w["o"].ptr, fmt, H, self.q_r, self.row_bytes["o"], 0, self.qkv.ptr, M,
+                                      self.qkv_r, h.ptr, h.ptr, stream))
+            check(L.yah_rmsnorm(h.ptr, H, M, H, NORM_EPS, NORM_GAIN, self.xn.ptr, H, stream))
+            check(L.yah_tp_linear_col(c, w["gate"].ptr, fmt, self.ff_r, H, self.row_bytes["gate"], self.xn.ptr, M, H,
+                                      self.g.ptr, F32, self.ff_r, EPI_STORE, None, 0, stream))
+            check(L.yah_tp_linear_col(c, w["up"].ptr, fmt, self.ff_r, H, self.row_bytes["up"], self.xn.ptr, M, H,
+                                      self.act.ptr, F16, self.ff_r, EPI_SWIGLU, self.g.ptr, self.ff_r, stream))
+            check(L.yah_tp_linear_row(c, w["down"].ptr, fmt, H, self.ff_r, self.row_bytes["down"], 0, self.act.ptr, M,
+                                      self.ff_r, h.ptr, h.ptr, stream))
+
+    def close(self):
+        for w in self.w:
+            for b in w.values():
+                b.close()
+        for b in (self.xn, self.qkv, self.g, self.act):
+            b.close()
