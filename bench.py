@@ -4,15 +4,19 @@
 Workloads (--workload):
   gemm   (default) BASELINE config 2: Q4_K prefill tile GEMM, M=2048 tokens, K=4096, N=14336, f16 out; TFLOP/s.
   gemv   BASELINE config 3 decode GEMV: Q4_K 4096 x 14336 weights, M tokens (--tokens, default 1); HBM GB/s.
+  stack  BASELINE config 4: the Llama-shaped Q4_K linear stack (32 layers, hidden 4096, QKV 6144, FF 14336) over
+         M=4096 tokens, tensor-parallel over the N GPUs (column-parallel QKV/gate/up, row-parallel o_proj/down with
+         one NCCL allreduce each; yet-another-halo-engine_b200/tp.py); TFLOP/s of the whole job, strong scaling.
 A step is one launch of the kernel over one batch. Inputs are resident in HBM when the timed region starts; the
 step rotates through input copies whose total exceeds L2 (126 MB), so no step reads inputs another step left in
 L2. Timing: W warm-up steps, then exactly K steps between a barrier + device synchronise on both sides, CUDA
 events on the launching stream, max over ranks. `e2e` repeats the metric through the public API with pinned host
 buffers: every step copies its activations host->device and its output device->host inside the timed region.
 
-Multi-GPU (torchrun, one process per GPU): every rank runs the same workload on its own batch (replicas, weak
-scaling; the single GEMM / GEMV has no exchange step). torch.distributed (gloo, CPU tensors) is used only for the
-barrier and the max over ranks.
+Multi-GPU (torchrun, one process per GPU): for gemm / gemv every rank runs the same workload on its own batch
+(replicas, weak scaling; the single GEMM / GEMV has no exchange step); the stack is sharded (the allreduces go
+through the library's own NCCL communicator). torch.distributed (gloo, CPU tensors) is used only for the barrier,
+the max over ranks and handing rank 0's NCCL id to the others.
 
 --impl reference: the reference's CPU path for the same metric (its test-suite oracle: gguf-py
 quants.dequantize -> f16 -> numpy matmul, engine/gpu/loom/tools/gemv_check.py:161-162), on the host cores, rank 0.
@@ -135,7 +139,7 @@ def run_ours(args, dist, rank, local_rank):
     pkg = ge.load_package()
     F, ops = pkg.formats, pkg.ops
     dev = pkg.Device(local_rank)
-    wl = gemm_workload(args) if args.workload == "gemm" else gemv_workload(args)
+    wl = gemv_workload(args) if args.workload == "gemv" else gemm_workload(args)
     t, M, K, N = wl["fmt"], wl["M"], wl["K"], wl["N"]
     gemv = args.workload == "gemv"
     w = F.synth_weights(t, N, K, seed=0)
@@ -245,6 +249,106 @@ def run_ours(args, dist, rank, local_rank):
     return line
 
 
+def run_stack(args, dist, rank, local_rank):
+    """The tensor-parallel layer stack: one step = one forward pass of all layers over M tokens."""
+    import __graft_entry__ as ge
+    pkg = ge.load_package()
+    F, tp = pkg.formats, pkg.tp
+    dev = pkg.Device(local_rank)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    shape = tp.StackShape(layers=args.layers)
+    M, H = args.stack_tokens, shape.hidden
+
+    def exchange(uid):
+        obj = [uid]
+        dist.broadcast_object_list(obj, src=0)
+        return obj[0]
+
+    comm = tp.Comm(world, rank, exchange if world > 1 else None)
+    # Each rank generates its own shards (seeded per rank; the full tensors would be their concatenation). Four
+    # distinct weight sets cycle over the layers: 4 x 122.7 MB / world > L2 at one GPU, and no layer finds the
+    # weights it reads in L2.
+    p = world
+    sets = []
+    for k in range(min(4, shape.layers)):
+        s0 = 5000 + 64 * k + 8 * rank
+        sets.append({"qkv": F.synth_weights(shape.fmt, shape.qkv // p, H, seed=s0),
+                     "o": F.synth_weights(shape.fmt, H, shape.n_q * shape.head_dim // p, seed=s0 + 1),
+                     "gate": F.synth_weights(shape.fmt, shape.ff // p, H, seed=s0 + 2),
+                     "up": F.synth_weights(shape.fmt, shape.ff // p, H, seed=s0 + 3),
+                     "down": F.synth_weights(shape.fmt, H, shape.ff // p, seed=s0 + 4)})
+    stack = tp.LlamaStack(dev, comm, shape, [sets[i % len(sets)] for i in range(shape.layers)], M)
+    h0 = np.random.default_rng(7).standard_normal((M, H)).astype(np.float32)
+    h0d, h = dev.upload(h0), dev.empty(M * H * 4)
+    stream = pkg.Stream()
+    s = stream.handle
+
+    def step():
+        pkg.lib().yah_memcpy_d2d(h.ptr, h0d.ptr, M * H * 4, s)  # every step starts from the same residual stream
+        stack.forward(h, s)
+
+    for _ in range(args.warmup):
+        step()
+    stream.synchronize()
+    e0, e1 = pkg.Event(), pkg.Event()
+    clocks = Clocks(local_rank)
+    barrier(dist)
+    dev.synchronize()
+    clocks.start()
+    time.sleep(0.3)
+    e0.record(s)
+    for _ in range(args.steps):
+        step()
+    e1.record(s)
+    e1.synchronize()
+    clk = clocks.stop()
+    barrier(dist)
+    ms_local = e0.elapsed_ms(e1)
+    ms = max_over_ranks(dist, ms_local)
+    if dev.status_word():
+        raise RuntimeError(f"kernel status word {dev.status_word()}")
+    # e2e: the residual stream in from pinned host memory and out again every step
+    hh = pkg.PinnedBuffer(M * H * 4)
+    hh.array(np.float32, (M, H))[...] = h0
+    barrier(dist)
+    e2, e3 = pkg.Event(), pkg.Event()
+    e2.record(s)
+    for _ in range(args.steps):
+        pkg.lib().yah_memcpy_h2d(h.ptr, hh.ptr, M * H * 4, s)
+        stack.forward(h, s)
+        pkg.lib().yah_memcpy_d2h(hh.ptr, h.ptr, M * H * 4, s)
+    e3.record(s)
+    e3.synchronize()
+    ms_e2e = max_over_ranks(dist, e2.elapsed_ms(e3))
+    out = h.download(np.float32, (M, H))
+    if not np.isfinite(out).all():
+        raise RuntimeError("non-finite residual stream")
+    flops = shape.flops(M)
+    per_step_ms = ms / args.steps
+    value = flops / (per_step_ms * 1e-3) / 1e12
+    pk = peaks()
+    achieved = flops / world / (ms_local / args.steps * 1e-3) / 1e12
+    line = {
+        "metric": "Q4_K layer-stack prefill TFLOP/s (tensor-parallel)", "value": round(value, 2), "unit": "TFLOP/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_step_ms, 4),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "f16 x GGUF-Q4_K -> f32 acc, f32 residual stream and allreduce", "data": "synthetic",
+        "config": {"workload": "q4k_layer_stack_tp", "layers": shape.layers, "hidden": H, "qkv": shape.qkv,
+                   "ff": shape.ff, "M_tokens": M, "parallelism": f"tp{world}",
+                   "l2": "4 distinct weight sets cycled over the layers (> L2 per GPU at tp1)"},
+        "e2e": {"value": round(flops / (ms_e2e / args.steps * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+                "h2d_bytes_per_step": M * H * 4, "d2h_bytes_per_step": M * H * 4},
+        "gpu_launches": args.steps * stack.launches_per_forward,
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": pk["tflops_sustained"],
+                     "unit": "TFLOP/s", "frac": round(achieved / pk["tflops_sustained"], 4), "traffic": None,
+                     "peak_src": pk["src"] + " (sustained)", "per_gpu": True},
+        "clocks": clk,
+    }
+    stack.close()
+    comm.close()
+    return line
+
+
 def load_traffic(name):
     """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary (profiles/*.json)."""
     p = os.path.join(ROOT, "profiles", f"{name}.traffic.json")
@@ -273,7 +377,7 @@ def cpu_reference_step(fmt, w, x, K, use_gguf=True):
 
 def cpu_baseline(args, seconds=10.0):
     """The CPU path timed on a bounded sample (rows of the weight) for the same metric."""
-    wl = gemm_workload(args) if args.workload == "gemm" else gemv_workload(args)
+    wl = gemv_workload(args) if args.workload == "gemv" else gemm_workload(args)
     import __graft_entry__ as ge
     F = ge.load_package().formats
     t, M, K, N = wl["fmt"], wl["M"], wl["K"], wl["N"]
@@ -309,7 +413,7 @@ def cpu_baseline(args, seconds=10.0):
 def run_reference(args, rank):
     if rank != 0:
         return None
-    wl = gemm_workload(args) if args.workload == "gemm" else gemv_workload(args)
+    wl = gemv_workload(args) if args.workload == "gemv" else gemm_workload(args)
     import __graft_entry__ as ge
     F = ge.load_package().formats
     t, M, K, N = wl["fmt"], wl["M"], wl["K"], wl["N"]
@@ -352,7 +456,9 @@ def main():
     ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="gemm", choices=["gemm", "gemv"])
+    ap.add_argument("--workload", default="gemm", choices=["gemm", "gemv", "stack"])
+    ap.add_argument("--layers", type=int, default=32, help="stack layers")
+    ap.add_argument("--stack-tokens", type=int, default=4096, help="stack tokens M")
     ap.add_argument("--tokens", type=int, default=1, help="gemv tokens (1..32)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
@@ -366,9 +472,12 @@ def main():
             print(json.dumps(line), flush=True)
         return
     dist = dist_init(args.gpus)
-    line = run_ours(args, dist, rank, local_rank)
+    if args.workload == "stack":
+        line = run_stack(args, dist, rank, local_rank)
+    else:
+        line = run_ours(args, dist, rank, local_rank)
     if rank == 0:
-        if not args.no_cpu_baseline:
+        if not args.no_cpu_baseline and args.workload != "stack":
             line["cpu_baseline"] = cpu_baseline(args)
         print(json.dumps(line), flush=True)
     if dist:
