@@ -98,21 +98,39 @@ struct KParams {
   int upr;              // 16-token units per row tile
   int ncta;             // CTAs per tile: 1, or 2 for a 2-SM pair
   int tma_store;        // 1: the output is written with TMA stores through shared memory (tmap_y is valid)
+  int aux_tma;          // 1: the epilogue's aux operand is prefetched by TMA (tmap_aux is valid)
 };
 
-template <int T, int XR>  // XR: activation rows a CTA stages (the tile's tokens, or half of them in a pair)
+template <int T, int XR, int AUXB = 0>  // XR: activation rows a CTA stages (the tile's tokens, or half in a pair)
 struct Smem {
   static constexpr int kWStage = ((kBM * Fmt<T>::kBox + 16) + 127) / 128 * 128;
   static constexpr int kXBytes = XCfg<XR>::kNSX * XCfg<XR>::kStage;
   static constexpr int kWOff = kXBytes;
   static constexpr int kOutOff = kWOff + Fmt<T>::kNSW * kWStage;  // 2 output staging buffers (TMA stores)
   static constexpr int kOutBuf = 4096;                            // 128 rows x 16 f16 or 8 f32 tokens
-  static constexpr int kBarOff = kOutOff + 2 * kOutBuf;
-  // barriers: xfull, xempty [NSX]; wfull, wempty [NSW]; afull, aempty [4]; accfull, accempty [2]; drain
-  static constexpr int kNumBars = 2 * XCfg<XR>::kNSX + 2 * Fmt<T>::kNSW + 2 * 4 + 5;
+  static constexpr int kAuxOff = kOutOff + 2 * kOutBuf;             // aux prefetch ring (AUXB bytes)
+  static constexpr int kBarOff = kAuxOff + AUXB;
+  // barriers: xfull, xempty [NSX]; wfull, wempty [NSW]; afull, aempty [4]; accfull, accempty [2]; drain;
+  // auxfull [4]
+  static constexpr int kNumBars = 2 * XCfg<XR>::kNSX + 2 * Fmt<T>::kNSW + 2 * 4 + 5 + 4;
   static constexpr int kTmemSlotOff = kBarOff + kNumBars * 8;
   static constexpr int kBytes = kTmemSlotOff + 16;
   static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-byte alignment of the base
+};
+
+// The epilogue's aux operand (residual, or the swiglu gate; f32 [M][ldaux]) is prefetched by TMA into a ring of
+// kDepth slots of 128 rows x CH tokens, ahead of the accumulator it is combined with, so the epilogue does not wait
+// one global round trip per CH tokens. The ring takes what shared memory the stages leave (4, 2 or no slots).
+constexpr int kSmemLimit = 227 * 1024;
+template <int T, int XR, int EPI, bool OUT_F16>
+struct AuxCfg {
+  static constexpr int kCH = OUT_F16 ? 16 : 8;
+  static constexpr int kSlot = kCH * 128 * 4;
+  static constexpr int kBase = Smem<T, XR, 0>::kAlloc;
+  static constexpr int kDepth = EPI == kEpiStore ? 0
+                                : kBase + 4 * kSlot <= kSmemLimit ? 4
+                                : kBase + 2 * kSlot <= kSmemLimit ? 2 : 0;
+  static constexpr int kBytes = kDepth * kSlot;
 };
 
 // The persistent schedule: CTA b owns units [b * total / G, (b + 1) * total / G) of the (row tile, 16-token unit)
@@ -144,9 +162,11 @@ __device__ __forceinline__ float silu_f(float g) { return g / (1.0f + __expf(-g)
 template <int T, int BN, int NACC, int EPI, bool OUT_F16, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
-                    const __grid_constant__ CUtensorMap tmap_y, const KParams p) {
+                    const __grid_constant__ CUtensorMap tmap_y, const __grid_constant__ CUtensorMap tmap_aux,
+                    const KParams p) {
   constexpr int XROWS = PAIR ? BN / 2 : BN;  // a CTA of a pair stages half of the tokens
-  using S = Smem<T, XROWS>;
+  using AC = AuxCfg<T, XROWS, EPI, OUT_F16>;
+  using S = Smem<T, XROWS, AC::kBytes>;
   constexpr int XSUB = XCfg<XROWS>::kSub;
   constexpr int XST = XCfg<XROWS>::kStage;
   constexpr int kNSX = XCfg<XROWS>::kNSX;
@@ -167,6 +187,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* accfull = aempty + 4;    // [2]
   uint64_t* accempty = accfull + 2;  // [2], counts both CTAs' epilogue warps
   uint64_t* drain = accempty + 2;
+  uint64_t* auxfull = drain + 1;     // [4]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::kTmemSlotOff);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -193,6 +214,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&accempty[i], 4 * NCTA);
     }
     mbar_init(drain, 1);
+    for (int i = 0; i < 4; ++i) mbar_init(&auxfull[i], 1);
     fence_barrier_init();
   }
   if (warp == kWarpMma) {
@@ -379,12 +401,24 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tl = tmem + ((uint32_t)(q * 32) << 16);
     float* part = p.scratch ? p.scratch + (size_t)blockIdx.x * BN * kBM + rloc : nullptr;
     uint8_t* obuf = smem + S::kOutOff;
+    constexpr int AD = AC::kDepth;
+    const bool atma = AD > 0 && p.aux_tma;
+    uint8_t* abuf = smem + S::kAuxOff;
+    uint32_t aux_used = 0;  // aux chunks consumed so far (slot aux_used % AD)
     while (ok && sc.next(rt, t0, nt)) {
       const int row0 = (rt * NCTA + (int)rank) * kBM;
       const int row = row0 + rloc;
       const bool row_ok = row < p.N;
+      const int ncks = (nt + CH - 1) / CH;  // aux chunks of this tile (its last accumulation chunk)
       for (int ch = 0; ch < nch; ++ch, ++u) {
         const uint32_t r = u % NACC;
+        if (atma && ch == nch - 1 && leader) {  // prefetch the first aux chunks while the MMAs finish
+          for (int k = 0; k < ncks && k < AD; ++k) {
+            const uint32_t sl = (aux_used + k) % AD;
+            mbar_arrive_expect_tx(&auxfull[sl], AC::kSlot);
+            tma_load_2d(abuf + sl * AC::kSlot, &tmap_aux, &auxfull[sl], row0, t0 + k * CH);
+          }
+        }
         if (!mbar_wait(&accfull[r], (u / NACC) & 1, p.status, kStatusTimeoutFull)) { ok = false; break; }
         tc_fence_after();
         const bool first = ch == 0, last = ch == nch - 1;
@@ -413,7 +447,23 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             continue;
           }
-          if (EPI != kEpiStore && row_ok) {
+          if (EPI != kEpiStore && atma) {
+            const uint32_t sl = aux_used % AD;
+            if (!mbar_wait(&auxfull[sl], (aux_used / AD) & 1, p.status, kStatusTimeoutFull)) { ok = false; break; }
+            const float* ab = reinterpret_cast<const float*>(abuf + sl * AC::kSlot);
+#pragma unroll
+            for (int jj = 0; jj < CH; ++jj) {
+              const float ax = ab[jj * kBM + rloc];
+              val[jj] = EPI == kEpiResid ? ax + val[jj] : silu_f(ax) * val[jj];
+            }
+            ++aux_used;
+            named_bar(1, 128);  // every thread has read this slot: refill it with the chunk AD ahead
+            const int k = j0 / CH + AD;
+            if (leader && k < ncks) {
+              mbar_arrive_expect_tx(&auxfull[sl], AC::kSlot);
+              tma_load_2d(abuf + sl * AC::kSlot, &tmap_aux, &auxfull[sl], row0, t0 + k * CH);
+            }
+          } else if (EPI != kEpiStore && row_ok) {
             float ax[CH];
 #pragma unroll
             for (int jj = 0; jj < CH; ++jj) ax[jj] = jj < jn ? __ldg(p.aux + (int64_t)(t0 + j0 + jj) * p.ldaux + row) : 0.f;
@@ -494,7 +544,8 @@ constexpr int kMinSmem = 120 * 1024;
 template <int T, int BN, int NACC, int EPI, bool OUT_F16, bool PAIR>
 cudaError_t launch_t(const QGemmArgs& a, cudaStream_t stream) {
   constexpr int XROWS = PAIR ? BN / 2 : BN;
-  using S = Smem<T, XROWS>;
+  using AC = AuxCfg<T, XROWS, EPI, OUT_F16>;
+  using S = Smem<T, XROWS, AC::kBytes>;
   EncodeTiledFn enc = encoder();
   if (!enc) return cudaErrorNotSupported;
   CUtensorMap mw, mx;
@@ -534,8 +585,21 @@ cudaError_t launch_t(const QGemmArgs& a, cudaStream_t stream) {
   } else {
     my = mx;  // unused
   }
+  CUtensorMap maux = mx;  // unused unless the aux operand is prefetched
+  const bool aux_tma = AC::kDepth > 0 && a.aux && (reinterpret_cast<uintptr_t>(a.aux) & 15) == 0 && a.ldaux % 4 == 0;
+  if (aux_tma) {
+    cuuint64_t dims[2] = {(cuuint64_t)a.N, (cuuint64_t)a.M};
+    cuuint64_t strides[1] = {(cuuint64_t)(a.ldaux * 4)};
+    cuuint32_t box[2] = {(cuuint32_t)kBM, (cuuint32_t)AC::kCH};
+    cuuint32_t es[2] = {1, 1};
+    if (enc(&maux, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(a.aux), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return cudaErrorInvalidValue;
+  }
   KParams p;
   p.tma_store = tma_store ? 1 : 0;
+  p.aux_tma = aux_tma ? 1 : 0;
   p.N = (int)a.N;
   p.K = (int)a.K;
   p.M = (int)a.M;
@@ -557,7 +621,7 @@ cudaError_t launch_t(const QGemmArgs& a, cudaStream_t stream) {
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
   if (e != cudaSuccess) return e;
   if (!PAIR) {
-    kern<<<grid, kThreads, smem_bytes, stream>>>(mw, mx, my, p);
+    kern<<<grid, kThreads, smem_bytes, stream>>>(mw, mx, my, maux, p);
     return cudaGetLastError();
   }
   cudaLaunchConfig_t cfg = {};
@@ -572,7 +636,7 @@ cudaError_t launch_t(const QGemmArgs& a, cudaStream_t stream) {
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, mw, mx, my, p);
+  return cudaLaunchKernelEx(&cfg, kern, mw, mx, my, maux, p);
 }
 
 template <int T, int BN, int NACC, bool PAIR>
