@@ -459,6 +459,7 @@ def main():
     ap.add_argument("--workload", default="gemm", choices=["gemm", "gemv", "stack"])
     ap.add_argument("--layers", type=int, default=32, help="stack layers")
     ap.add_argument("--stack-tokens", type=int, default=4096, help="stack tokens M")
+    ap.add_argument("--tile-table", default=None, help="tile table (tune.py output) installed before the run")
     ap.add_argument("--tokens", type=int, default=1, help="gemv tokens (1..32)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
@@ -472,6 +473,10 @@ def main():
             print(json.dumps(line), flush=True)
         return
     dist = dist_init(args.gpus)
+    if args.tile_table:
+        import __graft_entry__ as ge
+        tune = ge.load_package().tune
+        tune.apply(tune.load(args.tile_table))
     if args.workload == "stack":
         line = run_stack(args, dist, rank, local_rank)
     else:

@@ -142,6 +142,20 @@ int yah_qgemm_tile(const void* w, int ggml_type, int64_t N, int64_t K, int64_t w
                    const void* x, int64_t M, int64_t ldx, void* y, int y_dtype, int64_t ldy, int epilogue,
                    const void* aux, int64_t ldaux, int bn, int grid, int64_t kchunk, int cta_pair, void* stream);
 
+/* Tile table (opt-in): tuned tiles for yah_qgemm's automatic choice, the counterpart of the reference's tuned
+ * tables consumed by LoomPrefill::PickGemm (engine/model/loom_prefill.hpp:908-949; engine/tune/tune.py). A call
+ * (ggml_type, epilogue, y_dtype, N, K, M) uses the matching rule with the smallest m_max >= M (else the largest
+ * m_max); bn / grid / cta_pair as in yah_qgemm_tile. Tiles never change results (same accumulation chunks). The
+ * table is process-wide; yah_tile_rules_set replaces it. */
+typedef struct {
+  int ggml_type, epilogue, y_dtype;
+  int64_t N, K, m_max;
+  int bn, grid, cta_pair;
+} yah_tile_rule;
+int yah_tile_rules_set(const yah_tile_rule* rules, int n);
+int yah_tile_rules_clear(void);
+int yah_tile_rules_count(int* n);
+
 /* Decode GEMV, 1 <= M <= 32 tokens (replaces gen_gemv.py's gv_{plain,resid}_<fmt>_<M>_<K> kernels and the
  * LoomDecoder::Gemv call site, engine/model/loom_decoder.hpp:415-439). Same layouts and alignment rules as
  * yah_qgemm; epilogue YAH_EPI_STORE or YAH_EPI_RESID. Computes with the f32 weight values of the GGUF dequant,

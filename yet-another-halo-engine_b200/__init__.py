@@ -6,8 +6,9 @@ Modules:
   device   device memory, streams, events (the reference's LoomDevice role)
   ops      qgemm / qgemv / dequant: the reference's kernel kinds over the C ABI
   tp       tensor-parallel layer stack: shard planning, NCCL communicator, Llama-shaped linear stack
+  tune     tile-configuration search and the tile table read by yah_qgemm's automatic choice
 """
 from . import formats  # noqa: F401
 from ._lib import YahError, lib  # noqa: F401
-from . import device, ops, tp  # noqa: F401
+from . import device, ops, tp, tune  # noqa: F401
 from .device import Device, DeviceBuffer, Event, PinnedBuffer, Stream, device_count  # noqa: F401

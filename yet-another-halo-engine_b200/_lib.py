@@ -68,7 +68,16 @@ SYMBOLS = {
     "yah_tp_linear_row": (c_int, [c_vp, c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_vp,
                                   c_vp]),
     "yah_rmsnorm": (c_int, [c_vp, c_i64, c_i64, c_i64, c_f, c_f, c_vp, c_i64, c_vp]),
+    "yah_tile_rules_set": (c_int, [c_vp, c_int]),
+    "yah_tile_rules_clear": (c_int, []),
+    "yah_tile_rules_count": (c_int, [P(c_int)]),
 }
+
+
+class TileRule(ctypes.Structure):
+    """yah_tile_rule (include/yah_qgemm.h)."""
+    _fields_ = [("ggml_type", c_int), ("epilogue", c_int), ("y_dtype", c_int), ("N", c_i64), ("K", c_i64),
+                ("m_max", c_i64), ("bn", c_int), ("grid", c_int), ("cta_pair", c_int)]
 TP_ID_BYTES = 128
 
 # status codes (include/yah_qgemm.h)

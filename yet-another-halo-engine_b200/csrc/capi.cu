@@ -7,6 +7,7 @@
 #include <stdio.h>
 
 #include <mutex>
+#include <vector>
 #include <string>
 
 #include "../../include/yah_qgemm.h"
@@ -402,11 +403,64 @@ int yah_qgemm_tile(const void* w, int t, int64_t N, int64_t K, int64_t w_row_str
   return after_launch(yah::launch_qgemm_tc(a, (cudaStream_t)stream), "qgemm launch");
 }
 
+// The opt-in tile table (yah_tile_rules_set): the only mutable process-wide configuration of the library.
+std::vector<yah_tile_rule> g_rules;
+
+int yah_tile_rules_set(const yah_tile_rule* rules, int n) {
+  if (n < 0 || (n > 0 && !rules)) return fail(YAH_ERR_ARG, "bad rule list");
+  for (int i = 0; i < n; ++i) {
+    const yah_tile_rule& r = rules[i];
+    if (sb_bytes(r.ggml_type) == 0) return fail(YAH_ERR_ARG, "rule %d: unsupported type %d", i, r.ggml_type);
+    if (r.epilogue < YAH_EPI_STORE || r.epilogue > YAH_EPI_SWIGLU || (r.y_dtype != YAH_F32 && r.y_dtype != YAH_F16))
+      return fail(YAH_ERR_ARG, "rule %d: bad epilogue or output type", i);
+    if (r.N < 1 || r.K < 256 || r.m_max < 1 || r.grid < 0)
+      return fail(YAH_ERR_ARG, "rule %d: bad shape, token bound or grid", i);
+    const bool pair_ok = r.cta_pair == 1 && (r.bn == 256 || r.bn == 160 || r.bn == 128);
+    const bool single_ok = r.cta_pair == 0 && (r.bn == 192 || r.bn == 128 || r.bn == 64);
+    if (!pair_ok && !single_ok) return fail(YAH_ERR_ARG, "rule %d: bn %d is not a tile of cta_pair %d", i, r.bn, r.cta_pair);
+  }
+  std::lock_guard<std::mutex> lk(g_mu);
+  g_rules.assign(rules, rules + n);
+  return YAH_OK;
+}
+
+int yah_tile_rules_clear(void) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  g_rules.clear();
+  return YAH_OK;
+}
+
+int yah_tile_rules_count(int* n) {
+  if (!n) return fail(YAH_ERR_ARG, "null count");
+  std::lock_guard<std::mutex> lk(g_mu);
+  *n = (int)g_rules.size();
+  return YAH_OK;
+}
+
 int yah_qgemm(const void* w, int t, int64_t N, int64_t K, int64_t w_row_stride, int64_t kb_off, const void* x,
               int64_t M, int64_t ldx, void* y, int y_dtype, int64_t ldy, int epilogue, const void* aux, int64_t ldaux,
               void* stream) {
-  return yah_qgemm_tile(w, t, N, K, w_row_stride, kb_off, x, M, ldx, y, y_dtype, ldy, epilogue, aux, ldaux, 0, 0, 0,
-                        -1, stream);
+  // A tuned rule for this GEMM (the smallest token bound >= M, else the largest bound); otherwise the built-in
+  // choice: 2-SM pairs for plain stores, single CTAs with two accumulator regions when the epilogue reads an
+  // operand (its latency then overlaps the next tile's MMAs).
+  int bn = 0, grid = 0, pair = epilogue == YAH_EPI_STORE ? -1 : 0;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    const yah_tile_rule* best = nullptr;
+    for (const yah_tile_rule& r : g_rules) {
+      if (r.ggml_type != t || r.epilogue != epilogue || r.y_dtype != y_dtype || r.N != N || r.K != K) continue;
+      const bool fits = r.m_max >= M, best_fits = best && best->m_max >= M;
+      if (!best || (fits && (!best_fits || r.m_max < best->m_max)) || (!fits && !best_fits && r.m_max > best->m_max))
+        best = &r;
+    }
+    if (best) {
+      bn = best->bn;
+      grid = best->grid;
+      pair = best->cta_pair;
+    }
+  }
+  return yah_qgemm_tile(w, t, N, K, w_row_stride, kb_off, x, M, ldx, y, y_dtype, ldy, epilogue, aux, ldaux, bn, grid,
+                        0, pair, stream);
 }
 
 int yah_qgemv(const void* w, int t, int64_t N, int64_t K, int64_t w_row_stride, int64_t kb_off, const void* x,

@@ -55,6 +55,11 @@ def footprint(fmt, N, K, w_row_stride, kb_off, M, ldx, y_dtype, ldy):
 # ----------------------------------------------------------------------------------------------- raw pointers
 def qgemm_ptr(w, fmt, N, K, w_row_stride, kb_off, x, M, ldx, y, y_dtype, ldy, kind="kstore", aux=None, ldaux=0,
               stream=None, bn=0, grid=0, kchunk=0, pair=-1):
+    """yah_qgemm (automatic tile: the installed tile table, else the built-in choice) unless a tile is given."""
+    if bn == 0 and grid == 0 and kchunk == 0 and pair == -1:
+        check(lib().yah_qgemm(w, F.type_of(fmt), N, K, w_row_stride, kb_off, x, M, ldx, y, _dt(y_dtype), ldy,
+                              _epi(kind), aux, ldaux, stream))
+        return
     check(lib().yah_qgemm_tile(w, F.type_of(fmt), N, K, w_row_stride, kb_off, x, M, ldx, y, _dt(y_dtype), ldy,
                                _epi(kind), aux, ldaux, bn, grid, kchunk, pair, stream))
 
