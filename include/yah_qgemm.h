@@ -92,6 +92,12 @@ int yah_event_destroy(void* event);
 int yah_event_record(void* event, void* stream);
 int yah_event_synchronize(void* event);
 int yah_event_elapsed_ms(void* start, void* end, float* ms);
+/* CUDA graphs of library calls (decode loops are launch-bound): capture on a non-default stream (thread-local
+ * mode; make every call once before capturing it, so that its scratch is already allocated), instantiate, launch. */
+int yah_stream_begin_capture(void* stream);
+int yah_stream_end_capture(void* stream, void** graph_exec);
+int yah_graph_launch(void* graph_exec, void* stream);
+int yah_graph_destroy(void* graph_exec);
 /* Read and clear the current device's kernel status word: 0, or the code of a bounded wait that ran out
  * (1 data wait, 2 free-stage wait, 3 exit drain). A non-zero word means the output of that launch is invalid. */
 int yah_status_word(int* code);

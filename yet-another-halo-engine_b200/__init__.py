@@ -11,4 +11,4 @@ Modules:
 from . import formats  # noqa: F401
 from ._lib import YahError, lib  # noqa: F401
 from . import device, ops, tp, tune  # noqa: F401
-from .device import Device, DeviceBuffer, Event, PinnedBuffer, Stream, device_count  # noqa: F401
+from .device import Device, DeviceBuffer, Event, Graph, PinnedBuffer, Stream, device_count  # noqa: F401

@@ -43,6 +43,10 @@ SYMBOLS = {
     "yah_event_record": (c_int, [c_vp, c_vp]),
     "yah_event_synchronize": (c_int, [c_vp]),
     "yah_event_elapsed_ms": (c_int, [c_vp, c_vp, P(c_f)]),
+    "yah_stream_begin_capture": (c_int, [c_vp]),
+    "yah_stream_end_capture": (c_int, [c_vp, P(c_vp)]),
+    "yah_graph_launch": (c_int, [c_vp, c_vp]),
+    "yah_graph_destroy": (c_int, [c_vp]),
     "yah_status_word": (c_int, [P(c_int)]),
     "yah_qgemm_footprint": (c_int, [c_int, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_int, c_i64,
                                     P(c_i64), P(c_i64), P(c_i64)]),

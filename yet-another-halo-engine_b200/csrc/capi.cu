@@ -296,6 +296,36 @@ int yah_event_elapsed_ms(void* start, void* end, float* ms) {
   return YAH_OK;
 }
 
+int yah_stream_begin_capture(void* stream) {
+  if (!stream) return fail(YAH_ERR_ARG, "capture needs a non-default stream");
+  CK(cudaStreamBeginCapture((cudaStream_t)stream, cudaStreamCaptureModeThreadLocal));
+  return YAH_OK;
+}
+
+int yah_stream_end_capture(void* stream, void** graph_exec) {
+  if (!stream || !graph_exec) return fail(YAH_ERR_ARG, "null stream or graph");
+  *graph_exec = nullptr;
+  cudaGraph_t g = nullptr;
+  CK(cudaStreamEndCapture((cudaStream_t)stream, &g));
+  cudaGraphExec_t ge = nullptr;
+  const cudaError_t e = cudaGraphInstantiate(&ge, g, 0);
+  cudaGraphDestroy(g);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGraphInstantiate");
+  *graph_exec = ge;
+  return YAH_OK;
+}
+
+int yah_graph_launch(void* graph_exec, void* stream) {
+  if (!graph_exec) return fail(YAH_ERR_ARG, "null graph");
+  CK(cudaGraphLaunch((cudaGraphExec_t)graph_exec, (cudaStream_t)stream));
+  return YAH_OK;
+}
+
+int yah_graph_destroy(void* graph_exec) {
+  if (graph_exec) CK(cudaGraphExecDestroy((cudaGraphExec_t)graph_exec));
+  return YAH_OK;
+}
+
 int yah_status_word(int* code) {
   if (!code) return fail(YAH_ERR_ARG, "null code");
   DevState* s;

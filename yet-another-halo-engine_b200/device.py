@@ -139,6 +139,36 @@ class Event:
             pass
 
 
+class Graph:
+    """A CUDA graph of the library calls made on `stream` between begin() and end(); launch() replays them."""
+
+    def __init__(self, stream: "Stream"):
+        self.stream = stream
+        self.handle = None
+
+    def begin(self):
+        check(lib().yah_stream_begin_capture(self.stream.handle))
+
+    def end(self):
+        g = ctypes.c_void_p()
+        check(lib().yah_stream_end_capture(self.stream.handle, ctypes.byref(g)))
+        self.handle = g.value
+
+    def launch(self):
+        check(lib().yah_graph_launch(self.handle, self.stream.handle))
+
+    def close(self):
+        if self.handle:
+            lib().yah_graph_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 class Device:
     """One CUDA device (made current on construction)."""
 
