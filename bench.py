@@ -25,6 +25,7 @@ quants.dequantize -> f16 -> numpy matmul, engine/gpu/loom/tools/gemv_check.py:16
 from __future__ import annotations
 
 import argparse
+import importlib
 import json
 import os
 import subprocess
@@ -250,6 +251,7 @@ def run_ours(args, dist, rank, local_rank):
         "scaling": "weak", "vs_baseline": None, "dtype": "f16 x GGUF-Q4_K -> f32 acc", "data": "synthetic",
         "config": {"workload": wl["name"], "M_tokens": M, "K": K, "N": N, "weight_format": "Q4_K",
                    "out_dtype": wl["out"], "parallelism": f"replicas x{world}",
+                   "launch_overlap": bool(args.launch_overlap),
                    "l2": f"rotating {copies} input copies ({copies * per_copy / 2**20:.0f} MiB > L2)"},
         "e2e": {"value": round(e2e_val, 2), "unit": unit, "h2d_bytes_per_step": xbytes, "d2h_bytes_per_step": ybytes},
         "gpu_launches": args.steps,
@@ -472,6 +474,8 @@ def main():
     ap.add_argument("--tile-table", default=None, help="tile table (tune.py output) installed before the run")
     ap.add_argument("--tokens", type=int, default=1, help="gemv tokens (1..32)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--launch-overlap", type=int, default=1, choices=[0, 1],
+                    help="programmatic dependent launch of the GEMV (1, the library default) or plain stream order")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -483,6 +487,9 @@ def main():
             print(json.dumps(line), flush=True)
         return
     dist = dist_init(args.gpus)
+    import __graft_entry__ as ge
+    lib_mod = importlib.import_module(ge.load_package().__name__ + "._lib")
+    lib_mod.check(lib_mod.lib().yah_set_launch_overlap(args.launch_overlap))
     if args.tile_table:
         import __graft_entry__ as ge
         tune = ge.load_package().tune

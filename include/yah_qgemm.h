@@ -98,6 +98,11 @@ int yah_stream_begin_capture(void* stream);
 int yah_stream_end_capture(void* stream, void** graph_exec);
 int yah_graph_launch(void* graph_exec, void* stream);
 int yah_graph_destroy(void* graph_exec);
+/* Programmatic dependent launch of the decode GEMV (on by default). A GEMV launch may then begin while the kernel
+ * before it on the stream is finishing: it streams its weight tensor early and reads its activations, and writes
+ * its outputs, only after that kernel has completed. Contract: no kernel still in flight on the stream writes the
+ * weight tensor (weights are loaded, then only read). yah_set_launch_overlap(0) restores plain stream order. */
+int yah_set_launch_overlap(int on);
 /* Read and clear the current device's kernel status word: 0, or the code of a bounded wait that ran out
  * (1 data wait, 2 free-stage wait, 3 exit drain). A non-zero word means the output of that launch is invalid. */
 int yah_status_word(int* code);

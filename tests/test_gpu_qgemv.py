@@ -99,3 +99,47 @@ def test_qgemv_repeat_deterministic(pkg, F, dev):
     for _ in range(3):
         b = pkg.ops.qgemv(dev, w, t, x, N=N, K=K)
         assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
+@pytest.mark.parametrize("overlap", [1, 0])
+@pytest.mark.parametrize("M,K", [(1, 4096), (8, 8192)])
+def test_qgemv_dependent_chain(pkg, F, O, dev, overlap, M, K):
+    """Back-to-back launches on one stream where each GEMV reads the previous one's f16 output (a residual-free
+    layer chain) and writes the buffer the launch before it read. With programmatic launch the weights stream
+    early but activations and outputs wait for the preceding kernel; the result must equal the stepwise oracle.
+    Covers the resident-activation split (M = 1) and stream-K with activation copies held back (M = 8)."""
+    from importlib import import_module
+    L = import_module(pkg.__name__ + "._lib")
+    t = F.Q4_K
+    steps = 4
+    ws = []
+    for i in range(steps):  # d and dmin scaled by 2^-10 so the chain's activations stay near unit size
+        w = F.synth_weights(t, K, K, seed=70 + i)
+        hdr = w.reshape(K, K // 256, 144)[:, :, :4]
+        hdr[...] = (hdr.copy().view(np.float16) * np.float16(1 / 1024)).view(np.uint8)
+        ws.append(w)
+    wd = [dev.upload(w) for w in ws]
+    x0 = F.synth_activations(M, K, seed=69)
+    bufs = [dev.upload(x0), dev.empty(M * K * 2)]
+    s = pkg.Stream()
+    L.check(L.lib().yah_set_launch_overlap(overlap))
+    try:
+        for i in range(steps):
+            src, dst = bufs[i % 2], bufs[(i + 1) % 2]
+            pkg.ops.qgemv_ptr(wd[i].ptr, t, K, K, ws[i].shape[1], 0, src.ptr, M, K, dst.ptr, "f16", K,
+                              stream=s.handle)
+        s.synchronize()
+        got = bufs[steps % 2].download(np.float16, (M, K)).astype(np.float32)
+    finally:
+        L.check(L.lib().yah_set_launch_overlap(1))
+    x = x0
+    for i in range(steps):  # the oracle, step by step, rounding to f16 between steps as the device does
+        acc = O.gemm_ref(O.dequant_f32(t, ws[i], K, K), x)
+        x = acc.astype(np.float16)
+        if i < steps - 1:
+            continue
+        e = O.errors(got, acc)
+        assert e["finite"] and e["rel_fro"] <= 1e-3, e
+    for b in wd + bufs:
+        b.close()
+    s.close()

@@ -47,6 +47,7 @@ SYMBOLS = {
     "yah_stream_end_capture": (c_int, [c_vp, P(c_vp)]),
     "yah_graph_launch": (c_int, [c_vp, c_vp]),
     "yah_graph_destroy": (c_int, [c_vp]),
+    "yah_set_launch_overlap": (c_int, [c_int]),
     "yah_status_word": (c_int, [P(c_int)]),
     "yah_qgemm_footprint": (c_int, [c_int, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_int, c_i64,
                                     P(c_i64), P(c_i64), P(c_i64)]),

@@ -326,6 +326,11 @@ int yah_graph_destroy(void* graph_exec) {
   return YAH_OK;
 }
 
+int yah_set_launch_overlap(int on) {
+  yah::set_launch_overlap(on != 0);
+  return YAH_OK;
+}
+
 int yah_status_word(int* code) {
   if (!code) return fail(YAH_ERR_ARG, "null code");
   DevState* s;

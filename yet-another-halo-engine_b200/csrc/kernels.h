@@ -87,6 +87,11 @@ cudaError_t qgemv_static_setup(int device, void** base);
 cudaError_t launch_qgemv_static(const QGemvArgs& a, const GemvPlan& plan, void* base, cudaStream_t stream);
 cudaError_t qgemv_static_status(void* base, int* code, bool clear);
 
+// Programmatic dependent launch of the GEMV kernels (on by default): a launch may start while the preceding kernel
+// on its stream finishes, streaming its weights early; activations and outputs wait for that kernel to complete.
+bool launch_overlap();
+void set_launch_overlap(bool on);
+
 // Records an error for yah_last_error() and returns `code` (shared by the C ABI translation units).
 int set_error(int code, const char* fmt, ...);
 

@@ -27,6 +27,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "decode.cuh"
@@ -61,6 +62,7 @@ struct GvParams {
   int turns, ringst, ringlog;  // stage rings: stage k of a segment goes to ring k % turns (ringst = 2^ringlog)
   int wreg, xoff, sumoff, stage_bytes, stages, redoff, baroff;
   int xres, resoff, ressum;  // activations resident for the whole launch (row ranges, small M * K)
+  int xstride, sstride;      // resident layout: bytes per token of activations / of group sums
   const __half* x;
   int64_t ldx;
   int K;
@@ -92,10 +94,10 @@ __device__ __forceinline__ uint2 lds64(uint32_t addr) {
   return v;
 }
 
+// A pure register operation: plain asm, so the compiler may schedule it among the shared-memory loads.
 __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                          uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
       "{%0, %1, %2, %3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
@@ -121,24 +123,59 @@ __device__ __forceinline__ float magic_byte(uint32_t word, int byte) {
   return __uint_as_float(prmt(word, 0x4B000000u, (uint32_t)byte | 0x7650u));
 }
 
+// Where a super-block's activations and Q4_K group sums sit, seen from one lane (g = lane / 4, c = lane % 4).
+// x(n, j, cb): byte cb of this lane's part of 64-K chunk j, token tile n; the lane part is 16c (Q4_K, pieces c and
+// c + 4 = bytes 0 / 64) or 8c (Q6_K, Q8_0). shi / slo: the lane's two hi / lo group sums (groups 2c, 2c + 1).
+// Token rows past M read token M - 1: they only feed D columns that are never stored.
+//
+// XStage: a stage written by TMA (row = chunk * xrows + token, 128-byte swizzle; sums [hi, lo][xrows][8] f16).
+template <int NTW>
+struct XStage {
+  uint32_t xs, sums;
+  int xrows, c0, lane_b, lane_s;
+  int tok[NTW];
+  __device__ __forceinline__ uint32_t x(int n, int j, int cb) const {
+    const int row = (c0 + j) * xrows + tok[n], byte = cb + lane_b;
+    return xs + row * 128 + ((((byte >> 4) ^ row) & 7) << 4) + (byte & 15);
+  }
+  __device__ __forceinline__ uint32_t shi(int n) const { return sums + tok[n] * 16 + lane_s; }
+  __device__ __forceinline__ uint32_t slo(int n) const { return sums + (xrows + tok[n]) * 16 + lane_s; }
+};
+
+// XRes: resident activations in the launch-wide layout (token row t at t * xstride, chunk ch at ch * 128, no
+// swizzle: xstride = 2K + 64 puts consecutive tokens in opposite bank halves; sums [token][super-block][hi 8, lo 8]).
+// xu / su already hold this lane's offsets and this super-block's position, so every access is register + constant.
+template <int NTW>
+struct XRes {
+  uint32_t xu[NTW], su[NTW];
+  __device__ __forceinline__ uint32_t x(int n, int j, int cb) const { return xu[n] + j * 128 + cb; }
+  __device__ __forceinline__ uint32_t shi(int n) const { return su[n]; }
+  __device__ __forceinline__ uint32_t slo(int n) const { return su[n] + 16; }
+};
+
 // ------------------------------------------------------------------------------------------------ one super-block
-// A warp's 16 weight rows x one 256-K super-block, accumulated into y (rows g / g + 8, tokens tok0 + 8n + 2c + e).
-// w0 / w1: shared addresses of the super-block in rows g and g + 8; xs: the stage's activations (xrows token
-// rows per 64-K chunk, this super-block's first chunk c0); sums: this super-block's Q4_K group sums
-// ([hi, lo][xrows tokens][8] f16). Tokens >= M are zero and are not read.
-template <int T, int NTW>
-__device__ __forceinline__ void gv_superblock(uint32_t w0, uint32_t w1, uint32_t xs, int xrows, int c0, int tok0,
-                                              int M, uint32_t sums, float (&y)[NTW][4], int g, int c) {
-  bool tok[NTW];
-#pragma unroll
-  for (int n = 0; n < NTW; ++n) tok[n] = tok0 + 8 * n + g < M;
+// A warp's 16 weight rows x one 256-K super-block, accumulated into y (rows g / g + 8, tokens 8n + 2c + e of the
+// warp's token tiles). w0 / w1: shared addresses of the super-block in rows g and g + 8; xa: its activations.
+// The loads of a super-block are issued before its arithmetic (all of them for one token tile).
+template <int T, int NTW, class XA>
+__device__ __forceinline__ void gv_superblock(uint32_t w0, uint32_t w1, const XA& xa, float (&y)[NTW][4], int c) {
   if (T == 12) {
     const uint4 h0 = lds128(w0), h1 = lds128(w1);
+    uint2 q0[4], q1[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) q0[j] = lds64(w0 + 16 + 32 * j + 8 * c), q1[j] = lds64(w1 + 16 + 32 * j + 8 * c);
+    constexpr int PJ = NTW == 1 ? 4 : 1;  // 64-K chunks of activations loaded ahead
+    uint4 xl[PJ][NTW], xh[PJ][NTW];
+    uint32_t bh[NTW], bl[NTW];
+    if (NTW == 1) {
+#pragma unroll
+      for (int j = 0; j < PJ; ++j) xl[j][0] = lds128(xa.x(0, j, 0)), xh[j][0] = lds128(xa.x(0, j, 64));
+      bh[0] = lds32(xa.shi(0));
+      bl[0] = lds32(xa.slo(0));
+    }
     // 6-bit scales of groups 0-3 / 4-7 and mins of groups 0-3 / 4-7, one per byte
     const uint32_t sc0a = h0.y & 0x3F3F3F3Fu, sc0b = (h0.w & 0x0F0F0F0Fu) | ((h0.y >> 2) & 0x30303030u);
     const uint32_t sc1a = h1.y & 0x3F3F3F3Fu, sc1b = (h1.w & 0x0F0F0F0Fu) | ((h1.y >> 2) & 0x30303030u);
-    const uint32_t m0a = h0.z & 0x3F3F3F3Fu, m0b = ((h0.w >> 4) & 0x0F0F0F0Fu) | ((h0.z >> 2) & 0x30303030u);
-    const uint32_t m1a = h1.z & 0x3F3F3F3Fu, m1b = ((h1.w >> 4) & 0x0F0F0F0Fu) | ((h1.z >> 2) & 0x30303030u);
     // Low nibble q masked in place reads as q * 2^-24, high nibble as q * 2^-20 (exact f16 subnormals). The group
     // factor F = (2^23 + sc) * D - 2^23 * D = sc * D (one rounding) with D = d * 2^24 or d * 2^20 undoes that.
     const float d0 = h2f_bits(h0.x & 0xFFFFu), d1 = h2f_bits(h1.x & 0xFFFFu);
@@ -146,9 +183,13 @@ __device__ __forceinline__ void gv_superblock(uint32_t w0, uint32_t w1, uint32_t
     const float bl0 = dl0 * -8388608.0f, bh0 = dh0 * -8388608.0f, bl1 = dl1 * -8388608.0f, bh1 = dh1 * -8388608.0f;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
+      const int jx = NTW == 1 ? j : 0;
+      if (NTW > 1) {
+#pragma unroll
+        for (int n = 0; n < NTW; ++n) xl[0][n] = lds128(xa.x(n, j, 0)), xh[0][n] = lds128(xa.x(n, j, 64));
+      }
       // lane bytes 8c .. 8c + 7 of the 64-K block: low nibbles at positions 8c + (0..7) (group 2j), high nibbles
       // at 32 + 8c + (0..7) (group 2j + 1)
-      const uint2 q0 = lds64(w0 + 16 + 32 * j + 8 * c), q1 = lds64(w1 + 16 + 32 * j + 8 * c);
       const uint32_t s0 = j < 2 ? sc0a : sc0b, s1 = j < 2 ? sc1a : sc1b;
       const float fl0 = __fmaf_rn(magic_byte(s0, (2 * j) & 3), dl0, bl0);
       const float fh0 = __fmaf_rn(magic_byte(s0, (2 * j + 1) & 3), dh0, bh0);
@@ -158,7 +199,7 @@ __device__ __forceinline__ void gv_superblock(uint32_t w0, uint32_t w1, uint32_t
       uint32_t lo[2][4], hi[2][4];
 #pragma unroll
       for (int wi = 0; wi < 2; ++wi) {
-        const uint32_t u0 = wi ? q0.y : q0.x, u1 = wi ? q1.y : q1.x;
+        const uint32_t u0 = wi ? q0[j].y : q0[j].x, u1 = wi ? q1[j].y : q1[j].x;
         const uint32_t v0 = shr8_fma(u0), v1 = shr8_fma(u1);
         lo[wi][0] = u0 & 0x000F000Fu, lo[wi][1] = u1 & 0x000F000Fu, lo[wi][2] = v0 & 0x000F000Fu,
         lo[wi][3] = v1 & 0x000F000Fu;
@@ -168,15 +209,12 @@ __device__ __forceinline__ void gv_superblock(uint32_t w0, uint32_t w1, uint32_t
 #pragma unroll
       for (int n = 0; n < NTW; ++n) {
         // permuted activations: 16-byte piece c = units 2c, 2c + 1 (low nibbles), piece 4 + c (high nibbles)
-        const int row = (c0 + j) * xrows + tok0 + 8 * n + g;
-        const uint32_t al = xpiece(xs, row, c);  // piece 4 + c: the same row, 16-byte index bit 2 flipped
-        const uint4 xl = tok[n] ? lds128(al) : make_uint4(0u, 0u, 0u, 0u);
-        const uint4 xh = tok[n] ? lds128(al ^ 64u) : make_uint4(0u, 0u, 0u, 0u);
+        const uint4 a = xl[jx][NTW == 1 ? 0 : n], b = xh[jx][NTW == 1 ? 0 : n];
         float alo[4] = {0.f, 0.f, 0.f, 0.f}, ahi[4] = {0.f, 0.f, 0.f, 0.f};
-        mma16816(alo, lo[0][0], lo[0][1], lo[0][2], lo[0][3], xl.x, xl.y);
-        mma16816(ahi, hi[0][0], hi[0][1], hi[0][2], hi[0][3], xh.x, xh.y);
-        mma16816(alo, lo[1][0], lo[1][1], lo[1][2], lo[1][3], xl.z, xl.w);
-        mma16816(ahi, hi[1][0], hi[1][1], hi[1][2], hi[1][3], xh.z, xh.w);
+        mma16816(alo, lo[0][0], lo[0][1], lo[0][2], lo[0][3], a.x, a.y);
+        mma16816(ahi, hi[0][0], hi[0][1], hi[0][2], hi[0][3], b.x, b.y);
+        mma16816(alo, lo[1][0], lo[1][1], lo[1][2], lo[1][3], a.z, a.w);
+        mma16816(ahi, hi[1][0], hi[1][1], hi[1][2], hi[1][3], b.z, b.w);
         y[n][0] = __fmaf_rn(fh0, ahi[0], __fmaf_rn(fl0, alo[0], y[n][0]));
         y[n][1] = __fmaf_rn(fh0, ahi[1], __fmaf_rn(fl0, alo[1], y[n][1]));
         y[n][2] = __fmaf_rn(fh1, ahi[2], __fmaf_rn(fl1, alo[2], y[n][2]));
@@ -184,6 +222,8 @@ __device__ __forceinline__ void gv_superblock(uint32_t w0, uint32_t w1, uint32_t
       }
     }
     // - dmin * sum_g m_g X_g: A row g / g + 8 = mins of groups 2c, 2c + 1 (repeated at k + 8), B = X hi / lo
+    const uint32_t m0a = h0.z & 0x3F3F3F3Fu, m0b = ((h0.w >> 4) & 0x0F0F0F0Fu) | ((h0.z >> 2) & 0x30303030u);
+    const uint32_t m1a = h1.z & 0x3F3F3F3Fu, m1b = ((h1.w >> 4) & 0x0F0F0F0Fu) | ((h1.z >> 2) & 0x30303030u);
     const int mb = (2 * c) & 3;
     const uint32_t msel = (uint32_t)mb | 0x40u | ((uint32_t)(mb + 1) << 8) | 0x4000u;
     const uint32_t am0 = hsub2_u32(prmt(c < 2 ? m0a : m0b, 0x64646464u, msel), 0x64006400u);
@@ -191,11 +231,9 @@ __device__ __forceinline__ void gv_superblock(uint32_t w0, uint32_t w1, uint32_t
     const float n0 = -h2f_bits(h0.x >> 16), n1 = -h2f_bits(h1.x >> 16);
 #pragma unroll
     for (int n = 0; n < NTW; ++n) {
-      const int tau = tok0 + 8 * n + g;
-      const uint32_t bh = tok[n] ? lds32(sums + (tau * 8 + 2 * c) * 2) : 0u;
-      const uint32_t bl = tok[n] ? lds32(sums + (xrows * 8 + tau * 8 + 2 * c) * 2) : 0u;
+      if (NTW > 1) bh[n] = lds32(xa.shi(n)), bl[n] = lds32(xa.slo(n));
       float acc2[4] = {0.f, 0.f, 0.f, 0.f};
-      mma16816(acc2, am0, am1, am0, am1, bh, bl);
+      mma16816(acc2, am0, am1, am0, am1, bh[n], bl[n]);
       y[n][0] = __fmaf_rn(n0, acc2[0], y[n][0]);
       y[n][1] = __fmaf_rn(n0, acc2[1], y[n][1]);
       y[n][2] = __fmaf_rn(n1, acc2[2], y[n][2]);
@@ -203,7 +241,7 @@ __device__ __forceinline__ void gv_superblock(uint32_t w0, uint32_t w1, uint32_t
     }
   } else if (T == 14) {
     // ql[128], qh[64], int8 scales[16], d; x in natural order: unit 4u + c of a 64-K chunk = 16-byte piece
-    // 2u + (c >> 1), half c & 1
+    // 2u + (c >> 1), half c & 1 (byte 32u + 8c)
     const float dd0 = h2f_bits(lds_u16(w0 + 208)), dd1 = h2f_bits(lds_u16(w1 + 208));
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -226,8 +264,7 @@ __device__ __forceinline__ void gv_superblock(uint32_t w0, uint32_t w1, uint32_t
         const float f1 = dd1 * (float)(int)(int8_t)((scw1 >> (8 * u)) & 0xFFu);
 #pragma unroll
         for (int n = 0; n < NTW; ++n) {
-          const int row = (c0 + j) * xrows + tok0 + 8 * n + g;
-          const uint2 b = tok[n] ? lds64(xpiece(xs, row, 2 * u + (c >> 1)) + 8 * (c & 1)) : make_uint2(0u, 0u);
+          const uint2 b = lds64(xa.x(n, j, 32 * u));
           float t4[4] = {0.f, 0.f, 0.f, 0.f};
           mma16816(t4, a0, a1, a2, a3, b.x, b.y);
           y[n][0] = __fmaf_rn(f0, t4[0], y[n][0]);
@@ -237,7 +274,7 @@ __device__ __forceinline__ void gv_superblock(uint32_t w0, uint32_t w1, uint32_t
         }
       }
     }
-  } else {  // Q8_0: eight 34-byte blocks (d f16, 32 int8); unit 8(bk & 1) + 4hb + c of chunk bk >> 1
+  } else {  // Q8_0: eight 34-byte blocks (d f16, 32 int8); unit 8(bk & 1) + 4hb + c of chunk bk >> 1 (byte 8 * unit)
 #pragma unroll
     for (int bk = 0; bk < 8; ++bk) {
       const float d0 = h2f_bits(lds_u16(w0 + 34 * bk)), d1 = h2f_bits(lds_u16(w1 + 34 * bk));
@@ -255,9 +292,7 @@ __device__ __forceinline__ void gv_superblock(uint32_t w0, uint32_t w1, uint32_t
         const uint32_t a3 = hsub2_u32(prmt(q1, 0x64646464u, 0x4342u), kB);
 #pragma unroll
         for (int n = 0; n < NTW; ++n) {
-          const int row = (c0 + (bk >> 1)) * xrows + tok0 + 8 * n + g;
-          const int v = 8 * (bk & 1) + 4 * hb + c;
-          const uint2 b = tok[n] ? lds64(xpiece(xs, row, v >> 1) + 8 * (v & 1)) : make_uint2(0u, 0u);
+          const uint2 b = lds64(xa.x(n, bk >> 1, 64 * (bk & 1) + 32 * hb));
           mma16816(t4[n], a0, a1, a2, a3, b.x, b.y);
         }
       }
@@ -271,7 +306,6 @@ __device__ __forceinline__ void gv_superblock(uint32_t w0, uint32_t w1, uint32_t
     }
   }
 }
-
 // ------------------------------------------------------------------------------------------------ Q4_K helper
 __device__ __forceinline__ void gv_store_sum(uint32_t ss, int M, int t, int grp, float v) {
   const __half hv = __float2half_rn(v);
@@ -308,17 +342,14 @@ __device__ __forceinline__ void gv_prep_q4k(uint32_t xs, int slots, int M, uint3
     for (int s = 0; s < slots; ++s) {
       const uint32_t ss = sums + s * 32 * M;
       for (int nt = 0; nt < ntiles; ++nt) {
-        const int tau = 8 * nt + g;
+        const int tau = 8 * nt + g < M ? 8 * nt + g : M - 1;  // columns past M are never stored
         float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int ch = 0; ch < 16; ch += 2) {
           const uint32_t a = (g == (ch >> 1)) ? 0x3C003C00u : 0u;
-          uint2 b0 = make_uint2(0u, 0u), b1 = make_uint2(0u, 0u);
-          if (tau < M) {
-            const int v0 = 4 * (ch & 3) + c, v1 = 4 * ((ch + 1) & 3) + c;
-            b0 = lds64(xpiece(xs, (4 * s + (ch >> 2)) * M + tau, v0 >> 1) + 8 * (v0 & 1));
-            b1 = lds64(xpiece(xs, (4 * s + ((ch + 1) >> 2)) * M + tau, v1 >> 1) + 8 * (v1 & 1));
-          }
+          const int v0 = 4 * (ch & 3) + c, v1 = 4 * ((ch + 1) & 3) + c;
+          const uint2 b0 = lds64(xpiece(xs, (4 * s + (ch >> 2)) * M + tau, v0 >> 1) + 8 * (v0 & 1));
+          const uint2 b1 = lds64(xpiece(xs, (4 * s + ((ch + 1) >> 2)) * M + tau, v1 >> 1) + 8 * (v1 & 1));
           mma16816(d0, a, 0u, a, 0u, b0.x, b0.y);
           mma16816(d1, a, 0u, a, 0u, b1.x, b1.y);
         }
@@ -559,8 +590,8 @@ __device__ __forceinline__ bool gv_flush_rows(const GvParams& p, float (&y)[NTW]
 }
 
 // Resident activations (row ranges with small M * K): the compute warps copy all of x into shared memory once,
-// in the stage layout (row = 64-K chunk * M + token, swizzled), Q4_K already permuted, with the Q4_K group sums
-// ([super-block][hi, lo][token][8] f16). A thread takes one 16-byte piece (8 values); four consecutive pieces
+// token t at t * xstride (Q4_K already permuted), with the Q4_K group sums at ressum + t * sstride
+// ([super-block][hi 8, lo 8] f16). A thread takes one 16-byte piece (8 values); four consecutive pieces
 // are one group, added in f32 by two shuffles.
 template <int T>
 __device__ __forceinline__ void gv_prep_resident(const GvParams& p, uint32_t res, uint32_t ressum, int tid,
@@ -588,14 +619,17 @@ __device__ __forceinline__ void gv_prep_resident(const GvParams& p, uint32_t res
       float sum = ((a.x + a.y) + (b.x + b.y)) + ((e.x + e.y) + (f.x + f.y));
       sum += __shfl_xor_sync(0xffffffffu, sum, 1);
       sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-      if ((kp & 3) == 0) {
-        const int group = kp >> 2;
-        gv_store_sum(ressum + (group >> 3) * 32 * p.M, p.M, t, group & 7, sum);
+      if ((kp & 3) == 0) {  // group kp / 4 = super-block kp / 32, group (kp / 4) % 8: hi at + 0, lo at + 16
+        const uint32_t ss = ressum + t * p.sstride + (kp >> 5) * 32 + ((kp >> 2) & 7) * 2;
+        const __half hv = __float2half_rn(sum);
+        const __half lv = __float2half_rn(sum - __half2float(hv));
+        asm volatile("st.shared.b16 [%0], %1;" ::"r"(ss), "h"(__half_as_ushort(hv)) : "memory");
+        asm volatile("st.shared.b16 [%0], %1;" ::"r"(ss + 16), "h"(__half_as_ushort(lv)) : "memory");
       }
       v = make_uint4(prmt(v.x, v.y, 0x5410u), prmt(v.x, v.y, 0x7632u), prmt(v.z, v.w, 0x5410u),
                      prmt(v.z, v.w, 0x7632u));
     }
-    const uint32_t a = xpiece(res, (kp >> 3) * p.M + t, kp & 7);
+    const uint32_t a = res + t * p.xstride + kp * 16;
     asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
                  : "memory");
     }
@@ -627,6 +661,7 @@ __global__ void __launch_bounds__(GvRoles<T, CW>::kThreads, (CW == 8 && NTW == 1
     mbar_init(rfull, CW * 32);
     mbar_init(rdone, p.rgp * p.tsplit * 32);
     fence_barrier_init();
+    griddep_launch_dependents();
   }
   __syncthreads();
 
@@ -638,6 +673,11 @@ __global__ void __launch_bounds__(GvRoles<T, CW>::kThreads, (CW == 8 && NTW == 1
     const uint32_t bytes = (uint32_t)(p.ops * p.rb * p.opw + (p.xres ? 0 : 4 * p.sst * p.M * 128));
     int cnt[8] = {0, 0, 0, 0, 0, 0, 0, 0};  // stages issued per ring
     const int mask = p.ringst - 1;
+    // Under a programmatic launch the weights (which no kernel in flight writes) start streaming while the
+    // preceding kernel finishes; the activation copies of the first pass over the rings are held back until it
+    // has completed (griddepcontrol.wait), and issued before any stage is reused.
+    bool dep = p.xres != 0;  // resident activations: the producer copies none
+    int npend = 0, pend_st[kGvMaxStages], pend_k[kGvMaxStages];
     bool ok = true;
     for (int si = 0; si < W.nseg && ok; ++si) {
       const GvSeg sg = gv_seg<RANGES>(p, W, si);
@@ -647,6 +687,12 @@ __global__ void __launch_bounds__(GvRoles<T, CW>::kThreads, (CW == 8 && NTW == 1
       const int q = cnt[r]++;
       const int st = r * p.ringst + (q & mask), ph = (q >> p.ringlog) & 1;
       if (++r == p.turns) r = 0;
+      if (!dep && q >= p.ringst) {
+        griddep_wait();
+        dep = true;
+        for (int i = 0; i < npend; ++i)
+          tma_load_3d(smem + pend_st[i] * p.stage_bytes + p.xoff, &tmap_x, &full[pend_st[i]], 0, 0, pend_k[i]);
+      }
       if (!mbar_wait(&empty[st], ph ^ 1, p.status, kStatusTimeoutEmpty)) { ok = false; break; }
       uint8_t* base = smem + st * p.stage_bytes;
       mbar_arrive_expect_tx(&full[st], bytes);
@@ -655,8 +701,20 @@ __global__ void __launch_bounds__(GvRoles<T, CW>::kThreads, (CW == 8 && NTW == 1
         const int xw = T == 14 ? (int)(((sbg * 210) & ~int64_t(15)) >> 1) : (int)(sbg * (gv_sb_bytes(T) / 8));
         tma_load_2d(base + op * p.wreg, &tmap_w, &full[st], xw, (int)row0);
       }
-      if (!p.xres) tma_load_3d(base + p.xoff, &tmap_x, &full[st], 0, 0, 4 * sb0);
+      if (!p.xres) {
+        if (dep) {
+          tma_load_3d(base + p.xoff, &tmap_x, &full[st], 0, 0, 4 * sb0);
+        } else {
+          pend_st[npend] = st;
+          pend_k[npend++] = 4 * sb0;
+        }
       }
+      }
+    }
+    if (!dep) {
+      griddep_wait();
+      for (int i = 0; i < npend; ++i)
+        tma_load_3d(smem + pend_st[i] * p.stage_bytes + p.xoff, &tmap_x, &full[pend_st[i]], 0, 0, pend_k[i]);
     }
     for (int r = 0; r < p.turns; ++r)
       for (int q = (cnt[r] > p.ringst ? cnt[r] - p.ringst : 0); q < cnt[r]; ++q)
@@ -699,9 +757,21 @@ __global__ void __launch_bounds__(GvRoles<T, CW>::kThreads, (CW == 8 && NTW == 1
   const bool has_rows = rgi * 16 < p.rb;
   float* red = reinterpret_cast<float*>(smem + p.redoff);
   const uint32_t res = smem_u32(smem + p.resoff), ressum = smem_u32(smem + p.ressum);
+  griddep_wait();  // activations are read, and outputs written, only after the preceding kernel has completed
   if (p.xres) {
     gv_prep_resident<T>(p, res, ressum, threadIdx.x, CW * 32);
     named_bar(1, CW * 32);
+  }
+  // This lane's activation rows (token rows past M read token M - 1; those D columns are never stored) and its
+  // offsets in the resident layout.
+  const int lane_b = (T == 12 ? 16 : 8) * c;
+  int tokl[NTW];
+  uint32_t xlane[NTW], slane[NTW];
+#pragma unroll
+  for (int n = 0; n < NTW; ++n) {
+    tokl[n] = tok0 + 8 * n + g < p.M ? tok0 + 8 * n + g : p.M - 1;
+    xlane[n] = res + tokl[n] * p.xstride + lane_b;
+    slane[n] = ressum + tokl[n] * p.sstride + 4 * c;
   }
   float y[NTW][4];
 #pragma unroll
@@ -723,12 +793,23 @@ __global__ void __launch_bounds__(GvRoles<T, CW>::kThreads, (CW == 8 && NTW == 1
         uint32_t off = (uint32_t)(within * gv_sb_bytes(T));
         if (T == 14) off = (uint32_t)((((int64_t)p.kb_off + sb0 + op * p.P) * 210) & 15) + within * 210;
         const uint32_t w0 = base + op * p.wreg + (rgi * 16 + g) * p.opw + off;
-        if (p.xres)
-          gv_superblock<T, NTW>(w0, w0 + 8 * p.opw, res, p.M, 4 * (sb0 + pos), tok0, p.M,
-                                ressum + (sb0 + pos) * 32 * p.M, y, g, c);
-        else
-          gv_superblock<T, NTW>(w0, w0 + 8 * p.opw, base + p.xoff, p.M, 4 * pos, tok0, p.M,
-                                base + p.sumoff + pos * 32 * p.M, y, g, c);
+        if (p.xres) {
+          XRes<NTW> xa;
+#pragma unroll
+          for (int n = 0; n < NTW; ++n) xa.xu[n] = xlane[n] + (sb0 + pos) * 512, xa.su[n] = slane[n] + (sb0 + pos) * 32;
+          gv_superblock<T, NTW>(w0, w0 + 8 * p.opw, xa, y, c);
+        } else {
+          XStage<NTW> xa;
+          xa.xs = base + p.xoff;
+          xa.sums = base + p.sumoff + pos * 32 * p.M;
+          xa.xrows = p.M;
+          xa.c0 = 4 * pos;
+          xa.lane_b = lane_b;
+          xa.lane_s = 4 * c;
+#pragma unroll
+          for (int n = 0; n < NTW; ++n) xa.tok[n] = tokl[n];
+          gv_superblock<T, NTW>(w0, w0 + 8 * p.opw, xa, y, c);
+        }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[st]);
@@ -838,11 +919,22 @@ cudaError_t gv_launch(const QGemvArgs& a, const GemvPlan& pl, float* ws, int* co
   p.ws = ws;
   p.counters = counters;
   p.status = a.status;
+  p.xstride = (int)(a.K * 2 + 64);
+  p.sstride = (int)((a.K / 256) * 32 + 16);
   auto kern = qgemv_kernel<T, NTW, CW, RANGES>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, pl.smem);
   if (e != cudaSuccess) return e;
-  kern<<<pl.grid, GvRoles<T, CW>::kThreads, pl.smem, stream>>>(mw, mx, p);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(pl.grid);
+  cfg.blockDim = dim3(GvRoles<T, CW>::kThreads);
+  cfg.dynamicSmemBytes = pl.smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = launch_overlap() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, mw, mx, p);
 }
 
 template <int T>
@@ -859,6 +951,12 @@ cudaError_t gv_fmt(const QGemvArgs& a, const GemvPlan& pl, float* ws, int* count
 }
 
 }  // namespace
+
+namespace {
+std::atomic<int> g_launch_overlap{1};
+}  // namespace
+bool launch_overlap() { return g_launch_overlap.load(std::memory_order_relaxed) != 0; }
+void set_launch_overlap(bool on) { g_launch_overlap.store(on ? 1 : 0, std::memory_order_relaxed); }
 
 GemvPlan qgemv_plan(int type, int64_t N, int64_t K, int64_t M, int num_sms) {
   GemvPlan pl{};
@@ -892,8 +990,9 @@ GemvPlan qgemv_plan(int type, int64_t N, int64_t K, int64_t M, int num_sms) {
   const int red_bytes = (ranges && pl.slots > 1) ? pl.cw * 32 * pl.ntw * 4 * 4 : 0;
   const int bar_bytes = (3 * kGvMaxStages + 2) * 8;
   const bool two_per_sm = !ranges && pl.ntw == 1;
-  const int res_bytes = pl.xres ? (int)((M * K * 2 + 1023) / 1024 * 1024) : 0;
-  const int ressum_bytes = pl.xres && type == 12 ? (int)(((K / 256) * 32 * M + 1023) / 1024 * 1024) : 0;
+  // resident layout: M token rows of 2K + 64 bytes, M rows of group sums of 32 bytes per super-block + 16
+  const int res_bytes = pl.xres ? (int)((M * (K * 2 + 64) + 1023) / 1024 * 1024) : 0;
+  const int ressum_bytes = pl.xres && type == 12 ? (int)((M * ((K / 256) * 32 + 16) + 1023) / 1024 * 1024) : 0;
   const int budget = (two_per_sm ? 104 * 1024 : kGvSmemBudget) - red_bytes - bar_bytes - res_bytes - ressum_bytes;
   // Stages of ~8 KB of weights, so every CTA's first data arrives early; the warps of one super-block turn
   // (slots / sst turns) consume a ring of their own, of a power-of-two number of stages >= 2.
