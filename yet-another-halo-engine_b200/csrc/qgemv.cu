@@ -39,15 +39,22 @@ namespace {
 
 constexpr int kGvBlock = 128;    // stream-K row block
 constexpr int kGvMaxStages = 16;
-constexpr int kGvSmemBudget = 210 * 1024;
+constexpr int kGvSmemBudget = 225 * 1024;
 
 // Bytes per super-block and the most super-blocks one TMA copy of a row holds (box width <= 256 elements:
 // u64 elements for Q4_K / Q8_0, u16 for Q6_K, whose super-blocks are not 8-byte aligned).
 __host__ __device__ constexpr int gv_sb_bytes(int t) { return t == 8 ? 272 : t == 12 ? 144 : 210; }
 __host__ __device__ constexpr int gv_pmax(int t) { return t == 8 ? 4 : t == 12 ? 8 : 2; }
-// Shared-memory row width of one W copy of P super-blocks (Q6_K: a 16-byte aligned window around them).
+// Shared-memory row width of one W copy of P super-blocks (Q6_K: a 16-byte aligned window around them), padded to
+// an odd number of 16-byte units. TMA lays the copied rows out at this pitch; row g starts in 16-byte bank slot
+// (g * units) mod 8, so gcd(units, 8) of the 8 rows a warp's lane groups read (g = 0..7) share a slot: none for an odd
+// count, all 8 for 1152 bytes = 72 units (measured: half of all shared-load wavefronts were conflicts). The extra bytes
+// are the start of the next super-block, or zero fill past the end of the row.
+__host__ __device__ constexpr int gv_opw_raw(int t, int P) {
+  return t == 14 ? ((P * 210 + 14 + 15) / 16) * 16 : ((P * gv_sb_bytes(t) + 15) / 16) * 16;
+}
 __host__ __device__ constexpr int gv_opw(int t, int P) {
-  return t == 14 ? ((P * 210 + 14 + 15) / 16) * 16 : P * gv_sb_bytes(t);
+  return (gv_opw_raw(t, P) / 16) % 2 ? gv_opw_raw(t, P) : gv_opw_raw(t, P) + 16;
 }
 
 template <int T, int CW>
@@ -59,7 +66,7 @@ struct GvParams {
   int N, M, kb_off, nsb;
   int mode;                  // 0 row ranges, 1 stream-K
   int rb, rgp, slots, tsplit, sst, P, ops, opw;  // sst: super-blocks per stage (a divisor of slots)
-  int turns, ringst, ringlog;  // stage rings: stage k of a segment goes to ring k % turns (ringst = 2^ringlog)
+  int turns, ringst;         // stage rings: stage k of a segment goes to ring k % turns, ringst stages each
   int wreg, xoff, sumoff, stage_bytes, stages, redoff, baroff;
   int xres, resoff, ressum;  // activations resident for the whole launch (row ranges, small M * K)
   int xstride, sstride;      // resident layout: bytes per token of activations / of group sums
@@ -672,7 +679,6 @@ __global__ void __launch_bounds__(GvRoles<T, CW>::kThreads, (CW == 8 && NTW == 1
     tma_prefetch_desc(&tmap_x);
     const uint32_t bytes = (uint32_t)(p.ops * p.rb * p.opw + (p.xres ? 0 : 4 * p.sst * p.M * 128));
     int cnt[8] = {0, 0, 0, 0, 0, 0, 0, 0};  // stages issued per ring
-    const int mask = p.ringst - 1;
     // Under a programmatic launch the weights (which no kernel in flight writes) start streaming while the
     // preceding kernel finishes; the activation copies of the first pass over the rings are held back until it
     // has completed (griddepcontrol.wait), and issued before any stage is reused.
@@ -685,7 +691,7 @@ __global__ void __launch_bounds__(GvRoles<T, CW>::kThreads, (CW == 8 && NTW == 1
       int r = 0;
       for (int sb0 = sg.sb_begin; sb0 < sg.sb_end; sb0 += p.sst) {
       const int q = cnt[r]++;
-      const int st = r * p.ringst + (q & mask), ph = (q >> p.ringlog) & 1;
+      const int st = r * p.ringst + q % p.ringst, ph = (q / p.ringst) & 1;
       if (++r == p.turns) r = 0;
       if (!dep && q >= p.ringst) {
         griddep_wait();
@@ -718,7 +724,7 @@ __global__ void __launch_bounds__(GvRoles<T, CW>::kThreads, (CW == 8 && NTW == 1
     }
     for (int r = 0; r < p.turns; ++r)
       for (int q = (cnt[r] > p.ringst ? cnt[r] - p.ringst : 0); q < cnt[r]; ++q)
-        mbar_wait(&full[r * p.ringst + (q & mask)], (q >> p.ringlog) & 1, p.status, kStatusTimeoutDrain, false);
+        mbar_wait(&full[r * p.ringst + q % p.ringst], (q / p.ringst) & 1, p.status, kStatusTimeoutDrain, false);
     return;
   }
 
@@ -726,14 +732,13 @@ __global__ void __launch_bounds__(GvRoles<T, CW>::kThreads, (CW == 8 && NTW == 1
     // ---------------------------------------------------------------- Q4_K activation prep
     if (p.xres) return;
     int cnt[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    const int mask = p.ringst - 1;
     bool ok = true;
     for (int si = 0; si < W.nseg && ok; ++si) {
       const GvSeg sg = gv_seg<RANGES>(p, W, si);
       int r = 0;
       for (int sb0 = sg.sb_begin; sb0 < sg.sb_end; sb0 += p.sst) {
       const int q = cnt[r]++;
-      const int st = r * p.ringst + (q & mask), ph = (q >> p.ringlog) & 1;
+      const int st = r * p.ringst + q % p.ringst, ph = (q / p.ringst) & 1;
       if (++r == p.turns) r = 0;
       if (!mbar_wait(&full[st], ph, p.status, kStatusTimeoutFull)) { ok = false; break; }
       const uint32_t base = smem_u32(smem + st * p.stage_bytes);
@@ -776,13 +781,13 @@ __global__ void __launch_bounds__(GvRoles<T, CW>::kThreads, (CW == 8 && NTW == 1
   float y[NTW][4];
 #pragma unroll
   for (int n = 0; n < NTW; ++n) y[n][0] = y[n][1] = y[n][2] = y[n][3] = 0.f;
-  int lc = 0;  // this warp's ring: stages consumed so far
+  int lslot = 0, lph = 0;  // this warp's ring: next stage slot and its phase parity
   for (int si = 0; si < W.nseg; ++si) {
     const GvSeg sg = gv_seg<RANGES>(p, W, si);
     bool ok = true;
     for (int sb0 = sg.sb_begin + turn * p.sst; sb0 < sg.sb_end; sb0 += p.slots) {
-      const int st = turn * p.ringst + (lc & (p.ringst - 1)), ph = (lc >> p.ringlog) & 1;
-      ++lc;
+      const int st = turn * p.ringst + lslot, ph = lph;
+      if (++lslot == p.ringst) lslot = 0, lph ^= 1;
       if (!mbar_wait(&full[st], ph, p.status, kStatusTimeoutFull) ||
           (T == 12 && !p.xres && !mbar_wait(&sready[st], ph, p.status, kStatusTimeoutFull))) {
         ok = false;
@@ -889,8 +894,6 @@ cudaError_t gv_launch(const QGemvArgs& a, const GemvPlan& pl, float* ws, int* co
   p.sst = pl.sst;
   p.turns = pl.slots / pl.sst;
   p.ringst = pl.ringst;
-  p.ringlog = 0;
-  while ((1 << p.ringlog) < pl.ringst) ++p.ringlog;
   p.tsplit = pl.tsplit;
   p.P = pl.P;
   p.ops = pl.ops;
@@ -994,10 +997,13 @@ GemvPlan qgemv_plan(int type, int64_t N, int64_t K, int64_t M, int num_sms) {
   const int res_bytes = pl.xres ? (int)((M * (K * 2 + 64) + 1023) / 1024 * 1024) : 0;
   const int ressum_bytes = pl.xres && type == 12 ? (int)((M * ((K / 256) * 32 + 16) + 1023) / 1024 * 1024) : 0;
   const int budget = (two_per_sm ? 104 * 1024 : kGvSmemBudget) - red_bytes - bar_bytes - res_bytes - ressum_bytes;
-  // Stages of ~8 KB of weights, so every CTA's first data arrives early; the warps of one super-block turn
-  // (slots / sst turns) consume a ring of their own, of a power-of-two number of stages >= 2.
+  // Stage size: a TMA engine completes about one copy per ~0.27 us per SM whatever its size up to ~16 KB, so the
+  // weight copies of resident-activation launches are 16-32 KB (8 KB copies cap the stream near 4 TB/s); launches
+  // that also copy and permute activations per stage keep ~8 KB stages. The warps of one super-block turn
+  // (slots / sst turns) consume a ring of their own of >= 2 stages, as many as fit.
+  const int stage_cap = pl.xres ? 32 * 1024 : 8 * 1024;
   pl.sst = 1;
-  while (pl.sst < pl.slots && 2 * pl.sst * pl.rb * gv_sb_bytes(type) <= 8 * 1024) pl.sst *= 2;
+  while (pl.sst < pl.slots && 2 * pl.sst * pl.rb * gv_sb_bytes(type) <= stage_cap) pl.sst *= 2;
   for (;;) {
     pl.P = pl.sst < gv_pmax(type) ? pl.sst : gv_pmax(type);
     pl.ops = pl.sst / pl.P;
@@ -1010,8 +1016,7 @@ GemvPlan qgemv_plan(int type, int64_t N, int64_t K, int64_t M, int num_sms) {
     const int turns = pl.slots / pl.sst;
     int fit = budget / pl.stage_bytes;
     if (fit > kGvMaxStages) fit = kGvMaxStages;
-    pl.ringst = 1;
-    while (2 * pl.ringst * turns <= fit) pl.ringst *= 2;
+    pl.ringst = fit / turns;
     if (pl.ringst >= 2 || pl.sst == pl.slots) break;
     pl.sst *= 2;
   }
