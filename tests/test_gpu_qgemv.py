@@ -143,3 +143,23 @@ def test_qgemv_dependent_chain(pkg, F, O, dev, overlap, M, K):
     for b in wd + bufs:
         b.close()
     s.close()
+
+
+@pytest.mark.parametrize("N,K", [(4096, 4096), (4098, 4096), (2500, 8192), (4096, 14336)])
+@pytest.mark.parametrize("kind,out", [("plain", "f32"), ("resid", "f32"), ("plain", "f16")])
+def test_qgemv_q4k_one_token(pkg, F, O, dev, N, K, kind, out):
+    """The one-token Q4_K form (4 rows x 4 super-blocks per MMA): ragged row counts (4098 rows: a last CTA with a
+    partial row quad), 12- and 8-super-block stages, residual epilogue and f16 output."""
+    t = F.Q4_K
+    w = F.synth_weights(t, N, K, seed=N + 3 * K)
+    x = F.synth_activations(1, K, seed=7)
+    acc = O.gemm_ref(O.dequant_f32(t, w, N, K), x)
+    if kind == "resid":
+        resid = np.random.default_rng(8).standard_normal((1, N)).astype(np.float32)
+        check(O, pkg.ops.qgemv(dev, w, t, x, N=N, K=K, kind="resid", aux=resid), acc + resid)
+    elif out == "f16":
+        y16 = pkg.ops.qgemv(dev, w, t, x, N=N, K=K, out_dtype="f16")
+        e = O.errors(y16, acc)
+        assert e["rel_fro"] <= 1e-3 and (np.abs(y16 - acc) <= 2e-2 + O.f16_half_ulp(acc)).all()
+    else:
+        check(O, pkg.ops.qgemv(dev, w, t, x, N=N, K=K), acc)

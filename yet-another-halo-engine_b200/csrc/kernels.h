@@ -65,7 +65,8 @@ struct QGemvArgs {
 // Work split and shared-memory layout of a GEMV launch. Stream-K launches whose row blocks are split between CTAs
 // need `ws_floats` floats of partial sums and `counters` zeroed ints (both 0 otherwise).
 struct GemvPlan {
-  int mode;    // 0: each CTA owns a row range (no scratch); 1: stream-K over 128-row blocks (scratch when split)
+  int mode;    // 0: each CTA owns a row range (no scratch); 1: stream-K over 128-row blocks (scratch when split);
+               // 2: one Q4_K token, row ranges, 4-row x 4-super-block MMA units (no scratch)
   int grid;
   int rb, rgp, slots, tsplit, ntw, cw;  // stage rows, row groups, super-block slots, token split, tiles per warp
   int sst, ringst;                      // super-blocks per stage (divides slots), stages per ring

@@ -133,6 +133,13 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
 }
 
 // ---------------------------------------------------------------- TMA
+// Bulk prefetch of [src, src + bytes) into L2 (16-byte aligned, bytes a multiple of 16). L2 is the point of
+// coherence, so a prefetch issued before a producer kernel finishes writing the range is harmless: its writes
+// update the lines, and reads after griddepcontrol.wait see them.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(src)), "r"(bytes)
+               : "memory");
+}
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }

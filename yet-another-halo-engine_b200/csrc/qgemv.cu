@@ -38,6 +38,7 @@ namespace yah {
 namespace {
 
 constexpr int kGvBlock = 128;    // stream-K row block
+constexpr int kGvEarlyStages = 2;  // weight copies a programmatic launch issues before the preceding kernel ends
 constexpr int kGvMaxStages = 16;
 constexpr int kGvSmemBudget = 225 * 1024;
 
@@ -70,6 +71,7 @@ struct GvParams {
   int wreg, xoff, sumoff, stage_bytes, stages, redoff, baroff;
   int xres, resoff, ressum;  // activations resident for the whole launch (row ranges, small M * K)
   int xstride, sstride;      // resident layout: bytes per token of activations / of group sums
+  int sbstride;              // resident layout: bytes per super-block of activations (512, or padded)
   const __half* x;
   int64_t ldx;
   int K;
@@ -636,7 +638,7 @@ __device__ __forceinline__ void gv_prep_resident(const GvParams& p, uint32_t res
       v = make_uint4(prmt(v.x, v.y, 0x5410u), prmt(v.x, v.y, 0x7632u), prmt(v.z, v.w, 0x5410u),
                      prmt(v.z, v.w, 0x7632u));
     }
-    const uint32_t a = res + t * p.xstride + kp * 16;
+    const uint32_t a = res + t * p.xstride + (kp >> 5) * p.sbstride + (kp & 31) * 16;
     asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
                  : "memory");
     }
@@ -683,7 +685,7 @@ __global__ void __launch_bounds__(GvRoles<T, CW>::kThreads, (CW == 8 && NTW == 1
     // preceding kernel finishes; the activation copies of the first pass over the rings are held back until it
     // has completed (griddepcontrol.wait), and issued before any stage is reused.
     bool dep = p.xres != 0;  // resident activations: the producer copies none
-    int npend = 0, pend_st[kGvMaxStages], pend_k[kGvMaxStages];
+    int npend = 0, pend_st[kGvMaxStages], pend_k[kGvMaxStages], issued = 0;
     bool ok = true;
     for (int si = 0; si < W.nseg && ok; ++si) {
       const GvSeg sg = gv_seg<RANGES>(p, W, si);
@@ -693,6 +695,7 @@ __global__ void __launch_bounds__(GvRoles<T, CW>::kThreads, (CW == 8 && NTW == 1
       const int q = cnt[r]++;
       const int st = r * p.ringst + q % p.ringst, ph = (q / p.ringst) & 1;
       if (++r == p.turns) r = 0;
+      if (p.xres && ++issued == kGvEarlyStages + 1) griddep_wait();  // see qgemv_q4k_m1_kernel's producer
       if (!dep && q >= p.ringst) {
         griddep_wait();
         dep = true;
@@ -831,6 +834,236 @@ __global__ void __launch_bounds__(GvRoles<T, CW>::kThreads, (CW == 8 && NTW == 1
   }
 }
 
+// ------------------------------------------------------------------------------------------------ Q4_K, one token
+// One decode token against Q4_K weights, activations resident, row ranges. With a single token, seven of the eight
+// B columns of an m16n8k16 would be idle; this form spends them. The 16 A rows of an MMA are 4 weight rows x 4
+// super-blocks (lane row g: row g % 4 at super-block g / 4, lane row g + 8: the same row at super-block 2 + g / 4)
+// and B column n holds the activations of super-block n, so D[g][g / 4] and D[g + 8][2 + g / 4] are the products
+// of the right pairs (the other D entries mix a row with another super-block's activations and are dropped). Each
+// lane owns one (row, super-block) product: lanes c = 0 that of its row g, lanes c = 1 that of row g + 8, so a lane
+// forms the group scales of one super-block instead of two, and 28-row ranges split into 4-row quads with no padded
+// rows. A unit (4 rows x 4 super-blocks) ends with the lane values added across the unit by two shuffles and
+// stored per (row quad, super-block quad); the rows are summed in a fixed order at the end (deterministic).
+struct Gv1Params {
+  int N, nsb, kb_off, S, ringst, stage_bytes, opw, rb;
+  int units;                  // ceil(N / 4)
+  int resoff, ressum, partoff, baroff, xstride, sstride;
+  const __half* x;
+  int64_t ldx;
+  int K;
+  void* y;
+  int64_t ldy;
+  int y_f16, epi;
+  const float* aux;
+  int64_t ldaux;
+  int* status;
+};
+
+constexpr int kGv1Warps = 16;  // compute warps; warp 16 issues the weight copies
+// Bank layout of the one-token form. Activations: super-blocks 576 bytes apart, so the four columns of an MMA
+// (super-blocks n = 0..3 at n * 576 + 16 c) fill both halves of the 128-byte bank line. Weights: a copy pitch of
+// 2 mod 8 16-byte units, so the 8 (row, super-block) pairs of a lane group (rows 0..3 x offsets 0 / 144 bytes) start
+// in 8 different 16-byte bank slots.
+constexpr int kGv1SbStride = 576;
+__host__ __device__ constexpr int gv1_pitch(int S) { return (9 * S + ((2 - 9 * S) % 8 + 8) % 8) * 16; }
+
+__device__ __forceinline__ void gv1_store(const Gv1Params& p, int row, float v) {
+  if (p.epi == kEpiResid) v += p.aux[row];
+  if (p.y_f16) reinterpret_cast<__half*>(p.y)[row] = __float2half_rn(v);
+  else reinterpret_cast<float*>(p.y)[row] = v;
+}
+
+// One unit: weight rows at wg (lane row g) and wg + 288 (lane row g + 8), this lane's own header at wg + own,
+// activations xu (+ 128 j, + 64 for the high-nibble pieces) and group sums su of super-block column g % 4.
+// Returns the lane's product (zero for lanes c >= 2) before the cross-lane sum.
+__device__ __forceinline__ float gv1_unit(uint32_t wg, uint32_t own, uint32_t xu, uint32_t su, int c,
+                                          const float (&sel)[4]) {
+  const uint32_t wg8 = wg + 288;
+  const uint4 ho = lds128(wg + own), h0 = lds128(wg), h1 = lds128(wg8);
+  uint2 q0[4], q1[4];
+  uint4 xl[4], xh[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    q0[j] = lds64(wg + 16 + 32 * j + 8 * c);
+    q1[j] = lds64(wg8 + 16 + 32 * j + 8 * c);
+    xl[j] = lds128(xu + 128 * j);
+    xh[j] = lds128(xu + 128 * j + 64);
+  }
+  const uint32_t bh = lds32(su), bl = lds32(su + 16);
+  // this lane's group factors (see gv_superblock): F = (2^23 + sc) * D - 2^23 * D, D = d * 2^24 (low nibbles)
+  // or d * 2^20 (high nibbles)
+  const uint32_t sca = ho.y & 0x3F3F3F3Fu, scb = (ho.w & 0x0F0F0F0Fu) | ((ho.y >> 2) & 0x30303030u);
+  const float d = h2f_bits(ho.x & 0xFFFFu);
+  const float dl = d * 16777216.0f, dh = d * 1048576.0f, bl0 = dl * -8388608.0f, bh0 = dh * -8388608.0f;
+  float y[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t s = j < 2 ? sca : scb;
+    const float fl = __fmaf_rn(magic_byte(s, (2 * j) & 3), dl, bl0);
+    const float fh = __fmaf_rn(magic_byte(s, (2 * j + 1) & 3), dh, bh0);
+    uint32_t lo[2][4], hi[2][4];
+#pragma unroll
+    for (int wi = 0; wi < 2; ++wi) {
+      const uint32_t u0 = wi ? q0[j].y : q0[j].x, u1 = wi ? q1[j].y : q1[j].x;
+      const uint32_t v0 = shr8_fma(u0), v1 = shr8_fma(u1);
+      lo[wi][0] = u0 & 0x000F000Fu, lo[wi][1] = u1 & 0x000F000Fu, lo[wi][2] = v0 & 0x000F000Fu,
+      lo[wi][3] = v1 & 0x000F000Fu;
+      hi[wi][0] = u0 & 0x00F000F0u, hi[wi][1] = u1 & 0x00F000F0u, hi[wi][2] = v0 & 0x00F000F0u,
+      hi[wi][3] = v1 & 0x00F000F0u;
+    }
+    float alo[4] = {0.f, 0.f, 0.f, 0.f}, ahi[4] = {0.f, 0.f, 0.f, 0.f};
+    mma16816(alo, lo[0][0], lo[0][1], lo[0][2], lo[0][3], xl[j].x, xl[j].y);
+    mma16816(ahi, hi[0][0], hi[0][1], hi[0][2], hi[0][3], xh[j].x, xh[j].y);
+    mma16816(alo, lo[1][0], lo[1][1], lo[1][2], lo[1][3], xl[j].z, xl[j].w);
+    mma16816(ahi, hi[1][0], hi[1][1], hi[1][2], hi[1][3], xh[j].z, xh[j].w);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) y[e] = __fmaf_rn(fh, ahi[e], __fmaf_rn(fl, alo[e], y[e]));
+  }
+  // - dmin * sum_g m_g X_g, the mins of lane rows g / g + 8 from their own headers
+  const uint32_t m0a = h0.z & 0x3F3F3F3Fu, m0b = ((h0.w >> 4) & 0x0F0F0F0Fu) | ((h0.z >> 2) & 0x30303030u);
+  const uint32_t m1a = h1.z & 0x3F3F3F3Fu, m1b = ((h1.w >> 4) & 0x0F0F0F0Fu) | ((h1.z >> 2) & 0x30303030u);
+  const int mb = (2 * c) & 3;
+  const uint32_t msel = (uint32_t)mb | 0x40u | ((uint32_t)(mb + 1) << 8) | 0x4000u;
+  const uint32_t am0 = hsub2_u32(prmt(c < 2 ? m0a : m0b, 0x64646464u, msel), 0x64006400u);
+  const uint32_t am1 = hsub2_u32(prmt(c < 2 ? m1a : m1b, 0x64646464u, msel), 0x64006400u);
+  float acc2[4] = {0.f, 0.f, 0.f, 0.f};
+  mma16816(acc2, am0, am1, am0, am1, bh, bl);
+  const float nd = -h2f_bits(ho.x >> 16);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) y[e] = __fmaf_rn(nd, acc2[e], y[e]);
+  return sel[0] * y[0] + sel[1] * y[1] + sel[2] * y[2] + sel[3] * y[3];
+}
+
+__global__ void __launch_bounds__((kGv1Warps + 1) * 32, 1)
+    qgemv_q4k_m1_kernel(const __grid_constant__ CUtensorMap tmap_w, const Gv1Params p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.baroff);
+  uint64_t* empty = full + kGvMaxStages;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
+  const int G = gridDim.x;
+  const int rs = 4 * (int)((int64_t)blockIdx.x * p.units / G);
+  int re = 4 * (int)((int64_t)(blockIdx.x + 1) * p.units / G);
+  if (re > p.N) re = p.N;
+  const int nq = (re - rs + 3) / 4;   // row quads of this CTA
+  const int nst = p.nsb / p.S;        // stages (S divides the super-blocks)
+  const int sq = p.S / 4;             // super-block quads per stage
+  const int nsq = p.nsb / 4;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < p.ringst; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kGv1Warps);
+    }
+    fence_barrier_init();
+    griddep_launch_dependents();
+  }
+  __syncthreads();
+
+  if (warp == kGv1Warps) {
+    // ---------------------------------------------------------------- TMA producer (weights only)
+    if (lane != 0) return;
+    tma_prefetch_desc(&tmap_w);
+    // the activation row into L2 ahead of the compute warps' loads (issued before the weights)
+    if ((reinterpret_cast<uintptr_t>(p.x) & 15) == 0) bulk_prefetch_l2(p.x, (uint32_t)p.K * 2);
+    const uint32_t bytes = (uint32_t)(p.rb * p.opw);
+    int slot = 0, ph = 0;
+    for (int k = 0; k < nst; ++k) {
+      // Under a programmatic launch, no more than kGvEarlyStages copies go out before the preceding kernel has
+      // completed: a deeper early prefetch from every CTA queues ahead of the activation loads in the memory
+      // system and delays the start of the arithmetic (measured: 3.3 us of activation prep behind 5 early stages).
+      if (k == kGvEarlyStages) griddep_wait();
+      if (!mbar_wait(&empty[slot], ph ^ 1, p.status, kStatusTimeoutEmpty)) break;
+      mbar_arrive_expect_tx(&full[slot], bytes);
+      tma_load_2d(smem + slot * p.stage_bytes, &tmap_w, &full[slot], (int)((int64_t)(p.kb_off + k * p.S) * 18), rs);
+      if (++slot == p.ringst) slot = 0, ph ^= 1;
+    }
+    slot = 0, ph = 0;
+    for (int k = 0; k < nst; ++k) {  // exit drain: the last copies of the ring land before the CTA leaves
+      if (k >= nst - p.ringst) mbar_wait(&full[slot], ph, p.status, kStatusTimeoutDrain, false);
+      if (++slot == p.ringst) slot = 0, ph ^= 1;
+    }
+    return;
+  }
+
+  // ------------------------------------------------------------------ compute warps
+  const uint32_t res = smem_u32(smem + p.resoff), ressum = smem_u32(smem + p.ressum);
+  float* part = reinterpret_cast<float*>(smem + p.partoff);  // [row quad][super-block quad][4]
+  griddep_wait();  // activations are read, and outputs written, only after the preceding kernel has completed
+  {
+    // The token's activations into shared memory (see gv_prep_resident; one token, so piece kp of thread
+    // tid + 512 u needs no division): group sums (hi, lo f16) and the (x0, x2, x1, x3) permutation of every 4.
+    const int np = p.K / 8;
+    uint4 v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int kp = threadIdx.x + u * kGv1Warps * 32;
+      if (kp < np) v[u] = __ldg(reinterpret_cast<const uint4*>(p.x) + kp);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int kp = threadIdx.x + u * kGv1Warps * 32;
+      if (u * kGv1Warps * 32 >= np) break;  // uniform: np is a multiple of 32
+      const float2 a0 = __half22float2(*reinterpret_cast<const __half2*>(&v[u].x));
+      const float2 a1 = __half22float2(*reinterpret_cast<const __half2*>(&v[u].y));
+      const float2 a2 = __half22float2(*reinterpret_cast<const __half2*>(&v[u].z));
+      const float2 a3 = __half22float2(*reinterpret_cast<const __half2*>(&v[u].w));
+      float sum = ((a0.x + a0.y) + (a1.x + a1.y)) + ((a2.x + a2.y) + (a3.x + a3.y));
+      sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+      sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+      if (kp < np) {
+        if ((kp & 3) == 0) {
+          const uint32_t ss = ressum + (kp >> 5) * 32 + ((kp >> 2) & 7) * 2;
+          const __half hv = __float2half_rn(sum);
+          const __half lv = __float2half_rn(sum - __half2float(hv));
+          asm volatile("st.shared.b16 [%0], %1;" ::"r"(ss), "h"(__half_as_ushort(hv)) : "memory");
+          asm volatile("st.shared.b16 [%0], %1;" ::"r"(ss + 16), "h"(__half_as_ushort(lv)) : "memory");
+        }
+        const uint32_t a = res + (kp >> 5) * kGv1SbStride + (kp & 31) * 16;
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(prmt(v[u].x, v[u].y, 0x5410u)),
+                     "r"(prmt(v[u].x, v[u].y, 0x7632u)), "r"(prmt(v[u].z, v[u].w, 0x5410u)),
+                     "r"(prmt(v[u].z, v[u].w, 0x7632u))
+                     : "memory");
+      }
+    }
+  }
+  named_bar(1, kGv1Warps * 32);
+  // lane constants: which D element is this lane's product, whose header holds its scales, its activation column
+  float sel[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) sel[e] = (c == 0 && e == (g >> 2)) || (c == 1 && e == 2 + (g >> 2)) ? 1.f : 0.f;
+  const uint32_t own = c == 1 ? 288u : 0u;
+  const uint32_t xcol = res + (g & 3) * kGv1SbStride + 16 * c, scol = ressum + (g & 3) * 32 + 4 * c;
+  const int U = nq * sq;  // units per stage
+  int slot = 0, ph = 0;
+  bool ok = true;
+  for (int k = 0; k < nst; ++k) {
+    if (!mbar_wait(&full[slot], ph, p.status, kStatusTimeoutFull)) { ok = false; break; }
+    const uint32_t base = smem_u32(smem + slot * p.stage_bytes);
+    // unit i of stage k goes to warp (i + k U) mod 16: every warp gets the same share over the launch
+    int i = (warp - (k * U) % kGv1Warps + kGv1Warps) % kGv1Warps;
+    for (; i < U; i += kGv1Warps) {
+      const int rq = i / sq, sl = i - rq * sq;  // row quad, super-block quad within the stage
+      const int sbq = k * sq + sl;              // super-block quad of the row
+      const uint32_t wg = base + (4 * rq + (g & 3)) * p.opw + (4 * sl + (g >> 2)) * 144;
+      float v = gv1_unit(wg, own, xcol + sbq * 4 * kGv1SbStride, scol + sbq * 128, c, sel);
+      v += __shfl_xor_sync(0xffffffffu, v, 1);
+      v += __shfl_xor_sync(0xffffffffu, v, 16);
+      if (lane < 16 && c == 0) part[(rq * nsq + sbq) * 4 + g] = v;
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[slot]);
+    if (++slot == p.ringst) slot = 0, ph ^= 1;
+  }
+  named_bar(1, kGv1Warps * 32);
+  if (!ok || *(volatile int*)p.status != 0) return;
+  for (int r = threadIdx.x; r < re - rs; r += kGv1Warps * 32) {
+    const float* pr = part + (r >> 2) * nsq * 4 + (r & 3);
+    float acc = 0.f;
+    for (int s = 0; s < nsq; ++s) acc += pr[s * 4];
+    gv1_store(p, rs + r, acc);
+  }
+}
+
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -924,6 +1157,7 @@ cudaError_t gv_launch(const QGemvArgs& a, const GemvPlan& pl, float* ws, int* co
   p.status = a.status;
   p.xstride = (int)(a.K * 2 + 64);
   p.sstride = (int)((a.K / 256) * 32 + 16);
+  p.sbstride = 512;
   auto kern = qgemv_kernel<T, NTW, CW, RANGES>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, pl.smem);
   if (e != cudaSuccess) return e;
@@ -953,6 +1187,99 @@ cudaError_t gv_fmt(const QGemvArgs& a, const GemvPlan& pl, float* ws, int* count
   return gv_launch<T, 4, 8, false>(a, pl, ws, counters, s);
 }
 
+cudaError_t gv_launch_m1(const QGemvArgs& a, const GemvPlan& pl, cudaStream_t stream) {
+  EncodeTiledFn enc = gv_encoder();
+  if (!enc) return cudaErrorNotSupported;
+  CUtensorMap mw;
+  const int64_t window_bytes = (a.kb_off + a.K / 256) * 144;
+  cuuint64_t dims[2] = {(cuuint64_t)(window_bytes / 8), (cuuint64_t)a.N};
+  cuuint64_t strides[1] = {(cuuint64_t)a.w_row_stride};
+  cuuint32_t box[2] = {(cuuint32_t)(pl.opw / 8), (cuuint32_t)pl.rb};
+  cuuint32_t ones[2] = {1, 1};
+  if (enc(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void*>(a.w), dims, strides, box, ones,
+          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return cudaErrorInvalidValue;
+  Gv1Params p{};
+  p.N = (int)a.N;
+  p.nsb = (int)(a.K / 256);
+  p.kb_off = (int)a.kb_off;
+  p.S = pl.sst;
+  p.ringst = pl.ringst;
+  p.stage_bytes = pl.stage_bytes;
+  p.opw = pl.opw;
+  p.rb = pl.rb;
+  p.units = (int)((a.N + 3) / 4);
+  p.resoff = pl.resoff;
+  p.ressum = pl.ressum;
+  p.partoff = pl.redoff;
+  p.baroff = pl.baroff;
+  p.xstride = (int)((a.K / 256) * kGv1SbStride + 64);
+  p.sstride = (int)((a.K / 256) * 32 + 16);
+  p.x = static_cast<const __half*>(a.x);
+  p.ldx = a.ldx;
+  p.K = (int)a.K;
+  p.y = a.y;
+  p.ldy = a.ldy;
+  p.y_f16 = a.y_f16;
+  p.epi = a.epilogue;
+  p.aux = a.aux;
+  p.ldaux = a.ldaux;
+  p.status = a.status;
+  cudaError_t e = cudaFuncSetAttribute(qgemv_q4k_m1_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, pl.smem);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(pl.grid);
+  cfg.blockDim = dim3((kGv1Warps + 1) * 32);
+  cfg.dynamicSmemBytes = pl.smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = launch_overlap() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, qgemv_q4k_m1_kernel, mw, p);
+}
+
+// Plan of the one-token Q4_K form (mode 2), or false when the shape does not fit it.
+bool plan_m1(GemvPlan& pl, int64_t N, int64_t K, int num_sms) {
+  const int64_t units = (N + 3) / 4, nsb = K / 256;
+  if (nsb % 4 || K * 2 > 32 * 1024 || units < 4 * (int64_t)num_sms) return false;
+  const int64_t per_cta = (units + num_sms - 1) / num_sms;
+  if (4 * per_cta > 128) return false;
+  pl = GemvPlan{};
+  pl.mode = 2;
+  pl.grid = num_sms;
+  pl.rb = (int)(4 * per_cta);
+  pl.cw = kGv1Warps;
+  pl.ntw = 1;
+  // super-blocks per stage: a multiple of 4 dividing the row, one copy of at most ~36 KB (box <= 2048 bytes)
+  pl.sst = 4;
+  for (int S : {12, 8})
+    if (nsb % S == 0 && (int64_t)pl.rb * S * 144 <= 36 * 1024) { pl.sst = S; break; }
+  pl.P = pl.sst;
+  pl.ops = 1;
+  pl.opw = gv1_pitch(pl.sst);
+  pl.wreg = pl.rb * pl.opw;
+  pl.stage_bytes = (pl.wreg + 1023) / 1024 * 1024;
+  const int res_bytes = (int)((nsb * kGv1SbStride + 64 + 1023) / 1024 * 1024);
+  const int ressum_bytes = (int)((nsb * 32 + 16 + 1023) / 1024 * 1024);
+  const int part_bytes = (int)(((pl.rb / 4) * (nsb / 4) * 16 + 1023) / 1024 * 1024);
+  const int bar_bytes = 2 * kGvMaxStages * 8;
+  int fit = (kGvSmemBudget - res_bytes - ressum_bytes - part_bytes - bar_bytes) / pl.stage_bytes;
+  if (fit > kGvMaxStages) fit = kGvMaxStages;
+  if (fit < 2) return false;
+  pl.ringst = fit;
+  pl.stages = fit;
+  pl.resoff = pl.stages * pl.stage_bytes;
+  pl.ressum = pl.resoff + res_bytes;
+  pl.redoff = pl.ressum + ressum_bytes;
+  pl.baroff = pl.redoff + part_bytes;
+  pl.smem = pl.baroff + bar_bytes + 1024;
+  pl.xres = 1;
+  return true;
+}
+
 }  // namespace
 
 namespace {
@@ -963,6 +1290,7 @@ void set_launch_overlap(bool on) { g_launch_overlap.store(on ? 1 : 0, std::memor
 
 GemvPlan qgemv_plan(int type, int64_t N, int64_t K, int64_t M, int num_sms) {
   GemvPlan pl{};
+  if (type == 12 && M == 1 && plan_m1(pl, N, K, num_sms)) return pl;
   const int nt = pow2_ceil((int)((M + 7) / 8));  // token tiles of 8: 1, 2 or 4
   const int64_t units = (N + 3) / 4, nsb = K / 256;
   // Row ranges need >= 16 rows per CTA and pay off when the activations stay resident (no per-stage activation
@@ -1042,6 +1370,7 @@ GemvPlan qgemv_plan(int type, int64_t N, int64_t K, int64_t M, int num_sms) {
 cudaError_t launch_qgemv_ws(const QGemvArgs& a, const GemvPlan& plan, float* ws, int* counters,
                             cudaStream_t stream) {
   if (plan.ringst < 2) return cudaErrorInvalidConfiguration;
+  if (plan.mode == 2) return a.type == 12 && a.M == 1 ? gv_launch_m1(a, plan, stream) : cudaErrorInvalidValue;
   switch (a.type) {
     case 8: return gv_fmt<8>(a, plan, ws, counters, stream);
     case 12: return gv_fmt<12>(a, plan, ws, counters, stream);
