@@ -289,7 +289,10 @@ def run_stack(args, dist, rank, local_rank):
                      "gate": F.synth_weights(shape.fmt, shape.ff // p, H, seed=s0 + 2),
                      "up": F.synth_weights(shape.fmt, shape.ff // p, H, seed=s0 + 3),
                      "down": F.synth_weights(shape.fmt, H, shape.ff // p, seed=s0 + 4)})
-    stack = tp.LlamaStack(dev, comm, shape, [sets[i % len(sets)] for i in range(shape.layers)], M)
+    chunks = args.stack_chunks
+    if chunks > 1:
+        pkg.lib().yah_set_sm_budget(dev.sm_count - args.stack_nccl_sms)
+    stack = tp.LlamaStack(dev, comm, shape, [sets[i % len(sets)] for i in range(shape.layers)], M, chunks=chunks)
     h0 = np.random.default_rng(7).standard_normal((M, H)).astype(np.float32)
     h0d, h = dev.upload(h0), dev.empty(M * H * 4)
     stream = pkg.Stream()
@@ -346,7 +349,8 @@ def run_stack(args, dist, rank, local_rank):
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "f16 x GGUF-Q4_K -> f32 acc, f32 residual stream and allreduce", "data": "synthetic",
         "config": {"workload": "q4k_layer_stack_tp", "layers": shape.layers, "hidden": H, "qkv": shape.qkv,
-                   "ff": shape.ff, "M_tokens": M, "parallelism": f"tp{world}",
+                   "ff": shape.ff, "M_tokens": M, "parallelism": f"tp{world}", "token_chunks": chunks,
+                   "gemm_sms": (dev.sm_count - args.stack_nccl_sms) if chunks > 1 else dev.sm_count,
                    "l2": "4 distinct weight sets cycled over the layers (> L2 per GPU at tp1)"},
         "e2e": {"value": round(flops / (ms_e2e / args.steps * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
                 "h2d_bytes_per_step": M * H * 4, "d2h_bytes_per_step": M * H * 4},
@@ -471,6 +475,11 @@ def main():
     ap.add_argument("--workload", default="gemm", choices=["gemm", "gemv", "stack"])
     ap.add_argument("--layers", type=int, default=32, help="stack layers")
     ap.add_argument("--stack-tokens", type=int, default=4096, help="stack tokens M")
+    ap.add_argument("--stack-chunks", type=int, default=1,
+                    help="token chunks pipelined over a compute and a communication stream (measured slower at tp1 "
+                         "and tp2 on B200: the smaller GEMMs lose more than the overlapped allreduces gain)")
+    ap.add_argument("--stack-nccl-sms", type=int, default=8,
+                    help="SMs left to NCCL while chunked GEMMs run (the GEMMs' SM budget is the rest)")
     ap.add_argument("--tile-table", default=None, help="tile table (tune.py output) installed before the run")
     ap.add_argument("--tokens", type=int, default=1, help="gemv tokens (1..32)")
     ap.add_argument("--no-cpu-baseline", action="store_true")

@@ -103,6 +103,12 @@ int yah_graph_destroy(void* graph_exec);
  * its outputs, only after that kernel has completed. Contract: no kernel still in flight on the stream writes the
  * weight tensor (weights are loaded, then only read). yah_set_launch_overlap(0) restores plain stream order. */
 int yah_set_launch_overlap(int on);
+/* SMs the GEMM and GEMV launches may use on each device (0, the default: all). A caller that runs collectives
+ * concurrently with these kernels (the tensor-parallel stack overlaps its allreduces with the next token chunk's
+ * GEMMs) leaves the remaining SMs to the collectives' kernels, which otherwise wait for a persistent GEMM to end. */
+int yah_set_sm_budget(int sms);
+/* Make `stream` wait for the last work recorded on `event` (cudaStreamWaitEvent). */
+int yah_stream_wait_event(void* stream, void* event);
 /* Read and clear the current device's kernel status word: 0, or the code of a bounded wait that ran out
  * (1 data wait, 2 free-stage wait, 3 exit drain). A non-zero word means the output of that launch is invalid. */
 int yah_status_word(int* code);

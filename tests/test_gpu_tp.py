@@ -72,6 +72,33 @@ def test_small_stack_one_rank(pkg, O, dev, comm):
     assert dev.status_word() == 0
 
 
+@pytest.mark.parametrize("M,chunks", [(64, 2), (128, 4), (256, 2)])
+def test_small_stack_chunked_one_rank(pkg, O, dev, comm, M, chunks):
+    """The token-chunked forward (norms and GEMMs on the caller's stream, allreduces on a second stream handed over
+    by events, GEMMs under an SM budget) gives the stack reference; chunks of 32 rows take the decode GEMV."""
+    tp = pkg.tp
+    from importlib import import_module
+    L = import_module(pkg.__name__ + "._lib")
+    shape = tp.StackShape(layers=2, hidden=512, n_q=4, n_kv=2, head_dim=128, ff=1024)
+    full = [tp.layer_weights(shape, i) for i in range(shape.layers)]
+    stack = tp.LlamaStack(dev, comm, shape, [tp.shard_layer(shape, f, 1, 0) for f in full], M, chunks=chunks)
+    h0 = np.random.default_rng(73).standard_normal((M, shape.hidden)).astype(np.float32)
+    h = dev.upload(h0)
+    s = pkg.Stream()
+    L.check(L.lib().yah_set_sm_budget(dev.sm_count - 8))
+    try:
+        stack.forward(h, s.handle)
+        s.synchronize()
+    finally:
+        L.check(L.lib().yah_set_sm_budget(0))
+    got = h.download(np.float32, (M, shape.hidden))
+    e = O.errors(got, W.stack_ref(O, shape, full, h0, tp.NORM_GAIN, tp.NORM_EPS))
+    stack.close()
+    s.close()
+    assert e["finite"] and e["rel_fro"] <= 2e-3, e
+    assert dev.status_word() == 0
+
+
 def test_small_stack_two_ranks(pkg):
     """The same stack over two GPUs (column shards + two allreduces per layer) matches the reference."""
     if pkg.device_count() < 2:

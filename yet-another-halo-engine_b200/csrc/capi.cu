@@ -6,6 +6,7 @@
 #include <stdarg.h>
 #include <stdio.h>
 
+#include <atomic>
 #include <mutex>
 #include <vector>
 #include <string>
@@ -36,6 +37,10 @@ int cuda_fail(cudaError_t e, const char* what) {
     cudaError_t e_ = (call);                       \
     if (e_ != cudaSuccess) return cuda_fail(e_, #call); \
   } while (0)
+
+// SMs the GEMM / GEMV plans may use (0: all). A process that overlaps collectives with these kernels leaves the
+// rest to the collective's kernels.
+std::atomic<int> g_sm_budget{0};
 
 struct DevState {
   bool ready = false;
@@ -90,6 +95,11 @@ int dev_state(DevState** out) {
   }
   *out = &s;
   return YAH_OK;
+}
+
+int sms_of(const DevState* s) {
+  const int b = g_sm_budget.load(std::memory_order_relaxed);
+  return b > 0 && b < s->sms ? b : s->sms;
 }
 
 int sb_bytes(int type) {
@@ -331,6 +341,18 @@ int yah_set_launch_overlap(int on) {
   return YAH_OK;
 }
 
+int yah_set_sm_budget(int sms) {
+  if (sms < 0) return fail(YAH_ERR_ARG, "SM budget %d < 0", sms);
+  g_sm_budget.store(sms, std::memory_order_relaxed);
+  return YAH_OK;
+}
+
+int yah_stream_wait_event(void* stream, void* event) {
+  if (!event) return fail(YAH_ERR_ARG, "null event");
+  CK(cudaStreamWaitEvent((cudaStream_t)stream, (cudaEvent_t)event, 0));
+  return YAH_OK;
+}
+
 int yah_status_word(int* code) {
   if (!code) return fail(YAH_ERR_ARG, "null code");
   DevState* s;
@@ -412,8 +434,8 @@ int yah_qgemm_tile(const void* w, int t, int64_t N, int64_t K, int64_t w_row_str
   a.aux = static_cast<const float*>(aux);
   a.ldaux = ldaux;
   a.status = s->status;
-  a.num_sms = s->sms;
-  a.grid = grid > s->sms ? s->sms : grid;
+  a.num_sms = sms_of(s);
+  a.grid = grid > a.num_sms ? a.num_sms : grid;
   a.kchunk = kchunk;
   a.scratch = nullptr;
   {
@@ -508,7 +530,7 @@ int yah_qgemv(const void* w, int t, int64_t N, int64_t K, int64_t w_row_stride, 
   DevState* s;
   rc = dev_state(&s);
   if (rc) return rc;
-  const yah::GemvPlan plan = yah::qgemv_plan(t, N, K, M, s->sms);
+  const yah::GemvPlan plan = yah::qgemv_plan(t, N, K, M, sms_of(s));
   if (plan.ws_floats > 0) {
     std::lock_guard<std::mutex> lk(g_mu);
     rc = grow(reinterpret_cast<void**>(&s->ws), &s->ws_bytes, (size_t)plan.ws_floats * sizeof(float));
@@ -538,7 +560,7 @@ int yah_qgemv(const void* w, int t, int64_t N, int64_t K, int64_t w_row_stride, 
   a.aux = static_cast<const float*>(aux);
   a.ldaux = ldaux;
   a.status = s->status;
-  a.num_sms = s->sms;
+  a.num_sms = sms_of(s);
   return after_launch(yah::launch_qgemv_ws(a, plan, s->ws, s->counters, (cudaStream_t)stream), "qgemv launch");
 }
 

@@ -98,6 +98,10 @@ class Stream:
     def synchronize(self):
         check(lib().yah_stream_synchronize(self.handle))
 
+    def wait(self, event: "Event"):
+        """Later work on this stream waits for the work recorded on `event`."""
+        check(lib().yah_stream_wait_event(self.handle, event.handle))
+
     def close(self):
         if self.handle:
             lib().yah_stream_destroy(self.handle)

@@ -30,7 +30,7 @@ import numpy as np
 
 from . import formats as F
 from ._lib import EPI_RESID, EPI_STORE, EPI_SWIGLU, F16, F32, TP_ID_BYTES, check, lib  # noqa: F401
-from .device import Device, DeviceBuffer
+from .device import Device, DeviceBuffer, Event, Stream
 
 NORM_GAIN = 1.0 / 64.0
 NORM_EPS = 1e-6
@@ -159,10 +159,18 @@ class Comm:
 
 # ----------------------------------------------------------------------------------------------- the stack
 class LlamaStack:
-    """One rank's part of the linear layer stack: its weight shards on the device and the forward pass."""
+    """One rank's part of the linear layer stack: its weight shards on the device and the forward pass.
 
-    def __init__(self, dev: Device, comm: Comm, shape: StackShape, shards: list, M: int):
-        self.dev, self.comm, self.shape, self.M = dev, comm, shape, M
+    With `chunks` > 1 the M tokens go through the layers in that many row chunks, pipelined over two streams: the
+    norms and GEMMs of every chunk on the caller's stream, each row-parallel allreduce on a communication stream
+    once that chunk's GEMM is done, so the allreduce of chunk c runs under the GEMMs of chunk c + 1 (every op is
+    row-wise in the tokens, so chunks are independent until the end). Run it with an SM budget
+    (yah_set_sm_budget) below the device's SM count so that NCCL's kernels find free SMs while a GEMM runs."""
+
+    def __init__(self, dev: Device, comm: Comm, shape: StackShape, shards: list, M: int, chunks: int = 1):
+        if chunks < 1 or M % chunks:
+            raise ValueError(f"{M} tokens do not split into {chunks} chunks")
+        self.dev, self.comm, self.shape, self.M, self.chunks = dev, comm, shape, M, chunks
         p = comm.nranks
         self.q_r = shape.n_q * shape.head_dim // p
         self.qkv_r = shape.qkv // p
@@ -174,14 +182,20 @@ class LlamaStack:
         self.qkv = dev.empty(M * self.qkv_r * 2)
         self.g = dev.empty(M * self.ff_r * 4)
         self.act = dev.empty(M * self.ff_r * 2)
+        if chunks > 1:
+            self.comm_stream = Stream()
+            self.ev_gemm = [Event() for _ in range(chunks)]
+            self.ev_red = [Event() for _ in range(chunks)]
 
     @property
     def launches_per_forward(self) -> int:
-        """Library kernel launches per forward pass (2 norms + 5 linears per layer)."""
-        return 7 * self.shape.layers
+        """Library kernel launches per forward pass (2 norms + 5 linears per layer and token chunk)."""
+        return 7 * self.shape.layers * self.chunks
 
     def forward(self, h: DeviceBuffer, stream=None):
         """h (f32 [M][hidden], the residual stream, identical on every rank) is updated in place."""
+        if self.chunks > 1:
+            return self._forward_chunked(h, stream)
         L, s, M, H, fmt = lib(), self.shape, self.M, self.shape.hidden, self.shape.fmt
         c = self.comm.handle
         for w in self.w:
@@ -198,9 +212,57 @@ class LlamaStack:
             check(L.yah_tp_linear_row(c, w["down"].ptr, fmt, H, self.ff_r, self.row_bytes["down"], 0, self.act.ptr, M,
                                       self.ff_r, h.ptr, h.ptr, stream))
 
+    def _row_parallel(self, name: str, w, K_r: int, x_ptr: int, ldx: int, h_ptr: int, Mc: int, stream):
+        """The GEMM half of a row-parallel linear (yah_tp_linear_row without its allreduce): rank 0 adds the
+        residual (h, in place), the others store their partial into h; the allreduce follows on the communication
+        stream."""
+        L, fmt, H = lib(), self.shape.fmt, self.shape.hidden
+        r0 = self.comm.rank == 0
+        fn = L.yah_qgemv if Mc <= 32 else L.yah_qgemm
+        check(fn(w.ptr, fmt, H, K_r, self.row_bytes[name], 0, x_ptr, Mc, ldx, h_ptr, F32, H,
+                 EPI_RESID if r0 else EPI_STORE, h_ptr if r0 else None, H if r0 else 0, stream))
+
+    def _forward_chunked(self, h: DeviceBuffer, stream):
+        L, s, H, fmt, C = lib(), self.shape, self.shape.hidden, self.shape.fmt, self.chunks
+        Mc = self.M // C
+        c_h, cs = self.comm.handle, self.comm_stream
+        first = True
+        for w in self.w:
+            for half in (0, 1):
+                for c in range(C):
+                    hp = h.ptr + c * Mc * H * 4
+                    xn = self.xn.ptr + c * Mc * H * 2
+                    if not first:  # this chunk's previous allreduce is done before its rows are read again
+                        check(L.yah_stream_wait_event(stream, self.ev_red[c].handle))
+                    check(L.yah_rmsnorm(hp, H, Mc, H, NORM_EPS, NORM_GAIN, xn, H, stream))
+                    if half == 0:
+                        qkv = self.qkv.ptr + c * Mc * self.qkv_r * 2
+                        check(L.yah_tp_linear_col(c_h, w["qkv"].ptr, fmt, self.qkv_r, H, self.row_bytes["qkv"], xn,
+                                                  Mc, H, qkv, F16, self.qkv_r, EPI_STORE, None, 0, stream))
+                        self._row_parallel("o", w["o"], self.q_r, qkv, self.qkv_r, hp, Mc, stream)
+                    else:
+                        g = self.g.ptr + c * Mc * self.ff_r * 4
+                        act = self.act.ptr + c * Mc * self.ff_r * 2
+                        check(L.yah_tp_linear_col(c_h, w["gate"].ptr, fmt, self.ff_r, H, self.row_bytes["gate"], xn,
+                                                  Mc, H, g, F32, self.ff_r, EPI_STORE, None, 0, stream))
+                        check(L.yah_tp_linear_col(c_h, w["up"].ptr, fmt, self.ff_r, H, self.row_bytes["up"], xn, Mc,
+                                                  H, act, F16, self.ff_r, EPI_SWIGLU, g, self.ff_r, stream))
+                        self._row_parallel("down", w["down"], self.ff_r, act, self.ff_r, hp, Mc, stream)
+                    self.ev_gemm[c].record(stream)
+                    cs.wait(self.ev_gemm[c])
+                    check(L.yah_tp_allreduce_f32(c_h, hp, Mc * H, cs.handle))
+                    self.ev_red[c].record(cs.handle)
+                first = False
+        for c in range(C):
+            check(L.yah_stream_wait_event(stream, self.ev_red[c].handle))
+
     def close(self):
         for w in self.w:
             for b in w.values():
                 b.close()
         for b in (self.xn, self.qkv, self.g, self.act):
             b.close()
+        if self.chunks > 1:
+            for e in self.ev_gemm + self.ev_red:
+                e.close()
+            self.comm_stream.close()
