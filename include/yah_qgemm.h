@@ -107,6 +107,12 @@ int yah_set_launch_overlap(int on);
  * concurrently with these kernels (the tensor-parallel stack overlaps its allreduces with the next token chunk's
  * GEMMs) leaves the remaining SMs to the collectives' kernels, which otherwise wait for a persistent GEMM to end. */
 int yah_set_sm_budget(int sms);
+/* Self-test of the failure path (no counterpart in the reference): a one-warp kernel waits on an mbarrier that
+ * nothing arrives on, through the same bounded wait every kernel here uses, with a budget of `budget_cycles` SM
+ * cycles (1000 .. 2^31). The wait runs out, the kernel records its code in the device status word and returns; the
+ * call synchronises, reports the code (1 = a consumer's wait for data ran out) and clears the word. The device
+ * stays usable: no trap, no fault. */
+int yah_selftest_bounded_wait(int64_t budget_cycles, int* code);
 /* Make `stream` wait for the last work recorded on `event` (cudaStreamWaitEvent). */
 int yah_stream_wait_event(void* stream, void* event);
 /* Read and clear the current device's kernel status word: 0, or the code of a bounded wait that ran out

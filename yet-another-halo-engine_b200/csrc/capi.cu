@@ -13,6 +13,7 @@
 
 #include "../../include/yah_qgemm.h"
 #include "kernels.h"
+#include "ptx.cuh"
 
 namespace {
 
@@ -350,6 +351,36 @@ int yah_set_sm_budget(int sms) {
 int yah_stream_wait_event(void* stream, void* event) {
   if (!event) return fail(YAH_ERR_ARG, "null event");
   CK(cudaStreamWaitEvent((cudaStream_t)stream, (cudaEvent_t)event, 0));
+  return YAH_OK;
+}
+
+namespace {
+// Self-test of the failure path: one warp waits on an mbarrier that nothing arrives on, through the kernels' own
+// bounded wait with a short budget, so the wait runs out, records kStatusTimeoutFull in the status word and returns.
+__global__ void selftest_wait_kernel(int* status, long long budget) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    yah::mbar_init(&bar, 1);
+    yah::fence_barrier_init();
+  }
+  __syncthreads();
+  yah::mbar_wait(&bar, 0, status, yah::kStatusTimeoutFull, false, budget);
+}
+}  // namespace
+
+int yah_selftest_bounded_wait(int64_t budget_cycles, int* code) {
+  if (!code) return fail(YAH_ERR_ARG, "null code");
+  if (budget_cycles < 1000 || budget_cycles > (int64_t(1) << 31))
+    return fail(YAH_ERR_ARG, "budget %lld cycles outside [1000, 2^31]", (long long)budget_cycles);
+  DevState* s;
+  int rc = dev_state(&s);
+  if (rc) return rc;
+  CK(cudaMemset(s->status, 0, sizeof(int)));
+  selftest_wait_kernel<<<1, 32>>>(s->status, (long long)budget_cycles);
+  CK(cudaGetLastError());
+  CK(cudaDeviceSynchronize());
+  CK(cudaMemcpy(code, s->status, sizeof(int), cudaMemcpyDeviceToHost));
+  CK(cudaMemset(s->status, 0, sizeof(int)));
   return YAH_OK;
 }
 

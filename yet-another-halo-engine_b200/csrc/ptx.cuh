@@ -62,14 +62,14 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // runs out, or (honor_status) as soon as another role has reported a failure, so that every role leaves its loop
 // in bounded time. Exit drains pass honor_status = false: they wait for their own in-flight work either way.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code,
-                                          bool honor_status = true) {
+                                          bool honor_status = true, long long budget = kWaitBudgetCycles) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((it & 63) == 0) {
       if (honor_status && *(volatile int*)status != 0) return false;
-      if (clock64() - t0 > kWaitBudgetCycles) {
+      if (clock64() - t0 > budget) {
         set_status(status, code);
         return false;
       }
