@@ -4,13 +4,15 @@
 Workloads (--workload):
   gemm   (default) BASELINE config 2: Q4_K prefill tile GEMM, M=2048 tokens, K=4096, N=14336, f16 out; TFLOP/s.
   gemv   BASELINE config 3 decode GEMV: Q4_K 4096 x 14336 weights, M tokens (--tokens, default 1); HBM GB/s.
+  lmhead BASELINE config 5: Q6_K lm head, 128256 x 4096 weights (431 MB); --tokens <= 32: decode GEMV, HBM GB/s;
+         above: prefill GEMM, TFLOP/s.
   stack  BASELINE config 4: the Llama-shaped Q4_K linear stack (32 layers, hidden 4096, QKV 6144, FF 14336) over
          M=4096 tokens, tensor-parallel over the N GPUs (column-parallel QKV/gate/up, row-parallel o_proj/down with
          one NCCL allreduce each; yet-another-halo-engine_b200/tp.py); TFLOP/s of the whole job, strong scaling.
 A step is one launch of the kernel over one batch. Inputs are resident in HBM when the timed region starts; the
 step rotates through input copies whose total exceeds L2 (126 MB), so no step reads inputs another step left in
 L2. Timing: W warm-up steps, then exactly K steps between a barrier + device synchronise on both sides, CUDA
-events on the launching stream, max over ranks; gemm / gemv replay the K steps as one CUDA graph. `e2e` repeats
+events on the launching stream, max over ranks; gemm / gemv / lmhead replay the K steps as one CUDA graph. `e2e` repeats
 the metric through the public API with pinned host buffers: every step copies its activations host->device and its
 output device->host inside the timed region.
 
@@ -128,12 +130,20 @@ def cpu_cores():
 
 
 # ------------------------------------------------------------------------------------------------ workloads
-def gemm_workload(args):
-    return dict(name="q4k_prefill_gemm", fmt=12, M=2048, K=4096, N=14336, out="f16")
-
-
-def gemv_workload(args):
-    return dict(name="q4k_decode_gemv", fmt=12, M=args.tokens, K=14336, N=4096, out="f32")
+def workload_of(args):
+    """The single-kernel workloads: config 2 (Q4_K gate/up prefill GEMM), config 3 (Q4_K down decode GEMV at
+    --tokens), config 5 (Q6_K lm head, 128256 x 4096: decode GEMV for --tokens <= 32, prefill GEMM above)."""
+    if args.workload == "gemv":
+        return dict(name="q4k_decode_gemv", fmt=12, fmt_name="Q4_K", M=args.tokens, K=14336, N=4096, out="f32",
+                    gemv=True, metric=f"Q4_K decode GEMV HBM GB/s (M={args.tokens})")
+    if args.workload == "lmhead":
+        gemv = args.tokens <= 32
+        return dict(name="q6k_lm_head_" + ("decode_gemv" if gemv else "prefill_gemm"), fmt=14, fmt_name="Q6_K",
+                    M=args.tokens, K=4096, N=128256, out="f32" if gemv else "f16", gemv=gemv,
+                    metric=(f"Q6_K lm-head decode GEMV HBM GB/s (M={args.tokens})" if gemv
+                            else f"Q6_K lm-head prefill TFLOP/s (M={args.tokens})"))
+    return dict(name="q4k_prefill_gemm", fmt=12, fmt_name="Q4_K", M=2048, K=4096, N=14336, out="f16", gemv=False,
+                metric="Q4_K dequant-GEMM prefill TFLOP/s")
 
 
 def run_ours(args, dist, rank, local_rank):
@@ -141,9 +151,9 @@ def run_ours(args, dist, rank, local_rank):
     pkg = ge.load_package()
     F, ops = pkg.formats, pkg.ops
     dev = pkg.Device(local_rank)
-    wl = gemv_workload(args) if args.workload == "gemv" else gemm_workload(args)
+    wl = workload_of(args)
     t, M, K, N = wl["fmt"], wl["M"], wl["K"], wl["N"]
-    gemv = args.workload == "gemv"
+    gemv = wl["gemv"]
     w = F.synth_weights(t, N, K, seed=0)
     x = F.synth_activations(M, K, seed=1 + rank)
     wbytes, xbytes = w.nbytes, x.nbytes
@@ -226,7 +236,7 @@ def run_ours(args, dist, rank, local_rank):
     if gemv:
         alg_bytes = wbytes + xbytes + ybytes
         value = world * alg_bytes / (per_step_ms * 1e-3) / 1e9
-        unit, metric = "GB/s", f"Q4_K decode GEMV HBM GB/s (M={M})"
+        unit, metric = "GB/s", wl["metric"]
         achieved = alg_bytes / (ms_local / args.steps * 1e-3) / 1e9
         roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                 "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": None, "peak_src": pk["src"],
@@ -235,7 +245,7 @@ def run_ours(args, dist, rank, local_rank):
     else:
         flops = 2.0 * M * N * K
         value = world * flops / (per_step_ms * 1e-3) / 1e12
-        unit, metric = "TFLOP/s", "Q4_K dequant-GEMM prefill TFLOP/s"
+        unit, metric = "TFLOP/s", wl["metric"]
         achieved = flops / (ms_local / args.steps * 1e-3) / 1e12
         roof = {"bound": "tensor", "achieved": round(achieved, 1), "peak": pk["tflops"], "unit": "TFLOP/s",
                 "frac": round(achieved / pk["tflops"], 4), "traffic": None, "peak_src": pk["src"],
@@ -248,8 +258,9 @@ def run_ours(args, dist, rank, local_rank):
     line = {
         "metric": metric, "value": round(value, 2), "unit": unit, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(per_step_ms, 5), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f16 x GGUF-Q4_K -> f32 acc", "data": "synthetic",
-        "config": {"workload": wl["name"], "M_tokens": M, "K": K, "N": N, "weight_format": "Q4_K",
+        "scaling": "weak", "vs_baseline": None, "dtype": f"f16 x GGUF-{wl['fmt_name']} -> f32 acc",
+        "data": "synthetic",
+        "config": {"workload": wl["name"], "M_tokens": M, "K": K, "N": N, "weight_format": wl["fmt_name"],
                    "out_dtype": wl["out"], "parallelism": f"replicas x{world}",
                    "launch_overlap": bool(args.launch_overlap),
                    "l2": f"rotating {copies} input copies ({copies * per_copy / 2**20:.0f} MiB > L2)"},
@@ -393,7 +404,7 @@ def cpu_reference_step(fmt, w, x, K, use_gguf=True):
 
 def cpu_baseline(args, seconds=10.0):
     """The CPU path timed on a bounded sample (rows of the weight) for the same metric."""
-    wl = gemv_workload(args) if args.workload == "gemv" else gemm_workload(args)
+    wl = workload_of(args)
     import __graft_entry__ as ge
     F = ge.load_package().formats
     t, M, K, N = wl["fmt"], wl["M"], wl["K"], wl["N"]
@@ -414,7 +425,7 @@ def cpu_baseline(args, seconds=10.0):
         if el >= seconds or n >= 50:
             break
     per = el / n
-    if args.workload == "gemv":
+    if wl["gemv"]:
         val = (w.nbytes + x.nbytes + M * rows * 4) / per / 1e9
         unit = "GB/s"
     else:
@@ -429,7 +440,7 @@ def cpu_baseline(args, seconds=10.0):
 def run_reference(args, rank):
     if rank != 0:
         return None
-    wl = gemv_workload(args) if args.workload == "gemv" else gemm_workload(args)
+    wl = workload_of(args)
     import __graft_entry__ as ge
     F = ge.load_package().formats
     t, M, K, N = wl["fmt"], wl["M"], wl["K"], wl["N"]
@@ -448,19 +459,18 @@ def run_reference(args, rank):
         cpu_reference_step(t, w, x, K, use_gguf)
     el = time.perf_counter() - t0
     per = el / args.steps
-    if args.workload == "gemv":
+    metric = wl["metric"]
+    if wl["gemv"]:
         val, unit = (w.nbytes + x.nbytes + M * rows * 4) / per / 1e9, "GB/s"
-        metric = f"Q4_K decode GEMV HBM GB/s (M={M})"
     else:
         val, unit = 2.0 * M * rows * K / per / 1e12, "TFLOP/s"
-        metric = "Q4_K dequant-GEMM prefill TFLOP/s"
     sample = (f"{'gguf-py dequantize' if use_gguf else 'oracle C dequant'} + numpy f32 matmul of {rows} of {N} "
               f"weight rows x {M} tokens x K={K} per step")
     return {"impl": "reference", "metric": metric, "value": round(val, 5), "unit": unit,
             "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(per * 1e3, 3), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f16 weights (dequantised) x f16 -> f32", "data": "synthetic",
-            "config": {"workload": wl["name"], "M_tokens": M, "K": K, "N": N, "weight_format": "Q4_K"},
+            "config": {"workload": wl["name"], "M_tokens": M, "K": K, "N": N, "weight_format": wl["fmt_name"]},
             "cpu_baseline": {"value": round(val, 5), "unit": unit, "cores": cpu_cores(), "kind": kind,
                              "sample": sample},
             "e2e": {"value": round(val, 5), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -472,7 +482,7 @@ def main():
     ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="gemm", choices=["gemm", "gemv", "stack"])
+    ap.add_argument("--workload", default="gemm", choices=["gemm", "gemv", "lmhead", "stack"])
     ap.add_argument("--layers", type=int, default=32, help="stack layers")
     ap.add_argument("--stack-tokens", type=int, default=4096, help="stack tokens M")
     ap.add_argument("--stack-chunks", type=int, default=1,

@@ -98,6 +98,14 @@ int yah_stream_begin_capture(void* stream);
 int yah_stream_end_capture(void* stream, void** graph_exec);
 int yah_graph_launch(void* graph_exec, void* stream);
 int yah_graph_destroy(void* graph_exec);
+/* Row realignment at load time. TMA copies need 16-byte aligned row starts, but a GGUF tensor's rows are packed:
+ * Q6_K rows of K = 5120 (the reference's lm head, yah_gemv_q6k_f32.loom:1-16) are 4200 bytes. A loader copies such a
+ * tensor once into rows `dst_stride` bytes apart (a multiple of 16, >= row_bytes; e.g. 4208) and passes that stride
+ * as w_row_stride; the blocks inside a row are untouched. Stream-ordered device-to-device copy; dst 16-byte aligned.
+ * Replaces: the byte-offset tensor view of the reference loader (engine/model/weights.hpp:142-152), which needs no
+ * alignment on its hardware. */
+int yah_realign_rows(const void* src, int64_t rows, int64_t row_bytes, int64_t src_stride, void* dst,
+                     int64_t dst_stride, void* stream);
 /* Programmatic dependent launch of the decode GEMV (on by default). A GEMV launch may then begin while the kernel
  * before it on the stream is finishing: it streams its weight tensor early and reads its activations, and writes
  * its outputs, only after that kernel has completed. Contract: no kernel still in flight on the stream writes the

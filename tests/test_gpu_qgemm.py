@@ -192,3 +192,16 @@ def test_q6k_unaligned_rows_are_refused(pkg, F, dev):
 
 def test_status_word_clear(pkg, dev):
     assert dev.status_word() == 0
+
+
+def test_q6k_lm_head_k5120_prefill_realigned(pkg, F, O, dev):
+    """Prefill GEMM on the K = 5120 Q6_K lm head after row realignment (4200 -> 4208-byte stride)."""
+    t = F.Q6_K
+    N, K, M = 2048, 5120, 256
+    w = F.synth_weights(t, N, K, seed=53)
+    wd, stride = pkg.ops.realign(dev, w)
+    x = F.synth_activations(M, K, seed=54)
+    y = pkg.ops.qgemm(dev, wd, t, x, N=N, K=K, w_row_stride=stride)
+    e = O.errors(y, O.gemm_ref(O.dequant_f16(t, w, N, K), x))
+    assert e["finite"] and e["max_abs"] <= 2e-2 and e["rel_fro"] <= 1e-3, e
+    wd.close()

@@ -163,3 +163,19 @@ def test_qgemv_q4k_one_token(pkg, F, O, dev, N, K, kind, out):
         assert e["rel_fro"] <= 1e-3 and (np.abs(y16 - acc) <= 2e-2 + O.f16_half_ulp(acc)).all()
     else:
         check(O, pkg.ops.qgemv(dev, w, t, x, N=N, K=K), acc)
+
+
+@pytest.mark.parametrize("M", [1, 8, 32])
+def test_q6k_lm_head_k5120_realigned(pkg, F, O, dev, M):
+    """The reference's Q6_K lm head has K = 5120: packed rows of 4200 bytes, not 16-byte aligned. Rows realigned
+    once to a 4208-byte stride (yah_realign_rows; blocks untouched) run through the decode GEMV unchanged."""
+    t = F.Q6_K
+    N, K = 2048, 5120
+    w = F.synth_weights(t, N, K, seed=51)
+    assert w.shape[1] == 4200
+    wd, stride = pkg.ops.realign(dev, w)
+    assert stride == 4208
+    x = F.synth_activations(M, K, seed=52 + M)
+    y = pkg.ops.qgemv(dev, wd, t, x, N=N, K=K, w_row_stride=stride)
+    check(O, y, O.gemm_ref(O.dequant_f32(t, w, N, K), x))
+    wd.close()

@@ -342,6 +342,20 @@ int yah_set_launch_overlap(int on) {
   return YAH_OK;
 }
 
+int yah_realign_rows(const void* src, int64_t rows, int64_t row_bytes, int64_t src_stride, void* dst,
+                     int64_t dst_stride, void* stream) {
+  if (!src || !dst) return fail(YAH_ERR_ARG, "null pointer");
+  if (rows < 0 || row_bytes <= 0 || src_stride < row_bytes || dst_stride < row_bytes)
+    return fail(YAH_ERR_ARG, "bad sizes: rows %lld, row bytes %lld, strides %lld / %lld", (long long)rows,
+                (long long)row_bytes, (long long)src_stride, (long long)dst_stride);
+  if (!aligned16(dst) || dst_stride % 16)
+    return fail(YAH_ERR_ARG, "the destination rows must start 16-byte aligned (stride %lld)", (long long)dst_stride);
+  if (rows == 0) return YAH_OK;
+  CK(cudaMemcpy2DAsync(dst, (size_t)dst_stride, src, (size_t)src_stride, (size_t)row_bytes, (size_t)rows,
+                       cudaMemcpyDeviceToDevice, (cudaStream_t)stream));
+  return YAH_OK;
+}
+
 int yah_set_sm_budget(int sms) {
   if (sms < 0) return fail(YAH_ERR_ARG, "SM budget %d < 0", sms);
   g_sm_budget.store(sms, std::memory_order_relaxed);

@@ -130,6 +130,24 @@ def qgemv(dev: Device, w, fmt, x, N=None, K=None, kind="plain", out_dtype="f32",
                  w_row_stride=w_row_stride, gemv=True)
 
 
+def realign(dev: Device, w, stride: int | None = None, stream=None):
+    """Copy GGUF rows (numpy [N][row_bytes] or a DeviceBuffer of packed rows) into rows `stride` bytes apart
+    (default: row_bytes rounded up to 16), as TMA needs; returns (DeviceBuffer, stride). For tensors whose packed
+    rows are not 16-byte multiples, e.g. Q6_K at K = 5120 (4200-byte rows)."""
+    src = _as_dev(dev, w)
+    rows, row_bytes = (w.shape[0], w.shape[1]) if isinstance(w, np.ndarray) else (None, None)
+    if rows is None:
+        raise ValueError("pass the host array (its shape gives rows and row bytes)")
+    stride = stride or (row_bytes + 15) // 16 * 16
+    dst = dev.empty(rows * stride)
+    check(lib().yah_realign_rows(src.ptr, rows, row_bytes, row_bytes, dst.ptr, stride, stream))
+    if stream is None:
+        dev.synchronize()
+    if src is not w:
+        src.close()
+    return dst, stride
+
+
 def dequant(dev: Device, w, fmt, N=None, K=None, kb_off=0, w_row_stride=None) -> np.ndarray:
     """f16 [N][K] of GGUF rows w with the GEMM's decode (bit-exact to the reference dequant)."""
     t = F.type_of(fmt)
