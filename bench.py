@@ -293,17 +293,21 @@ def run_stack(args, dist, rank, local_rank):
     # weights it reads in L2.
     p = world
     sets = []
+    # The speed mode's f16 partial sums overflow with the BASELINE weight distribution (layer outputs ~1e5-1e6), so
+    # it runs on weights whose d and dmin are scaled by 2^-8 (same bytes and work; reported in `data`).
+    scale = (lambda w: F.scale_q4k_d(w, 1 / 256)) if args.stack_mode == "speed" else (lambda w: w)
     for k in range(min(4, shape.layers)):
         s0 = 5000 + 64 * k + 8 * rank
-        sets.append({"qkv": F.synth_weights(shape.fmt, shape.qkv // p, H, seed=s0),
-                     "o": F.synth_weights(shape.fmt, H, shape.n_q * shape.head_dim // p, seed=s0 + 1),
-                     "gate": F.synth_weights(shape.fmt, shape.ff // p, H, seed=s0 + 2),
-                     "up": F.synth_weights(shape.fmt, shape.ff // p, H, seed=s0 + 3),
-                     "down": F.synth_weights(shape.fmt, H, shape.ff // p, seed=s0 + 4)})
+        sets.append({"qkv": scale(F.synth_weights(shape.fmt, shape.qkv // p, H, seed=s0)),
+                     "o": scale(F.synth_weights(shape.fmt, H, shape.n_q * shape.head_dim // p, seed=s0 + 1)),
+                     "gate": scale(F.synth_weights(shape.fmt, shape.ff // p, H, seed=s0 + 2)),
+                     "up": scale(F.synth_weights(shape.fmt, shape.ff // p, H, seed=s0 + 3)),
+                     "down": scale(F.synth_weights(shape.fmt, H, shape.ff // p, seed=s0 + 4))})
     chunks = args.stack_chunks
     if chunks > 1:
         pkg.lib().yah_set_sm_budget(dev.sm_count - args.stack_nccl_sms)
-    stack = tp.LlamaStack(dev, comm, shape, [sets[i % len(sets)] for i in range(shape.layers)], M, chunks=chunks)
+    stack = tp.LlamaStack(dev, comm, shape, [sets[i % len(sets)] for i in range(shape.layers)], M, chunks=chunks,
+                          mode=args.stack_mode)
     h0 = np.random.default_rng(7).standard_normal((M, H)).astype(np.float32)
     h0d, h = dev.upload(h0), dev.empty(M * H * 4)
     stream = pkg.Stream()
@@ -361,6 +365,7 @@ def run_stack(args, dist, rank, local_rank):
         "dtype": "f16 x GGUF-Q4_K -> f32 acc, f32 residual stream and allreduce", "data": "synthetic",
         "config": {"workload": "q4k_layer_stack_tp", "layers": shape.layers, "hidden": H, "qkv": shape.qkv,
                    "ff": shape.ff, "M_tokens": M, "parallelism": f"tp{world}", "token_chunks": chunks,
+                   "partial_sums": "f32 (parity mode)" if args.stack_mode == "parity" else "f16 (speed mode)",
                    "gemm_sms": (dev.sm_count - args.stack_nccl_sms) if chunks > 1 else dev.sm_count,
                    "l2": "4 distinct weight sets cycled over the layers (> L2 per GPU at tp1)"},
         "e2e": {"value": round(flops / (ms_e2e / args.steps * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
@@ -488,6 +493,8 @@ def main():
     ap.add_argument("--stack-chunks", type=int, default=1,
                     help="token chunks pipelined over a compute and a communication stream (measured slower at tp1 "
                          "and tp2 on B200: the smaller GEMMs lose more than the overlapped allreduces gain)")
+    ap.add_argument("--stack-mode", default="parity", choices=["parity", "speed"],
+                    help="row-parallel partial sums in f32 (parity) or f16 (speed: half the allreduce bytes)")
     ap.add_argument("--stack-nccl-sms", type=int, default=8,
                     help="SMs left to NCCL while chunked GEMMs run (the GEMMs' SM budget is the rest)")
     ap.add_argument("--tile-table", default=None, help="tile table (tune.py output) installed before the run")

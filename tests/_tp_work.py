@@ -70,7 +70,7 @@ def cpu_shard_worker(rank, world, port, out_q):
         dist.destroy_process_group()
 
 
-def gpu_stack_worker(rank, world, id_q, out_q):
+def gpu_stack_worker(rank, world, id_q, out_q, mode="parity"):
     """NCCL rank on GPU `rank`: the small stack sharded over `world` ranks vs the float64 reference."""
     import __graft_entry__ as ge
     from oracle import oracle as O
@@ -90,7 +90,9 @@ def gpu_stack_worker(rank, world, id_q, out_q):
 
     comm = tp.Comm(world, rank, exchange)
     full = [tp.layer_weights(shape, i) for i in range(shape.layers)]
-    stack = tp.LlamaStack(dev, comm, shape, [tp.shard_layer(shape, f, world, rank) for f in full], M)
+    if mode == "speed":  # f16 partial sums need weights whose layer outputs fit f16 (d, dmin scaled by 2^-6)
+        full = [{k: pkg.formats.scale_q4k_d(v, 1 / 64) for k, v in f.items()} for f in full]
+    stack = tp.LlamaStack(dev, comm, shape, [tp.shard_layer(shape, f, world, rank) for f in full], M, mode=mode)
     h0 = np.random.default_rng(72).standard_normal((M, shape.hidden)).astype(np.float32)
     h = dev.upload(h0)
     stack.forward(h)

@@ -114,6 +114,17 @@ def synth_weights(fmt, N: int, K: int, seed: int = 0) -> np.ndarray:
     return {Q8_0: synth_q8_0, Q4_K: synth_q4_k, Q6_K: synth_q6_k}[t](N, K, seed)
 
 
+def scale_q4k_d(w: np.ndarray, factor: float) -> np.ndarray:
+    """Q4_K rows with every super-block's d and dmin multiplied by `factor` (a power of two keeps them exact unless
+    they become f16 subnormals); returns a copy. The BASELINE distribution (d ~ |N(0, 0.01)|, non-negative nibbles)
+    gives layer outputs of ~1e5-1e6 in the synthetic stack, beyond f16; scaled weights keep a stack's f16 partial
+    sums finite."""
+    out = np.array(w, copy=True)
+    hdr = out.reshape(out.shape[0], -1, 144)[:, :, :4]
+    hdr[...] = (hdr.copy().view(np.float16) * np.float16(factor)).view(np.uint8)
+    return out
+
+
 def synth_activations(M: int, K: int, seed: int = 1) -> np.ndarray:
     """f16 [M][K] activations ~ N(0, 1) (one draw of M*K f32 normals, rounded to f16)."""
     rng = np.random.default_rng(seed)

@@ -18,7 +18,9 @@ Per layer (attention replaced by identity, so the o_proj input is the rank's que
     a   = silu(g) * (xn Wu_r^T)           f16 (the GEMM's swiglu epilogue)
     h   = h + allreduce(a Wd_r^T)
 
-The residual stream h is f32 [M][hidden] on every rank. The reference normalises every layer input
+Modes of the row-parallel partial sums: parity (f32 partials, rank 0's GEMM adds the residual, f32 allreduce) and
+speed (f16 partials from every rank's GEMM with no residual read, f16 allreduce, the sum added into the f32 residual
+stream by the next norm's pass). The residual stream h is f32 [M][hidden] on every rank in both. The reference normalises every layer input
 (docs/architecture.md:68); the fixed gain keeps silu(gate) * up inside the f16 range with the synthetic weights.
 """
 from __future__ import annotations
@@ -167,10 +169,15 @@ class LlamaStack:
     row-wise in the tokens, so chunks are independent until the end). Run it with an SM budget
     (yah_set_sm_budget) below the device's SM count so that NCCL's kernels find free SMs while a GEMM runs."""
 
-    def __init__(self, dev: Device, comm: Comm, shape: StackShape, shards: list, M: int, chunks: int = 1):
+    def __init__(self, dev: Device, comm: Comm, shape: StackShape, shards: list, M: int, chunks: int = 1,
+                 mode: str = "parity"):
         if chunks < 1 or M % chunks:
             raise ValueError(f"{M} tokens do not split into {chunks} chunks")
-        self.dev, self.comm, self.shape, self.M, self.chunks = dev, comm, shape, M, chunks
+        if mode not in ("parity", "speed"):
+            raise ValueError(f"mode {mode!r}: parity (f32 partial sums) or speed (f16 partial sums)")
+        if mode == "speed" and chunks != 1:
+            raise ValueError("the speed mode runs unchunked")
+        self.dev, self.comm, self.shape, self.M, self.chunks, self.mode = dev, comm, shape, M, chunks, mode
         p = comm.nranks
         self.q_r = shape.n_q * shape.head_dim // p
         self.qkv_r = shape.qkv // p
@@ -182,6 +189,7 @@ class LlamaStack:
         self.qkv = dev.empty(M * self.qkv_r * 2)
         self.g = dev.empty(M * self.ff_r * 4)
         self.act = dev.empty(M * self.ff_r * 2)
+        self.part = dev.empty(M * H * 2) if mode == "speed" else None  # f16 partial sums of the speed mode
         if chunks > 1:
             self.comm_stream = Stream()
             self.ev_gemm = [Event() for _ in range(chunks)]
@@ -189,13 +197,16 @@ class LlamaStack:
 
     @property
     def launches_per_forward(self) -> int:
-        """Library kernel launches per forward pass (2 norms + 5 linears per layer and token chunk)."""
-        return 7 * self.shape.layers * self.chunks
+        """Library kernel launches per forward pass (2 norms + 5 linears per layer and token chunk; the speed mode
+        adds the final add)."""
+        return 7 * self.shape.layers * self.chunks + (1 if self.mode == "speed" else 0)
 
     def forward(self, h: DeviceBuffer, stream=None):
         """h (f32 [M][hidden], the residual stream, identical on every rank) is updated in place."""
         if self.chunks > 1:
             return self._forward_chunked(h, stream)
+        if self.mode == "speed":
+            return self._forward_speed(h, stream)
         L, s, M, H, fmt = lib(), self.shape, self.M, self.shape.hidden, self.shape.fmt
         c = self.comm.handle
         for w in self.w:
@@ -221,6 +232,40 @@ class LlamaStack:
         fn = L.yah_qgemv if Mc <= 32 else L.yah_qgemm
         check(fn(w.ptr, fmt, H, K_r, self.row_bytes[name], 0, x_ptr, Mc, ldx, h_ptr, F32, H,
                  EPI_RESID if r0 else EPI_STORE, h_ptr if r0 else None, H if r0 else 0, stream))
+
+    def _forward_speed(self, h: DeviceBuffer, stream):
+        """Speed mode: the row-parallel GEMMs write f16 partial sums (no residual read), the allreduce moves f16
+        (half the bytes), and the sum is added into the f32 residual stream by the next norm's pass
+        (yah_add_rmsnorm); the last layer's sum by an add-only pass."""
+        L, M, H, fmt = lib(), self.M, self.shape.hidden, self.shape.fmt
+        c, part = self.comm.handle, self.part.ptr
+        pending = False
+        fn = L.yah_qgemv if M <= 32 else L.yah_qgemm
+
+        def norm():
+            if pending:
+                check(L.yah_add_rmsnorm(h.ptr, H, part, H, M, H, NORM_EPS, NORM_GAIN, self.xn.ptr, H, stream))
+            else:
+                check(L.yah_rmsnorm(h.ptr, H, M, H, NORM_EPS, NORM_GAIN, self.xn.ptr, H, stream))
+
+        for w in self.w:
+            norm()
+            check(L.yah_tp_linear_col(c, w["qkv"].ptr, fmt, self.qkv_r, H, self.row_bytes["qkv"], self.xn.ptr, M, H,
+                                      self.qkv.ptr, F16, self.qkv_r, EPI_STORE, None, 0, stream))
+            check(fn(w["o"].ptr, fmt, H, self.q_r, self.row_bytes["o"], 0, self.qkv.ptr, M, self.qkv_r, part, F16, H,
+                     EPI_STORE, None, 0, stream))
+            check(L.yah_tp_allreduce_f16(c, part, M * H, stream))
+            pending = True
+            norm()
+            check(L.yah_tp_linear_col(c, w["gate"].ptr, fmt, self.ff_r, H, self.row_bytes["gate"], self.xn.ptr, M, H,
+                                      self.g.ptr, F32, self.ff_r, EPI_STORE, None, 0, stream))
+            check(L.yah_tp_linear_col(c, w["up"].ptr, fmt, self.ff_r, H, self.row_bytes["up"], self.xn.ptr, M, H,
+                                      self.act.ptr, F16, self.ff_r, EPI_SWIGLU, self.g.ptr, self.ff_r, stream))
+            check(fn(w["down"].ptr, fmt, H, self.ff_r, self.row_bytes["down"], 0, self.act.ptr, M, self.ff_r, part,
+                     F16, H, EPI_STORE, None, 0, stream))
+            check(L.yah_tp_allreduce_f16(c, part, M * H, stream))
+        if pending:
+            check(L.yah_add_rmsnorm(h.ptr, H, part, H, M, H, NORM_EPS, NORM_GAIN, None, 0, stream))
 
     def _forward_chunked(self, h: DeviceBuffer, stream):
         L, s, H, fmt, C = lib(), self.shape, self.shape.hidden, self.shape.fmt, self.chunks
@@ -260,7 +305,7 @@ class LlamaStack:
         for w in self.w:
             for b in w.values():
                 b.close()
-        for b in (self.xn, self.qkv, self.g, self.act):
+        for b in (self.xn, self.qkv, self.g, self.act) + ((self.part,) if self.part else ()):
             b.close()
         if self.chunks > 1:
             for e in self.ev_gemm + self.ev_red:
