@@ -250,11 +250,11 @@ int yah_tp_linear_row(yah_tp_comm* comm, const void* w_shard, int ggml_type, int
  * weightless, with one gain (H and strides multiples of 4, h 16-byte and out 8-byte aligned). */
 int yah_rmsnorm(const float* h, int64_t ldh, int64_t M, int64_t H, float eps, float gain, void* out, int64_t ldo,
                 void* stream);
-/* Speed mode of the row-parallel linears (f16 partial sums): h += d (d f16 [M][ldd], the allreduced partials, added
- * in f32 and stored back to h), then, when out is not null, out = f16 RMSNorm of the new h as yah_rmsnorm. One pass
- * over h instead of an add kernel and a norm kernel. */
-int yah_add_rmsnorm(float* h, int64_t ldh, const void* d, int64_t ldd, int64_t M, int64_t H, float eps, float gain,
-                    void* out, int64_t ldo, void* stream);
+/* The residual update of the row-parallel linears: h += d (d [M][ldd] of d_dtype YAH_F16 or YAH_F32, the allreduced
+ * partial sums, added in f32 and stored back to h), then, when out is not null, out = f16 RMSNorm of the new h as
+ * yah_rmsnorm. One pass over h instead of an add kernel and a norm kernel. */
+int yah_add_rmsnorm(float* h, int64_t ldh, const void* d, int d_dtype, int64_t ldd, int64_t M, int64_t H, float eps,
+                    float gain, void* out, int64_t ldo, void* stream);
 /* ncclAllReduce(sum) of f16 in place (the speed mode's partials: half the bytes of yah_tp_allreduce_f32). */
 int yah_tp_allreduce_f16(yah_tp_comm* comm, void* buf, int64_t count, void* stream);
 

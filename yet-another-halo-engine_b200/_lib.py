@@ -49,7 +49,7 @@ SYMBOLS = {
     "yah_graph_destroy": (c_int, [c_vp]),
     "yah_set_launch_overlap": (c_int, [c_int]),
     "yah_set_sm_budget": (c_int, [c_int]),
-    "yah_add_rmsnorm": (c_int, [c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_f, c_f, c_vp, c_i64, c_vp]),
+    "yah_add_rmsnorm": (c_int, [c_vp, c_i64, c_vp, c_int, c_i64, c_i64, c_i64, c_f, c_f, c_vp, c_i64, c_vp]),
     "yah_tp_allreduce_f16": (c_int, [c_vp, c_vp, c_i64, c_vp]),
     "yah_realign_rows": (c_int, [c_vp, c_i64, c_i64, c_i64, c_vp, c_i64, c_vp]),
     "yah_selftest_bounded_wait": (c_int, [c_i64, P(c_int)]),

@@ -55,23 +55,30 @@ int nccl_fail(ncclResult_t r, const char* what) {
   return set_error(YAH_ERR_NCCL, "%s: %s", what, nccl()->get_error_string ? nccl()->get_error_string(r) : "?");
 }
 
-// One row per CTA: out = f16(h * gain / sqrt(mean(h^2) + eps)). ADD: first h += d (d f16, the allreduced partial
-// sums of the speed mode), stored back to h in f32; NORM false: the add alone (the last layer's update).
+// One row per CTA: out = f16(h * gain / sqrt(mean(h^2) + eps)). ADD: first h += d (the allreduced partial sums,
+// f16 in the speed mode or f32 in the parity mode), stored back to h in f32; NORM false: the add alone (the last
+// layer's update).
 constexpr int kNormThreads = 256;
 
-template <bool ADD, bool NORM>
+template <bool ADD, bool NORM, bool DF16>
 __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(float* __restrict__ h, int64_t ldh, int H,
-                                                               const __half* __restrict__ d, int64_t ldd, float eps,
+                                                               const void* __restrict__ d, int64_t ldd, float eps,
                                                                float gain, __half* __restrict__ out, int64_t ldo) {
   float* row = h + (int64_t)blockIdx.x * ldh;
   float ss = 0.f;
   for (int i = 4 * threadIdx.x; i < H; i += 4 * kNormThreads) {
     float4 v = *reinterpret_cast<const float4*>(row + i);
     if (ADD) {
-      const uint2 dd = *reinterpret_cast<const uint2*>(d + (int64_t)blockIdx.x * ldd + i);
-      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&dd.x));
-      const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&dd.y));
-      v.x += a.x, v.y += a.y, v.z += b.x, v.w += b.y;
+      float4 a;
+      if (DF16) {
+        const uint2 dd = *reinterpret_cast<const uint2*>(static_cast<const __half*>(d) + (int64_t)blockIdx.x * ldd + i);
+        const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&dd.x));
+        const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&dd.y));
+        a = make_float4(lo.x, lo.y, hi.x, hi.y);
+      } else {
+        a = *reinterpret_cast<const float4*>(static_cast<const float*>(d) + (int64_t)blockIdx.x * ldd + i);
+      }
+      v.x += a.x, v.y += a.y, v.z += a.z, v.w += a.w;
       *reinterpret_cast<float4*>(row + i) = v;  // re-read below by this same thread
     }
     ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
@@ -196,29 +203,34 @@ int yah_rmsnorm(const float* h, int64_t ldh, int64_t M, int64_t H, float eps, fl
                                                "8-byte aligned out");
   if (M > 0x7fffffff) return yah::set_error(YAH_ERR_ARG, "M too large");
   if (M == 0) return YAH_OK;
-  yah::rmsnorm_kernel<false, true><<<(unsigned)M, yah::kNormThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+  yah::rmsnorm_kernel<false, true, true><<<(unsigned)M, yah::kNormThreads, 0, static_cast<cudaStream_t>(stream)>>>(
       const_cast<float*>(h), ldh, (int)H, nullptr, 0, eps, gain, static_cast<__half*>(out), ldo);
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? YAH_OK : yah::set_error(YAH_ERR_CUDA, "rmsnorm launch: %s", cudaGetErrorString(e));
 }
 
-int yah_add_rmsnorm(float* h, int64_t ldh, const void* d, int64_t ldd, int64_t M, int64_t H, float eps, float gain,
-                    void* out, int64_t ldo, void* stream) {
-  if (!h || !d || M < 0 || H <= 0) return yah::set_error(YAH_ERR_ARG, "bad add_rmsnorm arguments");
+int yah_add_rmsnorm(float* h, int64_t ldh, const void* d, int d_dtype, int64_t ldd, int64_t M, int64_t H, float eps,
+                    float gain, void* out, int64_t ldo, void* stream) {
+  if (!h || !d || M < 0 || H <= 0 || (d_dtype != YAH_F16 && d_dtype != YAH_F32))
+    return yah::set_error(YAH_ERR_ARG, "bad add_rmsnorm arguments");
+  const uintptr_t dalign = d_dtype == YAH_F16 ? 7 : 15;
   if (H % 4 || ldh % 4 || ldd % 4 || ldh < H || ldd < H || (reinterpret_cast<uintptr_t>(h) & 15) ||
-      (reinterpret_cast<uintptr_t>(d) & 7) || (out && (ldo % 4 || ldo < H || (reinterpret_cast<uintptr_t>(out) & 7))))
+      (reinterpret_cast<uintptr_t>(d) & dalign) ||
+      (out && (ldo % 4 || ldo < H || (reinterpret_cast<uintptr_t>(out) & 7))))
     return yah::set_error(YAH_ERR_UNSUPPORTED, "add_rmsnorm needs H and strides multiples of 4, 16-byte aligned h, "
-                                               "8-byte aligned d and out");
+                                               "d aligned to 4 of its elements, 8-byte aligned out");
   if (M > 0x7fffffff) return yah::set_error(YAH_ERR_ARG, "M too large");
   if (M == 0) return YAH_OK;
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const __half* dh = static_cast<const __half*>(d);
-  if (out)
-    yah::rmsnorm_kernel<true, true><<<(unsigned)M, yah::kNormThreads, 0, s>>>(h, ldh, (int)H, dh, ldd, eps, gain,
-                                                                              static_cast<__half*>(out), ldo);
-  else
-    yah::rmsnorm_kernel<true, false><<<(unsigned)M, yah::kNormThreads, 0, s>>>(h, ldh, (int)H, dh, ldd, eps, gain,
-                                                                               nullptr, 0);
+  __half* o = static_cast<__half*>(out);
+  const dim3 grid((unsigned)M), block(yah::kNormThreads);
+  if (d_dtype == YAH_F16) {
+    if (o) yah::rmsnorm_kernel<true, true, true><<<grid, block, 0, s>>>(h, ldh, (int)H, d, ldd, eps, gain, o, ldo);
+    else yah::rmsnorm_kernel<true, false, true><<<grid, block, 0, s>>>(h, ldh, (int)H, d, ldd, eps, gain, o, 0);
+  } else {
+    if (o) yah::rmsnorm_kernel<true, true, false><<<grid, block, 0, s>>>(h, ldh, (int)H, d, ldd, eps, gain, o, ldo);
+    else yah::rmsnorm_kernel<true, false, false><<<grid, block, 0, s>>>(h, ldh, (int)H, d, ldd, eps, gain, o, 0);
+  }
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? YAH_OK : yah::set_error(YAH_ERR_CUDA, "add_rmsnorm launch: %s", cudaGetErrorString(e));
 }

@@ -6,8 +6,8 @@ GPUs of one box, one process per GPU:
   * column-parallel QKV, gate, up: a rank holds a row range of the GGUF tensor (no re-quantisation; QKV in whole
     head groups, so the rank's query heads stay together) and writes its slice of the outputs, no collective;
   * row-parallel o_proj, down: a rank holds a K window of every row (whole super-blocks; the precedent is the
-    reference's K-window GEMM form, gen_gemm_tile.py:262-264) and one ncclAllReduce(sum) of f32 partials gives the
-    result; rank 0 adds the residual in its GEMM epilogue.
+    reference's K-window GEMM form, gen_gemm_tile.py:262-264) and one ncclAllReduce(sum) of the partials gives the
+    result.
 Per layer (attention replaced by identity, so the o_proj input is the rank's query slice of the QKV output):
 
     xn  = rmsnorm(h)                      f16, weightless, gain 1/64
@@ -18,10 +18,11 @@ Per layer (attention replaced by identity, so the o_proj input is the rank's que
     a   = silu(g) * (xn Wu_r^T)           f16 (the GEMM's swiglu epilogue)
     h   = h + allreduce(a Wd_r^T)
 
-Modes of the row-parallel partial sums: parity (f32 partials, rank 0's GEMM adds the residual, f32 allreduce) and
-speed (f16 partials from every rank's GEMM with no residual read, f16 allreduce, the sum added into the f32 residual
-stream by the next norm's pass). The residual stream h is f32 [M][hidden] on every rank in both. The reference normalises every layer input
-(docs/architecture.md:68); the fixed gain keeps silu(gate) * up inside the f16 range with the synthetic weights.
+Row-parallel partial sums: every rank's GEMM stores plain partials (no residual read), one allreduce sums them in
+place, and the next norm's pass adds the sum into the f32 residual stream (yah_add_rmsnorm). Parity mode: f32
+partials and allreduce; speed mode: f16 (half the bytes). The residual stream h is f32 [M][hidden] on every rank.
+The reference normalises every layer input (docs/architecture.md:68); the fixed gain keeps silu(gate) * up inside
+the f16 range with the synthetic weights.
 """
 from __future__ import annotations
 
@@ -189,7 +190,8 @@ class LlamaStack:
         self.qkv = dev.empty(M * self.qkv_r * 2)
         self.g = dev.empty(M * self.ff_r * 4)
         self.act = dev.empty(M * self.ff_r * 2)
-        self.part = dev.empty(M * H * 2) if mode == "speed" else None  # f16 partial sums of the speed mode
+        # row-parallel partial sums, added into h by the next norm's pass (f32: parity, f16: speed)
+        self.part = dev.empty(M * H * (2 if mode == "speed" else 4)) if chunks == 1 else None
         if chunks > 1:
             self.comm_stream = Stream()
             self.ev_gemm = [Event() for _ in range(chunks)]
@@ -197,16 +199,20 @@ class LlamaStack:
 
     @property
     def launches_per_forward(self) -> int:
-        """Library kernel launches per forward pass (2 norms + 5 linears per layer and token chunk; the speed mode
-        adds the final add)."""
-        return 7 * self.shape.layers * self.chunks + (1 if self.mode == "speed" else 0)
+        """Library kernel launches per forward pass (2 norms + 5 linears per layer and token chunk; the unchunked
+        forward adds the final add)."""
+        return 7 * self.shape.layers * self.chunks + (1 if self.chunks == 1 else 0)
 
     def forward(self, h: DeviceBuffer, stream=None):
         """h (f32 [M][hidden], the residual stream, identical on every rank) is updated in place."""
         if self.chunks > 1:
             return self._forward_chunked(h, stream)
-        if self.mode == "speed":
-            return self._forward_speed(h, stream)
+        return self._forward_partials(h, stream)
+
+    def _forward_residual_epilogue(self, h: DeviceBuffer, stream=None):
+        """The parity mode through yah_tp_linear_row: rank 0's GEMM epilogue adds the residual, the allreduce sums
+        h + partials in place (kept as the reference form of the row-parallel linear; the stack runs
+        _forward_partials)."""
         L, s, M, H, fmt = lib(), self.shape, self.M, self.shape.hidden, self.shape.fmt
         c = self.comm.handle
         for w in self.w:
@@ -233,18 +239,22 @@ class LlamaStack:
         check(fn(w.ptr, fmt, H, K_r, self.row_bytes[name], 0, x_ptr, Mc, ldx, h_ptr, F32, H,
                  EPI_RESID if r0 else EPI_STORE, h_ptr if r0 else None, H if r0 else 0, stream))
 
-    def _forward_speed(self, h: DeviceBuffer, stream):
-        """Speed mode: the row-parallel GEMMs write f16 partial sums (no residual read), the allreduce moves f16
-        (half the bytes), and the sum is added into the f32 residual stream by the next norm's pass
-        (yah_add_rmsnorm); the last layer's sum by an add-only pass."""
+    def _forward_partials(self, h: DeviceBuffer, stream):
+        """Every rank's row-parallel GEMM stores its plain partial sums (no residual read, so no rank is slower
+        than the others before the allreduce); the allreduce sums them in place (f32 parity, f16 speed: half the
+        bytes); the next norm's pass adds the sum into the f32 residual stream (yah_add_rmsnorm), the last layer's
+        sum an add-only pass."""
         L, M, H, fmt = lib(), self.M, self.shape.hidden, self.shape.fmt
         c, part = self.comm.handle, self.part.ptr
+        speed = self.mode == "speed"
+        pdt = F16 if speed else F32
+        allreduce = L.yah_tp_allreduce_f16 if speed else L.yah_tp_allreduce_f32
         pending = False
         fn = L.yah_qgemv if M <= 32 else L.yah_qgemm
 
         def norm():
             if pending:
-                check(L.yah_add_rmsnorm(h.ptr, H, part, H, M, H, NORM_EPS, NORM_GAIN, self.xn.ptr, H, stream))
+                check(L.yah_add_rmsnorm(h.ptr, H, part, pdt, H, M, H, NORM_EPS, NORM_GAIN, self.xn.ptr, H, stream))
             else:
                 check(L.yah_rmsnorm(h.ptr, H, M, H, NORM_EPS, NORM_GAIN, self.xn.ptr, H, stream))
 
@@ -252,9 +262,9 @@ class LlamaStack:
             norm()
             check(L.yah_tp_linear_col(c, w["qkv"].ptr, fmt, self.qkv_r, H, self.row_bytes["qkv"], self.xn.ptr, M, H,
                                       self.qkv.ptr, F16, self.qkv_r, EPI_STORE, None, 0, stream))
-            check(fn(w["o"].ptr, fmt, H, self.q_r, self.row_bytes["o"], 0, self.qkv.ptr, M, self.qkv_r, part, F16, H,
+            check(fn(w["o"].ptr, fmt, H, self.q_r, self.row_bytes["o"], 0, self.qkv.ptr, M, self.qkv_r, part, pdt, H,
                      EPI_STORE, None, 0, stream))
-            check(L.yah_tp_allreduce_f16(c, part, M * H, stream))
+            check(allreduce(c, part, M * H, stream))
             pending = True
             norm()
             check(L.yah_tp_linear_col(c, w["gate"].ptr, fmt, self.ff_r, H, self.row_bytes["gate"], self.xn.ptr, M, H,
@@ -262,10 +272,10 @@ class LlamaStack:
             check(L.yah_tp_linear_col(c, w["up"].ptr, fmt, self.ff_r, H, self.row_bytes["up"], self.xn.ptr, M, H,
                                       self.act.ptr, F16, self.ff_r, EPI_SWIGLU, self.g.ptr, self.ff_r, stream))
             check(fn(w["down"].ptr, fmt, H, self.ff_r, self.row_bytes["down"], 0, self.act.ptr, M, self.ff_r, part,
-                     F16, H, EPI_STORE, None, 0, stream))
-            check(L.yah_tp_allreduce_f16(c, part, M * H, stream))
+                     pdt, H, EPI_STORE, None, 0, stream))
+            check(allreduce(c, part, M * H, stream))
         if pending:
-            check(L.yah_add_rmsnorm(h.ptr, H, part, H, M, H, NORM_EPS, NORM_GAIN, None, 0, stream))
+            check(L.yah_add_rmsnorm(h.ptr, H, part, pdt, H, M, H, NORM_EPS, NORM_GAIN, None, 0, stream))
 
     def _forward_chunked(self, h: DeviceBuffer, stream):
         L, s, H, fmt, C = lib(), self.shape, self.shape.hidden, self.shape.fmt, self.chunks
