@@ -362,7 +362,9 @@ def run_stack(args, dist, rank, local_rank):
         "metric": "Q4_K layer-stack prefill TFLOP/s (tensor-parallel)", "value": round(value, 2), "unit": "TFLOP/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_step_ms, 4),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-        "dtype": "f16 x GGUF-Q4_K -> f32 acc, f32 residual stream and allreduce", "data": "synthetic",
+        "dtype": "f16 x GGUF-Q4_K -> f32 acc, f32 residual stream",
+        "data": ("synthetic" if args.stack_mode == "parity" else
+                 "synthetic, Q4_K rule with d and dmin scaled by 2^-8 (f16 partial sums stay finite)"),
         "config": {"workload": "q4k_layer_stack_tp", "layers": shape.layers, "hidden": H, "qkv": shape.qkv,
                    "ff": shape.ff, "M_tokens": M, "parallelism": f"tp{world}", "token_chunks": chunks,
                    "partial_sums": "f32 (parity mode)" if args.stack_mode == "parity" else "f16 (speed mode)",

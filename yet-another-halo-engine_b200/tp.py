@@ -7,7 +7,7 @@ GPUs of one box, one process per GPU:
     head groups, so the rank's query heads stay together) and writes its slice of the outputs, no collective;
   * row-parallel o_proj, down: a rank holds a K window of every row (whole super-blocks; the precedent is the
     reference's K-window GEMM form, gen_gemm_tile.py:262-264) and one ncclAllReduce(sum) of the partials gives the
-    result.
+    result (see the modes below).
 Per layer (attention replaced by identity, so the o_proj input is the rank's query slice of the QKV output):
 
     xn  = rmsnorm(h)                      f16, weightless, gain 1/64
@@ -18,9 +18,10 @@ Per layer (attention replaced by identity, so the o_proj input is the rank's que
     a   = silu(g) * (xn Wu_r^T)           f16 (the GEMM's swiglu epilogue)
     h   = h + allreduce(a Wd_r^T)
 
-Row-parallel partial sums: every rank's GEMM stores plain partials (no residual read), one allreduce sums them in
-place, and the next norm's pass adds the sum into the f32 residual stream (yah_add_rmsnorm). Parity mode: f32
-partials and allreduce; speed mode: f16 (half the bytes). The residual stream h is f32 [M][hidden] on every rank.
+Row-parallel partial sums. Parity mode: f32; rank 0's GEMM epilogue adds the residual and the allreduce sums
+h + partials in place. Speed mode: every rank's GEMM stores f16 partials (no residual read), the f16 allreduce moves
+half the bytes, and the next norm's pass adds the sum into the f32 residual stream (yah_add_rmsnorm). The residual
+stream h is f32 [M][hidden] on every rank in both.
 The reference normalises every layer input (docs/architecture.md:68); the fixed gain keeps silu(gate) * up inside
 the f16 range with the synthetic weights.
 """
@@ -190,8 +191,8 @@ class LlamaStack:
         self.qkv = dev.empty(M * self.qkv_r * 2)
         self.g = dev.empty(M * self.ff_r * 4)
         self.act = dev.empty(M * self.ff_r * 2)
-        # row-parallel partial sums, added into h by the next norm's pass (f32: parity, f16: speed)
-        self.part = dev.empty(M * H * (2 if mode == "speed" else 4)) if chunks == 1 else None
+        # the speed mode's f16 row-parallel partial sums, added into h by the next norm's pass
+        self.part = dev.empty(M * H * 2) if mode == "speed" and chunks == 1 else None
         if chunks > 1:
             self.comm_stream = Stream()
             self.ev_gemm = [Event() for _ in range(chunks)]
@@ -201,18 +202,20 @@ class LlamaStack:
     def launches_per_forward(self) -> int:
         """Library kernel launches per forward pass (2 norms + 5 linears per layer and token chunk; the unchunked
         forward adds the final add)."""
-        return 7 * self.shape.layers * self.chunks + (1 if self.chunks == 1 else 0)
+        return 7 * self.shape.layers * self.chunks + (1 if self.part is not None else 0)
 
     def forward(self, h: DeviceBuffer, stream=None):
         """h (f32 [M][hidden], the residual stream, identical on every rank) is updated in place."""
         if self.chunks > 1:
             return self._forward_chunked(h, stream)
-        return self._forward_partials(h, stream)
+        if self.mode == "speed":
+            return self._forward_partials(h, stream)
+        return self._forward_residual_epilogue(h, stream)
 
     def _forward_residual_epilogue(self, h: DeviceBuffer, stream=None):
-        """The parity mode through yah_tp_linear_row: rank 0's GEMM epilogue adds the residual, the allreduce sums
-        h + partials in place (kept as the reference form of the row-parallel linear; the stack runs
-        _forward_partials)."""
+        """Parity mode through yah_tp_linear_row: rank 0's GEMM epilogue adds the residual and the f32 allreduce
+        sums h + partials in place (measured 3% faster at tp2 / tp4 than storing plain f32 partials and adding the
+        sum in the norm pass, the speed mode's scheme)."""
         L, s, M, H, fmt = lib(), self.shape, self.M, self.shape.hidden, self.shape.fmt
         c = self.comm.handle
         for w in self.w:
@@ -240,10 +243,10 @@ class LlamaStack:
                  EPI_RESID if r0 else EPI_STORE, h_ptr if r0 else None, H if r0 else 0, stream))
 
     def _forward_partials(self, h: DeviceBuffer, stream):
-        """Every rank's row-parallel GEMM stores its plain partial sums (no residual read, so no rank is slower
-        than the others before the allreduce); the allreduce sums them in place (f32 parity, f16 speed: half the
-        bytes); the next norm's pass adds the sum into the f32 residual stream (yah_add_rmsnorm), the last layer's
-        sum an add-only pass."""
+        """The speed mode: every rank's row-parallel GEMM stores its plain f16 partial sums (no residual read), the
+        allreduce sums them in place (half the bytes of f32), and the next norm's pass adds the sum into the f32
+        residual stream (yah_add_rmsnorm), the last layer's sum an add-only pass. (The same scheme with f32 partials
+        was measured 3% slower than the parity mode's residual epilogue.)"""
         L, M, H, fmt = lib(), self.M, self.shape.hidden, self.shape.fmt
         c, part = self.comm.handle, self.part.ptr
         speed = self.mode == "speed"
