@@ -409,75 +409,119 @@ def cpu_reference_step(fmt, w, x, K, use_gguf=True):
     return x.astype(np.float32) @ wq.astype(np.float32).T
 
 
-def cpu_baseline(args, seconds=10.0):
-    """The CPU path timed on a bounded sample (rows of the weight) for the same metric."""
-    wl = workload_of(args)
+def cpu_jobs(args, frac):
+    """The bounded CPU sample of the workload: a list of (format, weight rows, activations, K, full rows) and its
+    algorithmic size (FLOPs, bytes). `frac` is the fraction of every weight's rows taken, so a stack sample keeps
+    the stack's FLOP mix (QKV, o_proj, gate, up, down of one layer over all M tokens)."""
     import __graft_entry__ as ge
     F = ge.load_package().formats
-    t, M, K, N = wl["fmt"], wl["M"], wl["K"], wl["N"]
-    rows = min(N, 2048)
-    w = F.synth_weights(t, rows, K, seed=0)
-    x = F.synth_activations(M, K, seed=1)
+    if args.workload == "stack":
+        shape = ge.load_package().tp.StackShape(layers=args.layers)
+        M, H = args.stack_tokens, shape.hidden
+        mats = [(shape.qkv, H), (H, shape.n_q * shape.head_dim), (shape.ff, H), (shape.ff, H), (H, shape.ff)]
+        fmt = shape.fmt
+    else:
+        wl = workload_of(args)
+        M, fmt = wl["M"], wl["fmt"]
+        mats = [(wl["N"], wl["K"])]
+    xs, jobs = {}, []
+    for i, (n, k) in enumerate(mats):
+        rows = max(16, min(n, int(round(n * frac))))
+        if k not in xs:
+            xs[k] = F.synth_activations(M, k, seed=1 + k)
+        jobs.append((fmt, F.synth_weights(fmt, rows, k, seed=i), xs[k], k, n))
+    flops = sum(2.0 * M * w.shape[0] * k for _, w, _, k, _ in jobs)
+    nbytes = sum(w.nbytes + x.nbytes + M * w.shape[0] * 4 for _, w, x, _, _ in jobs)
+    return jobs, flops, nbytes
+
+
+def cpu_run(jobs, use_gguf):
+    for fmt, w, x, k, _ in jobs:
+        cpu_reference_step(fmt, w, x, k, use_gguf)
+
+
+def cpu_sample_text(args, jobs, use_gguf, runs_note):
+    M = jobs[0][2].shape[0]
+    mats = ", ".join(f"{w.shape[0]} of {n} rows x K={k}" for _, w, _, k, n in jobs)
+    what = "one layer of the stack: " if args.workload == "stack" else ""
+    return (f"{'gguf-py dequantize' if use_gguf else 'oracle C dequant'} + numpy f32 matmul, {what}{mats}, "
+            f"{M} tokens; {runs_note}; OPENBLAS_NUM_THREADS={os.environ.get('OPENBLAS_NUM_THREADS', 'unset')}")
+
+
+def cpu_kind():
     try:
         import gguf  # noqa: F401
-        use_gguf, kind = True, "reference"
+        return True, "reference"
     except ImportError:
-        use_gguf, kind = False, "port"
-    cpu_reference_step(t, w, x, K, use_gguf)  # warm-up
+        return False, "port"
+
+
+def cpu_metric(args, flops, nbytes, per):
+    gemv = args.workload != "stack" and workload_of(args)["gemv"]
+    return (nbytes / per / 1e9, "GB/s") if gemv else (flops / per / 1e12, "TFLOP/s")
+
+
+def cpu_baseline(args, seconds=10.0):
+    """The CPU path timed on a bounded sample (rows of each weight) for the same metric."""
+    use_gguf, kind = cpu_kind()
+    frac = 1 / 16 if args.workload == "stack" else min(1.0, 2048 / workload_of(args)["N"])
+    jobs, flops, nbytes = cpu_jobs(args, frac)
+    cpu_run(jobs, use_gguf)  # warm-up
     n, t0 = 0, time.perf_counter()
     while True:
-        cpu_reference_step(t, w, x, K, use_gguf)
+        cpu_run(jobs, use_gguf)
         n += 1
         el = time.perf_counter() - t0
         if el >= seconds or n >= 50:
             break
     per = el / n
-    if wl["gemv"]:
-        val = (w.nbytes + x.nbytes + M * rows * 4) / per / 1e9
-        unit = "GB/s"
-    else:
-        val = 2.0 * M * rows * K / per / 1e12
-        unit = "TFLOP/s"
+    val, unit = cpu_metric(args, flops, nbytes, per)
     return {"value": round(val, 5), "unit": unit, "cores": cpu_cores(), "kind": kind,
-            "sample": f"{'gguf-py dequantize' if use_gguf else 'oracle C dequant'} + numpy f32 matmul of {rows} of "
-                      f"{N} weight rows x {M} tokens x K={K}, {n} runs ({per * 1e3:.1f} ms each); "
-                      f"OPENBLAS_NUM_THREADS={os.environ.get('OPENBLAS_NUM_THREADS', 'unset')}"}
+            "sample": cpu_sample_text(args, jobs, use_gguf, f"{n} runs, {per * 1e3:.1f} ms each")}
 
 
-def run_reference(args, rank):
+def run_reference(args, rank, budget_s=150.0):
+    """The reference's CPU path on the same metric and config, rank 0 only. Each step is one bounded sample; when
+    the first warm-up step shows that K steps would take more than `budget_s`, every weight's sampled rows shrink
+    by the same factor so that the run still ends within a few minutes."""
     if rank != 0:
         return None
-    wl = workload_of(args)
-    import __graft_entry__ as ge
-    F = ge.load_package().formats
-    t, M, K, N = wl["fmt"], wl["M"], wl["K"], wl["N"]
-    rows = min(N, 1024)
-    w = F.synth_weights(t, rows, K, seed=0)
-    x = F.synth_activations(M, K, seed=1)
-    try:
-        import gguf  # noqa: F401
-        use_gguf, kind = True, "reference"
-    except ImportError:
-        use_gguf, kind = False, "port"
+    use_gguf, kind = cpu_kind()
+    frac = 1 / 16 if args.workload == "stack" else min(1.0, 1024 / workload_of(args)["N"])
+    jobs, flops, nbytes = cpu_jobs(args, frac)
+    t0 = time.perf_counter()
+    cpu_run(jobs, use_gguf)
+    first = time.perf_counter() - t0
+    if first * (args.steps + args.warmup) > budget_s:
+        frac *= budget_s / (first * (args.steps + args.warmup))
+        jobs, flops, nbytes = cpu_jobs(args, frac)
     for _ in range(args.warmup):
-        cpu_reference_step(t, w, x, K, use_gguf)
+        cpu_run(jobs, use_gguf)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        cpu_reference_step(t, w, x, K, use_gguf)
+        cpu_run(jobs, use_gguf)
     el = time.perf_counter() - t0
     per = el / args.steps
-    metric = wl["metric"]
-    if wl["gemv"]:
-        val, unit = (w.nbytes + x.nbytes + M * rows * 4) / per / 1e9, "GB/s"
+    val, unit = cpu_metric(args, flops, nbytes, per)
+    sample = cpu_sample_text(args, jobs, use_gguf, "per step")
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if args.workload == "stack":
+        import __graft_entry__ as ge
+        shape = ge.load_package().tp.StackShape(layers=args.layers)
+        metric = "Q4_K layer-stack prefill TFLOP/s (tensor-parallel)"
+        config = {"workload": "q4k_layer_stack_tp", "layers": shape.layers, "hidden": shape.hidden,
+                  "qkv": shape.qkv, "ff": shape.ff, "M_tokens": args.stack_tokens, "parallelism": f"tp{world}"}
+        scaling = "strong"
     else:
-        val, unit = 2.0 * M * rows * K / per / 1e12, "TFLOP/s"
-    sample = (f"{'gguf-py dequantize' if use_gguf else 'oracle C dequant'} + numpy f32 matmul of {rows} of {N} "
-              f"weight rows x {M} tokens x K={K} per step")
+        wl = workload_of(args)
+        metric = wl["metric"]
+        config = {"workload": wl["name"], "M_tokens": wl["M"], "K": wl["K"], "N": wl["N"],
+                  "weight_format": wl["fmt_name"]}
+        scaling = "weak"
     return {"impl": "reference", "metric": metric, "value": round(val, 5), "unit": unit,
-            "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(per * 1e3, 3), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "f16 weights (dequantised) x f16 -> f32", "data": "synthetic",
-            "config": {"workload": wl["name"], "M_tokens": M, "K": K, "N": N, "weight_format": wl["fmt_name"]},
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(per * 1e3, 3), "higher_is_better": True, "scaling": scaling, "vs_baseline": None,
+            "dtype": "f16 weights (dequantised) x f16 -> f32", "data": "synthetic", "config": config,
             "cpu_baseline": {"value": round(val, 5), "unit": unit, "cores": cpu_cores(), "kind": kind,
                              "sample": sample},
             "e2e": {"value": round(val, 5), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -527,7 +571,7 @@ def main():
     else:
         line = run_ours(args, dist, rank, local_rank)
     if rank == 0:
-        if not args.no_cpu_baseline and args.workload != "stack":
+        if not args.no_cpu_baseline and int(os.environ.get("WORLD_SIZE", "1")) == 1:
             line["cpu_baseline"] = cpu_baseline(args)
         print(json.dumps(line), flush=True)
     if dist:
