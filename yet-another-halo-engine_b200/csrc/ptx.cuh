@@ -187,6 +187,16 @@ __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wa
 __device__ __forceinline__ void named_bar(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
+// Named barrier that also returns whether `v` was set in any of the `count` threads.
+__device__ __forceinline__ bool named_bar_or(int id, int count, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n.reg .pred p, q;\nsetp.ne.u32 p, %3, 0;\nbarrier.cta.red.or.pred q, %1, %2, p;\nselp.u32 %0, 1, 0, q;\n}"
+      : "=r"(r)
+      : "r"(id), "r"(count), "r"((uint32_t)v)
+      : "memory");
+  return r != 0;
+}
 
 __device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&v)[8]) {
   asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"

@@ -843,7 +843,9 @@ __global__ void __launch_bounds__(GvRoles<T, CW>::kThreads, (CW == 8 && NTW == 1
 // lane owns one (row, super-block) product: lanes c = 0 that of its row g, lanes c = 1 that of row g + 8, so a lane
 // forms the group scales of one super-block instead of two, and 28-row ranges split into 4-row quads with no padded
 // rows. A unit (4 rows x 4 super-blocks) ends with the lane values added across the unit by two shuffles and
-// stored per (row quad, super-block quad); the rows are summed in a fixed order at the end (deterministic).
+// stored per (row quad, super-block quad); the rows are summed in a fixed order at the end (deterministic). Warps
+// take units from a shared counter in stage order, so whichever warp runs ahead takes more of them (which warp
+// computes a unit does not change its result).
 struct Gv1Params {
   int N, nsb, kb_off, S, ringst, stage_bytes, opw, rb;
   int units;                  // ceil(N / 4)
@@ -949,11 +951,13 @@ __global__ void __launch_bounds__((kGv1Warps + 1) * 32, 1)
   const int nst = p.nsb / p.S;        // stages (S divides the super-blocks)
   const int sq = p.S / 4;             // super-block quads per stage
   const int nsq = p.nsb / 4;
+  int* next_unit = reinterpret_cast<int*>(empty + kGvMaxStages);  // the CTA's unit counter, stage-major order
   if (threadIdx.x == 0) {
     for (int i = 0; i < p.ringst; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], kGv1Warps);
     }
+    *next_unit = 0;
     fence_barrier_init();
     griddep_launch_dependents();
   }
@@ -1034,28 +1038,47 @@ __global__ void __launch_bounds__((kGv1Warps + 1) * 32, 1)
   const uint32_t own = c == 1 ? 288u : 0u;
   const uint32_t xcol = res + (g & 3) * kGv1SbStride + 16 * c, scol = ressum + (g & 3) * 32 + 4 * c;
   const int U = nq * sq;  // units per stage
-  int slot = 0, ph = 0;
-  bool ok = true;
-  for (int k = 0; k < nst; ++k) {
-    if (!mbar_wait(&full[slot], ph, p.status, kStatusTimeoutFull)) { ok = false; break; }
-    const uint32_t base = smem_u32(smem + slot * p.stage_bytes);
-    // unit i of stage k goes to warp (i + k U) mod 16: every warp gets the same share over the launch
-    int i = (warp - (k * U) % kGv1Warps + kGv1Warps) % kGv1Warps;
-    for (; i < U; i += kGv1Warps) {
-      const int rq = i / sq, sl = i - rq * sq;  // row quad, super-block quad within the stage
-      const int sbq = k * sq + sl;              // super-block quad of the row
-      const uint32_t wg = base + (4 * rq + (g & 3)) * p.opw + (4 * sl + (g >> 2)) * 144;
-      float v = gv1_unit(wg, own, xcol + sbq * 4 * kGv1SbStride, scol + sbq * 128, c, sel);
-      v += __shfl_xor_sync(0xffffffffu, v, 1);
-      v += __shfl_xor_sync(0xffffffffu, v, 16);
-      if (lane < 16 && c == 0) part[(rq * nsq + sbq) * 4 + g] = v;
+  // This warp's stage kw (ring slot, phase), whether it has waited for that stage's copy, and its next unit u
+  // (stage-major index). A warp releases a stage (arrives on its empty barrier) once it takes a unit of a later
+  // stage or the units run out, so a warp waiting for stage s has released every stage before s.
+  int slot = 0, ph = 0, kw = 0, kbase = 0;
+  bool ok = true, waited = false;
+  int u = lane == 0 ? atomicAdd(next_unit, 1) : 0;
+  u = __shfl_sync(0xffffffffu, u, 0);
+  while (u < nst * U) {
+    while (u >= kbase + U) {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);
+      if (++slot == p.ringst) slot = 0, ph ^= 1;
+      ++kw, kbase += U, waited = false;
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[slot]);
-    if (++slot == p.ringst) slot = 0, ph ^= 1;
+    if (!waited) {
+      if (!mbar_wait(&full[slot], ph, p.status, kStatusTimeoutFull)) { ok = false; break; }
+      waited = true;
+    }
+    const int un = lane == 0 ? atomicAdd(next_unit, 1) : 0;  // the next unit, fetched ahead of this one
+    const uint32_t base = smem_u32(smem + slot * p.stage_bytes);
+    const int i = u - kbase;
+    const int rq = i / sq, sl = i - rq * sq;  // row quad, super-block quad within the stage
+    const int sbq = kw * sq + sl;             // super-block quad of the row
+    const uint32_t wg = base + (4 * rq + (g & 3)) * p.opw + (4 * sl + (g >> 2)) * 144;
+    float v = gv1_unit(wg, own, xcol + sbq * 4 * kGv1SbStride, scol + sbq * 128, c, sel);
+    v += __shfl_xor_sync(0xffffffffu, v, 1);
+    v += __shfl_xor_sync(0xffffffffu, v, 16);
+    if (lane < 16 && c == 0) part[(rq * nsq + sbq) * 4 + g] = v;
+    u = __shfl_sync(0xffffffffu, un, 0);
   }
-  named_bar(1, kGv1Warps * 32);
-  if (!ok || *(volatile int*)p.status != 0) return;
+  if (ok) {
+    for (; kw < nst; ++kw) {  // release the stages this warp took no unit of
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);
+      if (++slot == p.ringst) slot = 0, ph ^= 1;
+    }
+  }
+  // a wait that gave up in any warp of this CTA leaves the CTA's outputs unwritten (the status word says why); the
+  // CTA-wide test is a barrier reduction, not a read of the status word, which would cost a global-memory round
+  // trip at the end of every CTA
+  if (named_bar_or(1, kGv1Warps * 32, !ok)) return;
   for (int r = threadIdx.x; r < re - rs; r += kGv1Warps * 32) {
     const float* pr = part + (r >> 2) * nsq * 4 + (r & 3);
     float acc = 0.f;
@@ -1265,7 +1288,7 @@ bool plan_m1(GemvPlan& pl, int64_t N, int64_t K, int num_sms) {
   const int res_bytes = (int)((nsb * kGv1SbStride + 64 + 1023) / 1024 * 1024);
   const int ressum_bytes = (int)((nsb * 32 + 16 + 1023) / 1024 * 1024);
   const int part_bytes = (int)(((pl.rb / 4) * (nsb / 4) * 16 + 1023) / 1024 * 1024);
-  const int bar_bytes = 2 * kGvMaxStages * 8;
+  const int bar_bytes = 2 * kGvMaxStages * 8 + 16;  // full and empty barriers, the unit counter
   int fit = (kGvSmemBudget - res_bytes - ressum_bytes - part_bytes - bar_bytes) / pl.stage_bytes;
   if (fit > kGvMaxStages) fit = kGvMaxStages;
   if (fit < 2) return false;
