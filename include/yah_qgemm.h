@@ -168,7 +168,11 @@ int yah_qgemm(const void* w, int ggml_type, int64_t N, int64_t K, int64_t w_row_
  *           so chunked calls on different streams of one device must not overlap;
  *   cta_pair  1: 2-SM pairs (256 weight rows per tile, tcgen05 cta_group::2 over clusters of 2 CTAs),
  *           0: one CTA per 128-row tile, -1: auto (pairs where the device supports clusters).
- * Every (bn, grid, cta_pair) choice gives identical results for a given kchunk. */
+ * Split K: with grid = 0, chunked accumulation (kchunk a multiple of 256) and fewer (row tile, 16-token unit)
+ * pieces than the device holds CTAs (pairs), every accumulation chunk of a tile runs on its own CTA and the chunk
+ * results are added in chunk order by a second kernel that also applies the epilogue (a library-owned per-device
+ * workspace of chunks * M * N * 4 bytes, same stream rule as the scratch). An explicit grid never splits.
+ * Every (bn, grid, cta_pair) choice, split or not, gives identical results for a given kchunk. */
 int yah_qgemm_tile(const void* w, int ggml_type, int64_t N, int64_t K, int64_t w_row_stride, int64_t kb_off,
                    const void* x, int64_t M, int64_t ldx, void* y, int y_dtype, int64_t ldy, int epilogue,
                    const void* aux, int64_t ldaux, int bn, int grid, int64_t kchunk, int cta_pair, void* stream);

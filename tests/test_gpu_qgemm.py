@@ -205,3 +205,42 @@ def test_q6k_lm_head_k5120_prefill_realigned(pkg, F, O, dev):
     e = O.errors(y, O.gemm_ref(O.dequant_f16(t, w, N, K), x))
     assert e["finite"] and e["max_abs"] <= 2e-2 and e["rel_fro"] <= 1e-3, e
     wd.close()
+
+
+@pytest.mark.parametrize("name", FMTS)
+@pytest.mark.parametrize("M", [1, 8, 32])
+@pytest.mark.parametrize("pair", [0, 1])
+def test_split_k_matches_unsplit(pkg, F, O, dev, name, M, pair):
+    """Few tokens: with an automatic grid the accumulation chunks of a tile run on separate CTAs (split K) and are
+    added in chunk order afterwards. Bit-identical to the unsplit GEMM (an explicit grid never splits) for every
+    epilogue, and within the bar of the oracle."""
+    t = F.type_of(name)
+    N, K = 1024, 8192  # 4 or 8 row tiles x 4 chunks of 2048
+    w = F.synth_weights(t, N, K, seed=21)
+    x = F.synth_activations(M, K, seed=22)
+    rng = np.random.default_rng(23)
+    aux = rng.standard_normal((M, N)).astype(np.float32) * 3
+    acc = O.gemm_ref(O.dequant_f16(t, w, N, K), x)
+    for kind, out, ref in (("kstore", "f32", acc), ("kstore", "f16", acc), ("kres", "f32", acc + aux),
+                           ("swiglu", "f16", O.epilogue_ref(acc, 2, aux))):
+        a = None if kind == "kstore" else aux
+        ys = pkg.ops.qgemm(dev, w, t, x, N=N, K=K, kind=kind, out_dtype=out, aux=a, pair=pair)
+        yu = pkg.ops.qgemm(dev, w, t, x, N=N, K=K, kind=kind, out_dtype=out, aux=a, pair=pair, grid=dev.sm_count)
+        assert ys.dtype == yu.dtype
+        assert np.array_equal(ys.view(np.uint8), yu.view(np.uint8)), (kind, out)
+        check(O, ys, ref, f16=ys.dtype == np.float16)
+
+
+def test_split_k_config3_decode_shapes(pkg, F, O, dev):
+    """The config 3 down projection (N = 4096, K = 14336: 7 chunks) at M = 32 through the automatic choice (split
+    K), on a sample of 256 weight rows, and the ragged token count M = 17."""
+    t = F.Q4_K
+    N, K = 4096, 14336
+    w = F.synth_weights(t, N, K, seed=31)
+    rows = np.random.default_rng(2).choice(N, 256, replace=False)
+    for M in (32, 17):
+        x = F.synth_activations(M, K, seed=32 + M)
+        y = pkg.ops.qgemm(dev, w, t, x, N=N, K=K)
+        yu = pkg.ops.qgemm(dev, w, t, x, N=N, K=K, grid=dev.sm_count)
+        assert np.array_equal(y.view(np.uint32), yu.view(np.uint32))
+        check(O, y[:, rows], O.gemm_ref(O.dequant_f16(t, w[rows], len(rows), K), x))

@@ -54,6 +54,8 @@ struct DevState {
   size_t counters_n = 0;
   float* gemm_scratch = nullptr;  // chunked-accumulation sums of the tile GEMM
   size_t gemm_scratch_bytes = 0;
+  float* gemm_kpart = nullptr;    // split-K chunk results of the tile GEMM
+  size_t gemm_kpart_bytes = 0;
   int max_pairs = -1;             // resident 2-CTA clusters of the tile GEMM (-1: not queried yet)
 };
 
@@ -495,12 +497,29 @@ int yah_qgemm_tile(const void* w, int t, int64_t N, int64_t K, int64_t w_row_str
     return fail(YAH_ERR_ARG, "bn %d is not a %s tile width (pairs: 256, 160, 128; single CTAs: 192, 128, 64)", bn,
                 a.pair ? "2-SM pair" : "single-CTA");
   a.bn = bn;
+  // Split K: with an automatic grid, when the (row tile, 16-token unit) space is smaller than the CTAs (pairs) the
+  // device holds, every accumulation chunk of a tile becomes its own unit (chunks of whole super-blocks). The
+  // result is bit-identical to the unsplit GEMM with the same chunk length.
+  a.nsplit = 1;
+  if (grid == 0 && kchunk < K && kchunk % 256 == 0) {
+    const int ncta = a.pair ? 2 : 1;
+    const int64_t units = (N + 128 * ncta - 1) / (128 * ncta) * ((M + 15) / 16);
+    int64_t slots = a.num_sms / ncta;
+    if (a.pair && slots > a.max_pairs) slots = a.max_pairs;
+    if (units < slots) a.nsplit = (int)((K + kchunk - 1) / kchunk);
+  }
   if (kchunk < K) {
     std::lock_guard<std::mutex> lk(g_mu);
     const size_t need = (size_t)yah::qgemm_grid(a) * bn * 128 * sizeof(float);
     rc = grow(reinterpret_cast<void**>(&s->gemm_scratch), &s->gemm_scratch_bytes, need);
     if (rc) return rc;
     a.scratch = s->gemm_scratch;
+    if (a.nsplit > 1) {
+      rc = grow(reinterpret_cast<void**>(&s->gemm_kpart), &s->gemm_kpart_bytes,
+                (size_t)a.nsplit * (size_t)M * (size_t)N * sizeof(float));
+      if (rc) return rc;
+      a.kpart = s->gemm_kpart;
+    }
   }
   return after_launch(yah::launch_qgemm_tc(a, (cudaStream_t)stream), "qgemm launch");
 }

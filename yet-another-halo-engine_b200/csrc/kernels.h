@@ -31,6 +31,8 @@ struct QGemmArgs {
   float* scratch;       // grid * bn * 128 f32 chunk sums when kchunk < K, else unused
   int pair;             // 1: 2-SM pairs (tcgen05 cta_group::2, clusters of 2), 0: one CTA per tile
   int max_pairs;        // resident 2-CTA clusters the device holds (pair mode)
+  int nsplit = 1;       // > 1: each accumulation chunk of a tile is its own work unit (split K, one chunk each)
+  float* kpart = nullptr;  // nsplit * M * N f32 chunk results when nsplit > 1, summed in chunk order afterwards
 };
 
 // Resident 2-CTA clusters of the tile-GEMM kernel on the current device (0 if clusters are unavailable).

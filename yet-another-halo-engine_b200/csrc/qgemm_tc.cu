@@ -33,6 +33,10 @@
 // in a per-CTA scratch buffer (L2-resident) while the MMA fills the other region.
 // Tiles are 128 weight rows x up to BN tokens. The persistent schedule splits the (row tile, 16-token unit) space
 // into equal contiguous ranges per CTA, so every SM gets the same MMA work (no wave-quantisation tail).
+// Split K (few tokens, so too few tiles for the SMs): every accumulation chunk of a tile is a work unit of its own;
+// a CTA writes its chunk's f32 result to a workspace and split_reduce_kernel adds the chunks of each output in
+// chunk order and applies the epilogue, the same additions in the same order as the single-CTA chunk sum, so the
+// result is bit-identical to the unsplit GEMM with the same chunk length.
 // Every mbarrier wait is bounded (ptx.cuh mbar_wait); on a timeout the kernel records a status code, drains its
 // own in-flight TMA copies and MMAs, frees TMEM and returns.
 #include <cuda.h>
@@ -97,6 +101,7 @@ struct KParams {
   int64_t total_units;  // row tiles (of 128 rows, or 256 for a pair) x 16-token units
   int upr;              // 16-token units per row tile
   int ncta;             // CTAs per tile: 1, or 2 for a 2-SM pair
+  int nsplit;           // 1, or the accumulation chunks of a tile when each is its own unit (split K)
   int tma_store;        // 1: the output is written with TMA stores through shared memory (tmap_y is valid)
   int aux_tma;          // 1: the epilogue's aux operand is prefetched by TMA (tmap_aux is valid)
 };
@@ -133,20 +138,23 @@ struct AuxCfg {
   static constexpr int kBytes = kDepth * kSlot;
 };
 
-// The persistent schedule: CTA b owns units [b * total / G, (b + 1) * total / G) of the (row tile, 16-token unit)
-// space, walked row tile by row tile, at most BN / 16 units per tile.
+// The persistent schedule: CTA b owns units [b * total / G, (b + 1) * total / G) of the (row tile, chunk, 16-token
+// unit) space, walked row tile by row tile, at most BN / 16 units per tile. kp is the accumulation chunk under
+// split K (0 otherwise).
 template <int BN>
 struct Sched {
   int64_t u, end;
-  int upr, M;
-  __device__ Sched(const KParams& p) : upr(p.upr), M(p.M) {
+  int upr, M, nsplit;
+  __device__ Sched(const KParams& p) : upr(p.upr), M(p.M), nsplit(p.nsplit) {
     const int64_t G = gridDim.x / p.ncta, b = blockIdx.x / p.ncta;  // a pair shares one range
     u = b * p.total_units / G;
     end = (b + 1) * p.total_units / G;
   }
-  __device__ bool next(int& rt, int& t0, int& nt) {
+  __device__ bool next(int& rt, int& kp, int& t0, int& nt) {
     if (u >= end) return false;
-    rt = (int)(u / upr);
+    const int vt = (int)(u / upr);
+    rt = vt / nsplit;
+    kp = vt - rt * nsplit;
     const int tu = (int)(u % upr);
     int nu = min(BN / 16, upr - tu);
     if ((int64_t)nu > end - u) nu = (int)(end - u);
@@ -159,7 +167,7 @@ struct Sched {
 
 __device__ __forceinline__ float silu_f(float g) { return g / (1.0f + __expf(-g)); }
 
-template <int T, int BN, int NACC, int EPI, bool OUT_F16, bool PAIR>
+template <int T, int BN, int NACC, int EPI, bool OUT_F16, bool PAIR, bool SPLIT>
 __global__ void __launch_bounds__(kThreads, 1)
     qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                     const __grid_constant__ CUtensorMap tmap_y, const __grid_constant__ CUtensorMap tmap_aux,
@@ -195,6 +203,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int nst = p.K / 128;                  // 128-K stages per tile
   const int sch = p.kcb / 2;                  // stages per accumulation chunk
   const int nch = (nst + sch - 1) / sch;      // accumulation chunks per tile
+  constexpr bool split = SPLIT;               // one chunk per work unit (then p.nsplit == nch)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kNSX; ++i) {
@@ -239,13 +248,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       tma_prefetch_desc(&tmap_x);
       Sched<BN> sc(p);
-      int rt, t0, nt;
+      int rt, kp, t0, nt;
       uint32_t s = 0;  // stages issued
       bool ok = true;
-      while (ok && sc.next(rt, t0, nt)) {
+      while (ok && sc.next(rt, kp, t0, nt)) {
         // a pair splits the tile's tokens: CTA r holds columns [r * n / 2, (r + 1) * n / 2) of the MMA's N
         const int ty = PAIR ? t0 + (int)rank * (((nt + 31) & ~31) / 2) : t0;
-        for (int st = 0; st < nst; ++st, ++s) {
+        const int st0 = split ? kp * sch : 0, st1 = split ? min(nst, st0 + sch) : nst;
+        for (int st = st0; st < st1; ++st, ++s) {
           const uint32_t xs = s % kNSX, xph = (s / kNSX) & 1;
           if (!mbar_wait(&xempty[xs], xph ^ 1, p.status, kStatusTimeoutEmpty)) { ok = false; break; }
           mbar_arrive_expect_tx(&xfull[xs], XST);
@@ -261,12 +271,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       tma_prefetch_desc(&tmap_w);
       Sched<BN> sc(p);
-      int rt, t0, nt;
+      int rt, kp, t0, nt;
       uint32_t s = 0;
       bool ok = true;
-      while (ok && sc.next(rt, t0, nt)) {
+      while (ok && sc.next(rt, kp, t0, nt)) {
         const int row0 = (rt * NCTA + (int)rank) * kBM;
-        for (int sb = 0; sb < p.K / 256; ++sb, ++s) {
+        const int sb0 = split ? kp * sch / 2 : 0, sb1 = split ? min(nst, (kp + 1) * sch) / 2 : p.K / 256;
+        for (int sb = sb0; sb < sb1; ++sb, ++s) {
           const uint32_t ws = s % NSW, wph = (s / NSW) & 1;
           if (!mbar_wait(&wempty[ws], wph ^ 1, p.status, kStatusTimeoutEmpty)) { ok = false; break; }
           mbar_arrive_expect_tx(&wfull[ws], kBM * WBOX);
@@ -284,15 +295,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------------ MMA issuer (pair: first CTA only)
     if (lane == 0 && rank == 0) {
       Sched<BN> sc(p);
-      int rt, t0, nt;
+      int rt, kp, t0, nt;
       uint32_t s = 0, u = 0;  // stage and accumulation-unit counters
       bool ok = true;
       const uint64_t bd0 = sdesc_sw128(smem_u32(smem));
       const uint64_t bstep = (uint64_t)(XST >> 4), bsub = (uint64_t)(XSUB >> 4);
       const uint32_t a0 = tmem + ACOL;
-      while (ok && sc.next(rt, t0, nt)) {
+      while (ok && sc.next(rt, kp, t0, nt)) {
         const uint32_t idesc = PAIR ? idesc_f16_f32(2 * kBM, (nt + 31) & ~31) : idesc_f16_f32(kBM, (nt + 15) & ~15);
-        for (int ch = 0; ok && ch < nch; ++ch, ++u) {
+        const int ch0 = split ? kp : 0, ch1 = split ? kp + 1 : nch;
+        for (int ch = ch0; ok && ch < ch1; ++ch, ++u) {
           const uint32_t r = u % NACC, rph = (u / NACC) & 1;
           const bool acc_free = mbar_wait(&accempty[r], rph ^ 1, p.status, kStatusTimeoutEmpty);
           if (!acc_free) { ok = false; break; }
@@ -347,13 +359,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;                   // TMEM lane quarter
     const int r = q * 32 + lane;              // row within the CTA's 128 rows
     Sched<BN> sc(p);
-    int rt, t0, nt;
+    int rt, kp, t0, nt;
     uint32_t s = 0;
     bool ok = true;
     const uint32_t wbase = smem_u32(smem + S::kWOff);
     const uint32_t tl = tmem + ((uint32_t)(q * 32) << 16) + ACOL + 32 * half;
-    while (ok && sc.next(rt, t0, nt)) {
-      for (int st = 0; st < nst; ++st, ++s) {
+    while (ok && sc.next(rt, kp, t0, nt)) {
+      const int st0 = split ? kp * sch : 0, st1 = split ? min(nst, st0 + sch) : nst;
+      for (int st = st0; st < st1; ++st, ++s) {
         if ((s & 1) != parity) continue;
         const int kb = 2 * st + half;              // 64-K block within the tile
         const uint32_t sbc = (s >> 1), ws = sbc % NSW, wph = (sbc / NSW) & 1;  // super-block = 2 stages
@@ -395,7 +408,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int rloc = q * 32 + lane;
     const bool leader = warp == kWarpEpi0 && lane == 0;  // issues the TMA stores
     Sched<BN> sc(p);
-    int rt, t0, nt;
+    int rt, kp, t0, nt;
     uint32_t u = 0, nbuf = 0;
     bool ok = true;
     const uint32_t tl = tmem + ((uint32_t)(q * 32) << 16);
@@ -405,14 +418,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool atma = AD > 0 && p.aux_tma;
     uint8_t* abuf = smem + S::kAuxOff;
     uint32_t aux_used = 0;  // aux chunks consumed so far (slot aux_used % AD)
-    while (ok && sc.next(rt, t0, nt)) {
+    while (ok && sc.next(rt, kp, t0, nt)) {
       const int row0 = (rt * NCTA + (int)rank) * kBM;
       const int row = row0 + rloc;
       const bool row_ok = row < p.N;
       const int ncks = (nt + CH - 1) / CH;  // aux chunks of this tile (its last accumulation chunk)
-      for (int ch = 0; ch < nch; ++ch, ++u) {
+      const int ch0 = split ? kp : 0, ch1 = split ? kp + 1 : nch;
+      // split K: this chunk's result goes to rows kp * M + t of the [nsplit * M][N] workspace (p.y)
+      const int64_t tsplit = split ? (int64_t)kp * p.M : 0;
+      for (int ch = ch0; ch < ch1; ++ch, ++u) {
         const uint32_t r = u % NACC;
-        if (atma && ch == nch - 1 && leader) {  // prefetch the first aux chunks while the MMAs finish
+        if (atma && ch == ch1 - 1 && leader) {  // prefetch the first aux chunks while the MMAs finish
           for (int k = 0; k < ncks && k < AD; ++k) {
             const uint32_t sl = (aux_used + k) % AD;
             mbar_arrive_expect_tx(&auxfull[sl], AC::kSlot);
@@ -421,7 +437,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (!mbar_wait(&accfull[r], (u / NACC) & 1, p.status, kStatusTimeoutFull)) { ok = false; break; }
         tc_fence_after();
-        const bool first = ch == 0, last = ch == nch - 1;
+        const bool first = ch == ch0, last = ch == ch1 - 1;
         for (int j0 = 0; j0 < nt; j0 += CH) {
           uint32_t v[CH];
           if constexpr (CH == 16) tmem_ld16(tl + r * BN + j0, v); else tmem_ld8(tl + r * BN + j0, v);
@@ -492,7 +508,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int jj = 0; jj < CH; ++jj) {
               if (jj >= jn) break;
-              const int64_t t = t0 + j0 + jj;
+              const int64_t t = tsplit + t0 + j0 + jj;
               if (OUT_F16)
                 reinterpret_cast<__half*>(p.y)[t * p.ldy + row] = __float2half_rn(val[jj]);
               else
@@ -541,7 +557,7 @@ EncodeTiledFn encoder() {
 // Dynamic shared memory is at least this much, so that one CTA (which owns all 512 TMEM columns) fills an SM.
 constexpr int kMinSmem = 120 * 1024;
 
-template <int T, int BN, int NACC, int EPI, bool OUT_F16, bool PAIR>
+template <int T, int BN, int NACC, int EPI, bool OUT_F16, bool PAIR, bool SPLIT = false>
 cudaError_t launch_t(const QGemmArgs& a, cudaStream_t stream) {
   constexpr int XROWS = PAIR ? BN / 2 : BN;
   using AC = AuxCfg<T, XROWS, EPI, OUT_F16>;
@@ -572,7 +588,8 @@ cudaError_t launch_t(const QGemmArgs& a, cudaStream_t stream) {
   }
   CUtensorMap my;
   const int esz = a.y_f16 ? 2 : 4;
-  const bool tma_store = (reinterpret_cast<uintptr_t>(a.y) & 15) == 0 && (a.ldy * esz) % 16 == 0;
+  // (split K writes the workspace with plain stores: its rows kp * M + t are not the output tensor's rows)
+  const bool tma_store = !SPLIT && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0 && (a.ldy * esz) % 16 == 0;
   if (tma_store) {
     cuuint64_t dims[2] = {(cuuint64_t)a.N, (cuuint64_t)a.M};
     cuuint64_t strides[1] = {(cuuint64_t)(a.ldy * esz)};
@@ -613,10 +630,11 @@ cudaError_t launch_t(const QGemmArgs& a, cudaStream_t stream) {
   p.status = a.status;
   p.upr = (int)((a.M + 15) / 16);
   p.ncta = PAIR ? 2 : 1;
+  p.nsplit = SPLIT ? a.nsplit : 1;
   const int64_t rtiles = (a.N + kBM * p.ncta - 1) / (kBM * p.ncta);
-  p.total_units = rtiles * p.upr;
+  p.total_units = rtiles * p.nsplit * p.upr;
   const int grid = qgemm_grid(a);
-  auto kern = qgemm_tc_kernel<T, BN, NACC, EPI, OUT_F16, PAIR>;
+  auto kern = qgemm_tc_kernel<T, BN, NACC, EPI, OUT_F16, PAIR, SPLIT>;
   const int smem_bytes = S::kAlloc > kMinSmem ? S::kAlloc : kMinSmem;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
   if (e != cudaSuccess) return e;
@@ -647,6 +665,37 @@ cudaError_t launch_epi(const QGemmArgs& a, cudaStream_t s) {
                  : launch_t<T, BN, NACC, kEpiStore, false, PAIR>(a, s);
 }
 
+// Split K: out[t][r] = epilogue(sum of the nsplit chunk results part[c][t][r], added in chunk order); the additions,
+// and the epilogue's arithmetic, are those of the single-CTA chunked epilogue above.
+template <int EPI, bool OUT_F16>
+__global__ void split_reduce_kernel(const float* __restrict__ part, int nsplit, int M, int N, void* y, int64_t ldy,
+                                    const float* __restrict__ aux, int64_t ldaux) {
+  const int64_t total = (int64_t)M * N;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t t = i / N, r = i - t * N;
+    float acc = __ldcs(part + i);
+    for (int c = 1; c < nsplit; ++c) acc = acc + __ldcs(part + (int64_t)c * total + i);
+    if (EPI == kEpiResid) acc = aux[t * ldaux + r] + acc;
+    if (EPI == kEpiSwiglu) acc = silu_f(aux[t * ldaux + r]) * acc;
+    if (OUT_F16) reinterpret_cast<__half*>(y)[t * ldy + r] = __float2half_rn(acc);
+    else reinterpret_cast<float*>(y)[t * ldy + r] = acc;
+  }
+}
+
+template <int EPI, bool OUT_F16>
+cudaError_t launch_split_reduce(const QGemmArgs& a, cudaStream_t stream) {
+  const int64_t total = a.M * a.N;
+  int64_t blocks = (total + 255) / 256;
+  if (blocks > 8LL * a.num_sms) blocks = 8LL * a.num_sms;
+  split_reduce_kernel<EPI, OUT_F16><<<(int)blocks, 256, 0, stream>>>(a.kpart, a.nsplit, (int)a.M, (int)a.N, a.y,
+                                                                     a.ldy, a.aux, a.ldaux);
+  return cudaGetLastError();
+}
+
+// Split K: the tile kernel (plain f32 stores into the workspace) and then the ordered reduction with the epilogue.
+template <int T>
+cudaError_t launch_split(const QGemmArgs& a, cudaStream_t s);
+
 // Instantiated tiles: pairs at BN 256 (one accumulator region, 4 A stages), 160 and 128 (two regions); single
 // CTAs at BN 192, 128 and 64 (two regions). The C ABI only passes these combinations.
 template <int T>
@@ -663,13 +712,38 @@ cudaError_t launch_fmt(const QGemmArgs& a, cudaStream_t s) {
   return cudaErrorInvalidValue;
 }
 
+template <int T>
+cudaError_t launch_split(const QGemmArgs& a, cudaStream_t s) {
+  QGemmArgs b = a;  // the tile kernel writes the chunk results: f32, plain store, [nsplit * M][N]
+  b.y = a.kpart;
+  b.y_f16 = 0;
+  b.ldy = a.N;
+  b.epilogue = kEpiStore;
+  b.aux = nullptr;
+  b.ldaux = 0;
+  cudaError_t e = cudaErrorInvalidValue;
+  if (b.pair) {
+    if (b.bn == 256) e = launch_t<T, 256, 1, kEpiStore, false, true, true>(b, s);
+    if (b.bn == 160) e = launch_t<T, 160, 2, kEpiStore, false, true, true>(b, s);
+    if (b.bn == 128) e = launch_t<T, 128, 2, kEpiStore, false, true, true>(b, s);
+  } else {
+    if (b.bn == 192) e = launch_t<T, 192, 2, kEpiStore, false, false, true>(b, s);
+    if (b.bn == 128) e = launch_t<T, 128, 2, kEpiStore, false, false, true>(b, s);
+    if (b.bn == 64) e = launch_t<T, 64, 2, kEpiStore, false, false, true>(b, s);
+  }
+  if (e != cudaSuccess) return e;
+  if (a.epilogue == kEpiResid) return launch_split_reduce<kEpiResid, false>(a, s);
+  if (a.epilogue == kEpiSwiglu) return launch_split_reduce<kEpiSwiglu, true>(a, s);
+  return a.y_f16 ? launch_split_reduce<kEpiStore, true>(a, s) : launch_split_reduce<kEpiStore, false>(a, s);
+}
+
 }  // namespace
 
 bool tensor_map_encoder_available() { return encoder() != nullptr; }
 
 int qgemm_grid(const QGemmArgs& a) {
   const int ncta = a.pair ? 2 : 1;
-  const int64_t units = (a.N + kBM * ncta - 1) / (kBM * ncta) * ((a.M + 15) / 16);
+  const int64_t units = (a.N + kBM * ncta - 1) / (kBM * ncta) * ((a.M + 15) / 16) * (a.nsplit > 1 ? a.nsplit : 1);
   int64_t grid = a.grid > 0 ? a.grid : a.num_sms;
   if (a.pair) {
     grid = grid / 2 < a.max_pairs ? grid / 2 : a.max_pairs;  // pairs that can be resident at once
@@ -695,7 +769,7 @@ int qgemm_max_pairs(int type, int bn) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   int n = 0;
-  const void* k = (const void*)qgemm_tc_kernel<12, 256, 1, kEpiStore, true, true>;
+  const void* k = (const void*)qgemm_tc_kernel<12, 256, 1, kEpiStore, true, true, false>;
   (void)type;
   (void)bn;
   if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kMinSmem) != cudaSuccess) return 0;
@@ -704,6 +778,15 @@ int qgemm_max_pairs(int type, int bn) {
 }
 
 cudaError_t launch_qgemm_tc(const QGemmArgs& a, cudaStream_t stream) {
+  if (a.nsplit > 1) {
+    if (!a.kpart) return cudaErrorInvalidValue;
+    switch (a.type) {
+      case 8: return launch_split<8>(a, stream);
+      case 12: return launch_split<12>(a, stream);
+      case 14: return launch_split<14>(a, stream);
+      default: return cudaErrorInvalidValue;
+    }
+  }
   switch (a.type) {
     case 8: return launch_fmt<8>(a, stream);
     case 12: return launch_fmt<12>(a, stream);
