@@ -42,6 +42,7 @@ extern "C" {
 #define YAH_ERR_CUDA 4        /* a CUDA runtime or driver call failed */
 #define YAH_ERR_DEVICE 5      /* no sm_100 device, or a kernel reported a bounded-wait timeout */
 #define YAH_ERR_NCCL 6        /* a collective failed (tensor-parallel layer) */
+#define YAH_ERR_IO 7          /* a file could not be opened or mapped, or is not a well-formed GGUF file */
 
 /* GGML type ids (engine/core/gguf.hpp GgmlType). */
 #define YAH_Q8_0 8
@@ -261,6 +262,51 @@ int yah_add_rmsnorm(float* h, int64_t ldh, const void* d, int d_dtype, int64_t l
                     float gain, void* out, int64_t ldo, void* stream);
 /* ncclAllReduce(sum) of f16 in place (the speed mode's partials: half the bytes of yah_tp_allreduce_f32). */
 int yah_tp_allreduce_f16(yah_tp_comm* comm, void* buf, int64_t count, void* stream);
+
+/* ---- GGUF files: the quant-block loader (engine/core/gguf.hpp:74-105 core::Gguf, engine/core/gguf.cpp) ----
+ * yah_gguf_open maps a GGUF (version 2 or 3) file read-only and parses its metadata and tensor table; the tensor
+ * bytes are not copied. Every read is bounds-checked: a truncated or malformed file is refused with YAH_ERR_IO, a
+ * tensor type of unknown block size with YAH_ERR_UNSUPPORTED. Tensors are described as the reference's TensorRef
+ * (engine/model/weights.hpp:15-25): dims in GGUF order, dims[0] = ne0 = the row length (K of a linear weight),
+ * dims[1] = ne1 = the row count (N); `offset` is from the start of the tensor-data region (aligned to
+ * general.alignment, default 32). A weight tensor's rows are then exactly the layout the GEMM / GEMV take. */
+typedef struct yah_gguf yah_gguf;
+typedef struct {
+  char name[128];   /* NUL-terminated (GGUF names of up to 127 bytes) */
+  int ggml_type;
+  int n_dims;       /* 1..4; unused dims are 1 */
+  int64_t dims[4];
+  uint64_t offset;  /* bytes from the start of the tensor-data region */
+  uint64_t bytes;   /* dims product / block elements * block bytes */
+} yah_gguf_tensor;
+int yah_gguf_open(const char* path, yah_gguf** out);
+int yah_gguf_close(yah_gguf* g);
+int yah_gguf_version(const yah_gguf* g, uint32_t* version);
+int yah_gguf_tensor_count(const yah_gguf* g, int64_t* n);
+int yah_gguf_tensor_info(const yah_gguf* g, int64_t index, yah_gguf_tensor* out);
+/* index of the tensor called `name` (core::Gguf::Find); YAH_ERR_ARG and index -1 when there is none. */
+int yah_gguf_find(const yah_gguf* g, const char* name, int64_t* index);
+/* host view of the tensor-data region (core::Gguf::tensor_data_base / tensor_data_size). */
+int yah_gguf_data(const yah_gguf* g, const void** base, uint64_t* bytes);
+/* Metadata (core::Gguf::Meta): the GGUF value kind of `key` (0 u8, 1 i8, 2 u16, 3 i16, 4 u32, 5 i32, 6 f32,
+ * 7 bool, 8 string, 9 array, 10 u64, 11 i64, 12 f64) and, for arrays, the element count (1 otherwise); the value of
+ * an integer or bool key (signed keys sign-extended, u64 keys as their two's complement bits); of a numeric key as a
+ * double; of a string key (copied NUL-terminated into buf of cap bytes, truncated to fit; *len = its full length). */
+int yah_gguf_meta_kind(const yah_gguf* g, const char* key, int* kind, uint64_t* count);
+int yah_gguf_meta_int(const yah_gguf* g, const char* key, int64_t* value);
+int yah_gguf_meta_float(const yah_gguf* g, const char* key, double* value);
+int yah_gguf_meta_string(const yah_gguf* g, const char* key, char* buf, int64_t cap, int64_t* len);
+
+/* Device copies of the tensor-data region (LoomWeights, engine/model/loom_runtime.hpp:487-516): device buffers of
+ * at most chunk_bytes (0 = 1 GiB, a single larger tensor gets a chunk of its own) cut at tensor boundaries, each
+ * followed by 64 KB of zeros, on the current device; the copy is complete when the call returns. yah_weights_ref
+ * returns the device address of [offset, offset + bytes) of the region (a tensor's offset and bytes), which must lie
+ * in one chunk: the tensor's rows as the GEMM / GEMV take them, no repacking. */
+typedef struct yah_weights yah_weights;
+int yah_weights_upload(const yah_gguf* g, uint64_t chunk_bytes, void* stream, yah_weights** out);
+int yah_weights_ref(const yah_weights* w, uint64_t offset, uint64_t bytes, const void** dev);
+int yah_weights_chunk_count(const yah_weights* w, int64_t* n);
+int yah_weights_free(yah_weights* w);
 
 #if defined(__GNUC__)
 #pragma GCC visibility pop

@@ -7,8 +7,9 @@ Modules:
   ops      qgemm / qgemv / dequant: the reference's kernel kinds over the C ABI
   tp       tensor-parallel layer stack: shard planning, NCCL communicator, Llama-shaped linear stack
   tune     tile-configuration search and the tile table read by yah_qgemm's automatic choice
+  gguf_file  GGUF reader and device weight chunks (the reference's core::Gguf / LoomWeights)
 """
 from . import formats  # noqa: F401
 from ._lib import YahError, lib  # noqa: F401
-from . import device, ops, tp, tune  # noqa: F401
+from . import device, gguf_file, ops, tp, tune  # noqa: F401
 from .device import Device, DeviceBuffer, Event, Graph, PinnedBuffer, Stream, device_count  # noqa: F401

@@ -82,7 +82,28 @@ SYMBOLS = {
     "yah_tile_rules_set": (c_int, [c_vp, c_int]),
     "yah_tile_rules_clear": (c_int, []),
     "yah_tile_rules_count": (c_int, [P(c_int)]),
+    "yah_gguf_open": (c_int, [ctypes.c_char_p, P(c_vp)]),
+    "yah_gguf_close": (c_int, [c_vp]),
+    "yah_gguf_version": (c_int, [c_vp, P(ctypes.c_uint32)]),
+    "yah_gguf_tensor_count": (c_int, [c_vp, P(c_i64)]),
+    "yah_gguf_tensor_info": (c_int, [c_vp, c_i64, c_vp]),
+    "yah_gguf_find": (c_int, [c_vp, ctypes.c_char_p, P(c_i64)]),
+    "yah_gguf_data": (c_int, [c_vp, P(c_vp), P(ctypes.c_uint64)]),
+    "yah_gguf_meta_kind": (c_int, [c_vp, ctypes.c_char_p, P(c_int), P(ctypes.c_uint64)]),
+    "yah_gguf_meta_int": (c_int, [c_vp, ctypes.c_char_p, P(c_i64)]),
+    "yah_gguf_meta_float": (c_int, [c_vp, ctypes.c_char_p, P(ctypes.c_double)]),
+    "yah_gguf_meta_string": (c_int, [c_vp, ctypes.c_char_p, ctypes.c_char_p, c_i64, P(c_i64)]),
+    "yah_weights_upload": (c_int, [c_vp, ctypes.c_uint64, c_vp, P(c_vp)]),
+    "yah_weights_ref": (c_int, [c_vp, ctypes.c_uint64, ctypes.c_uint64, P(c_vp)]),
+    "yah_weights_chunk_count": (c_int, [c_vp, P(c_i64)]),
+    "yah_weights_free": (c_int, [c_vp]),
 }
+
+
+class GgufTensorInfo(ctypes.Structure):
+    """yah_gguf_tensor (include/yah_qgemm.h)."""
+    _fields_ = [("name", ctypes.c_char * 128), ("ggml_type", c_int), ("n_dims", c_int), ("dims", c_i64 * 4),
+                ("offset", ctypes.c_uint64), ("bytes", ctypes.c_uint64)]
 
 
 class TileRule(ctypes.Structure):
@@ -92,7 +113,7 @@ class TileRule(ctypes.Structure):
 TP_ID_BYTES = 128
 
 # status codes (include/yah_qgemm.h)
-OK, ERR_ARG, ERR_UNSUPPORTED, ERR_SIZE, ERR_CUDA, ERR_DEVICE, ERR_NCCL = range(7)
+OK, ERR_ARG, ERR_UNSUPPORTED, ERR_SIZE, ERR_CUDA, ERR_DEVICE, ERR_NCCL, ERR_IO = range(8)
 F32, F16 = 0, 1
 EPI_STORE, EPI_RESID, EPI_SWIGLU = 0, 1, 2
 

@@ -29,6 +29,17 @@ int fail(int code, const char* fmt, ...) {
   return code;
 }
 
+}  // namespace
+
+namespace yah {
+int set_error(int code, const std::string& msg) {
+  g_err = msg;
+  return code;
+}
+}  // namespace yah
+
+namespace {
+
 int cuda_fail(cudaError_t e, const char* what) {
   return fail(YAH_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
 }

@@ -2,9 +2,14 @@
 // Every launcher assumes its arguments were validated by the C ABI and returns a cudaError_t.
 #pragma once
 #include <cuda_runtime.h>
+
+#include <string>
 #include <stdint.h>
 
 namespace yah {
+
+// Records the calling thread's last error message (yah_last_error) and returns `code` (capi.cu).
+int set_error(int code, const std::string& msg);
 
 enum Epilogue : int { kEpiStore = 0, kEpiResid = 1, kEpiSwiglu = 2 };
 
