@@ -178,6 +178,16 @@ int yah_qgemm_tile(const void* w, int ggml_type, int64_t N, int64_t K, int64_t w
                    const void* x, int64_t M, int64_t ldx, void* y, int y_dtype, int64_t ldy, int epilogue,
                    const void* aux, int64_t ldaux, int bn, int grid, int64_t kchunk, int cta_pair, void* stream);
 
+/* The fused gate+up SwiGLU of the feed-forward block (the reference's ffn kind, gen_gemm_tile.py:316-318, :1675):
+ * y[M][ldy] = f16(silu(x W_gate^T) * (x W_up^T)), both weight tensors of the same type, shape and row stride. One
+ * tile GEMM: each CTA decodes 64 gate rows and the same 64 up rows into its 128 TMEM lanes and its epilogue
+ * combines them, so the f32 gate tensor never goes through memory. Results are identical to yah_qgemm of the gate
+ * (f32 out) followed by yah_qgemm of the up weights with YAH_EPI_SWIGLU on that gate, for the same accumulation
+ * chunks (2048 when K > 4096, else none). bn / cta_pair as in yah_qgemm_tile (0 / -1 = automatic). */
+int yah_qgemm_ffn(const void* w_gate, const void* w_up, int ggml_type, int64_t N, int64_t K, int64_t w_row_stride,
+                  int64_t kb_off, const void* x, int64_t M, int64_t ldx, void* y, int64_t ldy, int bn, int cta_pair,
+                  void* stream);
+
 /* Tile table (opt-in): tuned tiles for yah_qgemm's automatic choice, the counterpart of the reference's tuned
  * tables consumed by LoomPrefill::PickGemm (engine/model/loom_prefill.hpp:908-949; engine/tune/tune.py). A call
  * (ggml_type, epilogue, y_dtype, N, K, M) uses the matching rule with the smallest m_max >= M (else the largest

@@ -244,3 +244,41 @@ def test_split_k_config3_decode_shapes(pkg, F, O, dev):
         yu = pkg.ops.qgemm(dev, w, t, x, N=N, K=K, grid=dev.sm_count)
         assert np.array_equal(y.view(np.uint32), yu.view(np.uint32))
         check(O, y[:, rows], O.gemm_ref(O.dequant_f16(t, w[rows], len(rows), K), x))
+
+
+@pytest.mark.parametrize("name", FMTS)
+@pytest.mark.parametrize("pair,bn", [(-1, 0), (1, 160), (0, 192), (0, 64)])
+@pytest.mark.parametrize("M,N,K", [(96, 320, 2048), (33, 200, 2048), (300, 64, 8192)])  # Q6_K rows: K % 2048
+def test_ffn_matches_gate_then_up(pkg, F, O, dev, name, pair, bn, M, N, K):
+    """The fused gate+up SwiGLU (one GEMM, gate and up rows in the two halves of a CTA's TMEM lanes) gives the bits
+    of the gate GEMM (f32) followed by the up GEMM with the swiglu epilogue, and is within the bar of the oracle;
+    ragged N (tiles of 64 output rows), ragged M, and K above 4096 (chunked accumulation)."""
+    t = F.type_of(name)
+    wg = F.synth_weights(t, N, K, seed=41)
+    wu = F.synth_weights(t, N, K, seed=42)
+    # Q4_K / Q6_K activations scaled by 2^-6 (exact) keep silu(gate) * up inside the f16 range at these K; the Q8_0
+    # weights are ~50x smaller and need no scaling (scaled, its outputs would sit in f16's subnormal range)
+    scale = 1.0 if name == "q8_0" else 1 / 64
+    x = (F.synth_activations(M, K, seed=43).astype(np.float32) * scale).astype(np.float16)
+    y = pkg.ops.qgemm_ffn(dev, wg, wu, t, x, N=N, K=K, bn=bn, pair=pair)
+    g = pkg.ops.qgemm(dev, wg, t, x, N=N, K=K, out_dtype="f32")
+    ref2 = pkg.ops.qgemm(dev, wu, t, x, N=N, K=K, kind="swiglu", aux=g)
+    assert y.dtype == np.float16 and np.isfinite(y).all()
+    assert np.array_equal(y.view(np.uint16), ref2.view(np.uint16))
+    gref = O.gemm_ref(O.dequant_f16(t, wg, N, K), x)
+    uref = O.gemm_ref(O.dequant_f16(t, wu, N, K), x)
+    check(O, y, O.epilogue_ref(uref, 2, gref.astype(np.float32)), f16=True)
+
+
+def test_ffn_k_window(pkg, F, O, dev):
+    """The fused gate+up on a K window of longer rows (kb_off and the row stride)."""
+    t = F.Q4_K
+    M, N, K, kb_off = 40, 256, 1024, 4
+    Kf = K + 256 * kb_off + 512
+    wg = F.synth_weights(t, N, Kf, seed=51)
+    wu = F.synth_weights(t, N, Kf, seed=52)
+    x = (F.synth_activations(M, K, seed=53).astype(np.float32) / 64).astype(np.float16)
+    y = pkg.ops.qgemm_ffn(dev, wg, wu, t, x, N=N, K=K, kb_off=kb_off, w_row_stride=wg.shape[1])
+    gref = O.gemm_ref(O.dequant_f16(t, wg, N, K, kb_off=kb_off), x)
+    uref = O.gemm_ref(O.dequant_f16(t, wu, N, K, kb_off=kb_off), x)
+    check(O, y, O.epilogue_ref(uref, 2, gref.astype(np.float32)), f16=True)

@@ -63,6 +63,8 @@ SYMBOLS = {
                           c_vp, c_i64, c_vp]),
     "yah_qgemm_tile": (c_int, [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_int, c_i64,
                                c_int, c_vp, c_i64, c_int, c_int, c_i64, c_int, c_vp]),
+    "yah_qgemm_ffn": (c_int, [c_vp, c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_i64, c_int,
+                              c_int, c_vp]),
     "yah_qgemv": (c_int, [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_int, c_i64, c_int,
                           c_vp, c_i64, c_vp]),
     "yah_qgemv_noalloc": (c_int, [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_int, c_i64,

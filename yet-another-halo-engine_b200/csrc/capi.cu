@@ -535,6 +535,61 @@ int yah_qgemm_tile(const void* w, int t, int64_t N, int64_t K, int64_t w_row_str
   return after_launch(yah::launch_qgemm_tc(a, (cudaStream_t)stream), "qgemm launch");
 }
 
+int yah_qgemm_ffn(const void* w_gate, const void* w_up, int t, int64_t N, int64_t K, int64_t w_row_stride,
+                  int64_t kb_off, const void* x, int64_t M, int64_t ldx, void* y, int64_t ldy, int bn, int cta_pair,
+                  void* stream) {
+  int rc = check_linear(w_gate, t, N, K, w_row_stride, kb_off, x, M, ldx, y, YAH_F16, ldy, YAH_EPI_STORE, nullptr, 0);
+  if (rc) return rc;
+  rc = check_linear(w_up, t, N, K, w_row_stride, kb_off, x, M, ldx, y, YAH_F16, ldy, YAH_EPI_STORE, nullptr, 0);
+  if (rc) return rc;
+  DevState* s;
+  rc = dev_state(&s);
+  if (rc) return rc;
+  const int64_t kchunk = K > 4096 ? 2048 : K;  // the automatic chunk of yah_qgemm_tile
+  yah::QGemmArgs a;
+  a.w = w_gate;
+  a.w2 = w_up;
+  a.type = t;
+  a.N = N;
+  a.K = K;
+  a.w_row_stride = w_row_stride;
+  a.kb_off = kb_off;
+  a.x = x;
+  a.M = M;
+  a.ldx = ldx;
+  a.y = y;
+  a.y_f16 = 1;
+  a.ldy = ldy;
+  a.epilogue = yah::kEpiFfn;
+  a.aux = nullptr;
+  a.ldaux = 0;
+  a.status = s->status;
+  a.num_sms = sms_of(s);
+  a.grid = 0;
+  a.kchunk = kchunk;
+  a.scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (s->max_pairs < 0) s->max_pairs = yah::qgemm_max_pairs(t, bn);
+  }
+  a.max_pairs = s->max_pairs;
+  a.pair = (cta_pair != 0 && a.max_pairs > 0) ? 1 : 0;
+  if (cta_pair == 1 && !a.pair) return fail(YAH_ERR_UNSUPPORTED, "2-CTA clusters are not available on this device");
+  if (bn == 0) bn = a.pair ? (kchunk < K ? 160 : 256) : 192;
+  if (a.pair ? (bn != 256 && bn != 160 && bn != 128) : (bn != 192 && bn != 128 && bn != 64))
+    return fail(YAH_ERR_ARG, "bn %d is not a %s tile width (pairs: 256, 160, 128; single CTAs: 192, 128, 64)", bn,
+                a.pair ? "2-SM pair" : "single-CTA");
+  a.bn = bn;
+  if (kchunk < K) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    const size_t need = (size_t)yah::qgemm_grid(a) * bn * 128 * sizeof(float);
+    rc = grow(reinterpret_cast<void**>(&s->gemm_scratch), &s->gemm_scratch_bytes, need);
+    if (rc) return rc;
+    a.scratch = s->gemm_scratch;
+  }
+  return after_launch(yah::launch_qgemm_tc(a, (cudaStream_t)stream), "qgemm_ffn launch");
+}
+
 // The opt-in tile table (yah_tile_rules_set): the only mutable process-wide configuration of the library.
 std::vector<yah_tile_rule> g_rules;
 

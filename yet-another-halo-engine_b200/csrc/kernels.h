@@ -11,7 +11,8 @@ namespace yah {
 // Records the calling thread's last error message (yah_last_error) and returns `code` (capi.cu).
 int set_error(int code, const std::string& msg);
 
-enum Epilogue : int { kEpiStore = 0, kEpiResid = 1, kEpiSwiglu = 2 };
+// kEpiFfn (tile GEMM only): y = f16(silu(x W^T) * (x w2^T)), the gate and up weights in one GEMM.
+enum Epilogue : int { kEpiStore = 0, kEpiResid = 1, kEpiSwiglu = 2, kEpiFfn = 3 };
 
 // Tile-GEMM problem (token-major): y[M][ldy] (+)= x[M][ldx] (f16) * W[N][K]^T, W in GGUF rows.
 struct QGemmArgs {
@@ -36,6 +37,7 @@ struct QGemmArgs {
   float* scratch;       // grid * bn * 128 f32 chunk sums when kchunk < K, else unused
   int pair;             // 1: 2-SM pairs (tcgen05 cta_group::2, clusters of 2), 0: one CTA per tile
   int max_pairs;        // resident 2-CTA clusters the device holds (pair mode)
+  const void* w2 = nullptr;  // kEpiFfn: the up weights (same type, shape and row stride as w, the gate weights)
   int nsplit = 1;       // > 1: each accumulation chunk of a tile is its own work unit (split K, one chunk each)
   float* kpart = nullptr;  // nsplit * M * N f32 chunk results when nsplit > 1, summed in chunk order afterwards
 };

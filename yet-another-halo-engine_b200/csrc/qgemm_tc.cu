@@ -132,7 +132,7 @@ struct AuxCfg {
   static constexpr int kCH = OUT_F16 ? 16 : 8;
   static constexpr int kSlot = kCH * 128 * 4;
   static constexpr int kBase = Smem<T, XR, 0>::kAlloc;
-  static constexpr int kDepth = EPI == kEpiStore ? 0
+  static constexpr int kDepth = (EPI == kEpiStore || EPI == kEpiFfn) ? 0
                                 : kBase + 4 * kSlot <= kSmemLimit ? 4
                                 : kBase + 2 * kSlot <= kSmemLimit ? 2 : 0;
   static constexpr int kBytes = kDepth * kSlot;
@@ -183,6 +183,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int NSW = Fmt<T>::kNSW;
   constexpr int WBOX = Fmt<T>::kBox;
   constexpr int NCTA = PAIR ? 2 : 1;
+  // weight rows whose outputs a CTA produces per tile: 128 (TMEM lanes), or 64 under kEpiFfn (lanes 0-63 gate,
+  // 64-127 the same rows of up)
+  constexpr int kTileRows = EPI == kEpiFfn ? 64 : kBM;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::kBarOff);
@@ -275,7 +278,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t s = 0;
       bool ok = true;
       while (ok && sc.next(rt, kp, t0, nt)) {
-        const int row0 = (rt * NCTA + (int)rank) * kBM;
+        const int row0 = (rt * NCTA + (int)rank) * kTileRows;
         const int sb0 = split ? kp * sch / 2 : 0, sb1 = split ? min(nst, (kp + 1) * sch) / 2 : p.K / 256;
         for (int sb = sb0; sb < sb1; ++sb, ++s) {
           const uint32_t ws = s % NSW, wph = (s / NSW) & 1;
@@ -285,7 +288,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           int xw;
           if (T == 14) xw = (int)(((sbg * 210) & ~int64_t(15)) >> 1);
           else xw = (int)(sbg * (Fmt<T>::kSB / 2));
-          tma_load_2d(smem + S::kWOff + ws * S::kWStage, &tmap_w, &wfull[ws], xw, row0);
+          if constexpr (EPI == kEpiFfn) {  // gate rows to stage rows 0-63, the same up rows to 64-127
+            tma_load_2d(smem + S::kWOff + ws * S::kWStage, &tmap_w, &wfull[ws], xw, row0);
+            tma_load_2d(smem + S::kWOff + ws * S::kWStage + 64 * WBOX, &tmap_aux, &wfull[ws], xw, row0);
+          } else {
+            tma_load_2d(smem + S::kWOff + ws * S::kWStage, &tmap_w, &wfull[ws], xw, row0);
+          }
         }
       }
       for (uint32_t i = (s > (uint32_t)NSW ? s - NSW : 0); i < s; ++i)
@@ -419,8 +427,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* abuf = smem + S::kAuxOff;
     uint32_t aux_used = 0;  // aux chunks consumed so far (slot aux_used % AD)
     while (ok && sc.next(rt, kp, t0, nt)) {
-      const int row0 = (rt * NCTA + (int)rank) * kBM;
-      const int row = row0 + rloc;
+      const int row0 = (rt * NCTA + (int)rank) * kTileRows;
+      const int row = row0 + (EPI == kEpiFfn ? (rloc & 63) : rloc);  // the output row of this lane's accumulator
       const bool row_ok = row < p.N;
       const int ncks = (nt + CH - 1) / CH;  // aux chunks of this tile (its last accumulation chunk)
       const int ch0 = split ? kp : 0, ch1 = split ? kp + 1 : nch;
@@ -460,6 +468,43 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int jj = 0; jj < CH; ++jj)
                 if (jj < jn) __stcg(part + (size_t)(j0 + jj) * kBM, val[jj]);
+            }
+            continue;
+          }
+          if constexpr (EPI == kEpiFfn) {
+            // lanes 64-127 hand their up values to lanes 0-63 (same output rows) through shared memory; those
+            // store f16(silu(gate) * up), the arithmetic of the swiglu epilogue
+            // (obuf: the f32 exchange [CH tokens][64 rows] in its first 4 KB, then two f16 [CH][64] staging tiles
+            // for the TMA stores)
+            float* ub = reinterpret_cast<float*>(obuf);
+            __half* sb = reinterpret_cast<__half*>(obuf + 4096 + (nbuf & 1) * 2048);
+            if (rloc >= 64) {
+#pragma unroll
+              for (int jj = 0; jj < CH; ++jj) ub[jj * 64 + rloc - 64] = val[jj];
+            }
+            if (p.tma_store && leader) bulk_wait_read<1>();  // the store that last used this staging tile read it
+            named_bar(1, 128);
+            if (rloc < 64) {
+              if (p.tma_store) {
+#pragma unroll
+                for (int jj = 0; jj < CH; ++jj) sb[jj * 64 + rloc] = __float2half_rn(silu_f(val[jj]) * ub[jj * 64 + rloc]);
+                fence_proxy_async();
+              } else if (row_ok) {
+#pragma unroll
+                for (int jj = 0; jj < CH; ++jj) {
+                  if (jj >= jn) break;
+                  reinterpret_cast<__half*>(p.y)[(int64_t)(t0 + j0 + jj) * p.ldy + row] =
+                      __float2half_rn(silu_f(val[jj]) * ub[jj * 64 + rloc]);
+                }
+              }
+            }
+            named_bar(1, 128);  // the exchange buffer takes the next CH tokens; the staging tile is complete
+            if (p.tma_store) {
+              if (leader) {
+                tma_store_2d(&tmap_y, sb, row0, t0 + j0);
+                bulk_commit();
+              }
+              ++nbuf;
             }
             continue;
           }
@@ -564,15 +609,16 @@ cudaError_t launch_t(const QGemmArgs& a, cudaStream_t stream) {
   using S = Smem<T, XROWS, AC::kBytes>;
   EncodeTiledFn enc = encoder();
   if (!enc) return cudaErrorNotSupported;
-  CUtensorMap mw, mx;
-  {
+  constexpr int kTileRows = EPI == kEpiFfn ? 64 : kBM;  // weight rows per CTA tile (per box, per tensor)
+  CUtensorMap mw, mx, mw2;
+  for (int k = 0; k < (EPI == kEpiFfn ? 2 : 1); ++k) {  // kEpiFfn: the gate and the up weights, 64-row boxes
     const int64_t window_bytes = (a.kb_off + a.K / 256) * Fmt<T>::kSB;
     cuuint64_t dims[2] = {(cuuint64_t)((window_bytes + 1) / 2), (cuuint64_t)a.N};
     cuuint64_t strides[1] = {(cuuint64_t)a.w_row_stride};
-    cuuint32_t box[2] = {(cuuint32_t)(Fmt<T>::kBox / 2), (cuuint32_t)kBM};
+    cuuint32_t box[2] = {(cuuint32_t)(Fmt<T>::kBox / 2), (cuuint32_t)kTileRows};
     cuuint32_t es[2] = {1, 1};
-    if (enc(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(a.w), dims, strides, box, es,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+    if (enc(k ? &mw2 : &mw, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(k ? a.w2 : a.w), dims, strides,
+            box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return cudaErrorInvalidValue;
   }
@@ -593,7 +639,7 @@ cudaError_t launch_t(const QGemmArgs& a, cudaStream_t stream) {
   if (tma_store) {
     cuuint64_t dims[2] = {(cuuint64_t)a.N, (cuuint64_t)a.M};
     cuuint64_t strides[1] = {(cuuint64_t)(a.ldy * esz)};
-    cuuint32_t box[2] = {(cuuint32_t)kBM, (cuuint32_t)(a.y_f16 ? 16 : 8)};
+    cuuint32_t box[2] = {(cuuint32_t)kTileRows, (cuuint32_t)(a.y_f16 ? 16 : 8)};
     cuuint32_t es[2] = {1, 1};
     if (enc(&my, a.y_f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, a.y, dims, strides,
             box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
@@ -602,7 +648,7 @@ cudaError_t launch_t(const QGemmArgs& a, cudaStream_t stream) {
   } else {
     my = mx;  // unused
   }
-  CUtensorMap maux = mx;  // unused unless the aux operand is prefetched
+  CUtensorMap maux = EPI == kEpiFfn ? mw2 : mx;  // the up weights (kEpiFfn), or the aux prefetch, else unused
   const bool aux_tma = AC::kDepth > 0 && a.aux && (reinterpret_cast<uintptr_t>(a.aux) & 15) == 0 && a.ldaux % 4 == 0;
   if (aux_tma) {
     cuuint64_t dims[2] = {(cuuint64_t)a.N, (cuuint64_t)a.M};
@@ -631,7 +677,7 @@ cudaError_t launch_t(const QGemmArgs& a, cudaStream_t stream) {
   p.upr = (int)((a.M + 15) / 16);
   p.ncta = PAIR ? 2 : 1;
   p.nsplit = SPLIT ? a.nsplit : 1;
-  const int64_t rtiles = (a.N + kBM * p.ncta - 1) / (kBM * p.ncta);
+  const int64_t rtiles = (a.N + kTileRows * p.ncta - 1) / (kTileRows * p.ncta);
   p.total_units = rtiles * p.nsplit * p.upr;
   const int grid = qgemm_grid(a);
   auto kern = qgemm_tc_kernel<T, BN, NACC, EPI, OUT_F16, PAIR, SPLIT>;
@@ -659,6 +705,7 @@ cudaError_t launch_t(const QGemmArgs& a, cudaStream_t stream) {
 
 template <int T, int BN, int NACC, bool PAIR>
 cudaError_t launch_epi(const QGemmArgs& a, cudaStream_t s) {
+  if (a.epilogue == kEpiFfn) return a.w2 ? launch_t<T, BN, NACC, kEpiFfn, true, PAIR>(a, s) : cudaErrorInvalidValue;
   if (a.epilogue == kEpiResid) return launch_t<T, BN, NACC, kEpiResid, false, PAIR>(a, s);
   if (a.epilogue == kEpiSwiglu) return launch_t<T, BN, NACC, kEpiSwiglu, true, PAIR>(a, s);
   return a.y_f16 ? launch_t<T, BN, NACC, kEpiStore, true, PAIR>(a, s)
@@ -743,7 +790,8 @@ bool tensor_map_encoder_available() { return encoder() != nullptr; }
 
 int qgemm_grid(const QGemmArgs& a) {
   const int ncta = a.pair ? 2 : 1;
-  const int64_t units = (a.N + kBM * ncta - 1) / (kBM * ncta) * ((a.M + 15) / 16) * (a.nsplit > 1 ? a.nsplit : 1);
+  const int rows = (a.epilogue == kEpiFfn ? 64 : kBM) * ncta;  // output rows per tile
+  const int64_t units = (a.N + rows - 1) / rows * ((a.M + 15) / 16) * (a.nsplit > 1 ? a.nsplit : 1);
   int64_t grid = a.grid > 0 ? a.grid : a.num_sms;
   if (a.pair) {
     grid = grid / 2 < a.max_pairs ? grid / 2 : a.max_pairs;  // pairs that can be resident at once
@@ -778,6 +826,7 @@ int qgemm_max_pairs(int type, int bn) {
 }
 
 cudaError_t launch_qgemm_tc(const QGemmArgs& a, cudaStream_t stream) {
+  if (a.nsplit > 1 && a.epilogue == kEpiFfn) return cudaErrorInvalidValue;  // the fused gate+up does not split
   if (a.nsplit > 1) {
     if (!a.kpart) return cudaErrorInvalidValue;
     switch (a.type) {

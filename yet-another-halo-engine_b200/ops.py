@@ -130,6 +130,32 @@ def qgemv(dev: Device, w, fmt, x, N=None, K=None, kind="plain", out_dtype="f32",
                  w_row_stride=w_row_stride, gemv=True)
 
 
+def qgemm_ffn_ptr(w_gate, w_up, fmt, N, K, w_row_stride, kb_off, x, M, ldx, y, ldy, bn=0, pair=-1, stream=None):
+    """yah_qgemm_ffn: y (f16) = silu(x W_gate^T) * (x W_up^T), one tile GEMM."""
+    check(lib().yah_qgemm_ffn(w_gate, w_up, F.type_of(fmt), N, K, w_row_stride, kb_off, x, M, ldx, y, ldy, bn, pair,
+                              stream))
+
+
+def qgemm_ffn(dev: Device, w_gate, w_up, fmt, x, N=None, K=None, kb_off=0, w_row_stride=None, bn=0, pair=-1):
+    """The fused gate+up SwiGLU (the reference's ffn kind) on numpy inputs: f16 [M][N]."""
+    t = F.type_of(fmt)
+    x = np.ascontiguousarray(x, dtype=np.float16)
+    M = x.shape[0]
+    K = K if K is not None else x.shape[1]
+    N = N if N is not None else w_gate.shape[0]
+    if w_row_stride is None:
+        w_row_stride = w_gate.shape[1] if isinstance(w_gate, np.ndarray) else F.row_bytes(t, K + 256 * kb_off)
+    gd, ud, xd = _as_dev(dev, w_gate), _as_dev(dev, w_up), dev.upload(x)
+    yd = dev.empty(M * N * 2)
+    qgemm_ffn_ptr(gd.ptr, ud.ptr, t, N, K, w_row_stride, kb_off, xd.ptr, M, x.shape[1], yd.ptr, N, bn, pair)
+    dev.synchronize()
+    y = yd.download(np.float16, (M, N))
+    code = dev.status_word()
+    if code:
+        raise RuntimeError(f"kernel reported bounded-wait failure code {code}")
+    return y
+
+
 def realign(dev: Device, w, stride: int | None = None, stream=None):
     """Copy GGUF rows (numpy [N][row_bytes] or a DeviceBuffer of packed rows) into rows `stride` bytes apart
     (default: row_bytes rounded up to 16), as TMA needs; returns (DeviceBuffer, stride). For tensors whose packed
