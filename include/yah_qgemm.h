@@ -183,7 +183,8 @@ int yah_qgemm_tile(const void* w, int ggml_type, int64_t N, int64_t K, int64_t w
  * tile GEMM: each CTA decodes 64 gate rows and the same 64 up rows into its 128 TMEM lanes and its epilogue
  * combines them, so the f32 gate tensor never goes through memory. Results are identical to yah_qgemm of the gate
  * (f32 out) followed by yah_qgemm of the up weights with YAH_EPI_SWIGLU on that gate, for the same accumulation
- * chunks (2048 when K > 4096, else none). bn / cta_pair as in yah_qgemm_tile (0 / -1 = automatic). */
+ * chunks (2048 when K > 4096, else none). bn / cta_pair as in yah_qgemm_tile (0 / -1 = automatic: single CTAs,
+ * 192 tokens). */
 int yah_qgemm_ffn(const void* w_gate, const void* w_up, int ggml_type, int64_t N, int64_t K, int64_t w_row_stride,
                   int64_t kb_off, const void* x, int64_t M, int64_t ldx, void* y, int64_t ldy, int bn, int cta_pair,
                   void* stream);

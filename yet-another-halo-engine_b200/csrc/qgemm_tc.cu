@@ -165,7 +165,11 @@ struct Sched {
   }
 };
 
-__device__ __forceinline__ float silu_f(float g) { return g / (1.0f + __expf(-g)); }
+// silu(g) = g / (1 + e^-g) with CUDA's fast exponential and fast division (__fdividef: ~2 ulp; a divisor that has
+// overflowed to infinity, g below about -88, gives g * 0 = -0, the limit). The IEEE division it replaces took its
+// slow path whenever e^-g overflowed, frequent with gate values of a few hundred, and halved the swiglu epilogue's
+// rate (914-1117 us against 535 us for the residual epilogue at 4096 x 14336 x 4096).
+__device__ __forceinline__ float silu_f(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
 
 template <int T, int BN, int NACC, int EPI, bool OUT_F16, bool PAIR, bool SPLIT>
 __global__ void __launch_bounds__(kThreads, 1)
