@@ -126,6 +126,47 @@ def shard_layer(shape: StackShape, full: dict, parts: int, part: int) -> dict:
     }
 
 
+# ----------------------------------------------------------------------------------------------- GGUF models
+# The tensors of one Llama-style block in a GGUF file (llama.cpp's names; the reference resolves its own model's
+# per-layer tensors the same way, engine/model/weights.hpp:27-52).
+GGUF_LAYER_TENSORS = {"q": "attn_q", "k": "attn_k", "v": "attn_v", "o": "attn_output", "gate": "ffn_gate",
+                      "up": "ffn_up", "down": "ffn_down"}
+
+
+def shape_from_gguf(g) -> StackShape:
+    """The stack's shape from a GGUF file's metadata ({arch}.block_count, embedding_length, feed_forward_length,
+    attention.head_count, attention.head_count_kv) and its weight format. The stack runs one format for all of its
+    linears, so a file whose block tensors mix formats (as some mixed-precision quantisations do) is refused."""
+    arch = g.meta("general.architecture")
+    key = lambda k: g.meta(f"{arch}.{k}")  # noqa: E731
+    hidden, n_q = key("embedding_length"), key("attention.head_count")
+    shape = StackShape(layers=key("block_count"), hidden=hidden, n_q=n_q, n_kv=key("attention.head_count_kv"),
+                       head_dim=hidden // n_q, ff=key("feed_forward_length"),
+                       fmt=g[f"blk.0.{GGUF_LAYER_TENSORS['gate']}.weight"].ggml_type)
+    for layer in range(shape.layers):
+        for part, name in GGUF_LAYER_TENSORS.items():
+            t = g[f"blk.{layer}.{name}.weight"]
+            if t.ggml_type != shape.fmt:
+                raise ValueError(f"{t.name} is GGML type {t.ggml_type}; the stack runs one format ({shape.fmt})")
+    return shape
+
+
+def layer_from_gguf(g, shape: StackShape, layer: int) -> dict:
+    """One block's full tensors as the stack takes them (host arrays, rows unchanged): QKV as the q, k and v rows
+    one after another, o_proj, gate, up, down. Shapes are checked against `shape` (GGUF dims: ne0 = row length)."""
+    H, qd, kvd = shape.hidden, shape.n_q * shape.head_dim, shape.n_kv * shape.head_dim
+    want = {"q": (H, qd), "k": (H, kvd), "v": (H, kvd), "o": (qd, H), "gate": (H, shape.ff), "up": (H, shape.ff),
+            "down": (shape.ff, H)}
+    rows = {}
+    for part, name in GGUF_LAYER_TENSORS.items():
+        t = g[f"blk.{layer}.{name}.weight"]
+        if t.dims != want[part]:
+            raise ValueError(f"{t.name} has dims {t.dims}, the shape needs {want[part]}")
+        rows[part] = np.array(g.data(t))  # a copy: the arrays outlive the mapping
+    return {"qkv": np.concatenate([rows["q"], rows["k"], rows["v"]]), "o": rows["o"], "gate": rows["gate"],
+            "up": rows["up"], "down": rows["down"]}
+
+
 # ----------------------------------------------------------------------------------------------- communicator
 class Comm:
     """An NCCL communicator of `nranks` processes, one per GPU (yah_tp_init on the current device).
