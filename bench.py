@@ -395,9 +395,14 @@ def load_traffic(name):
 
 
 # ------------------------------------------------------------------------------------------------ CPU paths
+CPU_PHASES = {"dequant": 0.0, "gemm": 0.0}  # seconds spent in each phase of cpu_reference_step since the last reset
+
+
 def cpu_reference_step(fmt, w, x, K, use_gguf=True):
-    """One dequant-then-GEMM on the host: gguf-py's dequantize (the reference's oracle) -> f16 -> f32 matmul."""
+    """One dequant-then-GEMM on the host: gguf-py's dequantize (the reference's oracle) -> f16 -> f32 matmul. The two
+    phases are timed separately into CPU_PHASES."""
     N = w.shape[0]
+    t0 = time.perf_counter()
     if use_gguf:
         from gguf import GGMLQuantizationType as T
         from gguf import quants
@@ -406,7 +411,21 @@ def cpu_reference_step(fmt, w, x, K, use_gguf=True):
     else:
         from oracle import oracle as O
         wq = O.dequant_f16(fmt, w, N, K)
-    return x.astype(np.float32) @ wq.astype(np.float32).T
+    t1 = time.perf_counter()
+    y = x.astype(np.float32) @ wq.astype(np.float32).T
+    CPU_PHASES["dequant"] += t1 - t0
+    CPU_PHASES["gemm"] += time.perf_counter() - t1
+    return y
+
+
+def cpu_phases_reset():
+    CPU_PHASES["dequant"] = CPU_PHASES["gemm"] = 0.0
+
+
+def cpu_phases_ms(runs):
+    """Milliseconds per run of the two phases since the last reset."""
+    return {"dequant_ms": round(CPU_PHASES["dequant"] / runs * 1e3, 3),
+            "gemm_ms": round(CPU_PHASES["gemm"] / runs * 1e3, 3)}
 
 
 def cpu_jobs(args, frac):
@@ -467,6 +486,7 @@ def cpu_baseline(args, seconds=10.0):
     frac = 1 / 16 if args.workload == "stack" else min(1.0, 2048 / workload_of(args)["N"])
     jobs, flops, nbytes = cpu_jobs(args, frac)
     cpu_run(jobs, use_gguf)  # warm-up
+    cpu_phases_reset()
     n, t0 = 0, time.perf_counter()
     while True:
         cpu_run(jobs, use_gguf)
@@ -477,7 +497,7 @@ def cpu_baseline(args, seconds=10.0):
     per = el / n
     val, unit = cpu_metric(args, flops, nbytes, per)
     return {"value": round(val, 5), "unit": unit, "cores": cpu_cores(), "kind": kind,
-            "sample": cpu_sample_text(args, jobs, use_gguf, f"{n} runs, {per * 1e3:.1f} ms each")}
+            "sample": cpu_sample_text(args, jobs, use_gguf, f"{n} runs, {per * 1e3:.1f} ms each"), **cpu_phases_ms(n)}
 
 
 def run_reference(args, rank, budget_s=150.0):
@@ -497,6 +517,7 @@ def run_reference(args, rank, budget_s=150.0):
         jobs, flops, nbytes = cpu_jobs(args, frac)
     for _ in range(args.warmup):
         cpu_run(jobs, use_gguf)
+    cpu_phases_reset()
     t0 = time.perf_counter()
     for _ in range(args.steps):
         cpu_run(jobs, use_gguf)
@@ -523,7 +544,7 @@ def run_reference(args, rank, budget_s=150.0):
             "ms_per_step": round(per * 1e3, 3), "higher_is_better": True, "scaling": scaling, "vs_baseline": None,
             "dtype": "f16 weights (dequantised) x f16 -> f32", "data": "synthetic", "config": config,
             "cpu_baseline": {"value": round(val, 5), "unit": unit, "cores": cpu_cores(), "kind": kind,
-                             "sample": sample},
+                             "sample": sample, **cpu_phases_ms(args.steps)},
             "e2e": {"value": round(val, 5), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 

@@ -32,7 +32,9 @@ def test_reference_line(workload, extra):
     assert line["impl"] == "reference"
     assert (line["metric"], line["unit"], line["config"]["workload"]) == (metric, unit, name)
     assert line["value"] > 0 and line["higher_is_better"] is True
-    assert line["cpu_baseline"]["value"] == line["value"] and line["cpu_baseline"]["cores"] >= 1
+    cb = line["cpu_baseline"]
+    assert cb["value"] == line["value"] and cb["cores"] >= 1
+    assert cb["dequant_ms"] > 0 and cb["gemm_ms"] > 0 and cb["dequant_ms"] + cb["gemm_ms"] <= line["ms_per_step"] * 1.01
     assert line["e2e"] == {"value": line["value"], "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
 
 
