@@ -63,7 +63,8 @@ class Gguf:
         info = GgufTensorInfo()
         for i in range(n.value):
             check(lib().yah_gguf_tensor_info(self.handle, i, ctypes.byref(info)))
-            self.tensors.append(TensorInfo(info.name.decode(), info.ggml_type, tuple(info.dims[:info.n_dims]),
+            self.tensors.append(TensorInfo(info.name.decode(errors="replace"), info.ggml_type,
+                                           tuple(info.dims[:info.n_dims]),
                                            info.offset, info.bytes))
         self._by_name = {t.name: t for t in self.tensors}
 
