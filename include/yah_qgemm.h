@@ -125,7 +125,13 @@ int yah_selftest_bounded_wait(int64_t budget_cycles, int* code);
 /* Make `stream` wait for the last work recorded on `event` (cudaStreamWaitEvent). */
 int yah_stream_wait_event(void* stream, void* event);
 /* Read and clear the current device's kernel status word: 0, or the code of a bounded wait that ran out
- * (1 data wait, 2 free-stage wait, 3 exit drain). A non-zero word means the output of that launch is invalid. */
+ * (1 data wait, 2 free-stage wait, 3 exit drain). A non-zero word means the output of that launch is invalid.
+ * The read is a blocking copy on the legacy default stream, which does not wait for work on streams created with
+ * cudaStreamNonBlocking (yah_stream_create makes such streams): synchronise the stream the kernels ran on first.
+ * When the word is non-zero the call also resets the GEMV's split-K arrival counters, which a CTA that left early
+ * may have left partly counted (it synchronises the device to do so); later calls then start from a clean state.
+ * The library keeps per-device state (this word, workspaces, the noalloc scratch address) for the life of the
+ * process: do not use it across cudaDeviceReset. */
 int yah_status_word(int* code);
 
 /* ---- kernels ------------------------------------------------------------------------------------------ */

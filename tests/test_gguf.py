@@ -183,3 +183,28 @@ def test_fuzzed_headers_never_read_out_of_range(pkg, gfile, tmp_path):
         assert rc in (0, 2, 7), rc
         seen.add(rc)
     assert 7 in seen
+
+
+def test_names_that_decode_alike_are_refused(pkg, F, tmp_path):
+    """Two tensor names that differ only in bytes that are not UTF-8 decode to the same Python string; the loader
+    keeps them apart, so the Python reader refuses the file instead of letting one name shadow the other."""
+    from gguf import GGMLQuantizationType as T
+    from yah_b200.gguf_file import Gguf
+    p = tmp_path / "names.gguf"
+    w = gguf.GGUFWriter(str(p), "llama")
+    w.add_tensor("blk.X", F.synth_weights(F.Q4_K, 4, 256, seed=1), raw_dtype=T.Q4_K)
+    w.add_tensor("blk.Y", F.synth_weights(F.Q4_K, 4, 256, seed=2), raw_dtype=T.Q4_K)
+    w.write_header_to_file()
+    w.write_kv_data_to_file()
+    w.write_tensors_to_file()
+    w.close()
+    raw = bytearray(p.read_bytes())
+    for name, byte in ((b"blk.X", 0xFF), (b"blk.Y", 0xFE)):
+        i = raw.index(struct.pack("<Q", len(name)) + name) + 8
+        raw[i + len(name) - 1] = byte
+    q = tmp_path / "names_bad.gguf"
+    q.write_bytes(bytes(raw))
+    with pytest.raises(ValueError, match="same name"):
+        Gguf(q)
+    with Gguf(p) as g:  # the unpatched file opens
+        assert [t.name for t in g.tensors] == ["blk.X", "blk.Y"]

@@ -407,7 +407,12 @@ int yah_selftest_bounded_wait(int64_t budget_cycles, int* code) {
   CK(cudaGetLastError());
   CK(cudaDeviceSynchronize());
   CK(cudaMemcpy(code, s->status, sizeof(int), cudaMemcpyDeviceToHost));
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (s->counters && s->counters_n) CK(cudaMemset(s->counters, 0, s->counters_n * sizeof(int)));
+  }
   CK(cudaMemset(s->status, 0, sizeof(int)));
+  CK(cudaDeviceSynchronize());
   return YAH_OK;
 }
 
@@ -417,7 +422,18 @@ int yah_status_word(int* code) {
   int rc = dev_state(&s);
   if (rc) return rc;
   CK(cudaMemcpy(code, s->status, sizeof(int), cudaMemcpyDeviceToHost));
-  if (*code) CK(cudaMemset(s->status, 0, sizeof(int)));
+  if (*code) {
+    // A launch whose wait ran out left early, possibly before adding itself to the GEMV's split counters (the last
+    // CTA of a row block resets them only when every CTA arrived). Clear them, so that later calls count from
+    // zero again, then the word itself.
+    CK(cudaDeviceSynchronize());
+    {
+      std::lock_guard<std::mutex> lk(g_mu);
+      if (s->counters && s->counters_n) CK(cudaMemset(s->counters, 0, s->counters_n * sizeof(int)));
+    }
+    CK(cudaMemset(s->status, 0, sizeof(int)));
+    CK(cudaDeviceSynchronize());
+  }
   return YAH_OK;
 }
 

@@ -66,7 +66,15 @@ class Gguf:
             self.tensors.append(TensorInfo(info.name.decode(errors="replace"), info.ggml_type,
                                            tuple(info.dims[:info.n_dims]),
                                            info.offset, info.bytes))
-        self._by_name = {t.name: t for t in self.tensors}
+        self._by_name = {}
+        for t in self.tensors:
+            # Names that are not valid UTF-8 decode with replacement characters, and ctypes' char array stops at
+            # an embedded NUL, so two tensors the loader keeps apart could map to one key: refuse such a file
+            # rather than let a lookup return the wrong tensor.
+            if t.name in self._by_name:
+                self.close()
+                raise ValueError(f"{path}: two tensors decode to the same name {t.name!r}")
+            self._by_name[t.name] = t
 
     def find(self, name: str) -> TensorInfo | None:
         return self._by_name.get(name)
