@@ -56,7 +56,8 @@ extern "C" {
 /* Epilogues: the reference kernel kinds (gen_gemm_tile.py:309-322, gen_gemv.py:16-19). */
 #define YAH_EPI_STORE 0  /* kstore / plain:  y = W x                                  */
 #define YAH_EPI_RESID 1  /* kres / resid:    y = aux + W x   (aux, y f32; y may be aux) */
-#define YAH_EPI_SWIGLU 2 /* swiglu:          y = f16(silu(aux) * W x)   (aux f32 gate)  */
+#define YAH_EPI_SWIGLU 2 /* swiglu:          y = silu(aux) * W x   (aux f32 gate; tile GEMM: y f16,
+                          * decode GEMV: y f32 or f16)                                                   */
 
 /* ---- library ----------------------------------------------------------------------------------------- */
 const char* yah_version(void);
@@ -209,16 +210,30 @@ int yah_tile_rules_set(const yah_tile_rule* rules, int n);
 int yah_tile_rules_clear(void);
 int yah_tile_rules_count(int* n);
 
-/* Decode GEMV, 1 <= M <= 32 tokens (replaces gen_gemv.py's gv_{plain,resid}_<fmt>_<M>_<K> kernels and the
+/* Decode GEMV, 1 <= M <= 32 tokens (replaces gen_gemv.py's gv_{plain,resid,swiglu}_<fmt>_<M>_<K> kernels and the
  * LoomDecoder::Gemv call site, engine/model/loom_decoder.hpp:415-439). Same layouts and alignment rules as
- * yah_qgemm; epilogue YAH_EPI_STORE or YAH_EPI_RESID. Computes with the f32 weight values of the GGUF dequant,
- * as the reference GEMV does (no f16 rounding of weights). One persistent CTA per SM streams an equal share of
- * the weight bytes; row blocks shared by two CTAs are summed through a library-owned per-device workspace
- * (allocated on first use, grown on demand), so concurrent calls on different streams of one device must not
- * overlap. Results are deterministic. */
+ * yah_qgemm; epilogue YAH_EPI_STORE, YAH_EPI_RESID, or YAH_EPI_SWIGLU (y = silu(aux) * W x with y f32 or f16; aux
+ * may be y itself when y is f32: each gate value is read before it is overwritten). Computes with the f32 weight
+ * values of the GGUF dequant, as the reference GEMV does (no f16 rounding of weights). Results are deterministic.
+ * Two kernels: Q4_K runs on the tcgen05 tensor cores (thread-block clusters split K and add their partial sums in
+ * distributed shared memory; no scratch); Q8_0 and Q6_K (and Q4_K shapes the first does not cover) run an mma.sync
+ * kernel whose row blocks shared by two CTAs are summed through a library-owned per-device workspace (allocated on
+ * first use, grown on demand), so concurrent calls on different streams of one device must not overlap. */
 int yah_qgemv(const void* w, int ggml_type, int64_t N, int64_t K, int64_t w_row_stride, int64_t kb_off,
               const void* x, int64_t M, int64_t ldx, void* y, int y_dtype, int64_t ldy, int epilogue,
               const void* aux, int64_t ldaux, void* stream);
+
+/* The reference GEMV's swiglu kind (gen_gemv.py:18, :97-98; called per layer at engine/model/loom_decoder.hpp:294):
+ * y[M][ldy] (f32) = silu(x W_gate^T) * (x W_up^T). The two weight tensors may differ in format and row stride (same
+ * N and K). Runs the gate GEMV into y, then the up GEMV with the swiglu kind over y in place: no other memory. */
+int yah_qgemv_swiglu(const void* w_gate, int gate_type, int64_t gate_row_stride, const void* w_up, int up_type,
+                     int64_t up_row_stride, int64_t N, int64_t K, const void* x, int64_t M, int64_t ldx, float* y,
+                     int64_t ldy, void* stream);
+
+/* Which decode GEMV kernel yah_qgemv and yah_qgemv_noalloc run (process-wide; for tests and measurements, no
+ * counterpart in the reference): 0 (default) the tcgen05 kernel where it covers the call, else the mma.sync kernel;
+ * 1 only the tcgen05 kernel (calls it does not cover fail with YAH_ERR_UNSUPPORTED); 2 only the mma.sync kernel. */
+int yah_set_gemv_impl(int impl);
 
 /* Decode GEMV that allocates nothing. This entry point has no counterpart in the reference engine.
  * For callers that cannot call cudaMalloc when they run the GEMV: code inside a CUDA-graph capture region, a

@@ -50,6 +50,10 @@ int cuda_fail(cudaError_t e, const char* what) {
     if (e_ != cudaSuccess) return cuda_fail(e_, #call); \
   } while (0)
 
+// Which decode GEMV runs (yah_set_gemv_impl): 0 the tcgen05 form where it covers the call, else the mma.sync form;
+// 1 only the tcgen05 form; 2 only the mma.sync form.
+std::atomic<int> g_gemv_impl{0};
+
 // SMs the GEMM / GEMV plans may use (0: all). A process that overlaps collectives with these kernels leaves the
 // rest to the collective's kernels.
 std::atomic<int> g_sm_budget{0};
@@ -130,9 +134,10 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 
 constexpr int64_t kMaxDim = (int64_t)1 << 30;
 
 // Shared checks of yah_qgemm / yah_qgemv.
+// gemv: the decode GEMV's rules (its swiglu kind also writes f32, in place over the gate when aux == y).
 int check_linear(const void* w, int type, int64_t N, int64_t K, int64_t w_row_stride, int64_t kb_off, const void* x,
                  int64_t M, int64_t ldx, const void* y, int y_dtype, int64_t ldy, int epilogue, const void* aux,
-                 int64_t ldaux) {
+                 int64_t ldaux, bool gemv = false) {
   const int sb = sb_bytes(type);
   if (!sb) return fail(YAH_ERR_UNSUPPORTED, "unsupported GGML type %d (supported: Q8_0=8, Q4_K=12, Q6_K=14)", type);
   if (!w || !x || !y) return fail(YAH_ERR_ARG, "null weight, input or output pointer");
@@ -158,7 +163,9 @@ int check_linear(const void* w, int type, int64_t N, int64_t K, int64_t w_row_st
     if (y_dtype != YAH_F32) return fail(YAH_ERR_UNSUPPORTED, "YAH_EPI_RESID writes f32");
   } else if (epilogue == YAH_EPI_SWIGLU) {
     if (!aux || ldaux < N) return fail(YAH_ERR_ARG, "YAH_EPI_SWIGLU needs aux f32 gate [M][ldaux >= N]");
-    if (y_dtype != YAH_F16) return fail(YAH_ERR_UNSUPPORTED, "YAH_EPI_SWIGLU writes f16");
+    if (y_dtype != YAH_F16 && !gemv) return fail(YAH_ERR_UNSUPPORTED, "YAH_EPI_SWIGLU of the tile GEMM writes f16");
+    if (y_dtype == YAH_F16 && aux == y)
+      return fail(YAH_ERR_ARG, "YAH_EPI_SWIGLU in place (aux == y) needs an f32 output");
   } else if (epilogue != YAH_EPI_STORE) {
     return fail(YAH_ERR_UNSUPPORTED, "epilogue %d", epilogue);
   }
@@ -170,6 +177,25 @@ int after_launch(cudaError_t e, const char* what) {
   return YAH_OK;
 }
 
+}  // namespace
+
+namespace {
+constexpr int kNotTaken = -1;
+
+// The tcgen05 decode GEMV for a call it covers (per the impl switch): its launch status, or kNotTaken when the call
+// goes to the mma.sync form. a.status must be set.
+int launch_gemv_tc(const yah::QGemvArgs& a, int dev, cudaStream_t stream) {
+  const int impl = g_gemv_impl.load(std::memory_order_relaxed);
+  if (impl == 2) return kNotTaken;
+  const yah::GemvTcPlan pl = yah::qgemv_tc_plan(a.type, a.N, a.K, a.M, a.num_sms, dev);
+  if (!pl.ok) {
+    if (impl == 1)
+      return fail(YAH_ERR_UNSUPPORTED, "the tcgen05 decode GEMV does not cover type %d, N=%lld, K=%lld, M=%lld",
+                  a.type, (long long)a.N, (long long)a.K, (long long)a.M);
+    return kNotTaken;
+  }
+  return after_launch(yah::launch_qgemv_tc(a, pl, stream), "qgemv (tcgen05) launch");
+}
 }  // namespace
 
 namespace yah {
@@ -671,26 +697,12 @@ int yah_qgemm(const void* w, int t, int64_t N, int64_t K, int64_t w_row_stride, 
 int yah_qgemv(const void* w, int t, int64_t N, int64_t K, int64_t w_row_stride, int64_t kb_off, const void* x,
               int64_t M, int64_t ldx, void* y, int y_dtype, int64_t ldy, int epilogue, const void* aux, int64_t ldaux,
               void* stream) {
-  int rc = check_linear(w, t, N, K, w_row_stride, kb_off, x, M, ldx, y, y_dtype, ldy, epilogue, aux, ldaux);
+  int rc = check_linear(w, t, N, K, w_row_stride, kb_off, x, M, ldx, y, y_dtype, ldy, epilogue, aux, ldaux, true);
   if (rc) return rc;
   if (M > 32) return fail(YAH_ERR_ARG, "yah_qgemv takes at most 32 tokens (M=%lld); use yah_qgemm", (long long)M);
-  if (epilogue == YAH_EPI_SWIGLU) return fail(YAH_ERR_UNSUPPORTED, "yah_qgemv: epilogue swiglu not provided");
   DevState* s;
   rc = dev_state(&s);
   if (rc) return rc;
-  const yah::GemvPlan plan = yah::qgemv_plan(t, N, K, M, sms_of(s));
-  if (plan.ws_floats > 0) {
-    std::lock_guard<std::mutex> lk(g_mu);
-    rc = grow(reinterpret_cast<void**>(&s->ws), &s->ws_bytes, (size_t)plan.ws_floats * sizeof(float));
-    if (rc) return rc;
-    if ((size_t)plan.counters > s->counters_n) {
-      size_t have = s->counters_n * sizeof(int);
-      rc = grow(reinterpret_cast<void**>(&s->counters), &have, (size_t)plan.counters * sizeof(int));
-      if (rc) return rc;
-      CK(cudaMemset(s->counters, 0, (size_t)plan.counters * sizeof(int)));
-      s->counters_n = (size_t)plan.counters;
-    }
-  }
   yah::QGemvArgs a;
   a.w = w;
   a.type = t;
@@ -709,16 +721,34 @@ int yah_qgemv(const void* w, int t, int64_t N, int64_t K, int64_t w_row_stride, 
   a.ldaux = ldaux;
   a.status = s->status;
   a.num_sms = sms_of(s);
+  {
+    int dev = 0;
+    CK(cudaGetDevice(&dev));
+    rc = launch_gemv_tc(a, dev, (cudaStream_t)stream);
+    if (rc != kNotTaken) return rc;
+  }
+  const yah::GemvPlan plan = yah::qgemv_plan(t, N, K, M, sms_of(s));
+  if (plan.ws_floats > 0) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    rc = grow(reinterpret_cast<void**>(&s->ws), &s->ws_bytes, (size_t)plan.ws_floats * sizeof(float));
+    if (rc) return rc;
+    if ((size_t)plan.counters > s->counters_n) {
+      size_t have = s->counters_n * sizeof(int);
+      rc = grow(reinterpret_cast<void**>(&s->counters), &have, (size_t)plan.counters * sizeof(int));
+      if (rc) return rc;
+      CK(cudaMemset(s->counters, 0, (size_t)plan.counters * sizeof(int)));
+      s->counters_n = (size_t)plan.counters;
+    }
+  }
   return after_launch(yah::launch_qgemv_ws(a, plan, s->ws, s->counters, (cudaStream_t)stream), "qgemv launch");
 }
 
 int yah_qgemv_noalloc(const void* w, int t, int64_t N, int64_t K, int64_t w_row_stride, int64_t kb_off,
                       const void* x, int64_t M, int64_t ldx, void* y, int y_dtype, int64_t ldy, int epilogue,
                       const void* aux, int64_t ldaux, void* stream) {
-  int rc = check_linear(w, t, N, K, w_row_stride, kb_off, x, M, ldx, y, y_dtype, ldy, epilogue, aux, ldaux);
+  int rc = check_linear(w, t, N, K, w_row_stride, kb_off, x, M, ldx, y, y_dtype, ldy, epilogue, aux, ldaux, true);
   if (rc) return rc;
   if (M > 32) return fail(YAH_ERR_ARG, "yah_qgemv_noalloc takes at most 32 tokens (M=%lld)", (long long)M);
-  if (epilogue == YAH_EPI_SWIGLU) return fail(YAH_ERR_UNSUPPORTED, "yah_qgemv_noalloc: epilogue swiglu not provided");
   // No call below allocates: device attributes, the driver's tensor-map encoder and the static scratch address.
   int dev = 0, sms = 0, major = 0;
   CK(cudaGetDevice(&dev));
@@ -727,6 +757,31 @@ int yah_qgemv_noalloc(const void* w, int t, int64_t N, int64_t K, int64_t w_row_
   if (major != 10) return fail(YAH_ERR_DEVICE, "device %d is not an sm_100 device", dev);
   if (!yah::tensor_map_encoder_available())
     return fail(YAH_ERR_DEVICE, "the driver does not provide cuTensorMapEncodeTiled");
+  {
+    // the tcgen05 form needs no scratch: only the variant's own status word
+    void* base = nullptr;
+    CK(yah::qgemv_static_setup(dev, &base));
+    yah::QGemvArgs a;
+    a.w = w;
+    a.type = t;
+    a.N = N;
+    a.K = K;
+    a.w_row_stride = w_row_stride;
+    a.kb_off = kb_off;
+    a.x = x;
+    a.M = M;
+    a.ldx = ldx;
+    a.y = y;
+    a.y_f16 = y_dtype == YAH_F16;
+    a.ldy = ldy;
+    a.epilogue = epilogue;
+    a.aux = static_cast<const float*>(aux);
+    a.ldaux = ldaux;
+    a.status = yah::qgemv_static_status_word(base);
+    a.num_sms = sms;
+    rc = launch_gemv_tc(a, dev, (cudaStream_t)stream);
+    if (rc != kNotTaken) return rc;
+  }
   const yah::GemvPlan plan = yah::qgemv_plan(t, N, K, M, sms);
   if ((size_t)plan.ws_floats > yah::qgemv_static_partials() || (size_t)plan.counters > yah::qgemv_static_counters())
     return fail(YAH_ERR_SIZE,
@@ -754,6 +809,23 @@ int yah_qgemv_noalloc(const void* w, int t, int64_t N, int64_t K, int64_t w_row_
   a.status = nullptr;  // set by the launcher: the variant's own status word
   a.num_sms = sms;
   return after_launch(yah::launch_qgemv_static(a, plan, base, (cudaStream_t)stream), "qgemv_noalloc launch");
+}
+
+int yah_set_gemv_impl(int impl) {
+  if (impl < 0 || impl > 2) return fail(YAH_ERR_ARG, "gemv impl %d (0 auto, 1 tcgen05, 2 mma.sync)", impl);
+  g_gemv_impl.store(impl, std::memory_order_relaxed);
+  return YAH_OK;
+}
+
+int yah_qgemv_swiglu(const void* w_gate, int gate_type, int64_t gate_row_stride, const void* w_up, int up_type,
+                     int64_t up_row_stride, int64_t N, int64_t K, const void* x, int64_t M, int64_t ldx, float* y,
+                     int64_t ldy, void* stream) {
+  if (!y) return fail(YAH_ERR_ARG, "null output");
+  // the gate GEMV into y (f32), then the up GEMV whose swiglu kind reads each gate value and overwrites it
+  int rc = yah_qgemv(w_gate, gate_type, N, K, gate_row_stride, 0, x, M, ldx, y, YAH_F32, ldy, YAH_EPI_STORE, nullptr,
+                     0, stream);
+  if (rc) return rc;
+  return yah_qgemv(w_up, up_type, N, K, up_row_stride, 0, x, M, ldx, y, YAH_F32, ldy, YAH_EPI_SWIGLU, y, ldy, stream);
 }
 
 int yah_qgemv_noalloc_status(int* code) {

@@ -88,6 +88,15 @@ GemvPlan qgemv_plan(int type, int64_t N, int64_t K, int64_t M, int num_sms);
 cudaError_t launch_qgemv_ws(const QGemvArgs& a, const GemvPlan& plan, float* ws, int* counters,
                             cudaStream_t stream);
 
+// Decode GEMV on tcgen05 (qgemv_tc.cu; Q4_K, M <= 32): clusters of ks CTAs split K, tiles of rt <= 128 weight rows,
+// tp MMA columns (16 or 32 token rows, the rest zero). No scratch: the K parts meet in distributed shared memory.
+struct GemvTcPlan {
+  int ok;      // 0: the tcgen05 form does not cover this call
+  int tp, ks, rt, tiles, grid, srange, sw, pitch;
+};
+GemvTcPlan qgemv_tc_plan(int type, int64_t N, int64_t K, int64_t M, int num_sms, int device);
+cudaError_t launch_qgemv_tc(const QGemvArgs& a, const GemvTcPlan& plan, cudaStream_t stream);
+
 // The allocation-free GEMV: its scratch is a file-scope device array in qgemv.cu. setup looks up its address on
 // `device` (which must be current) once and caches it; the launcher clears the split counters it needs and runs
 // the GEMV on that scratch; status reads (and optionally clears) the variant's own status word.
@@ -96,6 +105,7 @@ size_t qgemv_static_counters();
 cudaError_t qgemv_static_setup(int device, void** base);
 cudaError_t launch_qgemv_static(const QGemvArgs& a, const GemvPlan& plan, void* base, cudaStream_t stream);
 cudaError_t qgemv_static_status(void* base, int* code, bool clear);
+int* qgemv_static_status_word(void* base);
 
 // Programmatic dependent launch of the GEMV kernels (on by default): a launch may start while the preceding kernel
 // on its stream finishes, streaming its weights early; activations and outputs wait for that kernel to complete.

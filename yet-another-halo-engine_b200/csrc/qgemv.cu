@@ -383,8 +383,13 @@ __device__ __forceinline__ void gv_prep_q4k(uint32_t xs, int slots, int M, uint3
 }
 
 // ------------------------------------------------------------------------------------------------ outputs
+// silu(g) * v for the swiglu kind (the arithmetic of the tile GEMM's swiglu epilogue; aux may be the output itself:
+// each element is read before it is written, by the same thread).
+__device__ __forceinline__ float gv_silu(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
+
 __device__ __forceinline__ void gv_store(const GvParams& p, int t, int row, float v) {
   if (p.epi == kEpiResid) v += p.aux[(int64_t)t * p.ldaux + row];
+  if (p.epi == kEpiSwiglu) v = gv_silu(p.aux[(int64_t)t * p.ldaux + row]) * v;
   if (p.y_f16) reinterpret_cast<__half*>(p.y)[(int64_t)t * p.ldy + row] = __float2half_rn(v);
   else reinterpret_cast<float*>(p.y)[(int64_t)t * p.ldy + row] = v;
 }
@@ -549,15 +554,6 @@ __device__ __forceinline__ void gv_flush_streamk(const GvParams& p, const GvRang
       const int t = 8 * n + 2 * c + (e & 1), row = rb * kGvBlock + rloc + 8 * (e >> 1);
       if (t < p.M && row < p.N) gv_store(p, t, row, y[n][e]);
     }
-}
-
-__device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int x, int y,
-                                            int z) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], "
-      "[%2];" ::"r"(smem_u32(smem_dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
-      : "memory");
 }
 
 // Row ranges: the slots of each row group are added in slot order through shared memory (red[warp][lane][...]),
@@ -871,6 +867,7 @@ __host__ __device__ constexpr int gv1_pitch(int S) { return (9 * S + ((2 - 9 * S
 
 __device__ __forceinline__ void gv1_store(const Gv1Params& p, int row, float v) {
   if (p.epi == kEpiResid) v += p.aux[row];
+  if (p.epi == kEpiSwiglu) v = gv_silu(p.aux[row]) * v;
   if (p.y_f16) reinterpret_cast<__half*>(p.y)[row] = __float2half_rn(v);
   else reinterpret_cast<float*>(p.y)[row] = v;
 }
@@ -1458,6 +1455,8 @@ cudaError_t launch_qgemv_static(const QGemvArgs& a_in, const GemvPlan& plan, voi
   }
   return launch_qgemv_ws(a, plan, partials, counters, stream);
 }
+
+int* qgemv_static_status_word(void* base) { return reinterpret_cast<int*>(base); }
 
 cudaError_t qgemv_static_status(void* base, int* code, bool clear) {
   cudaError_t e = cudaMemcpy(code, base, sizeof(int), cudaMemcpyDeviceToHost);

@@ -1,0 +1,693 @@
+// Decode GEMV on the 5th-generation tensor cores (tcgen05): y[t][n] (+)= sum_k W[n][k] x[t][k] for M <= 32 tokens,
+// GGUF Q4_K weights, f16 activations, with the f32 weight values of the reference dequant (no f16 rounding of a
+// weight), as the reference GEMV computes them (engine/gpu/loom/tools/gen_gemv.py:7-9, kinds :16-19).
+//
+// Arithmetic. A Q4_K weight is w = d*sc*q - dmin*m (d, dmin f16; 6-bit sc, m per 32-value group; 4-bit q). Per
+// super-block s and output row n:
+//   y += d_s * D1_s - D2,   D1_s = sum_k f16(sc*q)_k x_k,   D2 = sum_{s,g} (dmin*m_g)_s X_{s,g}
+// where X_{s,g} = sum of the group's 32 activations. sc*q <= 945 is an exact f16 integer, so D1_s is a sum of exact
+// products (f32 accumulation in TMEM); dmin*m is a 17-bit multiple of ulp(dmin) >= 2^-24 and splits exactly into two
+// f16 parts hi + lo, X into an f32-accurate pair Xhi + Xlo, and the four exact products (hi + lo)(Xhi + Xlo) go through
+// two more MMAs per super-block that accumulate D2 over the whole K range. So the only rounding is the f32
+// accumulation; the epilogue applies d_s (one FMA per token and super-block) and subtracts D2.
+//
+// B200 design. Weight rows are the MMA's M side (128 TMEM lanes; a tile holds RT <= 128 rows), the tokens its N
+// side (16 or 32 columns; rows past M are zero), one 16 x 16 f16 K step per MMA:
+//   warp 22       weight producer: TMA of raw super-blocks, RT rows x SW (1 or 2) super-blocks per stage, rows
+//                 padded to an odd number of 16-byte units (no shared-memory bank conflicts for thread = row);
+//   warp 0        activation producer: per super-block one 3-D TMA copy of its 4 64-K chunks x TP token rows in
+//                 the 128-byte swizzle the MMA's K-major B descriptor expects;
+//   warps 2-17    decode: thread = row = TMEM lane, warp = (lane quarter, 64-K quarter of the super-block). Per
+//                 super-block a thread turns 32 nibble bytes into 32 cells of f16(sc*q) pairs (2 prmt + 4 and +
+//                 4 fma.rn.f16x2 per 8 weights) and its two groups' (hi, lo) min factors, and tcgen05.st's them into
+//                 an A buffer in TMEM;
+//   warp 1        MMA issuer (one thread): 16 MMAs into a D1 slot (A buffer x activation tile) and 2 into the tile's
+//                 D2 region (min factors x group sums), then commits that free the A buffer, the activation stage
+//                 and hand D1 to the epilogue;
+//   warps 18-21   epilogue: per super-block tcgen05.ld of D1, acc += d_s * D1; per tile acc -= D2, the cluster
+//                 reduction, the kind (plain / resid / swiglu) and the stores.
+// At the start (after griddepcontrol.wait) the decode and epilogue warps form the group sums of this CTA's K range
+// once (Xhi, Xlo in f16, 4 per group: Xhi Xlo Xhi Xlo against the A side's hi hi lo lo) in shared memory.
+// Work split: the K range is cut into KS equal parts (thread-block clusters of KS = 1, 2 or 4 CTAs, CTA rank = part)
+// and the rows into tiles of RT rows; persistent clusters walk the tiles. The KS partial sums of a tile meet in
+// distributed shared memory: every CTA parks its [M][RT] partial, and CTA r adds the KS partials of its RT / KS rows
+// in rank order (deterministic) and stores them. No global scratch.
+// Launch overlap: programmatic dependent launch as in the other GEMV (weights stream before griddepcontrol.wait;
+// activations are read and outputs written after it).
+// Every mbarrier wait is bounded (ptx.cuh); a wait that runs out records a status code and the CTA leaves its
+// loops, drains its own copies and MMAs, and frees TMEM.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <mutex>
+
+#include "decode.cuh"
+#include "kernels.h"
+#include "ptx.cuh"
+
+namespace yah {
+namespace {
+
+constexpr int kTcThreads = 736;  // 23 warps
+constexpr int kTcWarpX = 0, kTcWarpMma = 1, kTcWarpDq0 = 2, kTcWarpEpi0 = 18, kTcWarpW = 22;
+constexpr int kTcNA = 2;              // A buffers (TMEM): 128 columns of f16(sc*q) pairs + 16 of min factors
+constexpr int kTcACols = 144;
+constexpr int kTcNP = 8;              // per-row d ring (decode -> epilogue)
+constexpr int kTcWPitch2 = 304;       // weight stage row pitch for 2 super-blocks (19 x 16 B: odd)
+constexpr int kTcWPitch1 = 176;       // ... for 1 super-block (11 x 16 B)
+constexpr int kTcWStage = 128 * kTcWPitch2;  // 38912 bytes, a multiple of 1024
+
+template <int TP>
+struct TcCfg {
+  static constexpr int kND = TP == 16 ? 8 : 4;          // D1 slots
+  static constexpr int kD2Col = kTcNA * kTcACols;       // D2 regions [2][TP]
+  static constexpr int kD1Col = kD2Col + 2 * TP;        // D1 slots [kND][TP]
+  static_assert(kD1Col + kND * TP <= 512, "TMEM columns");
+  static constexpr int kNSW = TP == 16 ? 4 : 3;         // weight stages
+  static constexpr int kNSX = 3;                        // activation stages (one super-block each)
+  static constexpr int kXStage = TP * 512;              // 4 chunks x TP rows x 128 B
+  static constexpr int kMaxRange = TP == 16 ? 32 : 16;  // super-blocks per CTA (group sums kept for all of them)
+  static constexpr int kB2Tile = TP * 128;              // two super-blocks' 32 entries per 128-byte token row
+  static constexpr int kXOff = kTcWStage * kNSW;
+  static constexpr int kB2Off = kXOff + kNSX * kXStage;
+  static constexpr int kParOff = kB2Off + (kMaxRange / 2) * kB2Tile;
+  static constexpr int kExOff = kParOff + kTcNP * 128 * 4;
+  static constexpr int kBarOff = kExOff + TP * 128 * 4;
+  // wfull/wempty [NSW], xfull/xempty [NSX], afull/aempty [NA], dfull/dempty [ND], d2full/d2empty [2],
+  // pfull/pempty [NP], b2ready, exfull, exempty, drain
+  static constexpr int kNumBars = 2 * kNSW + 2 * kNSX + 2 * kTcNA + 2 * kND + 4 + 2 * kTcNP + 4;
+  static constexpr int kSlotOff = kBarOff + kNumBars * 8;
+  static constexpr int kBytes = kSlotOff + 16;
+  static constexpr int kAlloc = kBytes + 1024;
+  static_assert(kAlloc <= 227 * 1024, "shared memory");
+};
+
+struct TcParams {
+  int N, M, K, kb_off;
+  int rt;          // weight rows per tile (<= 128)
+  int tiles;       // ceil(N / rt)
+  int ks;          // CTAs per cluster = K parts
+  int srange;      // super-blocks per CTA (K / 256 / ks)
+  int sw;          // super-blocks per weight stage (1 or 2; divides srange)
+  int pitch;       // weight stage row pitch in bytes
+  const __half* x;
+  int64_t ldx;
+  void* y;
+  int64_t ldy;
+  const float* aux;
+  int64_t ldaux;
+  int* status;
+};
+
+// sc and m of group g (0..7) from the block header (d | dmin << 16, scales[0..11]) (gen_gemm_decode.py:946-967).
+__device__ __forceinline__ void q4k_group_sm(const uint4& hdr, int g, int& sc, int& m) {
+  const int gg = g & 3;
+  const uint32_t b1 = (hdr.y >> (8 * gg)) & 0xFFu, b2 = (hdr.z >> (8 * gg)) & 0xFFu, b3 = (hdr.w >> (8 * gg)) & 0xFFu;
+  if (g < 4) {
+    sc = (int)(b1 & 63);
+    m = (int)(b2 & 63);
+  } else {
+    sc = (int)((b3 & 15) | ((b1 >> 6) << 4));
+    m = (int)((b3 >> 4) | ((b2 >> 6) << 4));
+  }
+}
+
+__device__ __forceinline__ uint32_t f16x2_same(float v) { return pack_f16x2_rn(v, v); }
+
+// dmin * m as two f16 cells (hi, hi), (lo, lo): hi + lo == dmin * m exactly.
+__device__ __forceinline__ void min_cells(float dmin, int m, uint32_t& chi, uint32_t& clo) {
+  const float p = dmin * (float)m;  // exact: 11 x 6 bits
+  const __half hi = __float2half_rn(p);
+  const float rest = p - __half2float(hi);  // exact, a multiple of ulp(dmin) >= 2^-24
+  const unsigned short hb = __half_as_ushort(hi), lb = __half_as_ushort(__float2half_rn(rest));
+  chi = (uint32_t)hb | ((uint32_t)hb << 16);
+  clo = (uint32_t)lb | ((uint32_t)lb << 16);
+}
+
+// One thread's part of a staged Q4_K super-block (its row, 64-K quarter kq: groups 2kq and 2kq + 1): 32 A cells of
+// f16(sc * q) pairs in K order, the 4 min-factor cells of its two groups, and d.
+// The byte pair (b0, b1) of a qs word goes through prmt next to 0x64 bytes: f16 (1024 + b0, 1024 + b1); masking
+// keeps 1024 + low nibble or 1024 + 16 * high nibble, and one fma.rn.f16x2 gives sc * q exactly
+// ((1024 + q) sc - 1024 sc and (1024 + 16 q) (sc / 16) - 64 sc; every term is an exact f16).
+__device__ __forceinline__ void q4k_tc_decode(uint32_t rb, int kq, uint32_t (&v)[32], uint32_t (&a2)[4], float& d) {
+  const uint4 hdr = lds128(rb);
+  const uint4 qa = lds128(rb + 16 + 32 * kq);
+  const uint4 qb = lds128(rb + 32 + 32 * kq);
+  const uint32_t qs[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+  int sc0, m0, sc1, m1;
+  q4k_group_sm(hdr, 2 * kq, sc0, m0);
+  q4k_group_sm(hdr, 2 * kq + 1, sc1, m1);
+  const uint32_t s0 = f16x2_same((float)sc0), c0 = f16x2_same(-1024.0f * (float)sc0);
+  const uint32_t s1 = f16x2_same((float)sc1 * 0.0625f), c1 = f16x2_same(-64.0f * (float)sc1);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint32_t r01 = prmt(qs[i], 0x64646464u, 0x4140u);
+    const uint32_t r23 = prmt(qs[i], 0x64646464u, 0x4342u);
+    v[2 * i] = hfma2_u32(r01 & 0xFF0FFF0Fu, s0, c0);
+    v[2 * i + 1] = hfma2_u32(r23 & 0xFF0FFF0Fu, s0, c0);
+    v[16 + 2 * i] = hfma2_u32(r01 & 0xFFF0FFF0u, s1, c1);
+    v[17 + 2 * i] = hfma2_u32(r23 & 0xFFF0FFF0u, s1, c1);
+  }
+  d = h2f_bits(hdr.x & 0xFFFFu);
+  const float dmin = h2f_bits(hdr.x >> 16);
+  min_cells(dmin, m0, a2[0], a2[1]);
+  min_cells(dmin, m1, a2[2], a2[3]);
+}
+
+__device__ __forceinline__ float silu_tc(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
+
+template <int EPI, bool OUT_F16>
+__device__ __forceinline__ void tc_store(const TcParams& p, int t, int row, float v) {
+  if (EPI == kEpiResid) v = p.aux[(int64_t)t * p.ldaux + row] + v;
+  if (EPI == kEpiSwiglu) v = silu_tc(p.aux[(int64_t)t * p.ldaux + row]) * v;
+  if (OUT_F16) reinterpret_cast<__half*>(p.y)[(int64_t)t * p.ldy + row] = __float2half_rn(v);
+  else reinterpret_cast<float*>(p.y)[(int64_t)t * p.ldy + row] = v;
+}
+
+// Byte offset of f16 entry e (0..63) of token row t in a 128-byte-swizzled K-major tile.
+__device__ __forceinline__ uint32_t sw128_off(int t, int e) {
+  const int b = 2 * e;
+  return (uint32_t)(t * 128 + ((((b >> 4) ^ t) & 7) << 4) + (b & 15));
+}
+
+template <int TP, int EPI, bool OUT_F16>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    qgemv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
+                    const TcParams p) {
+  using C = TcCfg<TP>;
+  constexpr int ND = C::kND, NSW = C::kNSW, NSX = C::kNSX;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
+  uint64_t* wfull = bars;
+  uint64_t* wempty = wfull + NSW;
+  uint64_t* xfull = wempty + NSW;
+  uint64_t* xempty = xfull + NSX;
+  uint64_t* afull = xempty + NSX;
+  uint64_t* aempty = afull + kTcNA;
+  uint64_t* dfull = aempty + kTcNA;
+  uint64_t* dempty = dfull + ND;
+  uint64_t* d2full = dempty + ND;
+  uint64_t* d2empty = d2full + 2;
+  uint64_t* pfull = d2empty + 2;
+  uint64_t* pempty = pfull + kTcNP;
+  uint64_t* b2ready = pempty + kTcNP;
+  uint64_t* exfull = b2ready + 1;
+  uint64_t* exempty = exfull + 1;
+  uint64_t* drain = exempty + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kSlotOff);
+  float* params = reinterpret_cast<float*>(smem + C::kParOff);
+  float* ex = reinterpret_cast<float*>(smem + C::kExOff);
+
+  griddep_launch_dependents();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ks = p.ks;
+  const uint32_t rank = ks > 1 ? cluster_rank() : 0;
+  const int G = gridDim.x / ks, cid = blockIdx.x / ks;  // clusters, this cluster
+  const int sr = p.srange;
+  const int sbx0 = (int)rank * sr;                      // first super-block of this CTA's K range (in the window)
+  const int sb0 = p.kb_off + sbx0;                      // ... in the weight rows
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NSW; ++i) {
+      mbar_init(&wfull[i], 1);
+      mbar_init(&wempty[i], 16);
+    }
+    for (int i = 0; i < NSX; ++i) {
+      mbar_init(&xfull[i], 1);
+      mbar_init(&xempty[i], 1);
+    }
+    for (int i = 0; i < kTcNA; ++i) {
+      mbar_init(&afull[i], 16);
+      mbar_init(&aempty[i], 1);
+    }
+    for (int i = 0; i < ND; ++i) {
+      mbar_init(&dfull[i], 1);
+      mbar_init(&dempty[i], 4);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&d2full[i], 1);
+      mbar_init(&d2empty[i], 4);
+    }
+    for (int i = 0; i < kTcNP; ++i) {
+      mbar_init(&pfull[i], 4);
+      mbar_init(&pempty[i], 4);
+    }
+    mbar_init(b2ready, 20);
+    mbar_init(exfull, 4 * ks);
+    mbar_init(exempty, 4 * ks);
+    mbar_init(drain, 1);
+    fence_barrier_init();
+  }
+  if (warp == kTcWarpMma) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  if (ks > 1) cluster_sync(); else __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == kTcWarpW) {
+    // ------------------------------------------------------------------ weight producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmap_w);
+      uint32_t s = 0;
+      bool ok = true;
+      const int nst = sr / p.sw;
+      const uint32_t bytes = (uint32_t)(p.rt * p.pitch);
+      for (int tile = cid; ok && tile < p.tiles; tile += G) {
+        for (int js = 0; js < nst; ++js, ++s) {
+          const uint32_t ws = s % NSW, ph = (s / NSW) & 1;
+          if (!mbar_wait(&wempty[ws], ph ^ 1, p.status, kStatusTimeoutEmpty)) { ok = false; break; }
+          mbar_arrive_expect_tx(&wfull[ws], bytes);
+          tma_load_2d(smem + ws * kTcWStage, &tmap_w, &wfull[ws], (sb0 + js * p.sw) * 18, tile * p.rt);
+        }
+      }
+      for (uint32_t i = (s > (uint32_t)NSW ? s - NSW : 0); i < s; ++i)
+        mbar_wait(&wfull[i % NSW], (i / NSW) & 1, p.status, kStatusTimeoutDrain, false);
+    }
+  } else if (warp == kTcWarpX) {
+    // ------------------------------------------------------------------ activation producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmap_x);
+      griddep_wait();  // the activations may come from the preceding kernel
+      uint32_t s = 0;
+      bool ok = true;
+      for (int tile = cid; ok && tile < p.tiles; tile += G) {
+        for (int j = 0; j < sr; ++j, ++s) {
+          const uint32_t xs = s % NSX, ph = (s / NSX) & 1;
+          if (!mbar_wait(&xempty[xs], ph ^ 1, p.status, kStatusTimeoutEmpty)) { ok = false; break; }
+          mbar_arrive_expect_tx(&xfull[xs], C::kXStage);
+          tma_load_3d(smem + C::kXOff + xs * C::kXStage, &tmap_x, &xfull[xs], 0, 0, (sbx0 + j) * 4);
+        }
+      }
+      for (uint32_t i = (s > (uint32_t)NSX ? s - NSX : 0); i < s; ++i)
+        mbar_wait(&xfull[i % NSX], (i / NSX) & 1, p.status, kStatusTimeoutDrain, false);
+    }
+  } else if (warp == kTcWarpMma) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16_f32(128, TP);
+      const uint64_t bx0 = sdesc_sw128(smem_u32(smem + C::kXOff));
+      const uint64_t bb0 = sdesc_sw128(smem_u32(smem + C::kB2Off));
+      uint32_t i = 0, tc = 0;
+      bool ok = true, b2 = false;
+      for (int tile = cid; ok && tile < p.tiles; tile += G, ++tc) {
+        const uint32_t r2 = tc & 1;
+        if (!mbar_wait(&d2empty[r2], ((tc >> 1) & 1) ^ 1, p.status, kStatusTimeoutEmpty)) { ok = false; break; }
+        const uint32_t d2 = tmem + C::kD2Col + r2 * TP;
+        for (int j = 0; j < sr; ++j, ++i) {
+          const uint32_t as = i % kTcNA, xs = i % NSX, ds = i % ND;
+          if (!mbar_wait(&afull[as], (i / kTcNA) & 1, p.status, kStatusTimeoutFull)) { ok = false; break; }
+          if (!mbar_wait(&xfull[xs], (i / NSX) & 1, p.status, kStatusTimeoutFull)) { ok = false; break; }
+          if (!mbar_wait(&dempty[ds], ((i / ND) & 1) ^ 1, p.status, kStatusTimeoutEmpty)) { ok = false; break; }
+          if (!b2) {
+            if (!mbar_wait(b2ready, 0, p.status, kStatusTimeoutFull)) { ok = false; break; }
+            b2 = true;
+          }
+          tc_fence_after();
+          const uint32_t a = tmem + as * kTcACols;
+          const uint32_t dt = tmem + C::kD1Col + ds * TP;
+          const uint64_t bx = bx0 + (uint64_t)((xs * C::kXStage) >> 4);
+#pragma unroll
+          for (int c = 0; c < 16; ++c)
+            mma_f16_ts(dt, a + 8 * c, bx + (uint64_t)(((c >> 2) * TP * 128) >> 4) + (uint64_t)(2 * (c & 3)), idesc,
+                       c > 0 ? 1u : 0u);
+          const uint64_t bb = bb0 + (uint64_t)(((j >> 1) * C::kB2Tile) >> 4) + (uint64_t)(4 * (j & 1));
+          mma_f16_ts(d2, a + 128, bb, idesc, j > 0 ? 1u : 0u);
+          mma_f16_ts(d2, a + 136, bb + 2, idesc, 1u);
+          mma_commit(&aempty[as]);
+          mma_commit(&xempty[xs]);
+          mma_commit(&dfull[ds]);
+        }
+        if (!ok) break;
+        mma_commit(&d2full[r2]);
+      }
+      mma_commit(drain);
+      mbar_wait(drain, 0, p.status, kStatusTimeoutDrain, false);
+    }
+  } else if (warp < kTcWarpEpi0 + 4) {
+    // ------------------------------------------------------------------ group sums of this CTA's K range
+    // (decode and epilogue warps together, once): entry 4g + e of super-block j's 32 entries is Xhi, Xlo, Xhi, Xlo.
+    griddep_wait();
+    {
+      const int b = threadIdx.x - kTcWarpDq0 * 32;  // 0..639
+      const int total = sr * p.M * 8;
+      for (int e = b; e < total; e += 640) {
+        const int g = e & 7, t = (e >> 3) % p.M, j = (e >> 3) / p.M;
+        const uint4* src =
+            reinterpret_cast<const uint4*>(p.x + (int64_t)t * p.ldx + (int64_t)(sbx0 + j) * 256 + 32 * g);
+        float s = 0.f;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const uint4 v = __ldg(src + u);
+          const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            s += h2f_bits(w[k] & 0xFFFFu);
+            s += h2f_bits(w[k] >> 16);
+          }
+        }
+        const __half hi = __float2half_rn(s);
+        const __half lo = __float2half_rn(s - __half2float(hi));
+        const uint32_t pair = (uint32_t)__half_as_ushort(hi) | ((uint32_t)__half_as_ushort(lo) << 16);
+        uint8_t* tile = smem + C::kB2Off + (j >> 1) * C::kB2Tile;
+        *reinterpret_cast<uint2*>(tile + sw128_off(t, 32 * (j & 1) + 4 * g)) = make_uint2(pair, pair);
+      }
+      fence_proxy_async();  // the MMA (async proxy) reads these
+      __syncwarp();
+      if (lane == 0) mbar_arrive(b2ready);
+    }
+    if (warp < kTcWarpEpi0) {
+      // ---------------------------------------------------------------- decode
+      const int q = warp & 3, kq = (warp - kTcWarpDq0) >> 2;
+      const int r = q * 32 + lane;
+      const bool live = r < p.rt;
+      const uint32_t tl = tmem + ((uint32_t)(q * 32) << 16);
+      uint32_t i = 0;
+      bool ok = true;
+      for (int tile = cid; ok && tile < p.tiles; tile += G) {
+        for (int j = 0; j < sr; ++j, ++i) {
+          const uint32_t st = i / p.sw, ws = st % NSW, wph = (st / NSW) & 1;
+          const int sbw = (int)(i % p.sw);
+          const uint32_t as = i % kTcNA;
+          if (!mbar_wait(&wfull[ws], wph, p.status, kStatusTimeoutFull)) { ok = false; break; }
+          if (!mbar_wait(&aempty[as], ((i / kTcNA) & 1) ^ 1, p.status, kStatusTimeoutEmpty)) { ok = false; break; }
+          uint32_t v[32], a2[4];
+          float d = 0.f;
+          if (live) {
+            q4k_tc_decode(smem_u32(smem + ws * kTcWStage) + r * p.pitch + sbw * 144, kq, v, a2, d);
+          } else {
+#pragma unroll
+            for (int c = 0; c < 32; ++c) v[c] = 0u;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) a2[c] = 0u;
+          }
+          __syncwarp();
+          if (sbw == p.sw - 1 && lane == 0) mbar_arrive(&wempty[ws]);
+          tmem_st32(tl + as * kTcACols + 32 * kq, v);
+          tmem_st4(tl + as * kTcACols + 128 + 4 * kq, a2);
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&afull[as]);
+          if (kq == 0) {  // the row's d for the epilogue
+            const uint32_t ps = i % kTcNP;
+            if (!mbar_wait(&pempty[ps], ((i / kTcNP) & 1) ^ 1, p.status, kStatusTimeoutEmpty)) { ok = false; break; }
+            params[ps * 128 + r] = d;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&pfull[ps]);
+          }
+        }
+      }
+    } else {
+      // ---------------------------------------------------------------- epilogue
+      const int q = warp & 3;
+      const int r = q * 32 + lane;
+      const int et = threadIdx.x - kTcWarpEpi0 * 32;  // 0..127
+      const uint32_t tl = tmem + ((uint32_t)(q * 32) << 16);
+      const uint32_t ex_local = smem_u32(ex);
+      uint32_t i = 0, tc = 0;
+      bool ok = true;
+      for (int tile = cid; ok && tile < p.tiles; tile += G, ++tc) {
+        float acc[TP];
+#pragma unroll
+        for (int t = 0; t < TP; ++t) acc[t] = 0.f;
+        for (int j = 0; j < sr; ++j, ++i) {
+          const uint32_t ds = i % ND;
+          if (!mbar_wait(&dfull[ds], (i / ND) & 1, p.status, kStatusTimeoutFull)) { ok = false; break; }
+          tc_fence_after();
+          uint32_t v[TP];
+          if constexpr (TP == 16) tmem_ld16(tl + C::kD1Col + ds * TP, v); else tmem_ld32(tl + C::kD1Col + ds * TP, v);
+          tmem_wait_ld();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&dempty[ds]);
+          const uint32_t ps = i % kTcNP;
+          if (!mbar_wait(&pfull[ps], (i / kTcNP) & 1, p.status, kStatusTimeoutFull)) { ok = false; break; }
+          const float d = params[ps * 128 + r];
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&pempty[ps]);
+#pragma unroll
+          for (int t = 0; t < TP; ++t) acc[t] = fmaf(d, __uint_as_float(v[t]), acc[t]);
+        }
+        if (!ok) break;
+        {
+          const uint32_t r2 = tc & 1;
+          if (!mbar_wait(&d2full[r2], (tc >> 1) & 1, p.status, kStatusTimeoutFull)) { ok = false; break; }
+          tc_fence_after();
+          uint32_t v[TP];
+          if constexpr (TP == 16) tmem_ld16(tl + C::kD2Col + r2 * TP, v); else tmem_ld32(tl + C::kD2Col + r2 * TP, v);
+          tmem_wait_ld();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&d2empty[r2]);
+#pragma unroll
+          for (int t = 0; t < TP; ++t) acc[t] = acc[t] - __uint_as_float(v[t]);
+        }
+        const int row0 = tile * p.rt;
+        if (ks == 1) {
+          const int row = row0 + r;
+          if (r < p.rt && row < p.N) {
+#pragma unroll
+            for (int t = 0; t < TP; ++t)
+              if (t < p.M) tc_store<EPI, OUT_F16>(p, t, row, acc[t]);
+          }
+          continue;
+        }
+        // cluster reduction: park the partial [M][128], then add the KS partials of this CTA's row slice
+        if (!mbar_wait_cluster(exempty, (tc & 1) ^ 1, p.status, kStatusTimeoutEmpty)) { ok = false; break; }
+#pragma unroll
+        for (int t = 0; t < TP; ++t)
+          if (t < p.M) ex[t * 128 + r] = acc[t];
+        __syncwarp();
+        if (lane == 0)
+          for (int c = 0; c < ks; ++c) mbar_arrive_cluster_release(mapa_shared(smem_u32(exfull), (uint32_t)c));
+        if (!mbar_wait_cluster(exfull, tc & 1, p.status, kStatusTimeoutFull)) { ok = false; break; }
+        const int per = (p.rt + ks - 1) / ks;
+        const int r0 = (int)rank * per, r1 = min(p.rt, r0 + per);
+        const int nr = r1 - r0;
+        if (nr > 0) {
+          for (int e = et; e < nr * p.M; e += 128) {
+            const int t = e / nr, rr = r0 + e % nr;
+            const uint32_t off = ex_local + (uint32_t)(t * 128 + rr) * 4;
+            float s = ld_cluster_f32(mapa_shared(off, 0));
+            for (int c = 1; c < ks; ++c) s = s + ld_cluster_f32(mapa_shared(off, (uint32_t)c));
+            if (row0 + rr < p.N) tc_store<EPI, OUT_F16>(p, t, row0 + rr, s);
+          }
+        }
+        __syncwarp();
+        if (lane == 0)
+          for (int c = 0; c < ks; ++c) mbar_arrive_cluster_release(mapa_shared(smem_u32(exempty), (uint32_t)c));
+      }
+    }
+  }
+
+  tc_fence_before();
+  if (ks > 1) cluster_sync(); else __syncthreads();
+  if (warp == kTcWarpMma) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ------------------------------------------------------------------------------------------------ host side
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn tc_encoder() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* q = nullptr;
+    cudaDriverEntryPointQueryResult r;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &q, cudaEnableDefault, &r) == cudaSuccess &&
+        r == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(q);
+  });
+  return fn;
+}
+
+template <int TP, int EPI, bool OUT_F16>
+cudaError_t tc_launch(const QGemvArgs& a, const GemvTcPlan& pl, cudaStream_t stream) {
+  using C = TcCfg<TP>;
+  EncodeTiledFn enc = tc_encoder();
+  if (!enc) return cudaErrorNotSupported;
+  CUtensorMap mw, mx;
+  {
+    const int64_t window_u64 = (a.kb_off + a.K / 256) * 18;  // 144-byte super-blocks as u64 elements
+    cuuint64_t dims[2] = {(cuuint64_t)window_u64, (cuuint64_t)a.N};
+    cuuint64_t strides[1] = {(cuuint64_t)a.w_row_stride};
+    cuuint32_t box[2] = {(cuuint32_t)(pl.pitch / 8), (cuuint32_t)pl.rt};
+    cuuint32_t ones[2] = {1, 1};
+    if (enc(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void*>(a.w), dims, strides, box, ones,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return cudaErrorInvalidValue;
+  }
+  {
+    // activations as [K / 64][M][64]: one copy brings a super-block's 4 64-K chunks of TP token rows (rows past M
+    // are zero-filled)
+    cuuint64_t dims[3] = {64, (cuuint64_t)a.M, (cuuint64_t)(a.K / 64)};
+    cuuint64_t strides[2] = {(cuuint64_t)a.ldx * 2, 128};
+    cuuint32_t box[3] = {64, (cuuint32_t)TP, 4};
+    cuuint32_t ones[3] = {1, 1, 1};
+    if (enc(&mx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(a.x), dims, strides, box, ones,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return cudaErrorInvalidValue;
+  }
+  TcParams p;
+  p.N = (int)a.N;
+  p.M = (int)a.M;
+  p.K = (int)a.K;
+  p.kb_off = (int)a.kb_off;
+  p.rt = pl.rt;
+  p.tiles = pl.tiles;
+  p.ks = pl.ks;
+  p.srange = pl.srange;
+  p.sw = pl.sw;
+  p.pitch = pl.pitch;
+  p.x = static_cast<const __half*>(a.x);
+  p.ldx = a.ldx;
+  p.y = a.y;
+  p.ldy = a.ldy;
+  p.aux = a.aux;
+  p.ldaux = a.ldaux;
+  p.status = a.status;
+  auto kern = qgemv_tc_kernel<TP, EPI, OUT_F16>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kAlloc);
+  if (e != cudaSuccess) return e;
+  if (pl.ks > 1) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
+    (void)e;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(pl.grid);
+  cfg.blockDim = dim3(kTcThreads);
+  cfg.dynamicSmemBytes = C::kAlloc;
+  cfg.stream = stream;
+  cudaLaunchAttribute at[2];
+  int n = 0;
+  at[n].id = cudaLaunchAttributeClusterDimension;
+  at[n].val.clusterDim.x = pl.ks;
+  at[n].val.clusterDim.y = 1;
+  at[n].val.clusterDim.z = 1;
+  ++n;
+  if (launch_overlap()) {
+    at[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  cfg.attrs = at;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kern, mw, mx, p);
+}
+
+template <int TP>
+cudaError_t tc_epi(const QGemvArgs& a, const GemvTcPlan& pl, cudaStream_t s) {
+  if (a.epilogue == kEpiResid) return tc_launch<TP, kEpiResid, false>(a, pl, s);
+  if (a.epilogue == kEpiSwiglu)
+    return a.y_f16 ? tc_launch<TP, kEpiSwiglu, true>(a, pl, s) : tc_launch<TP, kEpiSwiglu, false>(a, pl, s);
+  return a.y_f16 ? tc_launch<TP, kEpiStore, true>(a, pl, s) : tc_launch<TP, kEpiStore, false>(a, pl, s);
+}
+
+// Resident clusters of `ks` CTAs of this kernel (one CTA per SM); 0 when the device cannot place them.
+int tc_max_clusters(int tp, int ks) {
+  const void* k = tp == 16 ? (const void*)qgemv_tc_kernel<16, kEpiStore, false>
+                           : (const void*)qgemv_tc_kernel<32, kEpiStore, false>;
+  const int smem = tp == 16 ? TcCfg<16>::kAlloc : TcCfg<32>::kAlloc;
+  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return 0;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(ks, 1, 1);
+  cfg.blockDim = dim3(kTcThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = ks;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, k, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return n;
+}
+
+struct ClusterCaps {
+  int dev = -1;
+  int n[2][5] = {};  // [tp == 32][ks]
+};
+
+}  // namespace
+
+GemvTcPlan qgemv_tc_plan(int type, int64_t N, int64_t K, int64_t M, int num_sms, int device) {
+  GemvTcPlan pl = {};
+  if (type != 12 || M < 1 || M > 32 || K % 256 || N < 1) return pl;
+  static std::mutex mu;
+  static ClusterCaps caps[64];
+  if (device < 0 || device >= 64) return pl;
+  const int tp = M <= 16 ? 16 : 32;
+  const int maxr = tp == 16 ? TcCfg<16>::kMaxRange : TcCfg<32>::kMaxRange;
+  int clusters[5] = {0, 0, 0, 0, 0};
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    ClusterCaps& c = caps[device];
+    if (c.dev != device) {
+      for (int t = 0; t < 2; ++t)
+        for (int k : {1, 2, 4}) c.n[t][k] = k == 1 ? 0 : tc_max_clusters(t ? 32 : 16, k);
+      c.dev = device;
+    }
+    for (int k : {2, 4}) clusters[k] = c.n[tp == 32][k];
+  }
+  clusters[1] = num_sms;
+  const int S = (int)(K / 256);
+  double best = 0;
+  for (int ks : {1, 2, 4}) {
+    if (S % ks) continue;
+    const int sr = S / ks;
+    if (sr > maxr) continue;
+    int slots = clusters[ks];
+    if (ks > 1 && slots * ks > num_sms) slots = num_sms / ks;
+    if (slots < 1) continue;
+    // fewest rounds of tiles with rows <= 128, then the smallest tile that keeps that round count
+    const int64_t tiles128 = (N + 127) / 128;
+    const int64_t rounds = (tiles128 + slots - 1) / slots;
+    int rt = (int)((N + rounds * slots - 1) / (rounds * slots));
+    if (rt < 1) rt = 1;
+    if (rt > 128) rt = 128;
+    const int64_t tiles = (N + rt - 1) / rt;
+    // per-CTA cost (cycles per super-block and tile): weight bytes at twice the fair share of HBM, the decode
+    // (one 16-warp pass per 32-row quarter), the 18 MMAs; plus the cross-CTA reduction per tile
+    const double mem = rt * 3.0;
+    const double dec = ((rt + 31) / 32) * 115.0 * (rt <= 64 ? 1.5 : 1.0);
+    const double mma = 9.0 * tp;
+    double cost = (double)rounds * sr * (mem > dec ? (mem > mma ? mem : mma) : (dec > mma ? dec : mma));
+    if (ks > 1) cost += (double)rounds * 300.0 * ks;
+    if (!pl.ok || cost < best) {
+      best = cost;
+      pl.ok = 1;
+      pl.tp = tp;
+      pl.ks = ks;
+      pl.rt = rt;
+      pl.tiles = (int)tiles;
+      pl.grid = (int)(tiles < slots ? tiles : slots) * ks;
+      pl.srange = sr;
+      pl.sw = sr % 2 == 0 ? 2 : 1;
+      pl.pitch = pl.sw == 2 ? kTcWPitch2 : kTcWPitch1;
+    }
+  }
+  return pl;
+}
+
+cudaError_t launch_qgemv_tc(const QGemvArgs& a, const GemvTcPlan& pl, cudaStream_t stream) {
+  if (!pl.ok || a.type != 12) return cudaErrorInvalidValue;
+  return pl.tp == 16 ? tc_epi<16>(a, pl, stream) : tc_epi<32>(a, pl, stream);
+}
+
+}  // namespace yah

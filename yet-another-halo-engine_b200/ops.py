@@ -97,7 +97,7 @@ def qgemm(dev: Device, w, fmt, x, N=None, K=None, kind="kstore", out_dtype="f32"
         w_row_stride = (w.shape[1] if isinstance(w, np.ndarray) else F.row_bytes(t, K + 256 * kb_off))
     N = N if N is not None else (w.shape[0] if isinstance(w, np.ndarray) else None)
     ep = _epi(kind)
-    if ep == EPI_SWIGLU:
+    if ep == EPI_SWIGLU and not gemv:  # the tile GEMM's swiglu writes f16; the GEMV's f32 or f16
         out_dtype = "f16"
     if ep == EPI_RESID:
         out_dtype = "f32"
@@ -125,9 +125,18 @@ def qgemm(dev: Device, w, fmt, x, N=None, K=None, kind="kstore", out_dtype="f32"
 
 def qgemv(dev: Device, w, fmt, x, N=None, K=None, kind="plain", out_dtype="f32", aux=None, kb_off=0,
           w_row_stride=None):
-    """Decode GEMV for M <= 32 tokens: same arguments as qgemm (kinds plain / resid)."""
+    """Decode GEMV for M <= 32 tokens: same arguments as qgemm (kinds plain / resid / swiglu; swiglu writes the
+    chosen out_dtype)."""
     return qgemm(dev, w, fmt, x, N=N, K=K, kind=kind, out_dtype=out_dtype, aux=aux, kb_off=kb_off,
                  w_row_stride=w_row_stride, gemv=True)
+
+
+def qgemv_swiglu_ptr(w_gate, gate_fmt, gate_row_stride, w_up, up_fmt, up_row_stride, N, K, x, M, ldx, y, ldy,
+                     stream=None):
+    """yah_qgemv_swiglu: y (f32) = silu(x W_gate^T) * (x W_up^T), the reference GEMV's swiglu kind (gen_gemv.py:18);
+    the two tensors may differ in format."""
+    check(lib().yah_qgemv_swiglu(w_gate, F.type_of(gate_fmt), gate_row_stride, w_up, F.type_of(up_fmt), up_row_stride,
+                                 N, K, x, M, ldx, y, ldy, stream))
 
 
 def qgemm_ffn_ptr(w_gate, w_up, fmt, N, K, w_row_stride, kb_off, x, M, ldx, y, ldy, bn=0, pair=-1, stream=None):
