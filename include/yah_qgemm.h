@@ -234,6 +234,9 @@ int yah_qgemv_swiglu(const void* w_gate, int gate_type, int64_t gate_row_stride,
  * counterpart in the reference): 0 (default) the tcgen05 kernel where it covers the call, else the mma.sync kernel;
  * 1 only the tcgen05 kernel (calls it does not cover fail with YAH_ERR_UNSUPPORTED); 2 only the mma.sync kernel. */
 int yah_set_gemv_impl(int impl);
+/* Which kernel and work split yah_qgemv would use on the current device for (type, N, K, M), as text (no
+ * counterpart in the reference; for logs and measurements). */
+int yah_qgemv_describe(int ggml_type, int64_t N, int64_t K, int64_t M, char* buf, int64_t cap);
 
 /* Decode GEMV that allocates nothing. This entry point has no counterpart in the reference engine.
  * For callers that cannot call cudaMalloc when they run the GEMV: code inside a CUDA-graph capture region, a

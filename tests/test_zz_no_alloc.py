@@ -54,10 +54,9 @@ def test_noalloc_gemv_matches_regular_gemv_twice():
     F, lib = pkg.formats, pkg.lib()
     from oracle import oracle as O
     dev = pkg.Device(0)
-    t = F.Q4_K
-    # Two different shapes, both split over K (so both use the scratch): the second call starts from whatever the
-    # first one left in the shared array.
-    for call, (M, N, K, seed) in enumerate([(8, 512, 4096, 31), (17, 1000, 2048, 32)]):
+    # Two different shapes and formats on the mma.sync kernel, both split over K (so both use the scratch): the
+    # second call starts from whatever the first one left in the shared array.
+    for call, (t, M, N, K, seed) in enumerate([(F.Q8_0, 8, 512, 4096, 31), (F.Q6_K, 17, 1000, 2048, 32)]):
         w = F.synth_weights(t, N, K, seed=seed)
         x = F.synth_activations(M, K, seed=seed + 100)
         ref = _run(lib, lib.yah_qgemv, dev, w, t, x, N, K)
@@ -72,7 +71,8 @@ def test_noalloc_gemv_matches_regular_gemv_twice():
 
 
 def test_noalloc_resid_one_token():
-    """One decode token with the residual epilogue (the one-token Q4_K form): y = resid + W x, same bits."""
+    """One decode token of Q4_K with the residual epilogue (the tcgen05 kernel, which needs no scratch; the entry
+    point then only uses its own status word): y = resid + W x, same bits."""
     pkg = ge.load_package()
     F, lib = pkg.formats, pkg.lib()
     dev = pkg.Device(0)
@@ -88,12 +88,14 @@ def test_noalloc_resid_one_token():
 
 
 def test_noalloc_refuses_scratch_beyond_its_array():
-    """A call whose split scratch exceeds the fixed array is refused before any launch (YAH_ERR_SIZE)."""
+    """A call whose split scratch exceeds the fixed array is refused before any launch (YAH_ERR_SIZE). Only the
+    mma.sync kernel uses scratch (the tcgen05 kernel adds its K parts in distributed shared memory), so Q8_0, which
+    runs on it, sizes the refused call."""
     pkg = ge.load_package()
     F, lib = pkg.formats, pkg.lib()
     dev = pkg.Device(0)
-    t = F.Q4_K
-    M, N, K = 8, 600_000, 4096  # stream-K over 4688 row blocks: more split counters than the array holds
+    t = F.Q8_0
+    M, N, K = 9, 530_000, 2048  # stream-K over 4141 row blocks: more split counters than the array holds
     wd = dev.empty(N * F.row_bytes(t, K)).fill(0)  # valid (all-zero) blocks, in case a launch did happen
     xd = dev.empty(M * K * 2).fill(0)
     yd = dev.empty(M * N * 4).fill(0)

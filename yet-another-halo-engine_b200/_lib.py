@@ -73,6 +73,7 @@ SYMBOLS = {
     "yah_qgemv_swiglu": (c_int, [c_vp, c_int, c_i64, c_vp, c_int, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_i64,
                                  c_vp]),
     "yah_set_gemv_impl": (c_int, [c_int]),
+    "yah_qgemv_describe": (c_int, [c_int, c_i64, c_i64, c_i64, ctypes.c_char_p, c_i64]),
     "yah_tp_available": (c_int, []),
     "yah_tp_unique_id": (c_int, [c_vp]),
     "yah_tp_init": (c_int, [P(c_vp), c_int, c_int, c_vp]),

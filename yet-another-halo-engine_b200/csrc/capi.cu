@@ -811,6 +811,32 @@ int yah_qgemv_noalloc(const void* w, int t, int64_t N, int64_t K, int64_t w_row_
   return after_launch(yah::launch_qgemv_static(a, plan, base, (cudaStream_t)stream), "qgemv_noalloc launch");
 }
 
+int yah_qgemv_describe(int t, int64_t N, int64_t K, int64_t M, char* buf, int64_t cap) {
+  if (!buf || cap < 1) return fail(YAH_ERR_ARG, "null or empty buffer");
+  if (!sb_bytes(t) || N < 1 || K < 256 || K % 256 || M < 1 || M > 32) return fail(YAH_ERR_ARG, "bad GEMV shape");
+  DevState* s;
+  int rc = dev_state(&s);
+  if (rc) return rc;
+  int dev = 0;
+  CK(cudaGetDevice(&dev));
+  const int impl = g_gemv_impl.load(std::memory_order_relaxed);
+  const yah::GemvTcPlan pl = impl == 2 ? yah::GemvTcPlan{} : yah::qgemv_tc_plan(t, N, K, M, sms_of(s), dev);
+  if (pl.ok) {
+    snprintf(buf, (size_t)cap,
+             "tcgen05: clusters of %d CTAs (K parts of %d super-blocks), %d tiles of %d rows, grid %d, %d MMA "
+             "columns, %d super-block(s) per weight stage",
+             pl.ks, pl.srange, pl.tiles, pl.rt, pl.grid, pl.tp, pl.sw);
+  } else if (impl == 1) {
+    return fail(YAH_ERR_UNSUPPORTED, "the tcgen05 decode GEMV does not cover this call");
+  } else {
+    const yah::GemvPlan g = yah::qgemv_plan(t, N, K, M, sms_of(s));
+    snprintf(buf, (size_t)cap, "mma.sync: mode %d (%s), grid %d, %lld partial floats, %lld counters", g.mode,
+             g.mode == 0 ? "row ranges" : g.mode == 1 ? "stream-K" : "one-token row ranges", g.grid,
+             (long long)g.ws_floats, (long long)g.counters);
+  }
+  return YAH_OK;
+}
+
 int yah_set_gemv_impl(int impl) {
   if (impl < 0 || impl > 2) return fail(YAH_ERR_ARG, "gemv impl %d (0 auto, 1 tcgen05, 2 mma.sync)", impl);
   g_gemv_impl.store(impl, std::memory_order_relaxed);
