@@ -49,33 +49,37 @@ namespace yah {
 namespace {
 
 constexpr int kTcThreads = 736;  // 23 warps
+// One MMA issuer. Measured on B200: a thread that issues tcgen05.mma waits ~45 cycles per instruction whatever its
+// size up to N = 64, and ~100 while other warps store to TMEM, so the small-N MMAs of a GEMV are issue-bound;
+// MMAs issued by two warps at once gave wrong results in whole 32-lane quarters, so the issue stays single.
 constexpr int kTcWarpX = 0, kTcWarpMma = 1, kTcWarpDq0 = 2, kTcWarpEpi0 = 18, kTcWarpW = 22;
-constexpr int kTcNA = 2;              // A buffers (TMEM): 128 columns of f16(sc*q) pairs + 16 of min factors
-constexpr int kTcACols = 144;
+constexpr int kTcACols = 144;         // an A buffer: 128 columns of f16(sc*q) pairs + 16 of min factors
 constexpr int kTcNP = 8;              // per-row d ring (decode -> epilogue)
 constexpr int kTcWPitch2 = 304;       // weight stage row pitch for 2 super-blocks (19 x 16 B: odd)
 constexpr int kTcWPitch1 = 176;       // ... for 1 super-block (11 x 16 B)
 constexpr int kTcWStage = 128 * kTcWPitch2;  // 38912 bytes, a multiple of 1024
 
+// TMEM (512 columns): NA A buffers, two D2 regions (alternate tiles), ND D1 slots. A super-block's A buffer and its
+// activation stage share ring index and are released together by one MMA commit.
 template <int TP>
 struct TcCfg {
-  static constexpr int kND = TP == 16 ? 8 : 4;          // D1 slots
-  static constexpr int kD2Col = kTcNA * kTcACols;       // D2 regions [2][TP]
+  static constexpr int kNA = TP == 16 ? 3 : 2;          // A buffers = activation stages
+  static constexpr int kD2Col = kNA * kTcACols;         // D2 regions [2][TP]
   static constexpr int kD1Col = kD2Col + 2 * TP;        // D1 slots [kND][TP]
-  static_assert(kD1Col + kND * TP <= 512, "TMEM columns");
+  static constexpr int kND = (512 - kD1Col) / TP > 8 ? 8 : (512 - kD1Col) / TP;
+  static_assert(kND >= 2, "TMEM columns");
   static constexpr int kNSW = TP == 16 ? 4 : 3;         // weight stages
-  static constexpr int kNSX = 3;                        // activation stages (one super-block each)
   static constexpr int kXStage = TP * 512;              // 4 chunks x TP rows x 128 B
   static constexpr int kMaxRange = TP == 16 ? 32 : 16;  // super-blocks per CTA (group sums kept for all of them)
   static constexpr int kB2Tile = TP * 128;              // two super-blocks' 32 entries per 128-byte token row
   static constexpr int kXOff = kTcWStage * kNSW;
-  static constexpr int kB2Off = kXOff + kNSX * kXStage;
+  static constexpr int kB2Off = kXOff + kNA * kXStage;
   static constexpr int kParOff = kB2Off + (kMaxRange / 2) * kB2Tile;
   static constexpr int kExOff = kParOff + kTcNP * 128 * 4;
   static constexpr int kBarOff = kExOff + TP * 128 * 4;
-  // wfull/wempty [NSW], xfull/xempty [NSX], afull/aempty [NA], dfull/dempty [ND], d2full/d2empty [2],
-  // pfull/pempty [NP], b2ready, exfull, exempty, drain
-  static constexpr int kNumBars = 2 * kNSW + 2 * kNSX + 2 * kTcNA + 2 * kND + 4 + 2 * kTcNP + 4;
+  // wfull/wempty [NSW], xfull/sbempty/afull [NA], dfull/dempty [ND], d2full/d2empty [2], pfull/pempty [NP],
+  // b2ready, exfull, exempty, drain
+  static constexpr int kNumBars = 2 * kNSW + 3 * kNA + 2 * kND + 4 + 2 * kTcNP + 4;
   static constexpr int kSlotOff = kBarOff + kNumBars * 8;
   static constexpr int kBytes = kSlotOff + 16;
   static constexpr int kAlloc = kBytes + 1024;
@@ -99,62 +103,89 @@ struct TcParams {
   int* status;
 };
 
-// sc and m of group g (0..7) from the block header (d | dmin << 16, scales[0..11]) (gen_gemm_decode.py:946-967).
-__device__ __forceinline__ void q4k_group_sm(const uint4& hdr, int g, int& sc, int& m) {
-  const int gg = g & 3;
-  const uint32_t b1 = (hdr.y >> (8 * gg)) & 0xFFu, b2 = (hdr.z >> (8 * gg)) & 0xFFu, b3 = (hdr.w >> (8 * gg)) & 0xFFu;
-  if (g < 4) {
-    sc = (int)(b1 & 63);
-    m = (int)(b2 & 63);
-  } else {
-    sc = (int)((b3 & 15) | ((b1 >> 6) << 4));
-    m = (int)((b3 >> 4) | ((b2 >> 6) << 4));
-  }
+// Two groups' min factors dmin * m (m given as f32 integers): cells (hi, hi), (lo, lo) for each, hi + lo ==
+// dmin * m exactly (a 17-bit multiple of ulp(dmin) >= 2^-24).
+__device__ __forceinline__ void min_cells2(float dmin, float ma, float mb, uint32_t* out) {
+  const float2 p = fmul2(make_float2(dmin, dmin), make_float2(ma, mb));  // exact
+  const uint32_t hi = pack_f16x2_rn(p.x, p.y);
+  const float2 hf = make_float2(__half2float(__ushort_as_half((unsigned short)(hi & 0xFFFFu))),
+                                __half2float(__ushort_as_half((unsigned short)(hi >> 16))));
+  const float2 rest = fadd2(p, make_float2(-hf.x, -hf.y));  // exact
+  const uint32_t lo = pack_f16x2_rn(rest.x, rest.y);
+  out[0] = prmt(hi, 0, 0x1010u);  // (hi_a, hi_a)
+  out[1] = prmt(lo, 0, 0x1010u);  // (lo_a, lo_a)
+  out[2] = prmt(hi, 0, 0x3232u);  // (hi_b, hi_b)
+  out[3] = prmt(lo, 0, 0x3232u);  // (lo_b, lo_b)
 }
 
-__device__ __forceinline__ uint32_t f16x2_same(float v) { return pack_f16x2_rn(v, v); }
-
-// dmin * m as two f16 cells (hi, hi), (lo, lo): hi + lo == dmin * m exactly.
-__device__ __forceinline__ void min_cells(float dmin, int m, uint32_t& chi, uint32_t& clo) {
-  const float p = dmin * (float)m;  // exact: 11 x 6 bits
-  const __half hi = __float2half_rn(p);
-  const float rest = p - __half2float(hi);  // exact, a multiple of ulp(dmin) >= 2^-24
-  const unsigned short hb = __half_as_ushort(hi), lb = __half_as_ushort(__float2half_rn(rest));
-  chi = (uint32_t)hb | ((uint32_t)hb << 16);
-  clo = (uint32_t)lb | ((uint32_t)lb << 16);
-}
-
-// One thread's part of a staged Q4_K super-block (its row, 64-K quarter kq: groups 2kq and 2kq + 1): 32 A cells of
-// f16(sc * q) pairs in K order, the 4 min-factor cells of its two groups, and d.
-// The byte pair (b0, b1) of a qs word goes through prmt next to 0x64 bytes: f16 (1024 + b0, 1024 + b1); masking
-// keeps 1024 + low nibble or 1024 + 16 * high nibble, and one fma.rn.f16x2 gives sc * q exactly
-// ((1024 + q) sc - 1024 sc and (1024 + 16 q) (sc / 16) - 64 sc; every term is an exact f16).
-__device__ __forceinline__ void q4k_tc_decode(uint32_t rb, int kq, uint32_t (&v)[32], uint32_t (&a2)[4], float& d) {
+// One thread's half of a staged Q4_K super-block (its row, groups 4h .. 4h + 3; `rb` the row's super-block in shared
+// memory): 64 A cells of f16(sc * q) pairs in K order into TMEM columns at `ta` (two stores of 32), the 8 min-factor
+// cells of its 4 groups at `tm`, and d.
+// The scales of the 4 groups come out as packed bytes in two vector operations (gen_gemm_decode.py:946-967). The byte
+// pair (b0, b1) of a qs word goes through prmt next to 0x64 bytes: f16 (1024 + b0, 1024 + b1); masking keeps
+// 1024 + low nibble or 1024 + 16 * high nibble, and one fma.rn.f16x2 gives sc * q exactly ((1024 + q) sc - 1024 sc
+// and (1024 + 16 q) (sc / 16) - 64 sc; every term is an exact f16).
+__device__ __forceinline__ float q4k_tc_decode_half(uint32_t rb, int h, uint32_t ta, uint32_t tm) {
   const uint4 hdr = lds128(rb);
-  const uint4 qa = lds128(rb + 16 + 32 * kq);
-  const uint4 qb = lds128(rb + 32 + 32 * kq);
-  const uint32_t qs[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-  int sc0, m0, sc1, m1;
-  q4k_group_sm(hdr, 2 * kq, sc0, m0);
-  q4k_group_sm(hdr, 2 * kq + 1, sc1, m1);
-  const uint32_t s0 = f16x2_same((float)sc0), c0 = f16x2_same(-1024.0f * (float)sc0);
-  const uint32_t s1 = f16x2_same((float)sc1 * 0.0625f), c1 = f16x2_same(-64.0f * (float)sc1);
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const uint32_t r01 = prmt(qs[i], 0x64646464u, 0x4140u);
-    const uint32_t r23 = prmt(qs[i], 0x64646464u, 0x4342u);
-    v[2 * i] = hfma2_u32(r01 & 0xFF0FFF0Fu, s0, c0);
-    v[2 * i + 1] = hfma2_u32(r23 & 0xFF0FFF0Fu, s0, c0);
-    v[16 + 2 * i] = hfma2_u32(r01 & 0xFFF0FFF0u, s1, c1);
-    v[17 + 2 * i] = hfma2_u32(r23 & 0xFFF0FFF0u, s1, c1);
+  uint32_t SC, MM;
+  if (h == 0) {
+    SC = hdr.y & 0x3F3F3F3Fu;
+    MM = hdr.z & 0x3F3F3F3Fu;
+  } else {
+    SC = (hdr.w & 0x0F0F0F0Fu) | ((hdr.y >> 2) & 0x30303030u);
+    MM = ((hdr.w >> 4) & 0x0F0F0F0Fu) | ((hdr.z >> 2) & 0x30303030u);
   }
-  d = h2f_bits(hdr.x & 0xFFFFu);
+  const float d = h2f_bits(hdr.x & 0xFFFFu);
   const float dmin = h2f_bits(hdr.x >> 16);
-  min_cells(dmin, m0, a2[0], a2[1]);
-  min_cells(dmin, m1, a2[2], a2[3]);
+  {
+    uint32_t a2[8];
+    // byte k of MM as the f32 2^23 + m, minus 2^23: m of group 4h + k
+    const float2 mlo = fadd2(make_float2(__uint_as_float(prmt(MM, 0x4B000000u, 0x7650u)),
+                                         __uint_as_float(prmt(MM, 0x4B000000u, 0x7651u))),
+                             make_float2(-kMagic23, -kMagic23));
+    const float2 mhi = fadd2(make_float2(__uint_as_float(prmt(MM, 0x4B000000u, 0x7652u)),
+                                         __uint_as_float(prmt(MM, 0x4B000000u, 0x7653u))),
+                             make_float2(-kMagic23, -kMagic23));
+    min_cells2(dmin, mlo.x, mlo.y, a2);
+    min_cells2(dmin, mhi.x, mhi.y, a2 + 4);
+    tmem_st8(tm, a2);
+  }
+#pragma unroll
+  for (int pr = 0; pr < 2; ++pr) {
+    // groups 4h + 2pr (low nibbles) and 4h + 2pr + 1 (high nibbles): qs bytes [64h + 32pr, +32)
+    const uint32_t se = hsub2_u32(prmt(SC, 0x64646464u, 0x4040u + 0x0101u * (2 * pr)), 0x64006400u);
+    const uint32_t so = hsub2_u32(prmt(SC, 0x64646464u, 0x4040u + 0x0101u * (2 * pr + 1)), 0x64006400u);
+    const uint32_t s0 = se, c0 = hmul2_u32(se, 0xE400E400u);       // sc, -1024 sc
+    const uint32_t s1 = hmul2_u32(so, 0x2C002C00u), c1 = hmul2_u32(so, 0xD400D400u);  // sc / 16, -64 sc
+    const uint4 qa = lds128(rb + 16 + 64 * h + 32 * pr);
+    const uint4 qb = lds128(rb + 32 + 64 * h + 32 * pr);
+    const uint32_t qs[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+    uint32_t v[32];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint32_t r01 = prmt(qs[i], 0x64646464u, 0x4140u);
+      const uint32_t r23 = prmt(qs[i], 0x64646464u, 0x4342u);
+      v[2 * i] = hfma2_u32(r01 & 0xFF0FFF0Fu, s0, c0);
+      v[2 * i + 1] = hfma2_u32(r23 & 0xFF0FFF0Fu, s0, c0);
+      v[16 + 2 * i] = hfma2_u32(r01 & 0xFFF0FFF0u, s1, c1);
+      v[17 + 2 * i] = hfma2_u32(r23 & 0xFFF0FFF0u, s1, c1);
+    }
+    tmem_st32(ta + 32 * pr, v);
+  }
+  return d;
 }
 
 __device__ __forceinline__ float silu_tc(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
+
+// The warps that execute warp-aligned tcgen05 instructions (decode, epilogue) wait with every lane and take the
+// result by a warp vote, so that a bounded wait that runs out sends the whole warp down the same path: a
+// .sync.aligned instruction must never be reached by only part of a warp.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* status, int code) {
+  return __all_sync(0xFFFFFFFFu, mbar_wait(bar, parity, status, code));
+}
+__device__ __forceinline__ bool warp_wait_cluster(uint64_t* bar, uint32_t parity, int* status, int code) {
+  return __all_sync(0xFFFFFFFFu, mbar_wait_cluster(bar, parity, status, code));
+}
 
 template <int EPI, bool OUT_F16>
 __device__ __forceinline__ void tc_store(const TcParams& p, int t, int row, float v) {
@@ -175,17 +206,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     qgemv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                     const TcParams p) {
   using C = TcCfg<TP>;
-  constexpr int ND = C::kND, NSW = C::kNSW, NSX = C::kNSX;
+  constexpr int NA = C::kNA, ND = C::kND, NSW = C::kNSW;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
   uint64_t* wfull = bars;
   uint64_t* wempty = wfull + NSW;
   uint64_t* xfull = wempty + NSW;
-  uint64_t* xempty = xfull + NSX;
-  uint64_t* afull = xempty + NSX;
-  uint64_t* aempty = afull + kTcNA;
-  uint64_t* dfull = aempty + kTcNA;
+  uint64_t* sbempty = xfull + NA;   // A buffer + activation stage of a super-block free again (MMA commit)
+  uint64_t* afull = sbempty + NA;   // the super-block's A buffer decoded (and its activations seen)
+  uint64_t* dfull = afull + NA;
   uint64_t* dempty = dfull + ND;
   uint64_t* d2full = dempty + ND;
   uint64_t* d2empty = d2full + 2;
@@ -211,15 +241,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < NSW; ++i) {
       mbar_init(&wfull[i], 1);
-      mbar_init(&wempty[i], 16);
+      mbar_init(&wempty[i], 8 * p.sw);  // the decode warps that read the stage: one group per super-block
     }
-    for (int i = 0; i < NSX; ++i) {
+    for (int i = 0; i < NA; ++i) {
       mbar_init(&xfull[i], 1);
-      mbar_init(&xempty[i], 1);
-    }
-    for (int i = 0; i < kTcNA; ++i) {
-      mbar_init(&afull[i], 16);
-      mbar_init(&aempty[i], 1);
+      mbar_init(&sbempty[i], 1);
+      mbar_init(&afull[i], 8);
     }
     for (int i = 0; i < ND; ++i) {
       mbar_init(&dfull[i], 1);
@@ -276,14 +303,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       bool ok = true;
       for (int tile = cid; ok && tile < p.tiles; tile += G) {
         for (int j = 0; j < sr; ++j, ++s) {
-          const uint32_t xs = s % NSX, ph = (s / NSX) & 1;
-          if (!mbar_wait(&xempty[xs], ph ^ 1, p.status, kStatusTimeoutEmpty)) { ok = false; break; }
+          const uint32_t xs = s % NA, ph = (s / NA) & 1;
+          if (!mbar_wait(&sbempty[xs], ph ^ 1, p.status, kStatusTimeoutEmpty)) { ok = false; break; }
           mbar_arrive_expect_tx(&xfull[xs], C::kXStage);
           tma_load_3d(smem + C::kXOff + xs * C::kXStage, &tmap_x, &xfull[xs], 0, 0, (sbx0 + j) * 4);
         }
       }
-      for (uint32_t i = (s > (uint32_t)NSX ? s - NSX : 0); i < s; ++i)
-        mbar_wait(&xfull[i % NSX], (i / NSX) & 1, p.status, kStatusTimeoutDrain, false);
+      for (uint32_t i = (s > (uint32_t)NA ? s - NA : 0); i < s; ++i)
+        mbar_wait(&xfull[i % NA], (i / NA) & 1, p.status, kStatusTimeoutDrain, false);
     }
   } else if (warp == kTcWarpMma) {
     // ------------------------------------------------------------------ MMA issuer
@@ -298,9 +325,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (!mbar_wait(&d2empty[r2], ((tc >> 1) & 1) ^ 1, p.status, kStatusTimeoutEmpty)) { ok = false; break; }
         const uint32_t d2 = tmem + C::kD2Col + r2 * TP;
         for (int j = 0; j < sr; ++j, ++i) {
-          const uint32_t as = i % kTcNA, xs = i % NSX, ds = i % ND;
-          if (!mbar_wait(&afull[as], (i / kTcNA) & 1, p.status, kStatusTimeoutFull)) { ok = false; break; }
-          if (!mbar_wait(&xfull[xs], (i / NSX) & 1, p.status, kStatusTimeoutFull)) { ok = false; break; }
+          const uint32_t as = i % NA, ds = i % ND;
+          if (!mbar_wait(&afull[as], (i / NA) & 1, p.status, kStatusTimeoutFull)) { ok = false; break; }
+          if (!mbar_wait(&xfull[as], (i / NA) & 1, p.status, kStatusTimeoutFull)) { ok = false; break; }
           if (!mbar_wait(&dempty[ds], ((i / ND) & 1) ^ 1, p.status, kStatusTimeoutEmpty)) { ok = false; break; }
           if (!b2) {
             if (!mbar_wait(b2ready, 0, p.status, kStatusTimeoutFull)) { ok = false; break; }
@@ -309,7 +336,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           tc_fence_after();
           const uint32_t a = tmem + as * kTcACols;
           const uint32_t dt = tmem + C::kD1Col + ds * TP;
-          const uint64_t bx = bx0 + (uint64_t)((xs * C::kXStage) >> 4);
+          const uint64_t bx = bx0 + (uint64_t)((as * C::kXStage) >> 4);
 #pragma unroll
           for (int c = 0; c < 16; ++c)
             mma_f16_ts(dt, a + 8 * c, bx + (uint64_t)(((c >> 2) * TP * 128) >> 4) + (uint64_t)(2 * (c & 3)), idesc,
@@ -317,8 +344,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           const uint64_t bb = bb0 + (uint64_t)(((j >> 1) * C::kB2Tile) >> 4) + (uint64_t)(4 * (j & 1));
           mma_f16_ts(d2, a + 128, bb, idesc, j > 0 ? 1u : 0u);
           mma_f16_ts(d2, a + 136, bb + 2, idesc, 1u);
-          mma_commit(&aempty[as]);
-          mma_commit(&xempty[xs]);
+          mma_commit(&sbempty[as]);
           mma_commit(&dfull[ds]);
         }
         if (!ok) break;
@@ -361,40 +387,35 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     if (warp < kTcWarpEpi0) {
       // ---------------------------------------------------------------- decode
-      const int q = warp & 3, kq = (warp - kTcWarpDq0) >> 2;
+      // two groups of 8 warps take alternate super-blocks; in a group, warp (lane quarter q, half h) decodes
+      // groups 4h .. 4h + 3 of its 32 rows
+      const int q = warp & 3, par = (warp - kTcWarpDq0) >> 3, h = ((warp - kTcWarpDq0) >> 2) & 1;
       const int r = q * 32 + lane;
-      const bool live = r < p.rt;
       const uint32_t tl = tmem + ((uint32_t)(q * 32) << 16);
       uint32_t i = 0;
       bool ok = true;
       for (int tile = cid; ok && tile < p.tiles; tile += G) {
         for (int j = 0; j < sr; ++j, ++i) {
+          if ((int)(i & 1) != par) continue;
           const uint32_t st = i / p.sw, ws = st % NSW, wph = (st / NSW) & 1;
           const int sbw = (int)(i % p.sw);
-          const uint32_t as = i % kTcNA;
-          if (!mbar_wait(&wfull[ws], wph, p.status, kStatusTimeoutFull)) { ok = false; break; }
-          if (!mbar_wait(&aempty[as], ((i / kTcNA) & 1) ^ 1, p.status, kStatusTimeoutEmpty)) { ok = false; break; }
-          uint32_t v[32], a2[4];
-          float d = 0.f;
-          if (live) {
-            q4k_tc_decode(smem_u32(smem + ws * kTcWStage) + r * p.pitch + sbw * 144, kq, v, a2, d);
-          } else {
-#pragma unroll
-            for (int c = 0; c < 32; ++c) v[c] = 0u;
-#pragma unroll
-            for (int c = 0; c < 4; ++c) a2[c] = 0u;
-          }
+          const uint32_t as = i % NA;
+          if (!warp_wait(&wfull[ws], wph, p.status, kStatusTimeoutFull)) { ok = false; break; }
+          if (!warp_wait(&sbempty[as], ((i / NA) & 1) ^ 1, p.status, kStatusTimeoutEmpty)) { ok = false; break; }
+          tc_fence_after();  // the MMAs that read this A buffer are complete: order the stores after them
+          // Every lane decodes and stores (the stores are warp-aligned): rows past the tile read the stage's
+          // unused rows, and the epilogue never reads their results.
+          const uint32_t ta = tl + as * kTcACols + 64 * h, tm = tl + as * kTcACols + 128 + 8 * h;
+          const float d = q4k_tc_decode_half(smem_u32(smem + ws * kTcWStage) + r * p.pitch + sbw * 144, h, ta, tm);
           __syncwarp();
-          if (sbw == p.sw - 1 && lane == 0) mbar_arrive(&wempty[ws]);
-          tmem_st32(tl + as * kTcACols + 32 * kq, v);
-          tmem_st4(tl + as * kTcACols + 128 + 4 * kq, a2);
+          if (lane == 0) mbar_arrive(&wempty[ws]);  // this warp's only read of the stage
           tmem_wait_st();
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&afull[as]);
-          if (kq == 0) {  // the row's d for the epilogue
+          if (h == 0) {  // the row's d for the epilogue
             const uint32_t ps = i % kTcNP;
-            if (!mbar_wait(&pempty[ps], ((i / kTcNP) & 1) ^ 1, p.status, kStatusTimeoutEmpty)) { ok = false; break; }
+            if (!warp_wait(&pempty[ps], ((i / kTcNP) & 1) ^ 1, p.status, kStatusTimeoutEmpty)) { ok = false; break; }
             params[ps * 128 + r] = d;
             __syncwarp();
             if (lane == 0) mbar_arrive(&pfull[ps]);
@@ -416,35 +437,42 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         for (int t = 0; t < TP; ++t) acc[t] = 0.f;
         for (int j = 0; j < sr; ++j, ++i) {
           const uint32_t ds = i % ND;
-          if (!mbar_wait(&dfull[ds], (i / ND) & 1, p.status, kStatusTimeoutFull)) { ok = false; break; }
+          if (!warp_wait(&dfull[ds], (i / ND) & 1, p.status, kStatusTimeoutFull)) { ok = false; break; }
           tc_fence_after();
-          uint32_t v[TP];
-          if constexpr (TP == 16) tmem_ld16(tl + C::kD1Col + ds * TP, v); else tmem_ld32(tl + C::kD1Col + ds * TP, v);
-          tmem_wait_ld();
+          const uint32_t ps = i % kTcNP;
+          if (!warp_wait(&pfull[ps], (i / kTcNP) & 1, p.status, kStatusTimeoutFull)) { ok = false; break; }
+          const float d = params[ps * 128 + r];
+#pragma unroll
+          for (int h16 = 0; h16 < TP / 16; ++h16) {  // 16 columns at a time (registers)
+            uint32_t v[16];
+            tmem_ld16(tl + C::kD1Col + ds * TP + 16 * h16, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int t = 0; t < 16; ++t) acc[16 * h16 + t] = fmaf(d, __uint_as_float(v[t]), acc[16 * h16 + t]);
+          }
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&dempty[ds]);
-          const uint32_t ps = i % kTcNP;
-          if (!mbar_wait(&pfull[ps], (i / kTcNP) & 1, p.status, kStatusTimeoutFull)) { ok = false; break; }
-          const float d = params[ps * 128 + r];
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&pempty[ps]);
-#pragma unroll
-          for (int t = 0; t < TP; ++t) acc[t] = fmaf(d, __uint_as_float(v[t]), acc[t]);
+          if (lane == 0) {
+            mbar_arrive(&dempty[ds]);
+            mbar_arrive(&pempty[ps]);
+          }
         }
         if (!ok) break;
         {
           const uint32_t r2 = tc & 1;
-          if (!mbar_wait(&d2full[r2], (tc >> 1) & 1, p.status, kStatusTimeoutFull)) { ok = false; break; }
+          if (!warp_wait(&d2full[r2], (tc >> 1) & 1, p.status, kStatusTimeoutFull)) { ok = false; break; }
           tc_fence_after();
-          uint32_t v[TP];
-          if constexpr (TP == 16) tmem_ld16(tl + C::kD2Col + r2 * TP, v); else tmem_ld32(tl + C::kD2Col + r2 * TP, v);
-          tmem_wait_ld();
+#pragma unroll
+          for (int h16 = 0; h16 < TP / 16; ++h16) {
+            uint32_t v[16];
+            tmem_ld16(tl + C::kD2Col + r2 * TP + 16 * h16, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int t = 0; t < 16; ++t) acc[16 * h16 + t] = acc[16 * h16 + t] - __uint_as_float(v[t]);
+          }
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&d2empty[r2]);
-#pragma unroll
-          for (int t = 0; t < TP; ++t) acc[t] = acc[t] - __uint_as_float(v[t]);
         }
         const int row0 = tile * p.rt;
         if (ks == 1) {
@@ -457,14 +485,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           continue;
         }
         // cluster reduction: park the partial [M][128], then add the KS partials of this CTA's row slice
-        if (!mbar_wait_cluster(exempty, (tc & 1) ^ 1, p.status, kStatusTimeoutEmpty)) { ok = false; break; }
+        if (!warp_wait_cluster(exempty, (tc & 1) ^ 1, p.status, kStatusTimeoutEmpty)) { ok = false; break; }
 #pragma unroll
         for (int t = 0; t < TP; ++t)
           if (t < p.M) ex[t * 128 + r] = acc[t];
         __syncwarp();
         if (lane == 0)
           for (int c = 0; c < ks; ++c) mbar_arrive_cluster_release(mapa_shared(smem_u32(exfull), (uint32_t)c));
-        if (!mbar_wait_cluster(exfull, tc & 1, p.status, kStatusTimeoutFull)) { ok = false; break; }
+        if (!warp_wait_cluster(exfull, tc & 1, p.status, kStatusTimeoutFull)) { ok = false; break; }
         const int per = (p.rt + ks - 1) / ks;
         const int r0 = (int)rank * per, r1 = min(p.rt, r0 + per);
         const int nr = r1 - r0;
