@@ -440,13 +440,16 @@ def run_decode_record(args, local_rank, launches=200):
             raise RuntimeError("kernel status word set")
         alg = k.wbytes + k.xbytes + k.ybytes
         us = ms / launches * 1e3
+        import ctypes
+        desc = ctypes.create_string_buffer(512)
+        pkg._lib.check(pkg.lib().yah_qgemv_describe(12, 4096, 14336, M, desc, 512))
         gbs = alg / (us * 1e-6) / 1e9
         out["by_M"][str(M)] = {"us_per_launch": round(us, 3), "GB/s": round(gbs, 1),
                                "GB/s_weights_only": round(k.wbytes / (us * 1e-6) / 1e9, 1),
                                "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": pk["hbm_gbs"],
                                             "unit": "GB/s", "frac": round(gbs / pk["hbm_gbs"], 4),
                                             "peak_src": pk["src"], "algorithmic_bytes_per_launch": alg},
-                               "clocks": clk}
+                               "clocks": clk, "kernel": desc.value.decode()}
         k.close()
     return out
 

@@ -68,7 +68,44 @@ def test_small_stack_one_rank(pkg, O, dev, comm):
     got = h.download(np.float32, (M, shape.hidden))
     e = O.errors(got, W.stack_ref(O, shape, full, h0, tp.NORM_GAIN, tp.NORM_EPS))
     stack.close()
-    assert e["finite"] and e["rel_fro"] <= 2e-3, e
+    assert e["finite"] and e["rel_fro"] <= 1e-3, e
+    assert dev.status_word() == 0
+
+
+def test_small_stack_layer0_sites(pkg, F, O, dev):
+    """Each of the five linears of the stack's first layer at the stack's own operands (QKV f16 out, o_proj with the
+    residual epilogue, gate f32, up with the swiglu epilogue, down with the residual), every one against the float64
+    oracle: relative Frobenius <= 1e-3 and max |y - ref| <= max(2e-2, 1e-4 max |ref|) (+ half an f16 ulp on f16
+    outputs). With the BASELINE weights the later sites' outputs reach ~3e5, where one f32 ulp is 0.03, so the
+    path's absolute 2e-2 (set for the configurations' outputs of ~1500) is scaled as the reference GEMV checker
+    scales its own bar, by max |ref| (engine/gpu/loom/tools/gemv_check.py:176-183)."""
+    tp = pkg.tp
+    shape = tp.StackShape(layers=1, hidden=512, n_q=4, n_kv=2, head_dim=128, ff=1024)
+    M, H, q = 64, shape.hidden, shape.n_q * shape.head_dim
+    W0 = tp.layer_weights(shape, 0)
+    deq = {k: O.dequant_f16(shape.fmt, v, v.shape[0], v.shape[1] // 144 * 256) for k, v in W0.items()}
+    h = np.random.default_rng(75).standard_normal((M, H)).astype(np.float32)
+
+    def close(y, ref, f16):
+        e = O.errors(y, ref)
+        assert e["finite"] and e["rel_fro"] <= 1e-3, e
+        lim = max(2e-2, 1e-4 * np.abs(ref).max()) + (O.f16_half_ulp(ref) if f16 else 0.0)
+        assert (np.abs(y.astype(np.float64) - ref) <= lim).all(), e
+
+    xn = W.rmsnorm_ref(h, tp.NORM_GAIN, tp.NORM_EPS)
+    qkv = pkg.ops.qgemm(dev, W0["qkv"], shape.fmt, xn, out_dtype="f16")
+    close(qkv, O.gemm_ref(deq["qkv"], xn), True)
+    qin = np.ascontiguousarray(qkv[:, :q])
+    ho = pkg.ops.qgemm(dev, W0["o"], shape.fmt, qin, kind="kres", aux=h)
+    close(ho, h.astype(np.float64) + O.gemm_ref(deq["o"], qin), False)
+    xn2 = W.rmsnorm_ref(ho, tp.NORM_GAIN, tp.NORM_EPS)
+    g = pkg.ops.qgemm(dev, W0["gate"], shape.fmt, xn2)
+    close(g, O.gemm_ref(deq["gate"], xn2), False)
+    act = pkg.ops.qgemm(dev, W0["up"], shape.fmt, xn2, kind="swiglu", aux=g)
+    g64 = g.astype(np.float64)
+    close(act, g64 / (1.0 + np.exp(-g64)) * O.gemm_ref(deq["up"], xn2), True)
+    hd = pkg.ops.qgemm(dev, W0["down"], shape.fmt, act, kind="kres", aux=ho)
+    close(hd, ho.astype(np.float64) + O.gemm_ref(deq["down"], act), False)
     assert dev.status_word() == 0
 
 
@@ -95,7 +132,7 @@ def test_small_stack_chunked_one_rank(pkg, O, dev, comm, M, chunks):
     e = O.errors(got, W.stack_ref(O, shape, full, h0, tp.NORM_GAIN, tp.NORM_EPS))
     stack.close()
     s.close()
-    assert e["finite"] and e["rel_fro"] <= 2e-3, e
+    assert e["finite"] and e["rel_fro"] <= 1e-3, e
     assert dev.status_word() == 0
 
 
@@ -116,7 +153,7 @@ def test_small_stack_speed_mode_one_rank(pkg, O, dev, comm, M):
     got = h.download(np.float32, (M, shape.hidden))
     e = O.errors(got, W.stack_ref(O, shape, full, h0, tp.NORM_GAIN, tp.NORM_EPS))
     stack.close()
-    assert e["finite"] and e["rel_fro"] <= 2e-3, e
+    assert e["finite"] and e["rel_fro"] <= 1e-3, e
     assert dev.status_word() == 0
 
 
@@ -135,4 +172,4 @@ def test_small_stack_two_ranks(pkg, mode):
     for p in procs:
         p.join(timeout=60)
     for rank, rel_fro, finite, status in res:
-        assert finite and rel_fro <= 2e-3 and status == 0, (rank, rel_fro, finite, status)
+        assert finite and rel_fro <= 1e-3 and status == 0, (rank, rel_fro, finite, status)

@@ -71,7 +71,7 @@ def test_noalloc_gemv_matches_regular_gemv_twice():
 
 
 def test_noalloc_resid_one_token():
-    """One decode token of Q4_K with the residual epilogue (the tcgen05 kernel, which needs no scratch; the entry
+    """One decode token of Q4_K with the residual epilogue (the one-token form, which needs no scratch; the entry
     point then only uses its own status word): y = resid + W x, same bits."""
     pkg = ge.load_package()
     F, lib = pkg.formats, pkg.lib()
