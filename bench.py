@@ -873,7 +873,10 @@ def main():
         if line is not None:
             print(json.dumps(line), flush=True)
         return
-    os.environ.setdefault("NCCL_DEBUG", "INFO")
+    # NCCL's own log of the communicator (rank, nRanks) is wanted in the output: raise NCCL_DEBUG to INFO (an
+    # environment default of VERSION or WARN would hide it) and keep it to the INIT subsystem.
+    if os.environ.get("NCCL_DEBUG", "").upper() not in ("INFO", "TRACE"):
+        os.environ["NCCL_DEBUG"] = "INFO"
     os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
     dist = dist_init(args.gpus)
     import __graft_entry__ as ge
