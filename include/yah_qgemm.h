@@ -215,10 +215,11 @@ int yah_tile_rules_count(int* n);
  * yah_qgemm; epilogue YAH_EPI_STORE, YAH_EPI_RESID, or YAH_EPI_SWIGLU (y = silu(aux) * W x with y f32 or f16; aux
  * may be y itself when y is f32: each gate value is read before it is overwritten). Computes with the f32 weight
  * values of the GGUF dequant, as the reference GEMV does (no f16 rounding of weights). Results are deterministic.
- * Two kernels: Q4_K with more than 8 tokens runs on the tcgen05 tensor cores (thread-block clusters split K and add
- * their partial sums in distributed shared memory; no scratch); the rest runs an mma.sync kernel whose row blocks
- * shared by two CTAs are summed through a library-owned per-device workspace (allocated on first use, grown on
- * demand), so concurrent calls on different streams of one device must not overlap. */
+ * Two kernels: an mma.sync kernel, and for Q4_K with more than 8 tokens whose activations are too many to keep in
+ * shared memory (the mma.sync kernel would then run stream-K) a tcgen05 kernel (thread-block clusters split K and
+ * add their partial sums in distributed shared memory; no scratch). The mma.sync kernel's stream-K form sums the row
+ * blocks shared by two CTAs through a library-owned per-device workspace (allocated on first use, grown on demand),
+ * so concurrent calls on different streams of one device must not overlap. */
 int yah_qgemv(const void* w, int ggml_type, int64_t N, int64_t K, int64_t w_row_stride, int64_t kb_off,
               const void* x, int64_t M, int64_t ldx, void* y, int y_dtype, int64_t ldy, int epilogue,
               const void* aux, int64_t ldaux, void* stream);
@@ -231,7 +232,8 @@ int yah_qgemv_swiglu(const void* w_gate, int gate_type, int64_t gate_row_stride,
                      int64_t ldy, void* stream);
 
 /* Which decode GEMV kernel yah_qgemv and yah_qgemv_noalloc run (process-wide; for tests and measurements, no
- * counterpart in the reference): 0 (default) the tcgen05 kernel for Q4_K above 8 tokens, else the mma.sync kernel;
+ * counterpart in the reference): 0 (default) the tcgen05 kernel for Q4_K above 8 tokens where the mma.sync kernel
+ * would run stream-K, else the mma.sync kernel;
  * 1 only the tcgen05 kernel (calls it does not cover fail with YAH_ERR_UNSUPPORTED); 2 only the mma.sync kernel. */
 int yah_set_gemv_impl(int impl);
 /* Which kernel and work split yah_qgemv would use on the current device for (type, N, K, M), as text (no

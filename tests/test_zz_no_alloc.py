@@ -95,7 +95,9 @@ def test_noalloc_refuses_scratch_beyond_its_array():
     F, lib = pkg.formats, pkg.lib()
     dev = pkg.Device(0)
     t = F.Q8_0
-    M, N, K = 9, 530_000, 2048  # stream-K over 4141 row blocks: more split counters than the array holds
+    # 32 tokens of K = 4096 (264 KB of activations: too many to keep resident, so stream-K) over 4141 row blocks:
+    # more split counters than the array holds
+    M, N, K = 32, 530_000, 4096
     wd = dev.empty(N * F.row_bytes(t, K)).fill(0)  # valid (all-zero) blocks, in case a launch did happen
     xd = dev.empty(M * K * 2).fill(0)
     yd = dev.empty(M * N * 4).fill(0)

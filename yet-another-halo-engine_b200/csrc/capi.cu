@@ -187,9 +187,10 @@ constexpr int kNotTaken = -1;
 int launch_gemv_tc(const yah::QGemvArgs& a, int dev, cudaStream_t stream) {
   const int impl = g_gemv_impl.load(std::memory_order_relaxed);
   if (impl == 2) return kNotTaken;
-  // Automatic choice, measured on B200 (4096 x 14336 and 14336 x 4096, Q4_K): the tcgen05 form takes 23-31 us at
-  // 1..32 tokens, its MMA issue the limit; the mma.sync form 12 us at one token, 15-24 us at 2..8, 39-74 us at 12..32.
-  if (impl == 0 && a.M <= 8) return kNotTaken;
+  // Automatic choice, measured on B200 (Q4_K 4096 x 14336 and 14336 x 4096): the tcgen05 form takes 23-31 us at
+  // 1..32 tokens, its MMA issue the limit; the mma.sync form 12 us at one token and 15-24 us while its activations
+  // stay resident (row ranges), but 24 us at 8 and 39-74 us at 12..32 tokens when it has to run stream-K.
+  if (impl == 0 && (a.M <= 8 || yah::qgemv_plan(a.type, a.N, a.K, a.M, a.num_sms).mode != 1)) return kNotTaken;
   const yah::GemvTcPlan pl = yah::qgemv_tc_plan(a.type, a.N, a.K, a.M, a.num_sms, dev);
   if (!pl.ok) {
     if (impl == 1)
@@ -823,8 +824,9 @@ int yah_qgemv_describe(int t, int64_t N, int64_t K, int64_t M, char* buf, int64_
   int dev = 0;
   CK(cudaGetDevice(&dev));
   const int impl = g_gemv_impl.load(std::memory_order_relaxed);
-  const yah::GemvTcPlan pl = (impl == 2 || (impl == 0 && M <= 8)) ? yah::GemvTcPlan{}
-                                                                   : yah::qgemv_tc_plan(t, N, K, M, sms_of(s), dev);
+  const bool auto_mma = impl == 0 && (M <= 8 || yah::qgemv_plan(t, N, K, M, sms_of(s)).mode != 1);
+  const yah::GemvTcPlan pl = (impl == 2 || auto_mma) ? yah::GemvTcPlan{}
+                                                     : yah::qgemv_tc_plan(t, N, K, M, sms_of(s), dev);
   if (pl.ok) {
     snprintf(buf, (size_t)cap,
              "tcgen05: clusters of %d CTAs (K parts of %d super-blocks), %d tiles of %d rows, grid %d, %d MMA "

@@ -1308,15 +1308,29 @@ std::atomic<int> g_launch_overlap{1};
 bool launch_overlap() { return g_launch_overlap.load(std::memory_order_relaxed) != 0; }
 void set_launch_overlap(bool on) { g_launch_overlap.store(on ? 1 : 0, std::memory_order_relaxed); }
 
+GemvPlan qgemv_plan_limit(int type, int64_t N, int64_t K, int64_t M, int num_sms, int64_t res_limit);
+
 GemvPlan qgemv_plan(int type, int64_t N, int64_t K, int64_t M, int num_sms) {
   GemvPlan pl{};
   if (type == 12 && M == 1 && plan_m1(pl, N, K, num_sms)) return pl;
+  // resident activations when they leave a ring of >= 2 weight stages, else stream-K
+  pl = qgemv_plan_limit(type, N, K, M, num_sms, 128 * 1024);
+  if (pl.mode == 0 && pl.ringst < 2) pl = qgemv_plan_limit(type, N, K, M, num_sms, 0);
+  return pl;
+}
+
+GemvPlan qgemv_plan_limit(int type, int64_t N, int64_t K, int64_t M, int num_sms, int64_t res_limit) {
+  GemvPlan pl{};
   const int nt = pow2_ceil((int)((M + 7) / 8));  // token tiles of 8: 1, 2 or 4
   const int64_t units = (N + 3) / 4, nsb = K / 256;
   // Row ranges need >= 16 rows per CTA and pay off when the activations stay resident (no per-stage activation
   // copies, permutes and group sums); otherwise stream-K over 128-row blocks shares each stage's activations
   // among 128 rows.
-  const bool ranges = units >= 4 * (int64_t)num_sms && M * K * 2 <= 32 * 1024;
+  // Resident activations (and Q4_K group sums) up to 128 KB, which leaves >= 2 weight stages of 32 KB beside them
+  // (measured on B200, Q4_K 4096 x 14336: M = 2 21.2 -> 15.2 us, M = 4 23.3 -> 17.5 us against the 32 KB limit;
+  // 14336 x 4096 M = 8 22.7 -> 16.2 us).
+  const int64_t res_need = M * (K * 2 + 64) + (type == 12 ? M * ((K / 256) * 32 + 16) : 0);
+  const bool ranges = units >= 4 * (int64_t)num_sms && res_need <= res_limit;
   pl.mode = ranges ? 0 : 1;
   if (ranges) {
     pl.grid = num_sms;
@@ -1337,7 +1351,7 @@ GemvPlan qgemv_plan(int type, int64_t N, int64_t K, int64_t M, int num_sms) {
     pl.ntw = nt;
     pl.slots = 1;
   }
-  pl.xres = ranges && M * K * 2 <= 32 * 1024;  // all activations fit beside the weight stages
+  pl.xres = ranges;  // all activations fit beside the weight stages
   const int red_bytes = (ranges && pl.slots > 1) ? pl.cw * 32 * pl.ntw * 4 * 4 : 0;
   const int bar_bytes = (3 * kGvMaxStages + 2) * 8;
   const bool two_per_sm = !ranges && pl.ntw == 1;
