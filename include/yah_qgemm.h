@@ -185,6 +185,22 @@ int yah_qgemm_tile(const void* w, int ggml_type, int64_t N, int64_t K, int64_t w
                    const void* x, int64_t M, int64_t ldx, void* y, int y_dtype, int64_t ldy, int epilogue,
                    const void* aux, int64_t ldaux, int bn, int grid, int64_t kchunk, int cta_pair, void* stream);
 
+/* Caller-owned workspace (no counterpart in the reference, whose kernels need none: its GEMMs never split K). The
+ * library-owned buffers of yah_qgemm / yah_qgemm_tile / yah_qgemv are shared by every call on a device; these
+ * variants take the workspace from the caller instead, so calls on different streams with different workspaces
+ * may overlap, and the call itself never allocates device memory.
+ * yah_qgemm_workspace_size: the bytes yah_qgemm_ws needs for (type, N, K, M, y_dtype, epilogue) and a tile choice
+ * (bn, grid, kchunk, cta_pair as in yah_qgemm_tile; 0 / -1 for the automatic ones); 0 when the call needs none
+ * (no chunked accumulation). yah_qgemm_ws: yah_qgemm_tile on that workspace (256-byte aligned, at least the queried
+ * size; NULL allowed when the size is 0; too small: YAH_ERR_SIZE). Same results, bit for bit, as yah_qgemm_tile
+ * with the same arguments. The workspace holds no state between calls. */
+int yah_qgemm_workspace_size(int ggml_type, int64_t N, int64_t K, int64_t M, int y_dtype, int epilogue, int bn,
+                             int grid, int64_t kchunk, int cta_pair, size_t* bytes);
+int yah_qgemm_ws(const void* w, int ggml_type, int64_t N, int64_t K, int64_t w_row_stride, int64_t kb_off,
+                 const void* x, int64_t M, int64_t ldx, void* y, int y_dtype, int64_t ldy, int epilogue,
+                 const void* aux, int64_t ldaux, int bn, int grid, int64_t kchunk, int cta_pair, void* workspace,
+                 size_t workspace_bytes, void* stream);
+
 /* The fused gate+up SwiGLU of the feed-forward block (the reference's ffn kind, gen_gemm_tile.py:316-318, :1675):
  * y[M][ldy] = f16(silu(x W_gate^T) * (x W_up^T)), both weight tensors of the same type, shape and row stride. One
  * tile GEMM: each CTA decodes 64 gate rows and the same 64 up rows into its 128 TMEM lanes and its epilogue
@@ -223,6 +239,16 @@ int yah_tile_rules_count(int* n);
 int yah_qgemv(const void* w, int ggml_type, int64_t N, int64_t K, int64_t w_row_stride, int64_t kb_off,
               const void* x, int64_t M, int64_t ldx, void* y, int y_dtype, int64_t ldy, int epilogue,
               const void* aux, int64_t ldaux, void* stream);
+
+/* yah_qgemv on a caller-owned workspace (see yah_qgemm_ws): yah_qgemv_workspace_size gives the bytes for (type, N,
+ * K, M) under the current kernel choice (yah_set_gemv_impl), 0 where the chosen form needs none (the tcgen05
+ * kernel and the row-range forms of the mma.sync kernel). yah_qgemv_ws clears the workspace's split counters on
+ * `stream` before its launch, so the workspace holds no state between calls. Same results, bit for bit, as
+ * yah_qgemv. */
+int yah_qgemv_workspace_size(int ggml_type, int64_t N, int64_t K, int64_t M, size_t* bytes);
+int yah_qgemv_ws(const void* w, int ggml_type, int64_t N, int64_t K, int64_t w_row_stride, int64_t kb_off,
+                 const void* x, int64_t M, int64_t ldx, void* y, int y_dtype, int64_t ldy, int epilogue,
+                 const void* aux, int64_t ldaux, void* workspace, size_t workspace_bytes, void* stream);
 
 /* The reference GEMV's swiglu kind (gen_gemv.py:18, :97-98; called per layer at engine/model/loom_decoder.hpp:294):
  * y[M][ldy] (f32) = silu(x W_gate^T) * (x W_up^T). The two weight tensors may differ in format and row stride (same

@@ -63,6 +63,10 @@ SYMBOLS = {
                           c_vp, c_i64, c_vp]),
     "yah_qgemm_tile": (c_int, [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_int, c_i64,
                                c_int, c_vp, c_i64, c_int, c_int, c_i64, c_int, c_vp]),
+    "yah_qgemm_workspace_size": (c_int, [c_int, c_i64, c_i64, c_i64, c_int, c_int, c_int, c_int, c_i64, c_int,
+                                         P(c_sz)]),
+    "yah_qgemm_ws": (c_int, [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_int, c_i64, c_int,
+                             c_vp, c_i64, c_int, c_int, c_i64, c_int, c_vp, c_sz, c_vp]),
     "yah_qgemm_ffn": (c_int, [c_vp, c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_i64, c_int,
                               c_int, c_vp]),
     "yah_qgemv": (c_int, [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_int, c_i64, c_int,
@@ -70,6 +74,9 @@ SYMBOLS = {
     "yah_qgemv_noalloc": (c_int, [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_int, c_i64,
                                   c_int, c_vp, c_i64, c_vp]),
     "yah_qgemv_noalloc_status": (c_int, [P(c_int)]),
+    "yah_qgemv_workspace_size": (c_int, [c_int, c_i64, c_i64, c_i64, P(c_sz)]),
+    "yah_qgemv_ws": (c_int, [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_int, c_i64, c_int,
+                             c_vp, c_i64, c_vp, c_sz, c_vp]),
     "yah_qgemv_swiglu": (c_int, [c_vp, c_int, c_i64, c_vp, c_int, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_i64,
                                  c_vp]),
     "yah_set_gemv_impl": (c_int, [c_int]),

@@ -182,23 +182,64 @@ int after_launch(cudaError_t e, const char* what) {
 namespace {
 constexpr int kNotTaken = -1;
 
+// The kernel the GEMV dispatch picks. Automatic choice, measured on B200 (Q4_K 4096 x 14336 and 14336 x 4096): the
+// tcgen05 form takes 23-31 us at 1..32 tokens, its MMA issue the limit; the mma.sync form 12 us at one token and
+// 15-24 us while its activations stay resident (row ranges), but 24 us at 8 and 39-74 us at 12..32 tokens when it
+// has to run stream-K. Returns the tcgen05 plan (ok = false: the mma.sync kernel runs); refuses (YAH_ERR_UNSUPPORTED
+// through *rc) a forced tcgen05 choice the kernel does not cover.
+yah::GemvTcPlan gemv_tc_choice(int t, int64_t N, int64_t K, int64_t M, int sms, int dev, int* rc) {
+  *rc = YAH_OK;
+  const int impl = g_gemv_impl.load(std::memory_order_relaxed);
+  if (impl == 2) return yah::GemvTcPlan{};
+  if (impl == 0 && (M <= 8 || yah::qgemv_plan(t, N, K, M, sms).mode != 1)) return yah::GemvTcPlan{};
+  const yah::GemvTcPlan pl = yah::qgemv_tc_plan(t, N, K, M, sms, dev);
+  if (!pl.ok && impl == 1)
+    *rc = fail(YAH_ERR_UNSUPPORTED, "the tcgen05 decode GEMV does not cover type %d, N=%lld, K=%lld, M=%lld", t,
+               (long long)N, (long long)K, (long long)M);
+  return pl;
+}
+
 // The tcgen05 decode GEMV for a call it covers (per the impl switch): its launch status, or kNotTaken when the call
 // goes to the mma.sync form. a.status must be set.
 int launch_gemv_tc(const yah::QGemvArgs& a, int dev, cudaStream_t stream) {
-  const int impl = g_gemv_impl.load(std::memory_order_relaxed);
-  if (impl == 2) return kNotTaken;
-  // Automatic choice, measured on B200 (Q4_K 4096 x 14336 and 14336 x 4096): the tcgen05 form takes 23-31 us at
-  // 1..32 tokens, its MMA issue the limit; the mma.sync form 12 us at one token and 15-24 us while its activations
-  // stay resident (row ranges), but 24 us at 8 and 39-74 us at 12..32 tokens when it has to run stream-K.
-  if (impl == 0 && (a.M <= 8 || yah::qgemv_plan(a.type, a.N, a.K, a.M, a.num_sms).mode != 1)) return kNotTaken;
-  const yah::GemvTcPlan pl = yah::qgemv_tc_plan(a.type, a.N, a.K, a.M, a.num_sms, dev);
-  if (!pl.ok) {
-    if (impl == 1)
-      return fail(YAH_ERR_UNSUPPORTED, "the tcgen05 decode GEMV does not cover type %d, N=%lld, K=%lld, M=%lld",
-                  a.type, (long long)a.N, (long long)a.K, (long long)a.M);
-    return kNotTaken;
-  }
+  int rc;
+  const yah::GemvTcPlan pl = gemv_tc_choice(a.type, a.N, a.K, a.M, a.num_sms, dev, &rc);
+  if (rc) return rc;
+  if (!pl.ok) return kNotTaken;
   return after_launch(yah::launch_qgemv_tc(a, pl, stream), "qgemv (tcgen05) launch");
+}
+
+yah::QGemvArgs gemv_args(const void* w, int t, int64_t N, int64_t K, int64_t w_row_stride, int64_t kb_off,
+                         const void* x, int64_t M, int64_t ldx, void* y, int y_dtype, int64_t ldy, int epilogue,
+                         const void* aux, int64_t ldaux, int* status, int sms) {
+  yah::QGemvArgs a;
+  a.w = w;
+  a.type = t;
+  a.N = N;
+  a.K = K;
+  a.w_row_stride = w_row_stride;
+  a.kb_off = kb_off;
+  a.x = x;
+  a.M = M;
+  a.ldx = ldx;
+  a.y = y;
+  a.y_f16 = y_dtype == YAH_F16;
+  a.ldy = ldy;
+  a.epilogue = epilogue;
+  a.aux = static_cast<const float*>(aux);
+  a.ldaux = ldaux;
+  a.status = status;
+  a.num_sms = sms;
+  return a;
+}
+
+// Caller workspace of the mma.sync GEMV: the split partial sums, then the split counters, each 256-byte aligned.
+size_t gemv_ws_floats_bytes(const yah::GemvPlan& p) {
+  return ((size_t)p.ws_floats * sizeof(float) + 255) & ~size_t(255);
+}
+size_t gemv_ws_bytes(const yah::GemvPlan& p) {
+  if (p.ws_floats <= 0) return 0;
+  return gemv_ws_floats_bytes(p) + (((size_t)p.counters * sizeof(int) + 255) & ~size_t(255));
 }
 }  // namespace
 
@@ -509,10 +550,29 @@ int yah_dequant(const void* w, int t, int64_t rows, int64_t K, int64_t w_row_str
                       "dequant launch");
 }
 
-int yah_qgemm_tile(const void* w, int t, int64_t N, int64_t K, int64_t w_row_stride, int64_t kb_off, const void* x,
-                   int64_t M, int64_t ldx, void* y, int y_dtype, int64_t ldy, int epilogue, const void* aux,
-                   int64_t ldaux, int bn, int grid, int64_t kchunk, int cta_pair, void* stream) {
-  int rc = check_linear(w, t, N, K, w_row_stride, kb_off, x, M, ldx, y, y_dtype, ldy, epilogue, aux, ldaux);
+}  // extern "C"
+
+namespace {
+
+// Workspace of a tile-GEMM call: the chunked-accumulation sums, then (split K) the chunk results, 256-byte aligned.
+struct GemmNeed {
+  size_t scratch = 0, kpart = 0;
+  size_t total() const { return scratch + kpart; }
+};
+
+size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+// Checks, tile choice and workspace needs of yah_qgemm_tile / yah_qgemm_ws. `sized` only: the pointers may be null
+// (a workspace-size query).
+int qgemm_prepare(const void* w, int t, int64_t N, int64_t K, int64_t w_row_stride, int64_t kb_off, const void* x,
+                  int64_t M, int64_t ldx, void* y, int y_dtype, int64_t ldy, int epilogue, const void* aux,
+                  int64_t ldaux, int bn, int grid, int64_t kchunk, int cta_pair, bool sized, yah::QGemmArgs& a,
+                  GemmNeed& need) {
+  // a size query checks the shape with stand-in pointers (aux distinct from y)
+  static const char kDummy[32] __attribute__((aligned(16))) = {};
+  int rc = sized ? check_linear(kDummy, t, N, K, w_row_stride, kb_off, kDummy, M, ldx, kDummy, y_dtype, ldy,
+                                epilogue, epilogue == YAH_EPI_STORE ? nullptr : kDummy + 16, ldaux)
+                 : check_linear(w, t, N, K, w_row_stride, kb_off, x, M, ldx, y, y_dtype, ldy, epilogue, aux, ldaux);
   if (rc) return rc;
   if (grid < 0) return fail(YAH_ERR_ARG, "negative grid");
   if (kchunk == 0) kchunk = K > 4096 ? 2048 : K;  // see the accuracy note in qgemm_tc.cu
@@ -521,7 +581,6 @@ int yah_qgemm_tile(const void* w, int t, int64_t N, int64_t K, int64_t w_row_str
   DevState* s;
   rc = dev_state(&s);
   if (rc) return rc;
-  yah::QGemmArgs a;
   a.w = w;
   a.type = t;
   a.N = N;
@@ -565,18 +624,73 @@ int yah_qgemm_tile(const void* w, int t, int64_t N, int64_t K, int64_t w_row_str
     if (a.pair && slots > a.max_pairs) slots = a.max_pairs;
     if (units < slots) a.nsplit = (int)((K + kchunk - 1) / kchunk);
   }
+  need = GemmNeed{};
   if (kchunk < K) {
+    need.scratch = align256((size_t)yah::qgemm_grid(a) * bn * 128 * sizeof(float));
+    if (a.nsplit > 1) need.kpart = align256((size_t)a.nsplit * (size_t)M * (size_t)N * sizeof(float));
+  }
+  return YAH_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int yah_qgemm_tile(const void* w, int t, int64_t N, int64_t K, int64_t w_row_stride, int64_t kb_off, const void* x,
+                   int64_t M, int64_t ldx, void* y, int y_dtype, int64_t ldy, int epilogue, const void* aux,
+                   int64_t ldaux, int bn, int grid, int64_t kchunk, int cta_pair, void* stream) {
+  yah::QGemmArgs a;
+  GemmNeed need;
+  int rc = qgemm_prepare(w, t, N, K, w_row_stride, kb_off, x, M, ldx, y, y_dtype, ldy, epilogue, aux, ldaux, bn, grid,
+                         kchunk, cta_pair, false, a, need);
+  if (rc) return rc;
+  if (need.scratch) {
+    DevState* s;
+    rc = dev_state(&s);
+    if (rc) return rc;
     std::lock_guard<std::mutex> lk(g_mu);
-    const size_t need = (size_t)yah::qgemm_grid(a) * bn * 128 * sizeof(float);
-    rc = grow(reinterpret_cast<void**>(&s->gemm_scratch), &s->gemm_scratch_bytes, need);
+    rc = grow(reinterpret_cast<void**>(&s->gemm_scratch), &s->gemm_scratch_bytes, need.scratch);
     if (rc) return rc;
     a.scratch = s->gemm_scratch;
-    if (a.nsplit > 1) {
-      rc = grow(reinterpret_cast<void**>(&s->gemm_kpart), &s->gemm_kpart_bytes,
-                (size_t)a.nsplit * (size_t)M * (size_t)N * sizeof(float));
+    if (need.kpart) {
+      rc = grow(reinterpret_cast<void**>(&s->gemm_kpart), &s->gemm_kpart_bytes, need.kpart);
       if (rc) return rc;
       a.kpart = s->gemm_kpart;
     }
+  }
+  return after_launch(yah::launch_qgemm_tc(a, (cudaStream_t)stream), "qgemm launch");
+}
+
+int yah_qgemm_workspace_size(int t, int64_t N, int64_t K, int64_t M, int y_dtype, int epilogue, int bn, int grid,
+                             int64_t kchunk, int cta_pair, size_t* bytes) {
+  if (!bytes) return fail(YAH_ERR_ARG, "null bytes");
+  yah::QGemmArgs a;
+  GemmNeed need;
+  const int64_t rs = yah_row_bytes(t, K);
+  int rc = qgemm_prepare(nullptr, t, N, K, rs > 0 ? (rs + 15) / 16 * 16 : 0, 0, nullptr, M, (K + 7) / 8 * 8, nullptr,
+                         y_dtype, N, epilogue, nullptr, N, bn, grid, kchunk, cta_pair, true, a, need);
+  if (rc) return rc;
+  *bytes = need.total();
+  return YAH_OK;
+}
+
+int yah_qgemm_ws(const void* w, int t, int64_t N, int64_t K, int64_t w_row_stride, int64_t kb_off, const void* x,
+                 int64_t M, int64_t ldx, void* y, int y_dtype, int64_t ldy, int epilogue, const void* aux,
+                 int64_t ldaux, int bn, int grid, int64_t kchunk, int cta_pair, void* workspace,
+                 size_t workspace_bytes, void* stream) {
+  yah::QGemmArgs a;
+  GemmNeed need;
+  int rc = qgemm_prepare(w, t, N, K, w_row_stride, kb_off, x, M, ldx, y, y_dtype, ldy, epilogue, aux, ldaux, bn, grid,
+                         kchunk, cta_pair, false, a, need);
+  if (rc) return rc;
+  if (need.total() > 0) {
+    if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & 255))
+      return fail(YAH_ERR_ARG, "this call needs a 256-byte aligned workspace of %zu bytes", need.total());
+    if (workspace_bytes < need.total())
+      return fail(YAH_ERR_SIZE, "workspace of %zu bytes; this call needs %zu (yah_qgemm_workspace_size)",
+                  workspace_bytes, need.total());
+    a.scratch = static_cast<float*>(workspace);
+    if (need.kpart) a.kpart = reinterpret_cast<float*>(static_cast<char*>(workspace) + need.scratch);
   }
   return after_launch(yah::launch_qgemm_tc(a, (cudaStream_t)stream), "qgemm launch");
 }
@@ -707,24 +821,8 @@ int yah_qgemv(const void* w, int t, int64_t N, int64_t K, int64_t w_row_stride, 
   DevState* s;
   rc = dev_state(&s);
   if (rc) return rc;
-  yah::QGemvArgs a;
-  a.w = w;
-  a.type = t;
-  a.N = N;
-  a.K = K;
-  a.w_row_stride = w_row_stride;
-  a.kb_off = kb_off;
-  a.x = x;
-  a.M = M;
-  a.ldx = ldx;
-  a.y = y;
-  a.y_f16 = y_dtype == YAH_F16;
-  a.ldy = ldy;
-  a.epilogue = epilogue;
-  a.aux = static_cast<const float*>(aux);
-  a.ldaux = ldaux;
-  a.status = s->status;
-  a.num_sms = sms_of(s);
+  const yah::QGemvArgs a = gemv_args(w, t, N, K, w_row_stride, kb_off, x, M, ldx, y, y_dtype, ldy, epilogue, aux,
+                                     ldaux, s->status, sms_of(s));
   {
     int dev = 0;
     CK(cudaGetDevice(&dev));
@@ -747,6 +845,55 @@ int yah_qgemv(const void* w, int t, int64_t N, int64_t K, int64_t w_row_stride, 
   return after_launch(yah::launch_qgemv_ws(a, plan, s->ws, s->counters, (cudaStream_t)stream), "qgemv launch");
 }
 
+int yah_qgemv_workspace_size(int t, int64_t N, int64_t K, int64_t M, size_t* bytes) {
+  if (!bytes) return fail(YAH_ERR_ARG, "null bytes");
+  if (!sb_bytes(t) || N < 1 || K < 256 || K % 256 || M < 1 || M > 32) return fail(YAH_ERR_ARG, "bad GEMV shape");
+  DevState* s;
+  int rc = dev_state(&s);
+  if (rc) return rc;
+  int dev = 0;
+  CK(cudaGetDevice(&dev));
+  const yah::GemvTcPlan pl = gemv_tc_choice(t, N, K, M, sms_of(s), dev, &rc);
+  if (rc) return rc;
+  *bytes = pl.ok ? 0 : gemv_ws_bytes(yah::qgemv_plan(t, N, K, M, sms_of(s)));
+  return YAH_OK;
+}
+
+int yah_qgemv_ws(const void* w, int t, int64_t N, int64_t K, int64_t w_row_stride, int64_t kb_off, const void* x,
+                 int64_t M, int64_t ldx, void* y, int y_dtype, int64_t ldy, int epilogue, const void* aux,
+                 int64_t ldaux, void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_linear(w, t, N, K, w_row_stride, kb_off, x, M, ldx, y, y_dtype, ldy, epilogue, aux, ldaux, true);
+  if (rc) return rc;
+  if (M > 32) return fail(YAH_ERR_ARG, "yah_qgemv_ws takes at most 32 tokens (M=%lld); use yah_qgemm", (long long)M);
+  DevState* s;
+  rc = dev_state(&s);
+  if (rc) return rc;
+  const yah::QGemvArgs a = gemv_args(w, t, N, K, w_row_stride, kb_off, x, M, ldx, y, y_dtype, ldy, epilogue, aux,
+                                     ldaux, s->status, sms_of(s));
+  {
+    int dev = 0;
+    CK(cudaGetDevice(&dev));
+    rc = launch_gemv_tc(a, dev, (cudaStream_t)stream);
+    if (rc != kNotTaken) return rc;
+  }
+  const yah::GemvPlan plan = yah::qgemv_plan(t, N, K, M, sms_of(s));
+  const size_t need = gemv_ws_bytes(plan);
+  float* part = nullptr;
+  int* counters = nullptr;
+  if (need > 0) {
+    if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & 255))
+      return fail(YAH_ERR_ARG, "this call needs a 256-byte aligned workspace of %zu bytes", need);
+    if (workspace_bytes < need)
+      return fail(YAH_ERR_SIZE, "workspace of %zu bytes; this call needs %zu (yah_qgemv_workspace_size)",
+                  workspace_bytes, need);
+    part = static_cast<float*>(workspace);
+    counters = reinterpret_cast<int*>(static_cast<char*>(workspace) + gemv_ws_floats_bytes(plan));
+    // the split counters start at zero on every call (the caller's buffer holds anything)
+    CK(cudaMemsetAsync(counters, 0, (size_t)plan.counters * sizeof(int), (cudaStream_t)stream));
+  }
+  return after_launch(yah::launch_qgemv_ws(a, plan, part, counters, (cudaStream_t)stream), "qgemv launch");
+}
+
 int yah_qgemv_noalloc(const void* w, int t, int64_t N, int64_t K, int64_t w_row_stride, int64_t kb_off,
                       const void* x, int64_t M, int64_t ldx, void* y, int y_dtype, int64_t ldy, int epilogue,
                       const void* aux, int64_t ldaux, void* stream) {
@@ -765,24 +912,8 @@ int yah_qgemv_noalloc(const void* w, int t, int64_t N, int64_t K, int64_t w_row_
     // the tcgen05 form needs no scratch: only the variant's own status word
     void* base = nullptr;
     CK(yah::qgemv_static_setup(dev, &base));
-    yah::QGemvArgs a;
-    a.w = w;
-    a.type = t;
-    a.N = N;
-    a.K = K;
-    a.w_row_stride = w_row_stride;
-    a.kb_off = kb_off;
-    a.x = x;
-    a.M = M;
-    a.ldx = ldx;
-    a.y = y;
-    a.y_f16 = y_dtype == YAH_F16;
-    a.ldy = ldy;
-    a.epilogue = epilogue;
-    a.aux = static_cast<const float*>(aux);
-    a.ldaux = ldaux;
-    a.status = yah::qgemv_static_status_word(base);
-    a.num_sms = sms;
+    const yah::QGemvArgs a = gemv_args(w, t, N, K, w_row_stride, kb_off, x, M, ldx, y, y_dtype, ldy, epilogue, aux,
+                                       ldaux, yah::qgemv_static_status_word(base), sms);
     rc = launch_gemv_tc(a, dev, (cudaStream_t)stream);
     if (rc != kNotTaken) return rc;
   }
@@ -794,24 +925,9 @@ int yah_qgemv_noalloc(const void* w, int t, int64_t N, int64_t K, int64_t w_row_
                 (long long)plan.ws_floats, (long long)M, (long long)N, plan.grid, yah::qgemv_static_partials());
   void* base = nullptr;
   CK(yah::qgemv_static_setup(dev, &base));
-  yah::QGemvArgs a;
-  a.w = w;
-  a.type = t;
-  a.N = N;
-  a.K = K;
-  a.w_row_stride = w_row_stride;
-  a.kb_off = kb_off;
-  a.x = x;
-  a.M = M;
-  a.ldx = ldx;
-  a.y = y;
-  a.y_f16 = y_dtype == YAH_F16;
-  a.ldy = ldy;
-  a.epilogue = epilogue;
-  a.aux = static_cast<const float*>(aux);
-  a.ldaux = ldaux;
-  a.status = nullptr;  // set by the launcher: the variant's own status word
-  a.num_sms = sms;
+  // status set by the launcher: the variant's own status word
+  const yah::QGemvArgs a = gemv_args(w, t, N, K, w_row_stride, kb_off, x, M, ldx, y, y_dtype, ldy, epilogue, aux,
+                                     ldaux, nullptr, sms);
   return after_launch(yah::launch_qgemv_static(a, plan, base, (cudaStream_t)stream), "qgemv_noalloc launch");
 }
 
@@ -823,17 +939,13 @@ int yah_qgemv_describe(int t, int64_t N, int64_t K, int64_t M, char* buf, int64_
   if (rc) return rc;
   int dev = 0;
   CK(cudaGetDevice(&dev));
-  const int impl = g_gemv_impl.load(std::memory_order_relaxed);
-  const bool auto_mma = impl == 0 && (M <= 8 || yah::qgemv_plan(t, N, K, M, sms_of(s)).mode != 1);
-  const yah::GemvTcPlan pl = (impl == 2 || auto_mma) ? yah::GemvTcPlan{}
-                                                     : yah::qgemv_tc_plan(t, N, K, M, sms_of(s), dev);
+  const yah::GemvTcPlan pl = gemv_tc_choice(t, N, K, M, sms_of(s), dev, &rc);
+  if (rc) return rc;
   if (pl.ok) {
     snprintf(buf, (size_t)cap,
              "tcgen05: clusters of %d CTAs (K parts of %d super-blocks), %d tiles of %d rows, grid %d, %d MMA "
              "columns, %d super-block(s) per weight stage",
              pl.ks, pl.srange, pl.tiles, pl.rt, pl.grid, pl.tp, pl.sw);
-  } else if (impl == 1) {
-    return fail(YAH_ERR_UNSUPPORTED, "the tcgen05 decode GEMV does not cover this call");
   } else {
     const yah::GemvPlan g = yah::qgemv_plan(t, N, K, M, sms_of(s));
     snprintf(buf, (size_t)cap, "mma.sync: mode %d (%s), grid %d, %lld partial floats, %lld counters", g.mode,
