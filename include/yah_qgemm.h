@@ -44,10 +44,16 @@ extern "C" {
 #define YAH_ERR_NCCL 6        /* a collective failed (tensor-parallel layer) */
 #define YAH_ERR_IO 7          /* a file could not be opened or mapped, or is not a well-formed GGUF file */
 
-/* GGML type ids (engine/core/gguf.hpp GgmlType). */
+/* GGML type ids (engine/core/gguf.hpp GgmlType). Q8_0, Q4_K and Q6_K are the benchmark configurations' formats;
+ * Q3_K, Q5_K and IQ4_XS (the reference's FMTS entries q3k / q5k / iq4xs, gen_gemm_decode.py:1707-1727) run on the
+ * same kernels. Weight rows must start 16-byte aligned: Q3_K rows when their super-block count is a multiple of 8,
+ * IQ4_XS rows when it is even (as Q6_K rows, a multiple of 8), Q5_K / Q4_K / Q8_0 rows always. */
 #define YAH_Q8_0 8
+#define YAH_Q3_K 11
 #define YAH_Q4_K 12
+#define YAH_Q5_K 13
 #define YAH_Q6_K 14
+#define YAH_IQ4_XS 23
 
 /* Element types of activations / outputs. */
 #define YAH_F32 0

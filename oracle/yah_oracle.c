@@ -10,8 +10,14 @@
  *   - engine/gpu/loom/tools/gen_gemm_decode.py:837-1069   Q4_K decode: w = f16(fma(d*sc, q, -dmin*m)), the 6-bit
  *                                                          sc/m unpack of :946-967 (Q4_SEL), Q4DFMA :54-56
  *   - engine/gpu/loom/tools/gen_gemm_decode.py:1243-1335  Q6_K decode: w = f16((d*sc) * (code - 32))
- *   - engine/core/gguf.cpp:27-35                           block sizes (Q8_0 32/34, Q4_K 256/144, Q6_K 256/210)
- * The arithmetic matches gguf-py 0.19.0 (gguf/quants.py Q8_0/Q4_K/Q6_K.dequantize_blocks) followed by
+ *   - engine/gpu/loom/tools/gen_gemm_decode.py:897-899, :1713-1716  Q5_K decode: Q4_K plus a fifth bit from the
+ *                                                          qh plane, qs at 48: w = f16((d*sc)*q - dmin*m)
+ *   - engine/gpu/loom/tools/gen_gemm_decode.py:1497-1546  Q3_K decode: q = (low | hbit << 2) - 4, the 6-bit signed
+ *                                                          scales, w = f16((d*(sc-32)) * q)
+ *   - engine/gpu/loom/tools/gen_gemm_decode.py:125-169    IQ4_XS decode: w = f16((d*(sc-32)) * kvalues[nibble])
+ *   - engine/core/gguf.cpp:27-35                           block sizes (Q8_0 32/34, Q3_K 256/110, Q4_K 256/144,
+ *                                                          Q5_K 256/176, Q6_K 256/210, IQ4_XS 256/136)
+ * The arithmetic matches gguf-py 0.19.0 (gguf/quants.py <format>.dequantize_blocks) followed by
  * astype(float16), which is the reference's own dequant oracle (engine/gpu/loom/tools/dq_bfp16_check.py:65).
  * Parity of this file with gguf-py is pinned by the committed vectors in tests/golden/.
  *
@@ -23,7 +29,7 @@
 #include <stdint.h>
 #include <string.h>
 
-enum { T_Q8_0 = 8, T_Q4_K = 12, T_Q6_K = 14 };
+enum { T_Q8_0 = 8, T_Q3_K = 11, T_Q4_K = 12, T_Q5_K = 13, T_Q6_K = 14, T_IQ4_XS = 23 };
 
 static float h2f(uint16_t h) {
   _Float16 v;
@@ -101,11 +107,76 @@ static void sb_q6_k(const uint8_t* b, float* out) {
   }
 }
 
+/* Q5_K: d f16 @0, dmin f16 @2, scales[12] @4 (the Q4_K unpack), qh[32] @16, qs[128] @48. Group g (32 values):
+ * q = nibble of qs[32*(g/2)+j] (low for even g) | ((qh[j] >> g) & 1) << 4. d*sc*q is exact, one rounding at the
+ * subtraction. */
+static void sb_q5_k(const uint8_t* b, float* out) {
+  float d = h2f((uint16_t)(b[0] | (b[1] << 8)));
+  float dmin = h2f((uint16_t)(b[2] | (b[3] << 8)));
+  const uint8_t* s = b + 4;
+  const uint8_t* qh = b + 16;
+  const uint8_t* qs = b + 48;
+  for (int g = 0; g < 8; ++g) {
+    int sc, m;
+    q4k_scale_min(s, g, &sc, &m);
+    float dsc = d * (float)sc;
+    float dm = dmin * (float)m;
+    for (int j = 0; j < 32; ++j) {
+      int byte = qs[32 * (g / 2) + j];
+      int q = ((g & 1) ? (byte >> 4) : (byte & 15)) | (((qh[j] >> g) & 1) << 4);
+      volatile float prod = dsc * (float)q;
+      out[32 * g + j] = prod - dm;
+    }
+  }
+}
+
+/* Q3_K: hmask[32] @0, qs[64] @32, scales[12] @96, d f16 @108. Element e = 128h + 32s + l (h < 2, s < 4, l < 32):
+ * low = (qs[32h + l] >> 2s) & 3, hbit = (hmask[l] >> (4h + s)) & 1, q = low - 4 * (1 - hbit). Sub-block i = e/16:
+ * sc = ((scales[i % 8] >> 4*(i / 8)) & 15 | ((scales[8 + i % 4] >> 2*(i / 4)) & 3) << 4) - 32. (d*sc)*q exact. */
+static void sb_q3_k(const uint8_t* b, float* out) {
+  const uint8_t* hm = b;
+  const uint8_t* qs = b + 32;
+  const uint8_t* sc = b + 96;
+  float d = h2f((uint16_t)(b[108] | (b[109] << 8)));
+  for (int e = 0; e < 256; ++e) {
+    int h = e / 128, s = (e % 128) / 32, l = e % 32, i = e / 16;
+    int low = (qs[32 * h + l] >> (2 * s)) & 3;
+    int hbit = (hm[l] >> (4 * h + s)) & 1;
+    int q = low - 4 * (1 - hbit);
+    int scale = (((sc[i % 8] >> (4 * (i / 8))) & 15) | (((sc[8 + i % 4] >> (2 * (i / 4))) & 3) << 4)) - 32;
+    volatile float dl = d * (float)scale;
+    out[e] = dl * (float)q;
+  }
+}
+
+/* IQ4_XS: d f16 @0, scales_h u16 @2, scales_l[4] @4, qs[128] @8. Group g (32 values): value w < 16 is the low nibble
+ * of qs[16g + w], w >= 16 the high nibble of qs[16g + w - 16]; sc = ((scales_l[g/2] >> 4*(g%2)) & 15 |
+ * ((scales_h >> 2g) & 3) << 4) - 32; w = (d*sc) * kvalues[nibble] (exact in f32). */
+static const int8_t kIq4Values[16] = {-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113};
+static void sb_iq4_xs(const uint8_t* b, float* out) {
+  float d = h2f((uint16_t)(b[0] | (b[1] << 8)));
+  int sh = b[2] | (b[3] << 8);
+  const uint8_t* sl = b + 4;
+  const uint8_t* qs = b + 8;
+  for (int g = 0; g < 8; ++g) {
+    int scale = (((sl[g / 2] >> (4 * (g % 2))) & 15) | (((sh >> (2 * g)) & 3) << 4)) - 32;
+    volatile float dl = d * (float)scale;
+    for (int w = 0; w < 32; ++w) {
+      int byte = qs[16 * g + (w & 15)];
+      int nib = w < 16 ? (byte & 15) : (byte >> 4);
+      out[32 * g + w] = dl * (float)kIq4Values[nib];
+    }
+  }
+}
+
 static int sb_bytes(int type) {
   switch (type) {
     case T_Q8_0: return 272;
+    case T_Q3_K: return 110;
     case T_Q4_K: return 144;
+    case T_Q5_K: return 176;
     case T_Q6_K: return 210;
+    case T_IQ4_XS: return 136;
     default: return 0;
   }
 }
@@ -113,8 +184,11 @@ static int sb_bytes(int type) {
 static void sb_decode(int type, const uint8_t* b, float* out) {
   switch (type) {
     case T_Q8_0: sb_q8_0(b, out); break;
+    case T_Q3_K: sb_q3_k(b, out); break;
     case T_Q4_K: sb_q4_k(b, out); break;
+    case T_Q5_K: sb_q5_k(b, out); break;
     case T_Q6_K: sb_q6_k(b, out); break;
+    case T_IQ4_XS: sb_iq4_xs(b, out); break;
   }
 }
 

@@ -8,7 +8,7 @@ It is run in the development container only (gguf-py and this script are never n
 
     python tests/golden/make_golden.py
 
-Per format (Q8_0, Q4_K, Q6_K) it writes tests/golden/dequant_<fmt>.npz with
+Per format (Q8_0, Q4_K, Q6_K, then Q5_K, Q3_K, IQ4_XS) it writes tests/golden/dequant_<fmt>.npz with
     blocks  uint8 [rows][row bytes]   the GGUF rows (seeded synthetic rows plus edge-case rows)
     K       int                       values per row
     f16     uint16 [rows][K]          gguf-py dequantize(...).astype(float16) bit patterns
@@ -31,7 +31,7 @@ import __graft_entry__ as ge  # noqa: E402
 
 F = ge.load_package().formats
 
-QT = {F.Q8_0: T.Q8_0, F.Q4_K: T.Q4_K, F.Q6_K: T.Q6_K}
+QT = {F.Q8_0: T.Q8_0, F.Q4_K: T.Q4_K, F.Q6_K: T.Q6_K, F.Q5_K: T.Q5_K, F.Q3_K: T.Q3_K, F.IQ4_XS: T.IQ4_XS}
 
 
 def f16b(v):
@@ -60,6 +60,35 @@ def edge_rows(fmt, K, rng):
             if kind == "ext":
                 b[:, 4:16] = 0xFF            # every sc / m = 63
                 b[:, 16:] = np.where(np.arange(128) % 2, 0xFF, 0x00).astype(np.uint8)
+        elif fmt == F.Q5_K:
+            b = r.reshape(-1, 176)
+            d, dm = {"neg": (-0.02, -0.007), "sub": (2.0e-6, 5.0e-7), "huge": (4000.0, 1.0), "ext": (0.03, 0.04)}[kind]
+            b[:, 0:2] = f16b(d)
+            b[:, 2:4] = f16b(dm)
+            if kind == "ext":
+                b[:, 4:16] = 0xFF            # every sc / m = 63
+                b[:, 16:48] = 0xFF           # every fifth bit set: quants 16..31
+                b[:, 48:] = np.where(np.arange(128) % 2, 0xFF, 0x00).astype(np.uint8)
+        elif fmt == F.Q3_K:
+            b = r.reshape(-1, 110)
+            d = {"neg": -0.015, "sub": 3.0e-6, "huge": 6000.0, "ext": 0.02}[kind]
+            b[:, 108:110] = f16b(d)
+            if kind == "ext":
+                b[:, 96:108] = np.array([0x00, 0xFF] * 6, np.uint8)  # scales -32 and +31
+                b[:, 0:32] = np.where(np.arange(32) % 2, 0xFF, 0x00).astype(np.uint8)
+                b[:, 32:96] = np.where(np.arange(64) % 3, 0xFF, 0x00).astype(np.uint8)
+            if kind == "sub":
+                b[:, 96:104] = 0x00          # low scale bits 0 and high bits from random bytes: some scales 0
+        elif fmt == F.IQ4_XS:
+            b = r.reshape(-1, 136)
+            d = {"neg": -0.015, "sub": 4.0e-6, "huge": 500.0, "ext": 0.02}[kind]
+            b[:, 0:2] = f16b(d)
+            if kind == "ext":
+                b[:, 2:8] = np.array([0x00, 0x00, 0xFF, 0x00, 0xF0, 0x0F], np.uint8)  # scales -32, +31 and 0 mixed
+                b[:, 8:] = np.where(np.arange(128) % 2, 0xFF, 0x00).astype(np.uint8)   # levels -127 and +113
+            if kind == "neg":
+                b[:, 2:4] = np.array([0xAA, 0xAA], np.uint8)  # high scale bits 2: with low bits 0, scale 0
+                b[:, 4:8] = 0x00
         else:
             b = r.reshape(-1, 210)
             d = {"neg": -0.015, "sub": 4.0e-6, "huge": 50.0, "ext": 0.02}[kind]
@@ -76,7 +105,7 @@ def edge_rows(fmt, K, rng):
 
 def main():
     rng = np.random.default_rng(20261201)
-    for fmt in (F.Q8_0, F.Q4_K, F.Q6_K):
+    for fmt in (F.Q8_0, F.Q4_K, F.Q6_K, F.Q5_K, F.Q3_K, F.IQ4_XS):
         name = F.NAMES[fmt].lower()
         K = 512
         syn = F.synth_weights(fmt, 8, K, seed=7 + fmt)

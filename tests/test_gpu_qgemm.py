@@ -13,7 +13,7 @@ import pytest
 from conftest import GOLDEN
 
 pytestmark = pytest.mark.gpu
-FMTS = ["q8_0", "q4_k", "q6_k"]
+FMTS = ["q8_0", "q4_k", "q6_k", "q5_k", "q3_k", "iq4_xs"]
 MAX_ABS, REL_FRO = 2e-2, 1e-3
 
 

@@ -9,7 +9,7 @@ import numpy as np
 import pytest
 
 pytestmark = pytest.mark.gpu
-FMTS = ["q8_0", "q4_k", "q6_k"]
+FMTS = ["q8_0", "q4_k", "q6_k", "q5_k", "q3_k", "iq4_xs"]
 
 
 def check(O, y, ref, rel_max=1e-4):
@@ -26,8 +26,8 @@ def test_qgemv(pkg, F, O, dev, name, M, N, K):
     """Shapes covering every work split: one item per CTA (128 x 256), row blocks shared by up to 8 CTAs
     (256 x 2048), CTA ranges ending inside row blocks (4096 x 4096, 2048 x 6144) and a ragged last row block."""
     t = F.type_of(name)
-    if t == F.Q6_K and K % 2048:
-        pytest.skip("Q6_K rows need a multiple of 8 super-blocks (16-byte row stride)")
+    if F.row_bytes(t, K) % 16:
+        pytest.skip("rows must be 16-byte multiples (Q6_K / Q3_K: 8 super-blocks, IQ4_XS: 2)")
     w = F.synth_weights(t, N, K, seed=N + K)
     x = F.synth_activations(M, K, seed=M)
     y = pkg.ops.qgemv(dev, w, t, x, N=N, K=K)

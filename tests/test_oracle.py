@@ -10,7 +10,7 @@ import pytest
 
 from conftest import GOLDEN
 
-FMTS = ["q8_0", "q4_k", "q6_k"]
+FMTS = ["q8_0", "q4_k", "q6_k", "q5_k", "q3_k", "iq4_xs"]
 
 
 @pytest.mark.parametrize("name", FMTS)

@@ -123,8 +123,11 @@ int sms_of(const DevState* s) {
 int sb_bytes(int type) {
   switch (type) {
     case YAH_Q8_0: return 272;
+    case YAH_Q3_K: return 110;
     case YAH_Q4_K: return 144;
+    case YAH_Q5_K: return 176;
     case YAH_Q6_K: return 210;
+    case YAH_IQ4_XS: return 136;
     default: return 0;
   }
 }
@@ -139,7 +142,7 @@ int check_linear(const void* w, int type, int64_t N, int64_t K, int64_t w_row_st
                  int64_t M, int64_t ldx, const void* y, int y_dtype, int64_t ldy, int epilogue, const void* aux,
                  int64_t ldaux, bool gemv = false) {
   const int sb = sb_bytes(type);
-  if (!sb) return fail(YAH_ERR_UNSUPPORTED, "unsupported GGML type %d (supported: Q8_0=8, Q4_K=12, Q6_K=14)", type);
+  if (!sb) return fail(YAH_ERR_UNSUPPORTED, "unsupported GGML type %d (supported: Q8_0=8, Q3_K=11, Q4_K=12, Q5_K=13, Q6_K=14, IQ4_XS=23)", type);
   if (!w || !x || !y) return fail(YAH_ERR_ARG, "null weight, input or output pointer");
   if (N < 1 || M < 1 || K < 256 || N > kMaxDim || M > kMaxDim || K > kMaxDim)
     return fail(YAH_ERR_ARG, "bad shape N=%lld K=%lld M=%lld", (long long)N, (long long)K, (long long)M);
@@ -150,8 +153,8 @@ int check_linear(const void* w, int type, int64_t N, int64_t K, int64_t w_row_st
                 (long long)((kb_off + K / 256) * sb));
   if (!aligned16(w) || w_row_stride % 16)
     return fail(YAH_ERR_UNSUPPORTED,
-                "weight rows must start 16-byte aligned (pointer %p, row stride %lld); Q6_K rows are aligned when "
-                "their super-block count is a multiple of 8",
+                "weight rows must start 16-byte aligned (pointer %p, row stride %lld); Q6_K and Q3_K rows are aligned "
+                "when their super-block count is a multiple of 8, IQ4_XS rows when it is even",
                 w, (long long)w_row_stride);
   if (!aligned16(x) || ldx < K || ldx % 8)
     return fail(YAH_ERR_ARG, "activations must be 16-byte aligned with ldx >= K and ldx %% 8 == 0 (ldx=%lld)",
@@ -260,9 +263,9 @@ const char* yah_version(void) { return "yah_b200 0.1 (sm_100a)"; }
 
 const char* yah_last_error(void) { return g_err.c_str(); }
 
-int yah_block_elements(int t) { return t == YAH_Q8_0 ? 32 : (t == YAH_Q4_K || t == YAH_Q6_K) ? 256 : 0; }
+int yah_block_elements(int t) { return t == YAH_Q8_0 ? 32 : sb_bytes(t) ? 256 : 0; }
 
-int yah_block_bytes(int t) { return t == YAH_Q8_0 ? 34 : t == YAH_Q4_K ? 144 : t == YAH_Q6_K ? 210 : 0; }
+int yah_block_bytes(int t) { return t == YAH_Q8_0 ? 34 : sb_bytes(t); }
 
 int64_t yah_row_bytes(int t, int64_t K) {
   const int be = yah_block_elements(t);

@@ -14,6 +14,9 @@
 //                      subtracting 2^23 leaves q*2^s exactly; the matching scale d*sc*2^-s is exact too.
 //   Q6_K (:1243-1335)  w = f16((d*sc) * (code - 32)) with d*sc and the product exact in f32 (int8 scales make
 //                      sc*(code - 32) too wide for exact f16 arithmetic, so this one stays in f32).
+//   Q5_K (:897-899, :1713-1716)  the Q4_K arithmetic with a 5-bit q (a fifth bit from the qh plane).
+//   Q3_K (:1497-1546)  w = f16((d*sc) * q), sc = 6-bit scale - 32, q = (2-bit low | hmask bit << 2) - 4; exact f32.
+//   IQ4_XS (:125-169)  w = f16((d*sc) * kvalues[nibble]), sc = 6-bit scale - 32; exact f32.
 // Pairs of f32 values go through the sm_100 packed-FP32 instructions (fma/add/mul .rn.f32x2): the same IEEE
 // operations, two per instruction.
 #pragma once
@@ -168,6 +171,110 @@ __device__ __forceinline__ void q6k_decode_kblock(const uint32_t (&QL)[16], cons
   }
 }
 
+// ------------------------------------------------------------------------------------------------ Q5_K
+// hdr: the Q4_K header (d, dmin, scales[12]); qs: qs bytes [32j, 32j + 32); qh: the 32 qh bytes. Group 2j takes the
+// low nibbles and qh bit 2j, group 2j + 1 the high nibbles and qh bit 2j + 1 (gguf-py Q5_K: q = ql | qh_bit << 4).
+__device__ __forceinline__ void q5k_decode_kblock(const uint4& hdr, const uint32_t (&qs)[8], const uint32_t (&qh)[8],
+                                                  int j, uint32_t (&out)[32]) {
+  float dsa, dma, dsb, dmb;
+  q4k_scales(hdr, j, dsa, dma, dsb, dmb);
+  // 5-bit q of bytes 0 / 1 (or 2 / 3) as magic floats q and 256 q, so the scales are (d*sc, d*sc / 256)
+  const float2 sa = make_float2(dsa, dsa * 0.00390625f), sb = make_float2(dsb, dsb * 0.00390625f);
+  const float2 na = make_float2(-dma, -dma), nb = make_float2(-dmb, -dmb);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint32_t hb = qh[i] >> (2 * j);
+    const uint32_t lo = (qs[i] & 0x0F0F0F0Fu) | ((hb << 4) & 0x10101010u);
+    const uint32_t hi = ((qs[i] >> 4) & 0x0F0F0F0Fu) | ((hb << 3) & 0x10101010u);
+    out[2 * i] = pack2(ffma2(sa, magic_pair(lo, 0x1Fu, 0x1F00u), na));
+    out[2 * i + 1] = pack2(ffma2(sa, magic_pair(lo >> 16, 0x1Fu, 0x1F00u), na));
+    out[16 + 2 * i] = pack2(ffma2(sb, magic_pair(hi, 0x1Fu, 0x1F00u), nb));
+    out[16 + 2 * i + 1] = pack2(ffma2(sb, magic_pair(hi >> 16, 0x1Fu, 0x1F00u), nb));
+  }
+}
+
+// A byte b of `code` (b = 0..3) as the f32 2^23 + code_b * 2^16.
+__device__ __forceinline__ float magic_hi_byte(uint32_t code, int b) {
+  return __uint_as_float(prmt(code, 0x4B000000u, 0x7044u | ((uint32_t)b << 8)));
+}
+
+// Four bytes c_b < 128 (+ a bias folded into `off`) times a scale, as two f16 pairs: values (c_b * 2^16 - off) * s,
+// with s = ds * 2^-16 (exact: the products are exact in f32, so one rounding to f16 as the reference). c_b must stay
+// below 128: bit 7 would land in the magic float's exponent.
+__device__ __forceinline__ void scaled_bytes(uint32_t code, float2 s, float off, uint32_t& p01, uint32_t& p23) {
+  const float2 o = make_float2(-off, -off);
+  const float2 c01 = fadd2(make_float2(magic_hi_byte(code, 0), magic_hi_byte(code, 1)), o);
+  const float2 c23 = fadd2(make_float2(magic_hi_byte(code, 2), magic_hi_byte(code, 3)), o);
+  p01 = pack2(fmul2(s, c01));
+  p23 = pack2(fmul2(s, c23));
+}
+
+// ------------------------------------------------------------------------------------------------ Q3_K
+// QS: qs bytes [32h, 32h + 32) (h = j / 2); HM: the 32 hmask bytes; LW: scale bytes [4(j % 2), 4(j % 2) + 4); HW:
+// scale bytes [8, 12); dbits: d. Values c = 32t + l (t = 0, 1; l < 32) of K block j: shift s = 2(j % 2) + t, hmask
+// bit 4h + s, sub-block 4j + 2t + l / 16.
+__device__ __forceinline__ void q3k_decode_kblock(const uint32_t (&QS)[8], const uint32_t (&HM)[8], uint32_t LW,
+                                                  uint32_t HW, uint32_t dbits, int j, uint32_t (&out)[32]) {
+  const float d = h2f_bits(dbits & 0xFFFFu);
+  const uint32_t sc = ((LW >> (4 * (j >> 1))) & 0x0F0F0F0Fu) | (((HW >> (2 * j)) & 0x03030303u) << 4);
+  float ds[4];
+#pragma unroll
+  for (int u = 0; u < 4; ++u) ds[u] = (d * (float)((int)((sc >> (8 * u)) & 0xFFu) - 32)) * 1.52587890625e-05f;
+  constexpr float kOff = 8650752.0f;  // 2^23 + 4 * 2^16: byte (q + 4) -> q * 2^16
+  const int h = j >> 1;
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    const int s = 2 * (j & 1) + t;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint32_t code = ((QS[i] >> (2 * s)) & 0x03030303u) | (((HM[i] >> (4 * h + s)) & 0x01010101u) << 2);
+      const float f = ds[2 * t + (i >> 2)];
+      scaled_bytes(code, make_float2(f, f), kOff, out[16 * t + 2 * i], out[16 * t + 2 * i + 1]);
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------------ IQ4_XS
+// Four nibbles (the low 4 bits of each byte of n) to the bytes kvalues[nibble] + 128 of the IQ4_NL level table
+// {-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113}: two 8-entry byte permutes, chosen per
+// byte by the nibble's bit 3.
+__device__ __forceinline__ uint32_t iq4_levels(uint32_t n) {
+  constexpr uint32_t kT0 = 0x3F2D1801u, kT1 = 0x766A5D4Fu, kT2 = 0xA6998D81u, kT3 = 0xF1D9C5B5u;
+  const uint32_t y = n | (n >> 4);                        // byte 0: n0 | n1 << 4, byte 2: n2 | n3 << 4
+  const uint32_t sel = prmt(y, 0u, 0x4420u) & 0x7777u;    // n0 | n1 << 4 | n2 << 8 | n3 << 12, each mod 8
+  const uint32_t lo = prmt(kT0, kT1, sel), hi = prmt(kT2, kT3, sel);
+  const uint32_t m = prmt(n << 4, 0u, 0xBA98u);           // 0xFF in the bytes whose nibble has bit 3 set
+  return (hi & m) | (lo & ~m);
+}
+
+// Four bytes (level + 128, up to 241: too wide for the 2^23 magic float's byte slot) times the group scale ds, as
+// two f16 pairs: each level is an exact f16 (1024 + byte - 1152), widened to f32, and ds * level is exact in f32.
+__device__ __forceinline__ void scaled_levels(uint32_t u, float2 ds, uint32_t& p01, uint32_t& p23) {
+  const uint32_t a = hsub2_u32(prmt(u, 0x64646464u, 0x4140u), 0x64806480u);  // bytes 0, 1
+  const uint32_t b = hsub2_u32(prmt(u, 0x64646464u, 0x4342u), 0x64806480u);  // bytes 2, 3
+  p01 = pack2(fmul2(ds, __half22float2(*reinterpret_cast<const __half2*>(&a))));
+  p23 = pack2(fmul2(ds, __half22float2(*reinterpret_cast<const __half2*>(&b))));
+}
+
+// H: bytes [0, 8) of the super-block (d, scales_h, scales_l[4]); QS: qs bytes [32j, 32j + 32) (groups 2j, 2j + 1).
+// Group g = 2j + t: values 0..15 the low nibbles of its 16 bytes, 16..31 the high nibbles.
+__device__ __forceinline__ void iq4xs_decode_kblock(uint2 H, const uint32_t (&QS)[8], int j, uint32_t (&out)[32]) {
+  const float d = h2f_bits(H.x & 0xFFFFu);
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    const int g = 2 * j + t;
+    const int sl = (int)((H.y >> (8 * j + 4 * t)) & 15u), sh = (int)((H.x >> (16 + 2 * g)) & 3u);
+    const float f = d * (float)((sl | (sh << 4)) - 32);
+    const float2 s2 = make_float2(f, f);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t w = QS[4 * t + i];
+      scaled_levels(iq4_levels(w & 0x0F0F0F0Fu), s2, out[16 * t + 2 * i], out[16 * t + 2 * i + 1]);
+      scaled_levels(iq4_levels((w >> 4) & 0x0F0F0F0Fu), s2, out[16 * t + 8 + 2 * i], out[16 * t + 9 + 2 * i]);
+    }
+  }
+}
+
 // ------------------------------------------------------------------------------------------------ shared-memory
 // Readers of one weight row of a staged super-block (the tile GEMM's TMA weight stage). `rb` is the shared address
 // of the row's first staged byte (16-byte aligned).
@@ -252,6 +359,75 @@ __device__ __forceinline__ void q6k_decode_smem(uint32_t rb, int j, int o, uint3
   }
 }
 
+__device__ __forceinline__ void q5k_decode_smem(uint32_t rb, int j, uint32_t (&out)[32]) {
+  const uint4 hdr = lds128(rb);
+  const uint4 h0 = lds128(rb + 16), h1 = lds128(rb + 32);
+  const uint4 a = lds128(rb + 48 + 32 * j), b = lds128(rb + 64 + 32 * j);
+  const uint32_t qh[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+  const uint32_t qs[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+  q5k_decode_kblock(hdr, qs, qh, j, out);
+}
+
+// Q3_K rows are staged as a 128-byte window from the 16-byte boundary at or below the super-block, which begins at
+// byte o = 4*OW + 2*odd2 of the window (o even, 0..14; o + 110 <= 124). Words at even byte offsets come from two
+// aligned words and one prmt (sel picks the half-word shift).
+template <int OW>
+__device__ __forceinline__ void q3k_decode_smem_o(uint32_t rb, int j, uint32_t sel, uint32_t (&out)[32]) {
+  const int h = j >> 1;
+  uint32_t L[12];
+#pragma unroll
+  for (int c = 0; c < 3; ++c) {
+    const uint4 v = lds128(rb + 32 + 32 * h + 16 * c);  // qs bytes 32h .. at window byte 32 + 32h + o
+    L[4 * c] = v.x;
+    L[4 * c + 1] = v.y;
+    L[4 * c + 2] = v.z;
+    L[4 * c + 3] = v.w;
+  }
+  uint32_t QS[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) QS[i] = prmt(L[OW + i], L[OW + i + 1], sel);
+#pragma unroll
+  for (int c = 0; c < 3; ++c) {
+    const uint4 v = lds128(rb + 16 * c);  // hmask bytes 0..31
+    L[4 * c] = v.x;
+    L[4 * c + 1] = v.y;
+    L[4 * c + 2] = v.z;
+    L[4 * c + 3] = v.w;
+  }
+  uint32_t HM[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) HM[i] = prmt(L[OW + i], L[OW + i + 1], sel);
+  const uint32_t lw = prmt(lds32(rb + 96 + 4 * (OW + (j & 1))), lds32(rb + 100 + 4 * (OW + (j & 1))), sel);
+  const uint32_t hw = prmt(lds32(rb + 104 + 4 * OW), lds32(rb + 108 + 4 * OW), sel);
+  const uint32_t D = prmt(lds32(rb + 108 + 4 * OW), lds32(rb + 112 + 4 * OW), sel);
+  q3k_decode_kblock(QS, HM, lw, hw, D, j, out);
+}
+
+__device__ __forceinline__ void q3k_decode_smem(uint32_t rb, int j, int o, uint32_t (&out)[32]) {
+  const uint32_t sel = (o & 2) ? 0x5432u : 0x3210u;
+  switch (o >> 2) {
+    case 0: q3k_decode_smem_o<0>(rb, j, sel, out); break;
+    case 1: q3k_decode_smem_o<1>(rb, j, sel, out); break;
+    case 2: q3k_decode_smem_o<2>(rb, j, sel, out); break;
+    default: q3k_decode_smem_o<3>(rb, j, sel, out); break;
+  }
+}
+
+// IQ4_XS rows are staged as a 144-byte window from the 16-byte boundary at or below the super-block, which begins
+// at byte o = 0 or 8 of the window (super-blocks are 8-byte aligned).
+__device__ __forceinline__ void iq4xs_decode_smem(uint32_t rb, int j, int o, uint32_t (&out)[32]) {
+  const uint32_t b = rb + o;
+  const uint2 H = lds64(b);
+  uint32_t QS[8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint2 v = lds64(b + 8 + 32 * j + 8 * i);
+    QS[2 * i] = v.x;
+    QS[2 * i + 1] = v.y;
+  }
+  iq4xs_decode_kblock(H, QS, j, out);
+}
+
 // ------------------------------------------------------------------------------------------------ global memory
 // A 32-bit little-endian word at a 2-byte aligned global address (read-only path).
 __device__ __forceinline__ uint32_t ldg_word2(const uint8_t* p) {
@@ -298,6 +474,41 @@ __device__ __forceinline__ void decode_global<14>(const uint8_t* sb, int j, uint
   q6k_decode_kblock(QL, QH, SC, D, jodd, out);
 }
 
-__host__ __device__ constexpr int superblock_bytes(int T) { return T == 8 ? 272 : (T == 12 ? 144 : 210); }
+template <>
+__device__ __forceinline__ void decode_global<13>(const uint8_t* sb, int j, uint32_t (&out)[32]) {
+  uint4 hdr;
+  hdr.x = ldg_word2(sb);
+  hdr.y = ldg_word2(sb + 4);
+  hdr.z = ldg_word2(sb + 8);
+  hdr.w = ldg_word2(sb + 12);
+  uint32_t qh[8], qs[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) qh[i] = ldg_word2(sb + 16 + 4 * i), qs[i] = ldg_word2(sb + 48 + 32 * j + 4 * i);
+  q5k_decode_kblock(hdr, qs, qh, j, out);
+}
+
+template <>
+__device__ __forceinline__ void decode_global<11>(const uint8_t* sb, int j, uint32_t (&out)[32]) {
+  const int h = j >> 1;
+  uint32_t QS[8], HM[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) QS[i] = ldg_word2(sb + 32 + 32 * h + 4 * i), HM[i] = ldg_word2(sb + 4 * i);
+  const uint32_t lw = ldg_word2(sb + 96 + 4 * (j & 1)), hw = ldg_word2(sb + 104);
+  const uint32_t D = __ldg(reinterpret_cast<const unsigned short*>(sb + 108));
+  q3k_decode_kblock(QS, HM, lw, hw, D, j, out);
+}
+
+template <>
+__device__ __forceinline__ void decode_global<23>(const uint8_t* sb, int j, uint32_t (&out)[32]) {
+  const uint2 H = make_uint2(ldg_word2(sb), ldg_word2(sb + 4));
+  uint32_t QS[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) QS[i] = ldg_word2(sb + 8 + 32 * j + 4 * i);
+  iq4xs_decode_kblock(H, QS, j, out);
+}
+
+__host__ __device__ constexpr int superblock_bytes(int T) {
+  return T == 8 ? 272 : T == 11 ? 110 : T == 12 ? 144 : T == 13 ? 176 : T == 14 ? 210 : T == 23 ? 136 : 0;
+}
 
 }  // namespace yah

@@ -47,6 +47,9 @@ cudaError_t launch_dequant(const void* w, int type, int64_t rows, int64_t K, int
     case 8: dequant_kernel<8><<<(int)blocks, 256, 0, stream>>>(wb, rows, nsb, row_stride, kb_off, out, ldo); break;
     case 12: dequant_kernel<12><<<(int)blocks, 256, 0, stream>>>(wb, rows, nsb, row_stride, kb_off, out, ldo); break;
     case 14: dequant_kernel<14><<<(int)blocks, 256, 0, stream>>>(wb, rows, nsb, row_stride, kb_off, out, ldo); break;
+    case 11: dequant_kernel<11><<<(int)blocks, 256, 0, stream>>>(wb, rows, nsb, row_stride, kb_off, out, ldo); break;
+    case 13: dequant_kernel<13><<<(int)blocks, 256, 0, stream>>>(wb, rows, nsb, row_stride, kb_off, out, ldo); break;
+    case 23: dequant_kernel<23><<<(int)blocks, 256, 0, stream>>>(wb, rows, nsb, row_stride, kb_off, out, ldo); break;
     default: return cudaErrorInvalidValue;
   }
   return cudaGetLastError();

@@ -1,4 +1,4 @@
-// Quantised tile GEMM for sm_100a: GGUF Q8_0 / Q4_K / Q6_K weights x f16 activations, f32 accumulation in TMEM.
+// Quantised tile GEMM for sm_100a: GGUF Q8_0 / Q3_K / Q4_K / Q5_K / Q6_K / IQ4_XS weights x f16 activations, f32 accumulation in TMEM.
 //
 // Reference: engine/gpu/loom/tools/gen_gemm_tile.py (the tile GEMM, kinds kstore / kres / swiglu :309-322, store
 // :1229-1245) with the decoders of engine/gpu/loom/tools/gen_gemm_decode.py. Like the reference, the weight tile
@@ -70,6 +70,20 @@ template <>
 struct Fmt<14> {  // Q6_K: a 224-B window from the 16-B boundary at or below the super-block
   static constexpr int kSB = 210, kBox = 224, kNSW = 2;
 };
+template <>
+struct Fmt<13> {  // Q5_K (176-B super-blocks stay 16-B aligned)
+  static constexpr int kSB = 176, kBox = 176, kNSW = 2;
+};
+template <>
+struct Fmt<11> {  // Q3_K: a 128-B window from the 16-B boundary at or below the super-block
+  static constexpr int kSB = 110, kBox = 128, kNSW = 3;
+};
+template <>
+struct Fmt<23> {  // IQ4_XS: a 144-B window (super-blocks are 8-B aligned)
+  static constexpr int kSB = 136, kBox = 144, kNSW = 3;
+};
+// Formats whose super-blocks do not all start 16-byte aligned: TMA copies a window from the boundary below.
+__host__ __device__ constexpr bool windowed(int T) { return T == 14 || T == 11 || T == 23; }
 
 // TMEM (512 columns) holds NACC accumulator regions of BN columns, then NA A stages of 128 K (64 columns).
 // NACC = 2 overlaps an epilogue with the next accumulation and is needed for chunked accumulation; NACC = 1
@@ -290,7 +304,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive_expect_tx(&wfull[ws], kBM * WBOX);
           const int64_t sbg = (int64_t)p.kb_off + sb;
           int xw;
-          if (T == 14) xw = (int)(((sbg * 210) & ~int64_t(15)) >> 1);
+          if (windowed(T)) xw = (int)(((sbg * Fmt<T>::kSB) & ~int64_t(15)) >> 1);
           else xw = (int)(sbg * (Fmt<T>::kSB / 2));
           if constexpr (EPI == kEpiFfn) {  // gate rows to stage rows 0-63, the same up rows to 64-127
             tma_load_2d(smem + S::kWOff + ws * S::kWStage, &tmap_w, &wfull[ws], xw, row0);
@@ -388,12 +402,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int j = kb & 3;
         const uint32_t rb = wbase + ws * S::kWStage + r * WBOX;
         uint32_t v[32];
+        const int o = windowed(T) ? (int)((((int64_t)p.kb_off + (kb >> 2)) * Fmt<T>::kSB) & 15) : 0;
         if (T == 12) {
           q4k_decode_smem(rb, j, v);
         } else if (T == 8) {
           q80_decode_smem(rb, j, v);
+        } else if (T == 13) {
+          q5k_decode_smem(rb, j, v);
+        } else if (T == 11) {
+          q3k_decode_smem(rb, j, o, v);
+        } else if (T == 23) {
+          iq4xs_decode_smem(rb, j, o, v);
         } else {
-          const int o = (int)((((int64_t)p.kb_off + (kb >> 2)) * 210) & 15);
           q6k_decode_smem(rb, j, o, v);
         }
         __syncwarp();  // the warp's only read of this weight slot is done
@@ -837,6 +857,9 @@ cudaError_t launch_qgemm_tc(const QGemmArgs& a, cudaStream_t stream) {
       case 8: return launch_split<8>(a, stream);
       case 12: return launch_split<12>(a, stream);
       case 14: return launch_split<14>(a, stream);
+      case 11: return launch_split<11>(a, stream);
+      case 13: return launch_split<13>(a, stream);
+      case 23: return launch_split<23>(a, stream);
       default: return cudaErrorInvalidValue;
     }
   }
@@ -844,6 +867,9 @@ cudaError_t launch_qgemm_tc(const QGemmArgs& a, cudaStream_t stream) {
     case 8: return launch_fmt<8>(a, stream);
     case 12: return launch_fmt<12>(a, stream);
     case 14: return launch_fmt<14>(a, stream);
+    case 11: return launch_fmt<11>(a, stream);
+    case 13: return launch_fmt<13>(a, stream);
+    case 23: return launch_fmt<23>(a, stream);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -1,4 +1,7 @@
 // Decode GEMV for M <= 32 tokens: y[t][n] (+)= sum_k W[n][k] x[t][k], GGUF weights, f16 activations.
+// Formats: Q8_0, Q4_K, Q6_K, and on the same kernel Q5_K (the Q4_K form with a fifth bit per quant from the qh
+// plane), Q3_K (the Q6_K form: exact small integers per 16-value sub-block) and IQ4_XS (levels of its non-linear
+// table as exact f16 integers, one scale per 32 values); reference GEMV lane setups gen_gemv.py:137-230.
 //
 // Reference: engine/gpu/loom/tools/gen_gemv.py (kinds plain / resid, :96-754). Like the reference GEMV, this
 // kernel never rounds a dequantised weight: it computes with the f32 weight values of the reference dequant
@@ -44,15 +47,22 @@ constexpr int kGvSmemBudget = 225 * 1024;
 
 // Bytes per super-block and the most super-blocks one TMA copy of a row holds (box width <= 256 elements:
 // u64 elements for Q4_K / Q8_0, u16 for Q6_K, whose super-blocks are not 8-byte aligned).
-__host__ __device__ constexpr int gv_sb_bytes(int t) { return t == 8 ? 272 : t == 12 ? 144 : 210; }
-__host__ __device__ constexpr int gv_pmax(int t) { return t == 8 ? 4 : t == 12 ? 8 : 2; }
+__host__ __device__ constexpr int gv_sb_bytes(int t) { return superblock_bytes(t); }
+// Q4_K and Q5_K share the nibble-pair algebra: permuted activations and per-group activation sums.
+__host__ __device__ constexpr bool gv_q4like(int t) { return t == 12 || t == 13; }
+// Formats whose super-blocks are not all 16-byte aligned (Q6_K 210, Q3_K 110, IQ4_XS 136 bytes) are copied as u16
+// windows from the 16-byte boundary at or below them; the others as whole u64 super-blocks.
+__host__ __device__ constexpr bool gv_windowed(int t) { return t == 14 || t == 11 || t == 23; }
+// Super-blocks per weight copy: a power of two (a stage of sst super-blocks, itself a power of two, is ops whole
+// copies), and at most 256 box elements (u64 for whole super-blocks, u16 for windows of up to P * bytes + 14).
+__host__ __device__ constexpr int gv_pmax(int t) { return t == 8 ? 4 : gv_q4like(t) ? 8 : t == 11 ? 4 : 2; }
 // Shared-memory row width of one W copy of P super-blocks (Q6_K: a 16-byte aligned window around them), padded to
 // an odd number of 16-byte units. TMA lays the copied rows out at this pitch; row g starts in 16-byte bank slot
 // (g * units) mod 8, so gcd(units, 8) of the 8 rows a warp's lane groups read (g = 0..7) share a slot: none for an odd
 // count, all 8 for 1152 bytes = 72 units (measured: half of all shared-load wavefronts were conflicts). The extra bytes
 // are the start of the next super-block, or zero fill past the end of the row.
 __host__ __device__ constexpr int gv_opw_raw(int t, int P) {
-  return t == 14 ? ((P * 210 + 14 + 15) / 16) * 16 : ((P * gv_sb_bytes(t) + 15) / 16) * 16;
+  return gv_windowed(t) ? ((P * gv_sb_bytes(t) + 14 + 15) / 16) * 16 : ((P * gv_sb_bytes(t) + 15) / 16) * 16;
 }
 __host__ __device__ constexpr int gv_opw(int t, int P) {
   return (gv_opw_raw(t, P) / 16) % 2 ? gv_opw_raw(t, P) : gv_opw_raw(t, P) + 16;
@@ -60,7 +70,7 @@ __host__ __device__ constexpr int gv_opw(int t, int P) {
 
 template <int T, int CW>
 struct GvRoles {
-  static constexpr int kThreads = (CW + (T == 12 ? 2 : 1)) * 32;  // compute warps + TMA warp (+ Q4_K helper)
+  static constexpr int kThreads = (CW + (gv_q4like(T) ? 2 : 1)) * 32;  // compute warps + TMA warp (+ Q4_K helper)
 };
 
 struct GvParams {
@@ -95,12 +105,6 @@ __device__ __forceinline__ uint32_t lds_word(uint32_t addr) {  // 4 bytes at an 
 
 __device__ __forceinline__ uint32_t lds_u16(uint32_t addr) {
   return (lds32(addr & ~3u) >> (8 * (addr & 3))) & 0xFFFFu;
-}
-
-__device__ __forceinline__ uint2 lds64(uint32_t addr) {
-  uint2 v;
-  asm volatile("ld.shared.v2.b32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
-  return v;
 }
 
 // A pure register operation: plain asm, so the compiler may schedule it among the shared-memory loads.
@@ -168,11 +172,15 @@ struct XRes {
 // The loads of a super-block are issued before its arithmetic (all of them for one token tile).
 template <int T, int NTW, class XA>
 __device__ __forceinline__ void gv_superblock(uint32_t w0, uint32_t w1, const XA& xa, float (&y)[NTW][4], int c) {
-  if (T == 12) {
+  if (gv_q4like(T)) {
+    // Q5_K: the same header, qs at 48 and the qh plane at 16 (bit g of qh byte p: the fifth bit of position p of
+    // group g); this lane's positions 8c .. 8c + 7 of every 32-value group read qh bytes 8c .. 8c + 7
+    constexpr int kQs = T == 13 ? 48 : 16;
     const uint4 h0 = lds128(w0), h1 = lds128(w1);
-    uint2 q0[4], q1[4];
+    uint2 q0[4], q1[4], qh0 = make_uint2(0u, 0u), qh1 = make_uint2(0u, 0u);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) q0[j] = lds64(w0 + 16 + 32 * j + 8 * c), q1[j] = lds64(w1 + 16 + 32 * j + 8 * c);
+    for (int j = 0; j < 4; ++j) q0[j] = lds64(w0 + kQs + 32 * j + 8 * c), q1[j] = lds64(w1 + kQs + 32 * j + 8 * c);
+    if (T == 13) qh0 = lds64(w0 + 16 + 8 * c), qh1 = lds64(w1 + 16 + 8 * c);
     constexpr int PJ = NTW == 1 ? 4 : 1;  // 64-K chunks of activations loaded ahead
     uint4 xl[PJ][NTW], xh[PJ][NTW];
     uint32_t bh[NTW], bl[NTW];
@@ -214,6 +222,15 @@ __device__ __forceinline__ void gv_superblock(uint32_t w0, uint32_t w1, const XA
         lo[wi][3] = v1 & 0x000F000Fu;
         hi[wi][0] = u0 & 0x00F000F0u, hi[wi][1] = u1 & 0x00F000F0u, hi[wi][2] = v0 & 0x00F000F0u,
         hi[wi][3] = v1 & 0x00F000F0u;
+        if (T == 13) {
+          // fifth bits: group 2j (low nibbles, q * 2^-24 -> bit 4 of the half) and 2j + 1 (high, bit 8);
+          // bytes 0 / 2 of the word in halves 0 / 1 of lo[.][0..1], bytes 1 / 3 in lo[.][2..3]
+          const uint32_t e0 = (wi ? qh0.y : qh0.x) >> (2 * j), e1 = (wi ? qh1.y : qh1.x) >> (2 * j);
+          lo[wi][0] |= (e0 << 4) & 0x00100010u, lo[wi][1] |= (e1 << 4) & 0x00100010u;
+          lo[wi][2] |= (e0 >> 4) & 0x00100010u, lo[wi][3] |= (e1 >> 4) & 0x00100010u;
+          hi[wi][0] |= (e0 << 7) & 0x01000100u, hi[wi][1] |= (e1 << 7) & 0x01000100u;
+          hi[wi][2] |= (e0 >> 1) & 0x01000100u, hi[wi][3] |= (e1 >> 1) & 0x01000100u;
+        }
       }
 #pragma unroll
       for (int n = 0; n < NTW; ++n) {
@@ -280,6 +297,85 @@ __device__ __forceinline__ void gv_superblock(uint32_t w0, uint32_t w1, const XA
           y[n][1] = __fmaf_rn(f0, t4[1], y[n][1]);
           y[n][2] = __fmaf_rn(f1, t4[2], y[n][2]);
           y[n][3] = __fmaf_rn(f1, t4[3], y[n][3]);
+        }
+      }
+    }
+  } else if (T == 11) {
+    // Q3_K: hmask[32] @0, qs[64] @32, scales[12] @96, d @108 (a window: w0 / w1 at even offsets). Sub-block 4j + u
+    // (16 values) of 64-K chunk j: 2-bit quants at shift s = 2(j % 2) + u / 2 of qs bytes 32h + 16(u % 2) + p
+    // (h = j / 2), hmask bit 4h + s; q = (low | hbit << 2) - 4 as an exact f16, then y += d * (sc - 32) * acc.
+    const float dd0 = h2f_bits(lds_u16(w0 + 108)), dd1 = h2f_bits(lds_u16(w1 + 108));
+    const uint32_t hw0 = lds_word(w0 + 104), hw1 = lds_word(w1 + 104);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int h = j >> 1;
+      const uint32_t lw0 = lds_word(w0 + 96 + 4 * (j & 1)), lw1 = lds_word(w1 + 96 + 4 * (j & 1));
+      const uint32_t sc0 = ((lw0 >> (4 * h)) & 0x0F0F0F0Fu) | (((hw0 >> (2 * j)) & 0x03030303u) << 4);
+      const uint32_t sc1 = ((lw1 >> (4 * h)) & 0x0F0F0F0Fu) | (((hw1 >> (2 * j)) & 0x03030303u) << 4);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int s = 2 * (j & 1) + (u >> 1), lo16 = 16 * (u & 1) + 4 * c;
+        const uint32_t c0w = ((lds_word(w0 + 32 + 32 * h + lo16) >> (2 * s)) & 0x03030303u) |
+                             (((lds_word(w0 + lo16) >> (4 * h + s)) & 0x01010101u) << 2);
+        const uint32_t c1w = ((lds_word(w1 + 32 + 32 * h + lo16) >> (2 * s)) & 0x03030303u) |
+                             (((lds_word(w1 + lo16) >> (4 * h + s)) & 0x01010101u) << 2);
+        constexpr uint32_t kB = 0x64046404u;  // f16 (1028, 1028) = 1024 + 4
+        const uint32_t a0 = hsub2_u32(prmt(c0w, 0x64646464u, 0x4140u), kB);
+        const uint32_t a2 = hsub2_u32(prmt(c0w, 0x64646464u, 0x4342u), kB);
+        const uint32_t a1 = hsub2_u32(prmt(c1w, 0x64646464u, 0x4140u), kB);
+        const uint32_t a3 = hsub2_u32(prmt(c1w, 0x64646464u, 0x4342u), kB);
+        const float f0 = dd0 * (float)((int)((sc0 >> (8 * u)) & 0xFFu) - 32);
+        const float f1 = dd1 * (float)((int)((sc1 >> (8 * u)) & 0xFFu) - 32);
+#pragma unroll
+        for (int n = 0; n < NTW; ++n) {
+          const uint2 b = lds64(xa.x(n, j, 32 * u));
+          float t4[4] = {0.f, 0.f, 0.f, 0.f};
+          mma16816(t4, a0, a1, a2, a3, b.x, b.y);
+          y[n][0] = __fmaf_rn(f0, t4[0], y[n][0]);
+          y[n][1] = __fmaf_rn(f0, t4[1], y[n][1]);
+          y[n][2] = __fmaf_rn(f1, t4[2], y[n][2]);
+          y[n][3] = __fmaf_rn(f1, t4[3], y[n][3]);
+        }
+      }
+    }
+  } else if (T == 23) {
+    // IQ4_XS: d @0, scales_h u16 @2, scales_l[4] @4, qs[128] @8 (a window: w0 / w1 8-byte aligned). Group g (32
+    // values) = sub-blocks of 16: the low nibbles of qs bytes 16g + p, then the high nibbles; each nibble becomes its
+    // level (an exact f16 integer), then y += d * (sc - 32) * acc per group.
+    const uint2 H0 = lds64(w0), H1 = lds64(w1);
+    const float dd0 = h2f_bits(H0.x & 0xFFFFu), dd1 = h2f_bits(H1.x & 0xFFFFu);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        const int g = 2 * j + t;
+        const float f0 = dd0 * (float)((int)(((H0.y >> (4 * g)) & 15u) | (((H0.x >> (16 + 2 * g)) & 3u) << 4)) - 32);
+        const float f1 = dd1 * (float)((int)(((H1.y >> (4 * g)) & 15u) | (((H1.x >> (16 + 2 * g)) & 3u) << 4)) - 32);
+        const uint32_t q0 = lds32(w0 + 8 + 16 * g + 4 * c), q1 = lds32(w1 + 8 + 16 * g + 4 * c);
+        float t4[NTW][4];
+#pragma unroll
+        for (int n = 0; n < NTW; ++n) t4[n][0] = t4[n][1] = t4[n][2] = t4[n][3] = 0.f;
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          const uint32_t l0 = iq4_levels((q0 >> (4 * hf)) & 0x0F0F0F0Fu);
+          const uint32_t l1 = iq4_levels((q1 >> (4 * hf)) & 0x0F0F0F0Fu);
+          constexpr uint32_t kB = 0x64806480u;  // f16 (1152, 1152) = 1024 + 128
+          const uint32_t a0 = hsub2_u32(prmt(l0, 0x64646464u, 0x4140u), kB);
+          const uint32_t a2 = hsub2_u32(prmt(l0, 0x64646464u, 0x4342u), kB);
+          const uint32_t a1 = hsub2_u32(prmt(l1, 0x64646464u, 0x4140u), kB);
+          const uint32_t a3 = hsub2_u32(prmt(l1, 0x64646464u, 0x4342u), kB);
+#pragma unroll
+          for (int n = 0; n < NTW; ++n) {
+            const uint2 b = lds64(xa.x(n, j, 32 * (2 * t + hf)));
+            mma16816(t4[n], a0, a1, a2, a3, b.x, b.y);
+          }
+        }
+#pragma unroll
+        for (int n = 0; n < NTW; ++n) {
+          y[n][0] = __fmaf_rn(f0, t4[n][0], y[n][0]);
+          y[n][1] = __fmaf_rn(f0, t4[n][1], y[n][1]);
+          y[n][2] = __fmaf_rn(f1, t4[n][2], y[n][2]);
+          y[n][3] = __fmaf_rn(f1, t4[n][3], y[n][3]);
         }
       }
     }
@@ -616,7 +712,7 @@ __device__ __forceinline__ void gv_prep_resident(const GvParams& p, uint32_t res
     const int L = L0 + u * nthreads, t = L / kp_total, kp = L - t * kp_total;
     if (L >= total) break;  // uniform across a warp: total and nthreads are multiples of 32
     uint4 v = vv[u];
-    if (T == 12) {
+    if (gv_q4like(T)) {
       const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&v.x));
       const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&v.y));
       const float2 e = __half22float2(*reinterpret_cast<const __half2*>(&v.z));
@@ -660,7 +756,7 @@ __global__ void __launch_bounds__(GvRoles<T, CW>::kThreads, (CW == 8 && NTW == 1
   if (threadIdx.x == 0) {
     for (int i = 0; i < p.turns * p.ringst; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], CW / p.turns + (T == 12 && !p.xres ? 1 : 0));
+      mbar_init(&empty[i], CW / p.turns + (gv_q4like(T) && !p.xres ? 1 : 0));
       mbar_init(&sready[i], 32);
     }
     mbar_init(rfull, CW * 32);
@@ -703,7 +799,8 @@ __global__ void __launch_bounds__(GvRoles<T, CW>::kThreads, (CW == 8 && NTW == 1
       mbar_arrive_expect_tx(&full[st], bytes);
       for (int op = 0; op < p.ops; ++op) {
         const int64_t sbg = (int64_t)p.kb_off + sb0 + op * p.P;
-        const int xw = T == 14 ? (int)(((sbg * 210) & ~int64_t(15)) >> 1) : (int)(sbg * (gv_sb_bytes(T) / 8));
+        const int xw = gv_windowed(T) ? (int)(((sbg * gv_sb_bytes(T)) & ~int64_t(15)) >> 1)
+                                      : (int)(sbg * (gv_sb_bytes(T) / 8));
         tma_load_2d(base + op * p.wreg, &tmap_w, &full[st], xw, (int)row0);
       }
       if (!p.xres) {
@@ -768,7 +865,7 @@ __global__ void __launch_bounds__(GvRoles<T, CW>::kThreads, (CW == 8 && NTW == 1
   }
   // This lane's activation rows (token rows past M read token M - 1; those D columns are never stored) and its
   // offsets in the resident layout.
-  const int lane_b = (T == 12 ? 16 : 8) * c;
+  const int lane_b = (gv_q4like(T) ? 16 : 8) * c;
   int tokl[NTW];
   uint32_t xlane[NTW], slane[NTW];
 #pragma unroll
@@ -788,14 +885,15 @@ __global__ void __launch_bounds__(GvRoles<T, CW>::kThreads, (CW == 8 && NTW == 1
       const int st = turn * p.ringst + lslot, ph = lph;
       if (++lslot == p.ringst) lslot = 0, lph ^= 1;
       if (!mbar_wait(&full[st], ph, p.status, kStatusTimeoutFull) ||
-          (T == 12 && !p.xres && !mbar_wait(&sready[st], ph, p.status, kStatusTimeoutFull))) {
+          (gv_q4like(T) && !p.xres && !mbar_wait(&sready[st], ph, p.status, kStatusTimeoutFull))) {
         ok = false;
         break;
       }
       if (has_rows && sb0 + pos < sg.sb_end) {
         const uint32_t base = smem_u32(smem + st * p.stage_bytes);
         uint32_t off = (uint32_t)(within * gv_sb_bytes(T));
-        if (T == 14) off = (uint32_t)((((int64_t)p.kb_off + sb0 + op * p.P) * 210) & 15) + within * 210;
+        if (gv_windowed(T))
+          off = (uint32_t)((((int64_t)p.kb_off + sb0 + op * p.P) * gv_sb_bytes(T)) & 15) + within * gv_sb_bytes(T);
         const uint32_t w0 = base + op * p.wreg + (rgi * 16 + g) * p.opw + off;
         if (p.xres) {
           XRes<NTW> xa;
@@ -1114,12 +1212,12 @@ cudaError_t gv_launch(const QGemvArgs& a, const GemvPlan& pl, float* ws, int* co
   {
     // weights: u64 elements for Q4_K / Q8_0 (whole super-blocks), u16 for Q6_K (a 16-byte aligned window)
     const int64_t window_bytes = (a.kb_off + a.K / 256) * gv_sb_bytes(T);
-    const int es = T == 14 ? 2 : 8;
+    const int es = gv_windowed(T) ? 2 : 8;
     cuuint64_t dims[2] = {(cuuint64_t)((window_bytes + es - 1) / es), (cuuint64_t)a.N};
     cuuint64_t strides[1] = {(cuuint64_t)a.w_row_stride};
     cuuint32_t box[2] = {(cuuint32_t)(pl.opw / es), (cuuint32_t)pl.rb};
     cuuint32_t ones[2] = {1, 1};
-    if (enc(&mw, T == 14 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void*>(a.w),
+    if (enc(&mw, gv_windowed(T) ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void*>(a.w),
             dims, strides, box, ones, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return cudaErrorInvalidValue;
@@ -1329,7 +1427,7 @@ GemvPlan qgemv_plan_limit(int type, int64_t N, int64_t K, int64_t M, int num_sms
   // Resident activations (and Q4_K group sums) up to 128 KB, which leaves >= 2 weight stages of 32 KB beside them
   // (measured on B200, Q4_K 4096 x 14336: M = 2 21.2 -> 15.2 us, M = 4 23.3 -> 17.5 us against the 32 KB limit;
   // 14336 x 4096 M = 8 22.7 -> 16.2 us).
-  const int64_t res_need = M * (K * 2 + 64) + (type == 12 ? M * ((K / 256) * 32 + 16) : 0);
+  const int64_t res_need = M * (K * 2 + 64) + (gv_q4like(type) ? M * ((K / 256) * 32 + 16) : 0);
   const bool ranges = units >= 4 * (int64_t)num_sms && res_need <= res_limit;
   pl.mode = ranges ? 0 : 1;
   if (ranges) {
@@ -1357,7 +1455,8 @@ GemvPlan qgemv_plan_limit(int type, int64_t N, int64_t K, int64_t M, int num_sms
   const bool two_per_sm = !ranges && pl.ntw == 1;
   // resident layout: M token rows of 2K + 64 bytes, M rows of group sums of 32 bytes per super-block + 16
   const int res_bytes = pl.xres ? (int)((M * (K * 2 + 64) + 1023) / 1024 * 1024) : 0;
-  const int ressum_bytes = pl.xres && type == 12 ? (int)((M * ((K / 256) * 32 + 16) + 1023) / 1024 * 1024) : 0;
+  const int ressum_bytes =
+      pl.xres && gv_q4like(type) ? (int)((M * ((K / 256) * 32 + 16) + 1023) / 1024 * 1024) : 0;
   const int budget = (two_per_sm ? 104 * 1024 : kGvSmemBudget) - red_bytes - bar_bytes - res_bytes - ressum_bytes;
   // Stage size: a TMA engine completes about one copy per ~0.27 us per SM whatever its size up to ~16 KB, so the
   // weight copies of resident-activation launches are 16-32 KB (8 KB copies cap the stream near 4 TB/s); launches
@@ -1373,7 +1472,7 @@ GemvPlan qgemv_plan_limit(int type, int64_t N, int64_t K, int64_t M, int num_sms
     pl.wreg = ((pl.rgp * 16 * pl.opw) + 127) / 128 * 128;
     pl.xoff = (pl.ops * pl.wreg + 1023) / 1024 * 1024;
     pl.sumoff = pl.xoff + (pl.xres ? 0 : 4 * pl.sst * (int)M * 128);
-    const int sum_bytes = type == 12 && !pl.xres ? pl.sst * 32 * (int)M : 0;
+    const int sum_bytes = gv_q4like(type) && !pl.xres ? pl.sst * 32 * (int)M : 0;
     pl.stage_bytes = (pl.sumoff + sum_bytes + 1023) / 1024 * 1024;
     const int turns = pl.slots / pl.sst;
     int fit = budget / pl.stage_bytes;
@@ -1409,6 +1508,9 @@ cudaError_t launch_qgemv_ws(const QGemvArgs& a, const GemvPlan& plan, float* ws,
     case 8: return gv_fmt<8>(a, plan, ws, counters, stream);
     case 12: return gv_fmt<12>(a, plan, ws, counters, stream);
     case 14: return gv_fmt<14>(a, plan, ws, counters, stream);
+    case 11: return gv_fmt<11>(a, plan, ws, counters, stream);
+    case 13: return gv_fmt<13>(a, plan, ws, counters, stream);
+    case 23: return gv_fmt<23>(a, plan, ws, counters, stream);
     default: return cudaErrorInvalidValue;
   }
 }
