@@ -15,7 +15,7 @@ def test_rule_struct_and_validation(pkg):
     assert L.yah_tile_rules_count(ctypes.byref(n)) == 0 and n.value == 2
     for bad in [T(12, 0, 1, 4096, 4096, 2048, 192, 0, 1),   # 192 is a single-CTA width
                 T(12, 0, 1, 4096, 4096, 2048, 256, 0, 0),   # 256 is a pair width
-                T(11, 0, 1, 4096, 4096, 2048, 192, 0, 0),   # unsupported format
+                T(10, 0, 1, 4096, 4096, 2048, 192, 0, 0),   # unsupported format (Q2_K)
                 T(12, 3, 1, 4096, 4096, 2048, 192, 0, 0),   # epilogue
                 T(12, 0, 1, 4096, 4096, 0, 192, 0, 0)]:     # token bound
         assert L.yah_tile_rules_set(ctypes.byref(bad), 1) == pkg._lib.ERR_ARG
