@@ -246,6 +246,22 @@ int yah_qgemv(const void* w, int ggml_type, int64_t N, int64_t K, int64_t w_row_
               const void* x, int64_t M, int64_t ldx, void* y, int y_dtype, int64_t ldy, int epilogue,
               const void* aux, int64_t ldaux, void* stream);
 
+/* yah_qgemv with the activations' element type chosen (x_dtype YAH_F16 or YAH_F32). The reference GEMV binds
+ * x f32[K] and y f32 (gen_gemv.py:4, :729; LoomDecoder::Gemv, engine/model/loom_decoder.hpp:432-434): with
+ * YAH_F32 this is that binding, with no conversion step. Each f32 value is split in the kernel's activation load
+ * into hi = f16(x) and lo = f16(x - hi) (22 significant bits; values need |x| < 65504), both multiplied with the
+ * f32 weight values and the two products added, so results stay within the reference checker's bar
+ * (max |y - ref| / max |ref| <= 1e-4, gemv_check.py:176-183). f32 activations always run the mma.sync kernel in
+ * its row-range form with the activations resident in shared memory (no workspace); tokens beyond what fits run
+ * as further launches (Q4_K at K = 14336: 2 tokens per launch). ldx counts elements of x_dtype. */
+int yah_qgemv_x(const void* w, int ggml_type, int64_t N, int64_t K, int64_t w_row_stride, int64_t kb_off,
+                const void* x, int x_dtype, int64_t M, int64_t ldx, void* y, int y_dtype, int64_t ldy, int epilogue,
+                const void* aux, int64_t ldaux, void* stream);
+/* yah_qgemv_swiglu with the activations' element type chosen, as yah_qgemv_x. */
+int yah_qgemv_swiglu_x(const void* w_gate, int gate_type, int64_t gate_row_stride, const void* w_up, int up_type,
+                       int64_t up_row_stride, int64_t N, int64_t K, const void* x, int x_dtype, int64_t M,
+                       int64_t ldx, float* y, int64_t ldy, void* stream);
+
 /* yah_qgemv on a caller-owned workspace (see yah_qgemm_ws): yah_qgemv_workspace_size gives the bytes for (type, N,
  * K, M) under the current kernel choice (yah_set_gemv_impl), 0 where the chosen form needs none (the tcgen05
  * kernel and the row-range forms of the mma.sync kernel). yah_qgemv_ws clears the workspace's split counters on

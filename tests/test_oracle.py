@@ -76,3 +76,16 @@ def test_plant_mistake_is_caught(F, O):
     got = O.dequant_f16(F.Q4_K, z["blocks"], z["blocks"].shape[0], int(z["K"])).view(np.uint16).copy()
     got[3, 17] ^= 1
     assert np.count_nonzero(got != z["f16"]) == 1
+
+
+def test_rounding_x_to_f16_misses_the_gemv_bar(F, O):
+    """The reference GEMV takes f32 activations (gen_gemv.py:4). The same GEMV with x rounded to f16 first is off by
+    more than the reference checker's max |y - ref| / max |ref| <= 1e-4 (gemv_check.py:176-183): the f32 operand has
+    to be kept (the GPU path splits it into two f16 parts)."""
+    t = F.Q4_K
+    N, K = 512, 14336
+    w = F.synth_weights(t, N, K, seed=31)
+    x = np.random.default_rng(32).standard_normal((1, K), dtype=np.float32)
+    wf = O.dequant_f32(t, w, N, K)
+    e = O.errors(O.gemm_ref(wf, x.astype(np.float16)), O.gemm_ref(wf, x))
+    assert e["rel_max"] > 1e-4, e

@@ -74,6 +74,10 @@ SYMBOLS = {
     "yah_qgemv_noalloc": (c_int, [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_int, c_i64,
                                   c_int, c_vp, c_i64, c_vp]),
     "yah_qgemv_noalloc_status": (c_int, [P(c_int)]),
+    "yah_qgemv_x": (c_int, [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_vp, c_int, c_i64, c_i64, c_vp, c_int, c_i64,
+                            c_int, c_vp, c_i64, c_vp]),
+    "yah_qgemv_swiglu_x": (c_int, [c_vp, c_int, c_i64, c_vp, c_int, c_i64, c_i64, c_i64, c_vp, c_int, c_i64, c_i64,
+                                   c_vp, c_i64, c_vp]),
     "yah_qgemv_workspace_size": (c_int, [c_int, c_i64, c_i64, c_i64, P(c_sz)]),
     "yah_qgemv_ws": (c_int, [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_int, c_i64, c_int,
                              c_vp, c_i64, c_vp, c_sz, c_vp]),

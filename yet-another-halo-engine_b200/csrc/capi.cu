@@ -848,6 +848,51 @@ int yah_qgemv(const void* w, int t, int64_t N, int64_t K, int64_t w_row_stride, 
   return after_launch(yah::launch_qgemv_ws(a, plan, s->ws, s->counters, (cudaStream_t)stream), "qgemv launch");
 }
 
+int yah_qgemv_x(const void* w, int t, int64_t N, int64_t K, int64_t w_row_stride, int64_t kb_off, const void* x,
+                int x_dtype, int64_t M, int64_t ldx, void* y, int y_dtype, int64_t ldy, int epilogue, const void* aux,
+                int64_t ldaux, void* stream) {
+  if (x_dtype == YAH_F16)
+    return yah_qgemv(w, t, N, K, w_row_stride, kb_off, x, M, ldx, y, y_dtype, ldy, epilogue, aux, ldaux, stream);
+  if (x_dtype != YAH_F32) return fail(YAH_ERR_UNSUPPORTED, "x_dtype %d (YAH_F16 or YAH_F32)", x_dtype);
+  int rc = check_linear(w, t, N, K, w_row_stride, kb_off, x, M, ldx, y, y_dtype, ldy, epilogue, aux, ldaux, true);
+  if (rc) return rc;
+  if (M > 32) return fail(YAH_ERR_ARG, "yah_qgemv_x takes at most 32 tokens (M=%lld)", (long long)M);
+  if (g_gemv_impl.load(std::memory_order_relaxed) == 1)
+    return fail(YAH_ERR_UNSUPPORTED, "the tcgen05 decode GEMV takes f16 activations only");
+  DevState* s;
+  rc = dev_state(&s);
+  if (rc) return rc;
+  const int sms = sms_of(s);
+  // tokens per launch: as many as stay resident (hi and lo rows) beside two weight stages
+  int64_t mc = M;
+  while (mc > 0 && yah::qgemv_plan_xf32(t, N, K, mc, sms).ringst < 2) --mc;
+  if (mc == 0)
+    return fail(YAH_ERR_UNSUPPORTED, "f32 activations of K=%lld do not fit in shared memory", (long long)K);
+  const int ysz = y_dtype == YAH_F16 ? 2 : 4;
+  for (int64_t m0 = 0; m0 < M; m0 += mc) {
+    const int64_t m = M - m0 < mc ? M - m0 : mc;
+    yah::QGemvArgs a = gemv_args(w, t, N, K, w_row_stride, kb_off, static_cast<const float*>(x) + m0 * ldx, m, ldx,
+                                 static_cast<char*>(y) + m0 * ldy * ysz, y_dtype, ldy, epilogue,
+                                 aux ? static_cast<const float*>(aux) + m0 * ldaux : nullptr, ldaux, s->status, sms);
+    a.x_f32 = 1;
+    const yah::GemvPlan plan = yah::qgemv_plan_xf32(t, N, K, m, sms);
+    rc = after_launch(yah::launch_qgemv_ws(a, plan, nullptr, nullptr, (cudaStream_t)stream), "qgemv (f32 x) launch");
+    if (rc) return rc;
+  }
+  return YAH_OK;
+}
+
+int yah_qgemv_swiglu_x(const void* w_gate, int gate_type, int64_t gate_row_stride, const void* w_up, int up_type,
+                       int64_t up_row_stride, int64_t N, int64_t K, const void* x, int x_dtype, int64_t M,
+                       int64_t ldx, float* y, int64_t ldy, void* stream) {
+  if (!y) return fail(YAH_ERR_ARG, "null output");
+  int rc = yah_qgemv_x(w_gate, gate_type, N, K, gate_row_stride, 0, x, x_dtype, M, ldx, y, YAH_F32, ldy,
+                       YAH_EPI_STORE, nullptr, 0, stream);
+  if (rc) return rc;
+  return yah_qgemv_x(w_up, up_type, N, K, up_row_stride, 0, x, x_dtype, M, ldx, y, YAH_F32, ldy, YAH_EPI_SWIGLU, y,
+                     ldy, stream);
+}
+
 int yah_qgemv_workspace_size(int t, int64_t N, int64_t K, int64_t M, size_t* bytes) {
   if (!bytes) return fail(YAH_ERR_ARG, "null bytes");
   if (!sb_bytes(t) || N < 1 || K < 256 || K % 256 || M < 1 || M > 32) return fail(YAH_ERR_ARG, "bad GEMV shape");

@@ -59,8 +59,9 @@ struct QGemvArgs {
   const void* w;
   int type;
   int64_t N, K, w_row_stride, kb_off;
-  const void* x;   // f16 [M][ldx]
+  const void* x;   // f16 [M][ldx], or f32 [M][ldx] when x_f32
   int64_t M, ldx;
+  int x_f32 = 0;   // GEMV only: f32 activations (row-range form with resident activations; see qgemv_plan_xf32)
   void* y;         // [M][ldy], f32 or f16
   int y_f16;
   int64_t ldy;
@@ -85,6 +86,9 @@ struct GemvPlan {
   int64_t ws_floats, counters;
 };
 GemvPlan qgemv_plan(int type, int64_t N, int64_t K, int64_t M, int num_sms);
+// Plan of an f32-activation GEMV of M tokens (2M hi / lo token rows, resident, row ranges); ringst < 2: too many
+// tokens to keep resident (the caller splits the tokens).
+GemvPlan qgemv_plan_xf32(int type, int64_t N, int64_t K, int64_t M, int num_sms);
 cudaError_t launch_qgemv_ws(const QGemvArgs& a, const GemvPlan& plan, float* ws, int* counters,
                             cudaStream_t stream);
 

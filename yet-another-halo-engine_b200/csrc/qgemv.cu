@@ -83,6 +83,8 @@ struct GvParams {
   int xstride, sstride;      // resident layout: bytes per token of activations / of group sums
   int sbstride;              // resident layout: bytes per super-block of activations (512, or padded)
   const __half* x;
+  const float* xf;           // f32 activations (xf32: M counts the hi / lo token rows, two per f32 token)
+  int xf32;
   int64_t ldx;
   int K;
   int64_t units;             // row ranges: ceil(N / 4)
@@ -684,20 +686,97 @@ __device__ __forceinline__ bool gv_flush_rows(const GvParams& p, float (&y)[NTW]
     for (int e = 0; e < 4; ++e) {
       const int t = tok0 + 8 * n + 2 * c + (e & 1);
       const int64_t row = row0 + rgi * 16 + g + 8 * (e >> 1);
-      if (t < p.M && row < row_end) gv_store(p, t, (int)row, y[n][e]);
+      if (p.xf32) {  // token rows t (hi) and t + 1 (lo) of one f32 token, both in this thread
+        if ((e & 1) == 0 && t < p.M && row < row_end) gv_store(p, t >> 1, (int)row, y[n][e] + y[n][e + 1]);
+      } else if (t < p.M && row < row_end) {
+        gv_store(p, t, (int)row, y[n][e]);
+      }
     }
   if (p.slots > 1) mbar_arrive(rdone);
   return true;
 }
 
+// One 16-byte piece (8 f16 activations, piece kp of token row t) into the resident layout; for Q4_K / Q5_K also the
+// group sum (hi, lo f16) and the (x0, x2, x1, x3) permutation of every 4. All 32 lanes of the warp take part (the
+// group sum is finished by two shuffles over the 4 pieces of a group).
+template <int T>
+__device__ __forceinline__ void gv_store_piece(const GvParams& p, uint32_t res, uint32_t ressum, int t, int kp,
+                                               uint4 v) {
+  if (gv_q4like(T)) {
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&v.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&v.y));
+    const float2 e = __half22float2(*reinterpret_cast<const __half2*>(&v.z));
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&v.w));
+    float sum = ((a.x + a.y) + (b.x + b.y)) + ((e.x + e.y) + (f.x + f.y));
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    if ((kp & 3) == 0) {  // group kp / 4 = super-block kp / 32, group (kp / 4) % 8: hi at + 0, lo at + 16
+      const uint32_t ss = ressum + t * p.sstride + (kp >> 5) * 32 + ((kp >> 2) & 7) * 2;
+      const __half hv = __float2half_rn(sum);
+      const __half lv = __float2half_rn(sum - __half2float(hv));
+      asm volatile("st.shared.b16 [%0], %1;" ::"r"(ss), "h"(__half_as_ushort(hv)) : "memory");
+      asm volatile("st.shared.b16 [%0], %1;" ::"r"(ss + 16), "h"(__half_as_ushort(lv)) : "memory");
+    }
+    v = make_uint4(prmt(v.x, v.y, 0x5410u), prmt(v.x, v.y, 0x7632u), prmt(v.z, v.w, 0x5410u),
+                   prmt(v.z, v.w, 0x7632u));
+  }
+  const uint32_t a = res + t * p.xstride + (kp >> 5) * p.sbstride + (kp & 31) * 16;
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
+// f32 activations (the reference GEMV's x f32 operand): each value splits exactly enough into hi = f16(x) and
+// lo = f16(x - hi) (22 significant bits; |x| < 65504), token t becoming the kernel's token rows 2t (hi) and 2t + 1
+// (lo); the two rows' products are added in the flush.
+__device__ __forceinline__ void gv_split_f32(const float4& a, const float4& b, uint4& hi, uint4& lo) {
+  const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+  uint32_t h[4], l[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __half2 hh = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+    const float2 hf = __half22float2(hh);
+    const __half2 ll = __floats2half2_rn(v[2 * i] - hf.x, v[2 * i + 1] - hf.y);
+    h[i] = *reinterpret_cast<const uint32_t*>(&hh);
+    l[i] = *reinterpret_cast<const uint32_t*>(&ll);
+  }
+  hi = make_uint4(h[0], h[1], h[2], h[3]);
+  lo = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
 // Resident activations (row ranges with small M * K): the compute warps copy all of x into shared memory once,
 // token t at t * xstride (Q4_K already permuted), with the Q4_K group sums at ressum + t * sstride
 // ([super-block][hi 8, lo 8] f16). A thread takes one 16-byte piece (8 values); four consecutive pieces
-// are one group, added in f32 by two shuffles.
+// are one group, added in f32 by two shuffles. f32 activations: a thread takes 8 values (32 bytes) of one token
+// and writes the hi and lo pieces of both of its token rows.
 template <int T>
 __device__ __forceinline__ void gv_prep_resident(const GvParams& p, uint32_t res, uint32_t ressum, int tid,
                                                  int nthreads) {
   const int kp_total = p.K / 8;  // pieces per token, a multiple of 32
+  if (p.xf32) {
+    const int total = (p.M / 2) * kp_total;
+    for (int L0 = tid; L0 < total; L0 += 2 * nthreads) {
+      float4 va[2], vb[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int L = L0 + u * nthreads, t = L / kp_total, kp = L - t * kp_total;
+        if (L < total) {
+          const float4* src = reinterpret_cast<const float4*>(p.xf + (int64_t)t * p.ldx + (int64_t)kp * 8);
+          va[u] = __ldg(src);
+          vb[u] = __ldg(src + 1);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int L = L0 + u * nthreads, t = L / kp_total, kp = L - t * kp_total;
+        if (L >= total) break;  // uniform across a warp: total and nthreads are multiples of 32
+        uint4 hi, lo;
+        gv_split_f32(va[u], vb[u], hi, lo);
+        gv_store_piece<T>(p, res, ressum, 2 * t, kp, hi);
+        gv_store_piece<T>(p, res, ressum, 2 * t + 1, kp, lo);
+      }
+    }
+    return;
+  }
   const int total = p.M * kp_total;
   // four loads in flight per thread before any is used: the prep costs one L2 round trip, not one per piece
   for (int L0 = tid; L0 < total; L0 += 4 * nthreads) {
@@ -709,30 +788,9 @@ __device__ __forceinline__ void gv_prep_resident(const GvParams& p, uint32_t res
     }
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
-    const int L = L0 + u * nthreads, t = L / kp_total, kp = L - t * kp_total;
-    if (L >= total) break;  // uniform across a warp: total and nthreads are multiples of 32
-    uint4 v = vv[u];
-    if (gv_q4like(T)) {
-      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&v.x));
-      const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&v.y));
-      const float2 e = __half22float2(*reinterpret_cast<const __half2*>(&v.z));
-      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&v.w));
-      float sum = ((a.x + a.y) + (b.x + b.y)) + ((e.x + e.y) + (f.x + f.y));
-      sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-      sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-      if ((kp & 3) == 0) {  // group kp / 4 = super-block kp / 32, group (kp / 4) % 8: hi at + 0, lo at + 16
-        const uint32_t ss = ressum + t * p.sstride + (kp >> 5) * 32 + ((kp >> 2) & 7) * 2;
-        const __half hv = __float2half_rn(sum);
-        const __half lv = __float2half_rn(sum - __half2float(hv));
-        asm volatile("st.shared.b16 [%0], %1;" ::"r"(ss), "h"(__half_as_ushort(hv)) : "memory");
-        asm volatile("st.shared.b16 [%0], %1;" ::"r"(ss + 16), "h"(__half_as_ushort(lv)) : "memory");
-      }
-      v = make_uint4(prmt(v.x, v.y, 0x5410u), prmt(v.x, v.y, 0x7632u), prmt(v.z, v.w, 0x5410u),
-                     prmt(v.z, v.w, 0x7632u));
-    }
-    const uint32_t a = res + t * p.xstride + (kp >> 5) * p.sbstride + (kp & 31) * 16;
-    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
-                 : "memory");
+      const int L = L0 + u * nthreads, t = L / kp_total, kp = L - t * kp_total;
+      if (L >= total) break;  // uniform across a warp: total and nthreads are multiples of 32
+      gv_store_piece<T>(p, res, ressum, t, kp, vv[u]);
     }
   }
 }
@@ -1260,6 +1318,9 @@ cudaError_t gv_launch(const QGemvArgs& a, const GemvPlan& pl, float* ws, int* co
   p.resoff = pl.resoff;
   p.ressum = pl.ressum;
   p.x = static_cast<const __half*>(a.x);
+  p.xf = static_cast<const float*>(a.x);
+  p.xf32 = a.x_f32;
+  if (a.x_f32) p.M = 2 * (int)a.M;
   p.ldx = a.ldx;
   p.K = (int)a.K;
   p.units = (a.N + 3) / 4;
@@ -1406,7 +1467,14 @@ std::atomic<int> g_launch_overlap{1};
 bool launch_overlap() { return g_launch_overlap.load(std::memory_order_relaxed) != 0; }
 void set_launch_overlap(bool on) { g_launch_overlap.store(on ? 1 : 0, std::memory_order_relaxed); }
 
-GemvPlan qgemv_plan_limit(int type, int64_t N, int64_t K, int64_t M, int num_sms, int64_t res_limit);
+GemvPlan qgemv_plan_limit(int type, int64_t N, int64_t K, int64_t M, int num_sms, int64_t res_limit,
+                          bool force_ranges = false);
+
+GemvPlan qgemv_plan_xf32(int type, int64_t N, int64_t K, int64_t M, int num_sms) {
+  // Row ranges with resident activations for the 2M hi / lo token rows, however few the rows (small N takes fewer
+  // CTAs); ringst < 2 means the rows do not fit beside two weight stages.
+  return qgemv_plan_limit(type, N, K, 2 * M, num_sms, int64_t(1) << 40, true);
+}
 
 GemvPlan qgemv_plan(int type, int64_t N, int64_t K, int64_t M, int num_sms) {
   GemvPlan pl{};
@@ -1417,7 +1485,8 @@ GemvPlan qgemv_plan(int type, int64_t N, int64_t K, int64_t M, int num_sms) {
   return pl;
 }
 
-GemvPlan qgemv_plan_limit(int type, int64_t N, int64_t K, int64_t M, int num_sms, int64_t res_limit) {
+GemvPlan qgemv_plan_limit(int type, int64_t N, int64_t K, int64_t M, int num_sms, int64_t res_limit,
+                          bool force_ranges) {
   GemvPlan pl{};
   const int nt = pow2_ceil((int)((M + 7) / 8));  // token tiles of 8: 1, 2 or 4
   const int64_t units = (N + 3) / 4, nsb = K / 256;
@@ -1428,10 +1497,10 @@ GemvPlan qgemv_plan_limit(int type, int64_t N, int64_t K, int64_t M, int num_sms
   // (measured on B200, Q4_K 4096 x 14336: M = 2 21.2 -> 15.2 us, M = 4 23.3 -> 17.5 us against the 32 KB limit;
   // 14336 x 4096 M = 8 22.7 -> 16.2 us).
   const int64_t res_need = M * (K * 2 + 64) + (gv_q4like(type) ? M * ((K / 256) * 32 + 16) : 0);
-  const bool ranges = units >= 4 * (int64_t)num_sms && res_need <= res_limit;
+  const bool ranges = force_ranges || (units >= 4 * (int64_t)num_sms && res_need <= res_limit);
   pl.mode = ranges ? 0 : 1;
   if (ranges) {
-    pl.grid = num_sms;
+    pl.grid = units < num_sms ? (int)units : num_sms;
     const int64_t per_cta = (units + pl.grid - 1) / pl.grid;
     pl.rb = (int)(4 * per_cta < 128 ? 4 * per_cta : 128);
     pl.rgp = pow2_ceil((pl.rb + 15) / 16);

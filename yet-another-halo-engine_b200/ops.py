@@ -70,6 +70,13 @@ def qgemv_ptr(w, fmt, N, K, w_row_stride, kb_off, x, M, ldx, y, y_dtype, ldy, ki
                           aux, ldaux, stream))
 
 
+def qgemv_x_ptr(w, fmt, N, K, w_row_stride, kb_off, x, M, ldx, y, y_dtype, ldy, kind="plain", aux=None, ldaux=0,
+                stream=None, x_dtype="f32"):
+    """yah_qgemv_x: the GEMV with the activations' element type chosen (ldx in elements of x_dtype)."""
+    check(lib().yah_qgemv_x(w, F.type_of(fmt), N, K, w_row_stride, kb_off, x, _dt(x_dtype), M, ldx, y, _dt(y_dtype),
+                            ldy, _epi(kind), aux, ldaux, stream))
+
+
 def dequant_ptr(w, fmt, rows, K, w_row_stride, kb_off, out, ldo, stream=None):
     check(lib().yah_dequant(w, F.type_of(fmt), rows, K, w_row_stride, kb_off, out, ldo, stream))
 
@@ -87,10 +94,14 @@ def _check_size(buf: DeviceBuffer, need: int, what: str):
 
 
 def qgemm(dev: Device, w, fmt, x, N=None, K=None, kind="kstore", out_dtype="f32", aux=None, kb_off=0,
-          w_row_stride=None, bn=0, grid=0, kchunk=0, pair=-1, gemv=False):
-    """y[M][N] = kind(x @ W^T) on the GPU; w: uint8 GGUF rows (numpy or DeviceBuffer), x: f16 [M][K] numpy."""
+          w_row_stride=None, bn=0, grid=0, kchunk=0, pair=-1, gemv=False, x_dtype="f16"):
+    """y[M][N] = kind(x @ W^T) on the GPU; w: uint8 GGUF rows (numpy or DeviceBuffer), x: f16 [M][K] numpy
+    (f32 with x_dtype="f32", GEMV only)."""
     t = F.type_of(fmt)
-    x = np.ascontiguousarray(x, dtype=np.float16)
+    x32 = x_dtype == "f32"
+    if x32 and not gemv:
+        raise ValueError("f32 activations are a GEMV operand only")
+    x = np.ascontiguousarray(x, dtype=np.float32 if x32 else np.float16)
     M = x.shape[0]
     K = K if K is not None else x.shape[1]
     if w_row_stride is None:
@@ -113,6 +124,8 @@ def qgemm(dev: Device, w, fmt, x, N=None, K=None, kind="kstore", out_dtype="f32"
         _check_size(auxd, M * N * 4, "aux")
     fn = qgemv_ptr if gemv else qgemm_ptr
     kw = {} if gemv else {"bn": bn, "grid": grid, "kchunk": kchunk, "pair": pair}
+    if x32:
+        fn, kw = qgemv_x_ptr, {"x_dtype": "f32"}
     fn(wd.ptr, t, N, K, w_row_stride, kb_off, xd.ptr, M, x.shape[1], yd.ptr, ydt, N, ep,
        auxd.ptr if auxd else None, N if auxd else 0, **kw)
     dev.synchronize()
@@ -124,11 +137,11 @@ def qgemm(dev: Device, w, fmt, x, N=None, K=None, kind="kstore", out_dtype="f32"
 
 
 def qgemv(dev: Device, w, fmt, x, N=None, K=None, kind="plain", out_dtype="f32", aux=None, kb_off=0,
-          w_row_stride=None):
+          w_row_stride=None, x_dtype="f16"):
     """Decode GEMV for M <= 32 tokens: same arguments as qgemm (kinds plain / resid / swiglu; swiglu writes the
-    chosen out_dtype)."""
+    chosen out_dtype); x_dtype="f32" passes x as f32, the reference GEMV's operand type."""
     return qgemm(dev, w, fmt, x, N=N, K=K, kind=kind, out_dtype=out_dtype, aux=aux, kb_off=kb_off,
-                 w_row_stride=w_row_stride, gemv=True)
+                 w_row_stride=w_row_stride, gemv=True, x_dtype=x_dtype)
 
 
 def qgemv_swiglu_ptr(w_gate, gate_fmt, gate_row_stride, w_up, up_fmt, up_row_stride, N, K, x, M, ldx, y, ldy,
