@@ -13,6 +13,8 @@ the same line:
             column-parallel QKV / gate / up, row-parallel o_proj / down each followed by one ncclAllReduce of f32
             partials through the library's own NCCL communicator (its rank count is reported); with the share of
             the forward spent in the allreduces and the per-site GEMM rates at the shard shapes.
+  lm_head   BASELINE config 5's decode lm head (Q6_K 128256 x 4096, M = 1 and 32), vocab-column sharded over the
+            N GPUs (16032 rows per rank at N = 8, ragged last row tiles): whole-job GB/s, max over ranks.
   sustained the config-2 GEMM over >= 2000 back-to-back launches (about half a second) with the SM clocks of that
             window: the figure under the power cap, beside the short run's burst figure.
 Other workloads (--workload): gemv (config 3, --tokens M), lmhead (config 5, Q6_K 128256 x 4096: GEMV for
@@ -454,6 +456,46 @@ def run_decode_record(args, local_rank, launches=200):
     return out
 
 
+def run_lmhead_record(args, dist, rank, local_rank, launches=50):
+    """Config 5's decode lm head (Q6_K 128256 x 4096, f32 logits) vocab-column sharded over the N GPUs: rank r
+    computes rows [r N / p, (r + 1) N / p) for all tokens, no collective (16032 rows at p = 8: ragged last row
+    tiles). GB/s of the whole job (the head's bytes once) over the max over ranks of the per-launch time."""
+    import __graft_entry__ as ge
+    pkg = ge.load_package()
+    dev = pkg.Device(local_rank)
+    pk = peaks()
+    world = world_size()
+    N, K = 128256, 4096
+    lo, hi = shard_rows(N, world, rank)
+    out = {"workload": "q6k_lm_head_decode_gemv (config 5: Q6_K 128256 x 4096)", "parallelism":
+           f"vocab column shards x{world}", "rows_per_rank": hi - lo, "launches_per_M": launches,
+           "scaling": "strong", "by_M": {}}
+    for M in args.lmhead_tokens:
+        k = Kernel(pkg, dev, 14, N, K, M, "f32", True, seed_w=0, seed_x=1, rows=(lo, hi))
+        for i in range(3):
+            k.step(i)
+        k.stream.synchronize()
+        g = k.graph(launches)
+        g.launch()
+        k.stream.synchronize()
+        ms, ms_local, clk = k.time_graph(g, dist, Clocks(local_rank))
+        g.close()
+        if dev.status_word():
+            raise RuntimeError("kernel status word set")
+        job = pkg.formats.row_bytes(14, K) * N + M * K * 2 + M * N * 4
+        shard = k.wbytes + k.xbytes + k.ybytes
+        us, us_local = ms / launches * 1e3, ms_local / launches * 1e3
+        rank_gbs = shard / (us_local * 1e-6) / 1e9
+        out["by_M"][str(M)] = {"us_per_launch": round(us, 3), "GB/s": round(job / (us * 1e-6) / 1e9, 1),
+                               "roofline_rank0": {"bound": "hbm", "achieved": round(rank_gbs, 1),
+                                                  "peak": pk["hbm_gbs"], "unit": "GB/s",
+                                                  "frac": round(rank_gbs / pk["hbm_gbs"], 4), "peak_src": pk["src"],
+                                                  "algorithmic_bytes_per_launch": shard},
+                               "clocks": clk}
+        k.close()
+    return out
+
+
 def stack_weights(F, shape, world, rank, scale=None):
     """Four distinct weight sets of this rank's shards (cycled over the layers: > L2 per GPU at tp1)."""
     p, H = world, shape.hidden
@@ -598,13 +640,18 @@ def run_stack_record(args, dist, rank, local_rank, steps=3, warmup=2):
 
 
 def run_ours(args, dist, rank, local_rank):
-    """--workload gemv / lmhead: one kernel, replicas on every rank (weak scaling)."""
+    """--workload gemv: one kernel, replicas on every rank (weak scaling). --workload lmhead: on N GPUs the
+    128256-row head is vocab-column sharded (rank r computes rows [r N / p, (r + 1) N / p) of the one tensor for all
+    tokens, no collective; 16032 rows at p = 8, so the last row tile of each shard is ragged), strong scaling."""
     import __graft_entry__ as ge
     pkg = ge.load_package()
     dev = pkg.Device(local_rank)
     wl = workload_of(args)
     world = world_size()
-    k = Kernel(pkg, dev, wl["fmt"], wl["N"], wl["K"], wl["M"], wl["out"], wl["gemv"], seed_w=0, seed_x=1 + rank)
+    shard = args.workload == "lmhead" and world > 1
+    rows = shard_rows(wl["N"], world, rank) if shard else None
+    k = Kernel(pkg, dev, wl["fmt"], wl["N"], wl["K"], wl["M"], wl["out"], wl["gemv"], seed_w=0,
+               seed_x=1 + (0 if shard else rank), rows=rows)
     for i in range(args.warmup):
         k.step(i)
     k.stream.synchronize()
@@ -619,31 +666,37 @@ def run_ours(args, dist, rank, local_rank):
     pk = peaks()
     per_step_ms = ms / args.steps
     M, N, K = wl["M"], wl["N"], wl["K"]
+    copies = 1 if shard else world  # the whole job: one head split over the ranks, or one head per rank
     if wl["gemv"]:
         alg = k.wbytes + k.xbytes + k.ybytes
-        value = world * alg / (per_step_ms * 1e-3) / 1e9
+        job = (pkg.formats.row_bytes(wl["fmt"], K) * N + M * K * 2 + M * N * 4) if shard else alg
+        value = copies * job / (per_step_ms * 1e-3) / 1e9
         unit = "GB/s"
         achieved = alg / (ms_local / args.steps * 1e-3) / 1e9
         roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                 "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": load_traffic(wl["name"]),
                 "peak_src": pk["src"], "algorithmic_bytes_per_launch": alg}
-        e2e_val = world * alg / (ms_e2e / args.steps * 1e-3) / 1e9
+        e2e_val = copies * job / (ms_e2e / args.steps * 1e-3) / 1e9
     else:
-        flops = 2.0 * M * N * K
-        value = world * flops / (per_step_ms * 1e-3) / 1e12
+        flops = 2.0 * M * k.N * K
+        job = 2.0 * M * N * K if shard else flops
+        value = copies * job / (per_step_ms * 1e-3) / 1e12
         unit = "TFLOP/s"
         achieved = flops / (ms_local / args.steps * 1e-3) / 1e12
         roof = {"bound": "tensor", "achieved": round(achieved, 1), "peak": pk["tflops"], "unit": "TFLOP/s",
                 "frac": round(achieved / pk["tflops"], 4), "traffic": load_traffic(wl["name"]),
                 "peak_src": pk["src"], "frac_of_sustained": round(achieved / pk["tflops_sustained"], 4),
                 "algorithmic_flops_per_launch": flops}
-        e2e_val = world * flops / (ms_e2e / args.steps * 1e-3) / 1e12
+        e2e_val = copies * job / (ms_e2e / args.steps * 1e-3) / 1e12
     line = {
         "metric": wl["metric"], "value": round(value, 2), "unit": unit, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(per_step_ms, 5), "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": round(per_step_ms, 5), "higher_is_better": True,
+        "scaling": "strong" if shard else "weak",
         "vs_baseline": None, "dtype": f"f16 x GGUF-{wl['fmt_name']} -> f32 acc", "data": "synthetic",
         "config": {"workload": wl["name"], "M_tokens": M, "K": K, "N": N, "weight_format": wl["fmt_name"],
-                   "out_dtype": wl["out"], "parallelism": f"replicas x{world}",
+                   "out_dtype": wl["out"],
+                   "parallelism": (f"vocab column shards x{world} ({k.N} rows on rank {rank})" if shard
+                                   else f"replicas x{world}"),
                    "launch_overlap": bool(args.launch_overlap), "l2": k.l2_note},
         "e2e": {"value": round(e2e_val, 2), "unit": unit, "h2d_bytes_per_step": k.xbytes,
                 "d2h_bytes_per_step": k.ybytes},
@@ -853,6 +906,9 @@ def main():
     ap.add_argument("--stack-tokens", type=int, default=4096, help="stack tokens M")
     ap.add_argument("--no-stack", dest="stack", action="store_false",
                     help="leave the nested config-4 tp_stack record out of the default line")
+    ap.add_argument("--no-lmhead", dest="lmhead", action="store_false",
+                    help="skip the nested config-5 vocab-sharded lm-head record")
+    ap.add_argument("--lmhead-tokens", type=int, nargs="+", default=[1, 32])
     ap.add_argument("--no-decode", dest="decode", action="store_false",
                     help="leave the nested config-3 decode record out of the default line")
     ap.add_argument("--no-sustained", dest="sustained", action="store_false",
@@ -892,6 +948,8 @@ def main():
         line = run_gemm_line(args, dist, rank, local_rank)
         if args.decode and world == 1:
             line["decode"] = run_decode_record(args, local_rank)
+        if args.lmhead:
+            line["lm_head"] = run_lmhead_record(args, dist, rank, local_rank)
         if args.stack:
             line["tp_stack"] = run_stack_record(args, dist, rank, local_rank)
     else:

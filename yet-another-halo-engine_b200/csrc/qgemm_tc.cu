@@ -118,6 +118,7 @@ struct KParams {
   int nsplit;           // 1, or the accumulation chunks of a tile when each is its own unit (split K)
   int tma_store;        // 1: the output is written with TMA stores through shared memory (tmap_y is valid)
   int aux_tma;          // 1: the epilogue's aux operand is prefetched by TMA (tmap_aux is valid)
+  int help;             // 1: the dequant warps help drain the accumulator (drain_share; one chunk per unit)
 };
 
 template <int T, int XR, int AUXB = 0>  // XR: activation rows a CTA stages (the tile's tokens, or half in a pair)
@@ -185,6 +186,38 @@ struct Sched {
 // rate (914-1117 us against 535 us for the residual epilogue at 4096 x 14336 x 4096).
 __device__ __forceinline__ float silu_f(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
 
+// Shared drain of a single accumulator region (NACC = 1, plain store): while a full accumulator is drained the MMAs
+// wait for it, and so do the dequant warps, whose A ring is full by then. So the epilogue warp and the four dequant
+// warps of each TMEM lane quarter drain it together: warp slot k (0 the epilogue warp, 1 + g the dequant warp of
+// group g) takes the CH-token chunks c with c % kDrainWarps == k and stores them straight to global memory (the 32
+// lanes of a warp are 32 consecutive output rows of one token: one coalesced store per token). tq: the TMEM address
+// of lane quarter q's accumulator.
+constexpr int kDrainWarps = 5;
+template <bool OUT_F16, int NCTA>
+__device__ __forceinline__ void drain_share(const KParams& p, uint32_t tq, int q, int lane, int slot, int rt,
+                                            uint32_t rank, int t0, int nt, int64_t tsplit) {
+  constexpr int CH = OUT_F16 ? 16 : 8;
+  const int row = (rt * NCTA + (int)rank) * kBM + q * 32 + lane;
+  const bool row_ok = row < p.N;
+  for (int j0 = slot * CH; j0 < nt; j0 += kDrainWarps * CH) {  // the same trip count for every lane
+    uint32_t v[CH];
+    if constexpr (CH == 16) tmem_ld16(tq + j0, v); else tmem_ld8(tq + j0, v);
+    tmem_wait_ld();
+    const int jn = min(CH, nt - j0);
+    if (row_ok) {
+#pragma unroll
+      for (int jj = 0; jj < CH; ++jj) {
+        if (jj >= jn) break;
+        const int64_t t = tsplit + t0 + j0 + jj;
+        if (OUT_F16)
+          reinterpret_cast<__half*>(p.y)[t * p.ldy + row] = __float2half_rn(__uint_as_float(v[jj]));
+        else
+          reinterpret_cast<float*>(p.y)[t * p.ldy + row] = __uint_as_float(v[jj]);
+      }
+    }
+  }
+}
+
 template <int T, int BN, int NACC, int EPI, bool OUT_F16, bool PAIR, bool SPLIT>
 __global__ void __launch_bounds__(kThreads, 1)
     qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
@@ -204,6 +237,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   // weight rows whose outputs a CTA produces per tile: 128 (TMEM lanes), or 64 under kEpiFfn (lanes 0-63 gate,
   // 64-127 the same rows of up)
   constexpr int kTileRows = EPI == kEpiFfn ? 64 : kBM;
+  // one accumulator region, a plain store and one accumulation chunk per unit: the dequant warps help drain it
+  // (drain_share; the host sets p.help)
+  constexpr bool HELP_T = NACC == 1 && EPI == kEpiStore;
+  const bool HELP = HELP_T && p.help != 0;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::kBarOff);
@@ -241,7 +278,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&accfull[i], 1);
-      mbar_init(&accempty[i], 4 * NCTA);
+      mbar_init(&accempty[i], (HELP ? 4 + 4 * kDqGroups : 4) * NCTA);
     }
     mbar_init(drain, 1);
     for (int i = 0; i < 4; ++i) mbar_init(&auxfull[i], 1);
@@ -390,10 +427,31 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     const uint32_t wbase = smem_u32(smem + S::kWOff);
     const uint32_t tl = tmem + ((uint32_t)(q * 32) << 16) + ACOL + 32 * half;
+    // HELP: the unit (tile) whose drain this warp still owes, helped once the warp has decoded the stages whose A
+    // slots the MMAs can refill only after that drain, or at the latest at the end of the next unit
+    int h_rt = -1, h_t0 = 0, h_nt = 0, h_kp = 0;
+    uint32_t h_u = 0, units = 0;
+    auto help = [&]() -> bool {
+      // warp-uniform: the drain's tcgen05.ld must never run on part of the warp
+      if (!__all_sync(0xffffffffu, mbar_wait(&accfull[0], h_u & 1, p.status, kStatusTimeoutFull))) return false;
+      tc_fence_after();
+      drain_share<OUT_F16, NCTA>(p, tmem + ((uint32_t)(q * 32) << 16), q, lane, 1 + g, h_rt, rank, h_t0, h_nt,
+                                 split ? (int64_t)h_kp * p.M : 0);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (PAIR) mbar_arrive_cluster(accempty_lead);
+        else mbar_arrive(&accempty[0]);
+      }
+      h_rt = -1;
+      return true;
+    };
     while (ok && sc.next(rt, kp, t0, nt)) {
       const int st0 = split ? kp * sch : 0, st1 = split ? min(nst, st0 + sch) : nst;
+      const uint32_t unit_start = s;
       for (int st = st0; st < st1; ++st, ++s) {
         if ((s & 1) != parity) continue;
+        if (HELP && h_rt >= 0 && s >= unit_start + kNA && !help()) { ok = false; break; }
         const int kb = 2 * st + half;              // 64-K block within the tile
         const uint32_t sbc = (s >> 1), ws = sbc % NSW, wph = (sbc / NSW) & 1;  // super-block = 2 stages
         const uint32_t as = s % kNA, aph = (s / kNA) & 1;
@@ -428,7 +486,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           else mbar_arrive(&afull[as]);
         }
       }
+      if (HELP && ok) {
+        if (h_rt >= 0 && !help()) { ok = false; break; }  // a unit too short to have triggered it
+        h_rt = rt, h_t0 = t0, h_nt = nt, h_kp = kp, h_u = units;
+      }
+      ++units;
     }
+    if (HELP && ok && h_rt >= 0) help();
   } else if (warp < kWarpW) {
     // ------------------------------------------------------------------ epilogue
     // Accumulator columns are drained CH at a time (CH = 16 f16 / 8 f32 tokens); the final values go to a
@@ -450,6 +514,24 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool atma = AD > 0 && p.aux_tma;
     uint8_t* abuf = smem + S::kAuxOff;
     uint32_t aux_used = 0;  // aux chunks consumed so far (slot aux_used % AD)
+    if (HELP_T && HELP) {  // this warp's share of each drain (drain_share, slot 0)
+      while (ok && sc.next(rt, kp, t0, nt)) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&accfull[0], u & 1, p.status, kStatusTimeoutFull))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        drain_share<OUT_F16, NCTA>(p, tl, q, lane, 0, rt, rank, t0, nt, split ? (int64_t)kp * p.M : 0);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if (PAIR) mbar_arrive_cluster(accempty_lead);
+          else mbar_arrive(&accempty[0]);
+        }
+        ++u;
+      }
+      ok = false;  // done: skip the staged epilogue below
+    }
     while (ok && sc.next(rt, kp, t0, nt)) {
       const int row0 = (rt * NCTA + (int)rank) * kTileRows;
       const int row = row0 + (EPI == kEpiFfn ? (rloc & 63) : rloc);  // the output row of this lane's accumulator
@@ -659,7 +741,10 @@ cudaError_t launch_t(const QGemmArgs& a, cudaStream_t stream) {
   CUtensorMap my;
   const int esz = a.y_f16 ? 2 : 4;
   // (split K writes the workspace with plain stores: its rows kp * M + t are not the output tensor's rows)
-  const bool tma_store = !SPLIT && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0 && (a.ldy * esz) % 16 == 0;
+  // a single accumulator region with a plain store and one accumulation chunk per unit is drained by 20 warps with
+  // direct stores (drain_share)
+  const bool help = NACC == 1 && EPI == kEpiStore && (SPLIT || a.kchunk <= 0 || a.kchunk >= a.K);
+  const bool tma_store = !help && !SPLIT && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0 && (a.ldy * esz) % 16 == 0;
   if (tma_store) {
     cuuint64_t dims[2] = {(cuuint64_t)a.N, (cuuint64_t)a.M};
     cuuint64_t strides[1] = {(cuuint64_t)(a.ldy * esz)};
@@ -687,6 +772,7 @@ cudaError_t launch_t(const QGemmArgs& a, cudaStream_t stream) {
   KParams p;
   p.tma_store = tma_store ? 1 : 0;
   p.aux_tma = aux_tma ? 1 : 0;
+  p.help = help ? 1 : 0;
   p.N = (int)a.N;
   p.K = (int)a.K;
   p.M = (int)a.M;
