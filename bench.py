@@ -32,7 +32,8 @@ weights rotating as in the device-timed leg).
 
 Multi-GPU (torchrun, one process per GPU): torch.distributed (gloo, CPU tensors) carries the barrier, the max over
 ranks and rank 0's NCCL id; the stack's allreduces go through the library's communicator (NCCL_DEBUG=INFO with the
-INIT subsystem is set unless the caller set NCCL_DEBUG, so NCCL's own log shows the communicator's nranks).
+INIT subsystem is set unless the caller set NCCL_DEBUG, so NCCL's own log shows the communicator's nranks; the
+JSON line is the last line of stdout: the process ends right after it, before NCCL's exit-time log).
 
 --impl reference: the reference's CPU path for the same metric (its test-suite oracle: gguf-py
 quants.dequantize -> f16 -> numpy matmul, engine/gpu/loom/tools/gemv_check.py:161-162) on the host cores, rank 0
@@ -961,6 +962,11 @@ def main():
     if dist:
         dist.barrier()
         dist.destroy_process_group()
+    # End the process here: NCCL's teardown at interpreter exit logs (under NCCL_DEBUG=INFO) after the JSON line,
+    # which must stay the last line of stdout. Every communicator, graph and buffer is released above.
+    sys.stdout.flush()
+    sys.stderr.flush()
+    os._exit(0)
 
 
 if __name__ == "__main__":

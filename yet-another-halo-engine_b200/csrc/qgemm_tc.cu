@@ -43,6 +43,7 @@
 #include <cuda_runtime.h>
 
 #include <mutex>
+#include <type_traits>
 
 #include "decode.cuh"
 #include "kernels.h"
@@ -189,30 +190,31 @@ __device__ __forceinline__ float silu_f(float g) { return __fdividef(g, 1.0f + _
 // Shared drain of a single accumulator region (NACC = 1, plain store): while a full accumulator is drained the MMAs
 // wait for it, and so do the dequant warps, whose A ring is full by then. So the epilogue warp and the four dequant
 // warps of each TMEM lane quarter drain it together: warp slot k (0 the epilogue warp, 1 + g the dequant warp of
-// group g) takes the CH-token chunks c with c % kDrainWarps == k and stores them straight to global memory (the 32
+// group g) takes the 8-token chunks c with c % kDrainWarps == k and stores them straight to global memory (the 32
 // lanes of a warp are 32 consecutive output rows of one token: one coalesced store per token). tq: the TMEM address
 // of lane quarter q's accumulator.
 constexpr int kDrainWarps = 5;
 template <bool OUT_F16, int NCTA>
 __device__ __forceinline__ void drain_share(const KParams& p, uint32_t tq, int q, int lane, int slot, int rt,
                                             uint32_t rank, int t0, int nt, int64_t tsplit) {
-  constexpr int CH = OUT_F16 ? 16 : 8;
+  constexpr int CH = 8;  // 8 tokens per chunk: up to 32 chunks over the 20 warps of a CTA
   const int row = (rt * NCTA + (int)rank) * kBM + q * 32 + lane;
   const bool row_ok = row < p.N;
-  for (int j0 = slot * CH; j0 < nt; j0 += kDrainWarps * CH) {  // the same trip count for every lane
+  using E = typename std::conditional<OUT_F16, __half, float>::type;
+  E* yp = reinterpret_cast<E*>(p.y) + (tsplit + t0 + slot * CH) * p.ldy + row;
+  const int64_t step = (int64_t)kDrainWarps * CH * p.ldy;
+  for (int j0 = slot * CH; j0 < nt; j0 += kDrainWarps * CH, yp += step) {  // the same trip count for every lane
     uint32_t v[CH];
-    if constexpr (CH == 16) tmem_ld16(tq + j0, v); else tmem_ld8(tq + j0, v);
+    tmem_ld8(tq + j0, v);
     tmem_wait_ld();
     const int jn = min(CH, nt - j0);
     if (row_ok) {
+      E* o = yp;
 #pragma unroll
-      for (int jj = 0; jj < CH; ++jj) {
+      for (int jj = 0; jj < CH; ++jj, o += p.ldy) {
         if (jj >= jn) break;
-        const int64_t t = tsplit + t0 + j0 + jj;
-        if (OUT_F16)
-          reinterpret_cast<__half*>(p.y)[t * p.ldy + row] = __float2half_rn(__uint_as_float(v[jj]));
-        else
-          reinterpret_cast<float*>(p.y)[t * p.ldy + row] = __uint_as_float(v[jj]);
+        if (OUT_F16) *reinterpret_cast<__half*>(o) = __float2half_rn(__uint_as_float(v[jj]));
+        else *reinterpret_cast<float*>(o) = __uint_as_float(v[jj]);
       }
     }
   }
