@@ -132,7 +132,8 @@ int yah_selftest_bounded_wait(int64_t budget_cycles, int* code);
 /* Make `stream` wait for the last work recorded on `event` (cudaStreamWaitEvent). */
 int yah_stream_wait_event(void* stream, void* event);
 /* Read and clear the current device's kernel status word: 0, or the code of a bounded wait that ran out
- * (1 data wait, 2 free-stage wait, 3 exit drain). A non-zero word means the output of that launch is invalid.
+ * (1 data wait, 2 free-stage wait, 3 exit drain, 4 a wait for another GPU's signal). A non-zero word means the
+ * output of that launch is invalid.
  * The read is a blocking copy on the legacy default stream, which does not wait for work on streams created with
  * cudaStreamNonBlocking (yah_stream_create makes such streams): synchronise the stream the kernels ran on first.
  * When the word is non-zero the call also resets the GEMV's split-K arrival counters, which a CTA that left early
@@ -347,6 +348,45 @@ int yah_add_rmsnorm(float* h, int64_t ldh, const void* d, int d_dtype, int64_t l
                     float gain, void* out, int64_t ldo, void* stream);
 /* ncclAllReduce(sum) of f16 in place (the speed mode's partials: half the bytes of yah_tp_allreduce_f32). */
 int yah_tp_allreduce_f16(yah_tp_comm* comm, void* buf, int64_t count, void* stream);
+/* ncclAllGather of count f32 from every rank into recv ([nranks][count]). */
+int yah_tp_allgather_f32(yah_tp_comm* comm, const float* send, float* recv, int64_t count, void* stream);
+
+/* ---- fused row-parallel reduce over peer memory (no counterpart in the single-GPU reference) ----
+ * The row-parallel linear's reduction written by its own GEMM: rank q's f32 partial of token t is stored by the
+ * GEMM's epilogue straight into the memory of the rank owning t (tokens split into nranks equal slices), over
+ * NVLink, so the transfer overlaps the GEMM tile by tile; the owner adds the nranks slots of its slice in rank order
+ * into its slice of the residual stream and writes the RMSNorm of it (f16) into every rank's activation buffer.
+ * Cross-GPU order uses flags in each rank's memory (release / acquire at system scope, epochs that only grow);
+ * every wait is bounded (2 s, then code 4 in the status word). Plain stores and flags: no multicast.
+ *
+ * yah_qgemm_sliced: yah_qgemm (plain store, f32) with output token t written to ys[t / slice_rows] + (t % slice_rows)
+ * * ldy (1..8 slices, slice_rows a multiple of 16; the slices may be other GPUs' memory).
+ * yah_tp_peers_create: device buffers of this rank (any device pointers; the allocations are shared through CUDA
+ * IPC, exchanged with one ncclAllGather) and the same buffers of every other rank as addresses usable here;
+ * yah_tp_peers_ptr gives buffer b of rank r. Collective: every rank calls it with the same nbufs.
+ * yah_tp_signal: after the preceding work on `stream`, int slot `slot` of buffer flag_buf on every rank := value.
+ * yah_tp_wait: later work on `stream` waits until this rank's ints [first, first + count) of flag_buf are >= value.
+ * yah_tp_reduce_norm: for rows r < rows of this rank's slice: h[r] += parts[0][r] + ... + parts[nparts-1][r]
+ * (slots part_stride floats apart, rows ldp apart; nparts 0: no add); then, unless out_buf < 0,
+ * f16(h[r] * gain / sqrt(mean(h[r]^2) + eps)) at row out_row0 + r (stride ldo) of buffer out_buf on every rank.
+ * yah_tp_linear_row_scatter: the row-parallel GEMM of this rank's K window with its partials scattered as above
+ * into slot `rank` of buffer recv_buf ([nranks][M / nranks][N] f32) on every rank; M must split into nranks slices
+ * of a multiple of 16 tokens. */
+typedef struct yah_tp_peers yah_tp_peers;
+int yah_qgemm_sliced(const void* w, int ggml_type, int64_t N, int64_t K, int64_t w_row_stride, int64_t kb_off,
+                     const void* x, int64_t M, int64_t ldx, void* const* ys, int nslices, int64_t slice_rows,
+                     int64_t ldy, void* stream);
+int yah_tp_peers_create(yah_tp_comm* comm, void* const* bufs, int nbufs, void* stream, yah_tp_peers** out);
+int yah_tp_peers_ptr(const yah_tp_peers* pe, int rank, int buf, void** ptr);
+int yah_tp_peers_destroy(yah_tp_peers* pe);
+int yah_tp_signal(const yah_tp_peers* pe, int flag_buf, int slot, int value, void* stream);
+int yah_tp_wait(const yah_tp_peers* pe, int flag_buf, int first, int count, int value, void* stream);
+int yah_tp_reduce_norm(const yah_tp_peers* pe, float* h, int64_t ldh, int64_t rows, int64_t H, const float* parts,
+                       int nparts, int64_t part_stride, int64_t ldp, float eps, float gain, int out_buf,
+                       int64_t out_row0, int64_t ldo, void* stream);
+int yah_tp_linear_row_scatter(const yah_tp_peers* pe, const void* w_shard, int ggml_type, int64_t N,
+                              int64_t K_local, int64_t w_row_stride, int64_t kb_off, const void* x, int64_t M,
+                              int64_t ldx, int recv_buf, void* stream);
 
 /* ---- GGUF files: the quant-block loader (engine/core/gguf.hpp:74-105 core::Gguf, engine/core/gguf.cpp) ----
  * yah_gguf_open maps a GGUF (version 2 or 3) file read-only and parses its metadata and tensor table; the tensor

@@ -70,6 +70,45 @@ def cpu_shard_worker(rank, world, port, out_q):
         dist.destroy_process_group()
 
 
+def cpu_fused_worker(rank, world, port, out_q):
+    """gloo rank: the fused mode's exchange restated on the CPU (oracle arithmetic). Each rank's row-parallel K-window
+    partial goes, token slice by token slice, to the slice's owner as slot `rank`; the owner adds the slots in rank
+    order into its slice of the residual stream and normalises it; the normalised slices gathered in owner order
+    must equal the single-rank result (residual + full product, then RMSNorm)."""
+    import torch.distributed as dist
+    import __graft_entry__ as ge
+    from oracle import oracle as O
+    pkg = ge.load_package()
+    F, tp = pkg.formats, pkg.tp
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=60))
+    try:
+        N, K, M = 256, 1024, 64
+        w = F.synth_weights(F.Q4_K, N, K, seed=80)
+        x = F.synth_activations(M, K, seed=81)
+        h = np.random.default_rng(82).standard_normal((M, N))
+        full = O.gemm_ref(O.dequant_f16(F.Q4_K, w, N, K), x)
+        want = rmsnorm_ref(h + full, 1 / 64, 1e-6)
+        k0, k1 = tp.k_window(K, world, rank)
+        partial = O.gemm_ref(O.dequant_f16(F.Q4_K, tp.take_k_window(w, F.Q4_K, k0, k1), N, k1 - k0), x[:, k0:k1])
+        parts = [None] * world
+        dist.all_gather_object(parts, partial)  # stands in for the GEMM's stores into the owners' slots
+        lo, hi = tp.token_slice(M, world, rank)
+        slots = np.stack([parts[q][lo:hi] for q in range(world)])  # [world][M / world][N]: slot q = rank q's partial
+        hs = h[lo:hi].copy()
+        for q in range(world):
+            hs = hs + slots[q]
+        mine = rmsnorm_ref(hs, 1 / 64, 1e-6)
+        gathered = [None] * world
+        dist.all_gather_object(gathered, (lo, mine))
+        got = np.concatenate([g[1] for g in sorted(gathered, key=lambda g: g[0])])
+        err = np.abs(got.astype(np.float64) - want.astype(np.float64))
+        ulp = np.spacing(np.abs(want).astype(np.float16)).astype(np.float64)
+        out_q.put((rank, bool((err <= ulp).all()), float(err.max())))
+    finally:
+        dist.destroy_process_group()
+
+
 def gpu_stack_worker(rank, world, id_q, out_q, mode="parity"):
     """NCCL rank on GPU `rank`: the small stack sharded over `world` ranks vs the float64 reference."""
     import __graft_entry__ as ge

@@ -157,10 +157,75 @@ def test_small_stack_speed_mode_one_rank(pkg, O, dev, comm, M):
     assert dev.status_word() == 0
 
 
-@pytest.mark.parametrize("mode", ["parity", "speed"])
+@pytest.mark.parametrize("M", [64, 128])
+def test_small_stack_fused_one_rank(pkg, O, dev, comm, M):
+    """Fused mode (partials scattered by the row-parallel GEMM's epilogue into token slices, reduce + RMSNorm +
+    all-gather by yah_tp_reduce_norm, flags between the steps) on one rank against the float64 stack reference;
+    a second forward of the same input gives the same bits (the flag epochs keep growing)."""
+    tp = pkg.tp
+    shape = tp.StackShape(layers=2, hidden=512, n_q=4, n_kv=2, head_dim=128, ff=1024)
+    full = [tp.layer_weights(shape, i) for i in range(shape.layers)]
+    stack = tp.LlamaStack(dev, comm, shape, [tp.shard_layer(shape, f, 1, 0) for f in full], M, mode="fused")
+    h0 = np.random.default_rng(75).standard_normal((M, shape.hidden)).astype(np.float32)
+    outs = []
+    for _ in range(2):
+        h = dev.upload(h0)
+        stack.forward(h)
+        dev.synchronize()
+        outs.append(h.download(np.float32, (M, shape.hidden)))
+    e = O.errors(outs[0], W.stack_ref(O, shape, full, h0, tp.NORM_GAIN, tp.NORM_EPS))
+    stack.close()
+    assert e["finite"] and e["rel_fro"] <= 1e-3, e
+    assert np.array_equal(outs[0].view(np.uint32), outs[1].view(np.uint32))
+    assert dev.status_word() == 0
+
+
+def test_qgemm_token_slices(pkg, F, dev):
+    """yah_qgemm_sliced: output token t lands at slice t // slice_rows, row t % slice_rows, the same bits as the plain
+    GEMM with the same accumulation (one chunk up to K = 8192, chunks of 2048 above)."""
+    L = pkg.lib()
+    t = F.Q4_K
+    for (M, N, K, sr) in ((256, 512, 2048, 64), (96, 384, 8192, 48), (64, 256, 10240, 16)):
+        w = F.synth_weights(t, N, K, seed=M + K)
+        x = F.synth_activations(M, K, seed=M)
+        ref = pkg.ops.qgemm(dev, w, t, x, N=N, K=K, out_dtype="f32", kchunk=-1 if K <= 8192 else 2048)
+        wd, xd = dev.upload(w), dev.upload(x)
+        ns = M // sr
+        slices = [dev.empty(sr * N * 4).fill(0xFF) for _ in range(ns)]
+        arr = (ctypes.c_void_p * ns)(*[b.ptr for b in slices])
+        assert L.yah_qgemm_sliced(wd.ptr, t, N, K, w.shape[1], 0, xd.ptr, M, K, arr, ns, sr, N, None) == 0, \
+            L.yah_last_error()
+        dev.synchronize()
+        got = np.concatenate([b.download(np.float32, (sr, N)) for b in slices])
+        assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)), (M, N, K)
+    bad = (ctypes.c_void_p * 1)(slices[0].ptr)
+    assert L.yah_qgemm_sliced(wd.ptr, t, N, K, w.shape[1], 0, xd.ptr, M, K, bad, 1, 40, N, None) == 1  # not % 16
+
+
+def test_peer_wait_runs_out(pkg, dev, comm):
+    """A wait on a flag nothing sets gives up after its budget with code 4 in the status word, without a fault; the
+    device then runs the next launches normally."""
+    tp = pkg.tp
+    L = pkg.lib()
+    flags = dev.empty(64 * 4).fill(0)
+    dev.synchronize()
+    pe = tp.Peers(comm, [flags])
+    pkg._lib.check(L.yah_tp_signal(pe.handle, 0, 3, 5, None))          # slot 3 := 5 on every rank (this one)
+    pkg._lib.check(L.yah_tp_wait(pe.handle, 0, 3, 1, 5, None))         # satisfied
+    dev.synchronize()
+    assert dev.status_word() == 0
+    pkg._lib.check(L.yah_tp_wait(pe.handle, 0, 3, 1, 6, None))         # nothing sets 6: runs out (~2 s)
+    dev.synchronize()
+    assert dev.status_word() == 4
+    assert flags.download(np.int32, (64,))[3] == 5
+    pe.close()
+    assert dev.status_word() == 0
+
+
+@pytest.mark.parametrize("mode", ["parity", "speed", "fused"])
 def test_small_stack_two_ranks(pkg, mode):
     """The same stack over two GPUs (column shards + two allreduces per layer) matches the reference, with f32
-    (parity) and f16 (speed) partial sums."""
+    (parity) and f16 (speed) partial sums, and with the fused reduce over peer memory (fused)."""
     if pkg.device_count() < 2:
         pytest.skip("needs two GPUs")
     ctx = mp.get_context("spawn")

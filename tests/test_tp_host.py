@@ -66,3 +66,27 @@ def test_two_gloo_ranks_column_and_row_parallel():
     for rank, col_err, row_rel in res:
         assert col_err == 0.0, (rank, col_err)
         assert row_rel <= 1e-12, (rank, row_rel)
+
+
+def test_token_slices(pkg):
+    tp = pkg.tp
+    assert [tp.token_slice(4096, 8, r) for r in (0, 7)] == [(0, 512), (3584, 4096)]
+    for bad in ((4096, 3), (96, 4)):  # not equal slices; slices of 24 tokens (not a multiple of 16)
+        with pytest.raises(ValueError):
+            tp.token_slice(*bad, 0)
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_gloo_ranks_fused_exchange(world):
+    """The fused mode's slot layout and rank-order reduction, restated with gloo ranks (W.cpu_fused_worker)."""
+    ctx = mp.get_context("spawn")
+    out_q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=W.cpu_fused_worker, args=(r, world, port, out_q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [out_q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, ok, err in res:
+        assert ok, (rank, err)

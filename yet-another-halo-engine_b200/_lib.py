@@ -85,6 +85,18 @@ SYMBOLS = {
                                  c_vp]),
     "yah_set_gemv_impl": (c_int, [c_int]),
     "yah_qgemv_describe": (c_int, [c_int, c_i64, c_i64, c_i64, ctypes.c_char_p, c_i64]),
+    "yah_tp_allgather_f32": (c_int, [c_vp, c_vp, c_vp, c_i64, c_vp]),
+    "yah_qgemm_sliced": (c_int, [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, P(c_vp), c_int, c_i64,
+                                 c_i64, c_vp]),
+    "yah_tp_peers_create": (c_int, [c_vp, P(c_vp), c_int, c_vp, P(c_vp)]),
+    "yah_tp_peers_ptr": (c_int, [c_vp, c_int, c_int, P(c_vp)]),
+    "yah_tp_peers_destroy": (c_int, [c_vp]),
+    "yah_tp_signal": (c_int, [c_vp, c_int, c_int, c_int, c_vp]),
+    "yah_tp_wait": (c_int, [c_vp, c_int, c_int, c_int, c_int, c_vp]),
+    "yah_tp_reduce_norm": (c_int, [c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_int, c_i64, c_i64, c_f, c_f, c_int,
+                                   c_i64, c_i64, c_vp]),
+    "yah_tp_linear_row_scatter": (c_int, [c_vp, c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_int,
+                                          c_vp]),
     "yah_tp_available": (c_int, []),
     "yah_tp_unique_id": (c_int, [c_vp]),
     "yah_tp_init": (c_int, [P(c_vp), c_int, c_int, c_vp]),

@@ -247,6 +247,14 @@ size_t gemv_ws_bytes(const yah::GemvPlan& p) {
 }  // namespace
 
 namespace yah {
+int device_status_word(int** status) {
+  DevState* s;
+  const int rc = dev_state(&s);
+  if (rc) return rc;
+  *status = s->status;
+  return YAH_OK;
+}
+
 int set_error(int code, const char* fmt, ...) {
   char buf[512];
   va_list ap;
@@ -675,6 +683,38 @@ int yah_qgemm_workspace_size(int t, int64_t N, int64_t K, int64_t M, int y_dtype
   if (rc) return rc;
   *bytes = need.total();
   return YAH_OK;
+}
+
+int yah_qgemm_sliced(const void* w, int t, int64_t N, int64_t K, int64_t w_row_stride, int64_t kb_off, const void* x,
+                     int64_t M, int64_t ldx, void* const* ys, int nslices, int64_t slice_rows, int64_t ldy,
+                     void* stream) {
+  if (!ys || nslices < 1 || nslices > yah::kMaxSlices)
+    return fail(YAH_ERR_ARG, "%d token slices (1..%d)", nslices, yah::kMaxSlices);
+  if (slice_rows < 16 || slice_rows % 16 || slice_rows * nslices < M)
+    return fail(YAH_ERR_ARG, "slice_rows %lld: a multiple of 16 with nslices * slice_rows >= M",
+                (long long)slice_rows);
+  for (int i = 0; i < nslices; ++i)
+    if (!ys[i] || (reinterpret_cast<uintptr_t>(ys[i]) & 3)) return fail(YAH_ERR_ARG, "slice %d: null or unaligned", i);
+  DevState* s;
+  int rc = dev_state(&s);
+  if (rc) return rc;
+  yah::QGemmArgs a;
+  GemmNeed need;
+  // an explicit grid: split K writes its chunks elsewhere first, so slices never split; up to K = 8192 one
+  // accumulation chunk (the shared-drain tile; chunked tiles store scalar-wise here, without TMA stores)
+  rc = qgemm_prepare(w, t, N, K, w_row_stride, kb_off, x, M, ldx, ys[0], YAH_F32, ldy, YAH_EPI_STORE, nullptr, 0, 0,
+                     sms_of(s), K <= 8192 ? -1 : 0, -1, false, a, need);
+  if (rc) return rc;
+  a.nsl = nslices;
+  a.slice_rows = slice_rows;
+  for (int i = 0; i < nslices; ++i) a.ysl[i] = ys[i];
+  if (need.scratch) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    rc = grow(reinterpret_cast<void**>(&s->gemm_scratch), &s->gemm_scratch_bytes, need.scratch);
+    if (rc) return rc;
+    a.scratch = s->gemm_scratch;
+  }
+  return after_launch(yah::launch_qgemm_tc(a, (cudaStream_t)stream), "qgemm (token slices) launch");
 }
 
 int yah_qgemm_ws(const void* w, int t, int64_t N, int64_t K, int64_t w_row_stride, int64_t kb_off, const void* x,

@@ -15,6 +15,8 @@ int set_error(int code, const std::string& msg);
 enum Epilogue : int { kEpiStore = 0, kEpiResid = 1, kEpiSwiglu = 2, kEpiFfn = 3 };
 
 // Tile-GEMM problem (token-major): y[M][ldy] (+)= x[M][ldx] (f16) * W[N][K]^T, W in GGUF rows.
+constexpr int kMaxSlices = 8;
+
 struct QGemmArgs {
   const void* w;        // weight rows (GGUF block layout)
   int type;             // GGML type id (8, 12, 14)
@@ -40,6 +42,11 @@ struct QGemmArgs {
   const void* w2 = nullptr;  // kEpiFfn: the up weights (same type, shape and row stride as w, the gate weights)
   int nsplit = 1;       // > 1: each accumulation chunk of a tile is its own work unit (split K, one chunk each)
   float* kpart = nullptr;  // nsplit * M * N f32 chunk results when nsplit > 1, summed in chunk order afterwards
+  // Token slices (kEpiStore only, no split): output token t goes to ysl[t / slice_rows] + (t % slice_rows) * ldy
+  // instead of y (slices of other GPUs' memory: a reduce-scatter written by the epilogue). 0: y.
+  int nsl = 0;
+  int64_t slice_rows = 0;
+  void* ysl[kMaxSlices] = {};
 };
 
 // Resident 2-CTA clusters of the tile-GEMM kernel on the current device (0 if clusters are unavailable).
@@ -121,5 +128,8 @@ int set_error(int code, const char* fmt, ...);
 
 // Tensor-map encoder resolved from the driver at first use (no libcuda link dependency).
 bool tensor_map_encoder_available();
+
+// The current device's status word (the device state is created on first use): for kernels outside capi.cu.
+int device_status_word(int** status);
 
 }  // namespace yah

@@ -14,6 +14,7 @@ enum : int {
   kStatusTimeoutFull = 1,   // a consumer waited too long for data
   kStatusTimeoutEmpty = 2,  // a producer waited too long for a free stage
   kStatusTimeoutDrain = 3,  // the exit drain of in-flight copies/MMAs ran out
+  kStatusTimeoutPeer = 4,   // a wait for another GPU's signal ran out (tensor-parallel layer)
 };
 
 // About 2^31 cycles (~1.1 s at 1.9 GHz): far beyond any legitimate wait of these kernels.

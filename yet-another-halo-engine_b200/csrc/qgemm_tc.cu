@@ -120,6 +120,9 @@ struct KParams {
   int tma_store;        // 1: the output is written with TMA stores through shared memory (tmap_y is valid)
   int aux_tma;          // 1: the epilogue's aux operand is prefetched by TMA (tmap_aux is valid)
   int help;             // 1: the dequant warps help drain the accumulator (drain_share; one chunk per unit)
+  int nsl;              // > 0: token slices (output token t at ysl[t / slice_rows] + (t % slice_rows) * ldy)
+  int64_t slice_rows;
+  void* ysl[kMaxSlices];
 };
 
 template <int T, int XR, int AUXB = 0>  // XR: activation rows a CTA stages (the tile's tokens, or half in a pair)
@@ -210,6 +213,10 @@ __device__ __forceinline__ void drain_share(const KParams& p, uint32_t tq, int q
     const int jn = min(CH, nt - j0);
     if (row_ok) {
       E* o = yp;
+      if (p.nsl > 0) {  // token slices: a chunk of 8 tokens never crosses one (slice_rows % 16 == 0)
+        const int64_t t = t0 + j0;
+        o = reinterpret_cast<E*>(p.ysl[t / p.slice_rows]) + (t % p.slice_rows) * p.ldy + row;
+      }
 #pragma unroll
       for (int jj = 0; jj < CH; ++jj, o += p.ldy) {
         if (jj >= jn) break;
@@ -218,6 +225,7 @@ __device__ __forceinline__ void drain_share(const KParams& p, uint32_t tq, int q
       }
     }
   }
+
 }
 
 template <int T, int BN, int NACC, int EPI, bool OUT_F16, bool PAIR, bool SPLIT>
@@ -495,6 +503,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       ++units;
     }
     if (HELP && ok && h_rt >= 0) help();
+    if (p.nsl > 0) __threadfence_system();  // token slices: see the epilogue's end
   } else if (warp < kWarpW) {
     // ------------------------------------------------------------------ epilogue
     // Accumulator columns are drained CH at a time (CH = 16 f16 / 8 f32 tokens); the final values go to a
@@ -662,10 +671,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int jj = 0; jj < CH; ++jj) {
               if (jj >= jn) break;
               const int64_t t = tsplit + t0 + j0 + jj;
+              void* yb = p.y;
+              int64_t tt = t;
+              if (p.nsl > 0) yb = p.ysl[t / p.slice_rows], tt = t % p.slice_rows;
               if (OUT_F16)
-                reinterpret_cast<__half*>(p.y)[t * p.ldy + row] = __float2half_rn(val[jj]);
+                reinterpret_cast<__half*>(yb)[tt * p.ldy + row] = __float2half_rn(val[jj]);
               else
-                reinterpret_cast<float*>(p.y)[t * p.ldy + row] = val[jj];
+                reinterpret_cast<float*>(yb)[tt * p.ldy + row] = val[jj];
             }
           }
           (void)ES;
@@ -679,6 +691,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     if (leader) bulk_wait_all();  // stores complete before the CTA (and its shared memory) goes away
+    // token slices may be other GPUs' memory: each storing thread's last stores are visible system-wide before the
+    // kernel ends (the launch that signals their completion follows in stream order); once per thread, at the end
+    if (p.nsl > 0) __threadfence_system();
   }
 
   tc_fence_before();
@@ -746,7 +761,8 @@ cudaError_t launch_t(const QGemmArgs& a, cudaStream_t stream) {
   // a single accumulator region with a plain store and one accumulation chunk per unit is drained by 20 warps with
   // direct stores (drain_share)
   const bool help = NACC == 1 && EPI == kEpiStore && (SPLIT || a.kchunk <= 0 || a.kchunk >= a.K);
-  const bool tma_store = !help && !SPLIT && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0 && (a.ldy * esz) % 16 == 0;
+  const bool tma_store = !help && !SPLIT && a.nsl == 0 && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0 &&
+                         (a.ldy * esz) % 16 == 0;
   if (tma_store) {
     cuuint64_t dims[2] = {(cuuint64_t)a.N, (cuuint64_t)a.M};
     cuuint64_t strides[1] = {(cuuint64_t)(a.ldy * esz)};
@@ -775,6 +791,9 @@ cudaError_t launch_t(const QGemmArgs& a, cudaStream_t stream) {
   p.tma_store = tma_store ? 1 : 0;
   p.aux_tma = aux_tma ? 1 : 0;
   p.help = help ? 1 : 0;
+  p.nsl = SPLIT ? 0 : a.nsl;
+  p.slice_rows = a.slice_rows;
+  for (int i = 0; i < kMaxSlices; ++i) p.ysl[i] = a.ysl[i];
   p.N = (int)a.N;
   p.K = (int)a.K;
   p.M = (int)a.M;
@@ -939,6 +958,10 @@ int qgemm_max_pairs(int type, int bn) {
 
 cudaError_t launch_qgemm_tc(const QGemmArgs& a, cudaStream_t stream) {
   if (a.nsplit > 1 && a.epilogue == kEpiFfn) return cudaErrorInvalidValue;  // the fused gate+up does not split
+  // token slices: plain stores of unsplit tiles, whole 16-token units per slice
+  if (a.nsl > 0 && (a.nsplit > 1 || a.epilogue != kEpiStore || a.nsl > kMaxSlices || a.slice_rows <= 0 ||
+                    a.slice_rows % 16 || a.slice_rows * a.nsl < a.M))
+    return cudaErrorInvalidValue;
   if (a.nsplit > 1) {
     if (!a.kpart) return cudaErrorInvalidValue;
     switch (a.type) {

@@ -19,7 +19,14 @@ Per layer (attention replaced by identity, so the o_proj input is the rank's que
     h   = h + allreduce(a Wd_r^T)
 
 Row-parallel partial sums. Parity mode: f32; rank 0's GEMM epilogue adds the residual and the allreduce sums
-h + partials in place. Speed mode: every rank's GEMM stores f16 partials (no residual read), the f16 allreduce moves
+h + partials in place. Fused mode (the parity arithmetic without the allreduce): the tokens are split into p equal
+slices, rank r owning slice r of the residual stream; each rank's row-parallel GEMM writes its f32 partial of a
+token straight into the owner's memory (yah_tp_linear_row_scatter, stores over NVLink while the GEMM runs), the
+owner adds the p slots in rank order into its residual slice and writes the RMSNorm of it (f16) into every rank's
+activation buffer (yah_tp_reduce_norm: the all-gather), with flags in each rank's memory ordering the ranks
+(yah_tp_signal / yah_tp_wait, bounded). Traffic per row-parallel linear and rank: (p - 1) / p of the f32 partial
+out and of the f16 activations back, against 2 (p - 1) / p of the f32 partial for the allreduce, and the scatter
+overlaps its GEMM. Speed mode: every rank's GEMM stores f16 partials (no residual read), the f16 allreduce moves
 half the bytes, and the next norm's pass adds the sum into the f32 residual stream (yah_add_rmsnorm). The residual
 stream h is f32 [M][hidden] on every rank in both.
 The reference normalises every layer input (docs/architecture.md:68); the fixed gain keeps silu(gate) * up inside
@@ -66,6 +73,15 @@ def qkv_rows(n_q: int, n_kv: int, head_dim: int, parts: int, part: int) -> list:
 def k_window(K: int, parts: int, part: int) -> tuple:
     """(k0, k1) of the row-parallel K window of `part`, in whole 256-value super-blocks."""
     return even_range(K, parts, part, align=256)
+
+
+def token_slice(M: int, parts: int, part: int) -> tuple:
+    """[lo, hi) of the tokens whose residual stream rank `part` owns in the fused mode (equal slices of a multiple of
+    16 tokens: the row-parallel GEMM writes 16-token units, so a unit never straddles two owners)."""
+    if M % parts or (M // parts) % 16:
+        raise ValueError(f"{M} tokens do not split into {parts} slices of a multiple of 16")
+    ms = M // parts
+    return part * ms, (part + 1) * ms
 
 
 def take_rows(w: np.ndarray, ranges: list) -> np.ndarray:
@@ -196,9 +212,33 @@ class Comm:
     def allreduce_f32(self, ptr: int, count: int, stream=None):
         check(lib().yah_tp_allreduce_f32(self.handle, ptr, count, stream))
 
+    def allgather_f32(self, send: int, recv: int, count: int, stream=None):
+        check(lib().yah_tp_allgather_f32(self.handle, send, recv, count, stream))
+
     def close(self):
         if self.handle:
             check(lib().yah_tp_destroy(self.handle))
+            self.handle = None
+
+
+class Peers:
+    """Device buffers of every rank (yah_tp_peers_*: CUDA IPC mappings exchanged over the communicator).
+    Collective: every rank creates it with the same number of buffers."""
+
+    def __init__(self, comm: Comm, bufs: list, stream=None):
+        arr = (ctypes.c_void_p * len(bufs))(*[b.ptr for b in bufs])
+        h = ctypes.c_void_p()
+        check(lib().yah_tp_peers_create(comm.handle, arr, len(bufs), stream, ctypes.byref(h)))
+        self.handle = h.value
+
+    def ptr(self, rank: int, buf: int) -> int:
+        p = ctypes.c_void_p()
+        check(lib().yah_tp_peers_ptr(self.handle, rank, buf, ctypes.byref(p)))
+        return p.value
+
+    def close(self):
+        if self.handle:
+            check(lib().yah_tp_peers_destroy(self.handle))
             self.handle = None
 
 
@@ -216,10 +256,13 @@ class LlamaStack:
                  mode: str = "parity"):
         if chunks < 1 or M % chunks:
             raise ValueError(f"{M} tokens do not split into {chunks} chunks")
-        if mode not in ("parity", "speed"):
-            raise ValueError(f"mode {mode!r}: parity (f32 partial sums) or speed (f16 partial sums)")
-        if mode == "speed" and chunks != 1:
-            raise ValueError("the speed mode runs unchunked")
+        if mode not in ("parity", "speed", "fused"):
+            raise ValueError(f"mode {mode!r}: parity (f32 partial sums), speed (f16 partial sums) or fused (f32 "
+                             "partial sums reduced over peer memory)")
+        if mode != "parity" and chunks != 1:
+            raise ValueError(f"the {mode} mode runs unchunked")
+        if mode == "fused":
+            token_slice(M, comm.nranks, comm.rank)  # raises when M does not split
         self.dev, self.comm, self.shape, self.M, self.chunks, self.mode = dev, comm, shape, M, chunks, mode
         p = comm.nranks
         self.q_r = shape.n_q * shape.head_dim // p
@@ -238,11 +281,22 @@ class LlamaStack:
             self.comm_stream = Stream()
             self.ev_gemm = [Event() for _ in range(chunks)]
             self.ev_red = [Event() for _ in range(chunks)]
+        self.peers = None
+        if mode == "fused":
+            self.ms = M // p
+            self.recv = dev.empty(M * H * 4)             # [p][M/p][H] f32: slot q holds rank q's partials
+            self.hs = dev.empty(self.ms * H * 4)         # this rank's slice of the residual stream
+            self.flags = dev.empty(2 * 32 * 4).fill(0)   # [2][32] int epochs: 0 partials landed, 1 activations
+            dev.synchronize()                            # zeroed before any rank can signal into it
+            self.peers = Peers(comm, [self.recv, self.xn, self.flags])
+            self.ep_r = self.ep_x = 0
 
     @property
     def launches_per_forward(self) -> int:
         """Library kernel launches per forward pass (2 norms + 5 linears per layer and token chunk; the unchunked
-        forward adds the final add)."""
+        forward adds the final add; the fused mode adds 8 signals / waits per layer and its first norm)."""
+        if self.mode == "fused":
+            return 15 * self.shape.layers + 1
         return 7 * self.shape.layers * self.chunks + (1 if self.part is not None else 0)
 
     def forward(self, h: DeviceBuffer, stream=None):
@@ -251,6 +305,8 @@ class LlamaStack:
             return self._forward_chunked(h, stream)
         if self.mode == "speed":
             return self._forward_partials(h, stream)
+        if self.mode == "fused":
+            return self._forward_fused(h, stream)
         return self._forward_residual_epilogue(h, stream)
 
     def _forward_residual_epilogue(self, h: DeviceBuffer, stream=None):
@@ -321,6 +377,53 @@ class LlamaStack:
         if pending:
             check(L.yah_add_rmsnorm(h.ptr, H, part, pdt, H, M, H, NORM_EPS, NORM_GAIN, None, 0, stream))
 
+    def _forward_fused(self, h: DeviceBuffer, stream=None):
+        """The fused mode (module docstring): h (f32 [M][hidden], identical on every rank) is updated in place; the
+        layers keep this rank's token slice of it and the last step gathers the slices back."""
+        L, M, H, fmt = lib(), self.M, self.shape.hidden, self.shape.fmt
+        c, pe, ms, rank, p = self.comm.handle, self.peers.handle, self.ms, self.comm.rank, self.comm.nranks
+        RECV, XN, FLAGS = 0, 1, 2
+        hs, recv = self.hs.ptr, self.recv.ptr
+        check(L.yah_memcpy_d2d(hs, h.ptr + rank * ms * H * 4, ms * H * 4, stream))
+
+        def reduce_norm(add: bool, norm: bool):
+            check(L.yah_tp_reduce_norm(pe, hs, H, ms, H, recv if add else None, p if add else 0, ms * H, H, NORM_EPS,
+                                       NORM_GAIN, XN if norm else -1, rank * ms, H, stream))
+
+        def exchange_partials():  # every rank's scatter into this rank's slots has landed
+            self.ep_r += 1
+            check(L.yah_tp_signal(pe, FLAGS, rank, self.ep_r, stream))
+            check(L.yah_tp_wait(pe, FLAGS, 0, p, self.ep_r, stream))
+
+        def publish_activations():  # every rank's normalised slice is in this rank's xn
+            self.ep_x += 1
+            check(L.yah_tp_signal(pe, FLAGS, 32 + rank, self.ep_x, stream))
+            check(L.yah_tp_wait(pe, FLAGS, 32, p, self.ep_x, stream))
+
+        reduce_norm(False, True)
+        publish_activations()
+        n = len(self.w)
+        for i, w in enumerate(self.w):
+            check(L.yah_tp_linear_col(c, w["qkv"].ptr, fmt, self.qkv_r, H, self.row_bytes["qkv"], self.xn.ptr, M, H,
+                                      self.qkv.ptr, F16, self.qkv_r, EPI_STORE, None, 0, stream))
+            check(L.yah_tp_linear_row_scatter(pe, w["o"].ptr, fmt, H, self.q_r, self.row_bytes["o"], 0, self.qkv.ptr,
+                                              M, self.qkv_r, RECV, stream))
+            exchange_partials()
+            reduce_norm(True, True)
+            publish_activations()
+            check(L.yah_tp_linear_col(c, w["gate"].ptr, fmt, self.ff_r, H, self.row_bytes["gate"], self.xn.ptr, M, H,
+                                      self.g.ptr, F32, self.ff_r, EPI_STORE, None, 0, stream))
+            check(L.yah_tp_linear_col(c, w["up"].ptr, fmt, self.ff_r, H, self.row_bytes["up"], self.xn.ptr, M, H,
+                                      self.act.ptr, F16, self.ff_r, EPI_SWIGLU, self.g.ptr, self.ff_r, stream))
+            check(L.yah_tp_linear_row_scatter(pe, w["down"].ptr, fmt, H, self.ff_r, self.row_bytes["down"], 0,
+                                              self.act.ptr, M, self.ff_r, RECV, stream))
+            exchange_partials()
+            last = i == n - 1
+            reduce_norm(True, not last)
+            if not last:
+                publish_activations()
+        self.comm.allgather_f32(hs, h.ptr, ms * H, stream)
+
     def _forward_chunked(self, h: DeviceBuffer, stream):
         L, s, H, fmt, C = lib(), self.shape, self.shape.hidden, self.shape.fmt, self.chunks
         Mc = self.M // C
@@ -365,3 +468,7 @@ class LlamaStack:
             for e in self.ev_gemm + self.ev_red:
                 e.close()
             self.comm_stream.close()
+        if self.peers is not None:
+            self.peers.close()
+            for b in (self.recv, self.hs, self.flags):
+                b.close()
