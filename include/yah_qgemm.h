@@ -381,6 +381,8 @@ int yah_tp_peers_ptr(const yah_tp_peers* pe, int rank, int buf, void** ptr);
 int yah_tp_peers_destroy(yah_tp_peers* pe);
 int yah_tp_signal(const yah_tp_peers* pe, int flag_buf, int slot, int value, void* stream);
 int yah_tp_wait(const yah_tp_peers* pe, int flag_buf, int first, int count, int value, void* stream);
+/* yah_tp_signal of slot base + rank followed by yah_tp_wait on [base, base + nranks), in one launch. */
+int yah_tp_barrier(const yah_tp_peers* pe, int flag_buf, int base, int value, void* stream);
 int yah_tp_reduce_norm(const yah_tp_peers* pe, float* h, int64_t ldh, int64_t rows, int64_t H, const float* parts,
                        int nparts, int64_t part_stride, int64_t ldp, float eps, float gain, int out_buf,
                        int64_t out_row0, int64_t ldo, void* stream);

@@ -218,6 +218,9 @@ def test_peer_wait_runs_out(pkg, dev, comm):
     dev.synchronize()
     assert dev.status_word() == 4
     assert flags.download(np.int32, (64,))[3] == 5
+    pkg._lib.check(L.yah_tp_barrier(pe.handle, 0, 8, 9, None))         # signal slot 8 + rank := 9, then wait on it
+    dev.synchronize()
+    assert dev.status_word() == 0 and flags.download(np.int32, (64,))[8] == 9
     pe.close()
     assert dev.status_word() == 0
 

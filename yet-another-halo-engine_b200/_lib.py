@@ -93,6 +93,7 @@ SYMBOLS = {
     "yah_tp_peers_destroy": (c_int, [c_vp]),
     "yah_tp_signal": (c_int, [c_vp, c_int, c_int, c_int, c_vp]),
     "yah_tp_wait": (c_int, [c_vp, c_int, c_int, c_int, c_int, c_vp]),
+    "yah_tp_barrier": (c_int, [c_vp, c_int, c_int, c_int, c_vp]),
     "yah_tp_reduce_norm": (c_int, [c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_int, c_i64, c_i64, c_f, c_f, c_int,
                                    c_i64, c_i64, c_vp]),
     "yah_tp_linear_row_scatter": (c_int, [c_vp, c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_int,

@@ -156,6 +156,32 @@ __global__ void tp_wait_kernel(const int* flags, int count, int value, int* stat
   }
 }
 
+// Signal and wait in one launch: thread i < n stores value into slot (base + rank) of rank i's flags (release,
+// system scope), then waits, bounded as tp_wait_kernel, until this rank's flag base + i is >= value.
+__global__ void tp_barrier_kernel(PtrTable flags, int n, int base, int rank, int value, const int* own, int* status,
+                                  unsigned long long budget_ns) {
+  const int i = threadIdx.x;
+  if (i >= n) return;
+  int* f = static_cast<int*>(flags.p[i]) + base + rank;
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
+  asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(f), "r"(value) : "memory");
+  const int* w = own + base + i;
+  const unsigned long long t0 = global_ns();
+  for (uint32_t it = 0;; ++it) {
+    int v;
+    asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(w) : "memory");
+    if (v >= value) return;
+    if ((it & 255) == 255) {
+      if (*(volatile int*)status != 0) return;
+      if (global_ns() - t0 > budget_ns) {
+        set_status(status, kStatusTimeoutPeer);
+        return;
+      }
+      __nanosleep(64);
+    }
+  }
+}
+
 // One row per CTA of this rank's token slice: h += parts[0] + parts[1] + ... (in slot order; the parts are the
 // other ranks' writes, read through L2), then (NORM) out = f16(h * gain / sqrt(mean(h^2) + eps)) written to row
 // out_row0 + row of every rank's output buffer.
@@ -526,6 +552,20 @@ int yah_tp_linear_row_scatter(const yah_tp_peers* pe, const void* w_shard, int g
   for (int o = 0; o < P; ++o)  // rank o's buffer, slot of this rank: [P][ms][N] f32
     ys[o] = static_cast<char*>(pe->ptr[recv_buf][o]) + (size_t)pe->rank * ms * N * sizeof(float);
   return yah_qgemm_sliced(w_shard, ggml_type, N, K_local, w_row_stride, kb_off, x, M, ldx, ys, P, ms, N, stream);
+}
+
+int yah_tp_barrier(const yah_tp_peers* pe, int flag_buf, int base, int value, void* stream) {
+  if (!pe || flag_buf < 0 || flag_buf >= pe->nbufs || base < 0) return yah::set_error(YAH_ERR_ARG, "bad barrier");
+  int* status = nullptr;
+  const int rc = yah::device_status_word(&status);
+  if (rc) return rc;
+  yah::PtrTable t{};
+  for (int r = 0; r < pe->nranks; ++r) t.p[r] = pe->ptr[flag_buf][r];
+  const int* own = static_cast<const int*>(pe->ptr[flag_buf][pe->rank]);
+  yah::tp_barrier_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(t, pe->nranks, base, pe->rank, value, own,
+                                                                          status, yah::kPeerWaitNs);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? YAH_OK : yah::set_error(YAH_ERR_CUDA, "barrier launch: %s", cudaGetErrorString(e));
 }
 
 }  // extern "C"

@@ -24,7 +24,7 @@ slices, rank r owning slice r of the residual stream; each rank's row-parallel G
 token straight into the owner's memory (yah_tp_linear_row_scatter, stores over NVLink while the GEMM runs), the
 owner adds the p slots in rank order into its residual slice and writes the RMSNorm of it (f16) into every rank's
 activation buffer (yah_tp_reduce_norm: the all-gather), with flags in each rank's memory ordering the ranks
-(yah_tp_signal / yah_tp_wait, bounded). Traffic per row-parallel linear and rank: (p - 1) / p of the f32 partial
+(yah_tp_barrier: a signal and a bounded wait in one launch). Traffic per row-parallel linear and rank: (p - 1) / p of the f32 partial
 out and of the f16 activations back, against 2 (p - 1) / p of the f32 partial for the allreduce, and the scatter
 overlaps its GEMM. Speed mode: every rank's GEMM stores f16 partials (no residual read), the f16 allreduce moves
 half the bytes, and the next norm's pass adds the sum into the f32 residual stream (yah_add_rmsnorm). The residual
@@ -294,9 +294,9 @@ class LlamaStack:
     @property
     def launches_per_forward(self) -> int:
         """Library kernel launches per forward pass (2 norms + 5 linears per layer and token chunk; the unchunked
-        forward adds the final add; the fused mode adds 8 signals / waits per layer and its first norm)."""
+        forward adds the final add; the fused mode adds 4 flag barriers per layer and its first norm)."""
         if self.mode == "fused":
-            return 15 * self.shape.layers + 1
+            return 11 * self.shape.layers + 1
         return 7 * self.shape.layers * self.chunks + (1 if self.part is not None else 0)
 
     def forward(self, h: DeviceBuffer, stream=None):
@@ -392,13 +392,11 @@ class LlamaStack:
 
         def exchange_partials():  # every rank's scatter into this rank's slots has landed
             self.ep_r += 1
-            check(L.yah_tp_signal(pe, FLAGS, rank, self.ep_r, stream))
-            check(L.yah_tp_wait(pe, FLAGS, 0, p, self.ep_r, stream))
+            check(L.yah_tp_barrier(pe, FLAGS, 0, self.ep_r, stream))
 
         def publish_activations():  # every rank's normalised slice is in this rank's xn
             self.ep_x += 1
-            check(L.yah_tp_signal(pe, FLAGS, 32 + rank, self.ep_x, stream))
-            check(L.yah_tp_wait(pe, FLAGS, 32, p, self.ep_x, stream))
+            check(L.yah_tp_barrier(pe, FLAGS, 32, self.ep_x, stream))
 
         reduce_norm(False, True)
         publish_activations()
