@@ -9,10 +9,12 @@ the same line:
   decode    BASELINE config 3 decode GEMV (Q4_K 4096 x 14336, M = 1 / 8 / 32 tokens): HBM GB/s and its fraction of
             the measured copy bandwidth, timed like the GEMM (N = 1 only).
   tp_stack  BASELINE config 4, the Llama-shaped Q4_K linear stack (32 layers, hidden 4096, QKV 6144, FF 14336,
-            4096 tokens) tensor-parallel over the N GPUs in parity mode on the BASELINE weight distribution:
-            column-parallel QKV / gate / up, row-parallel o_proj / down each followed by one ncclAllReduce of f32
-            partials through the library's own NCCL communicator (its rank count is reported); with the share of
-            the forward spent in the allreduces and the per-site GEMM rates at the shard shapes.
+            4096 tokens) tensor-parallel over the N GPUs on the BASELINE weight distribution with f32 partial sums:
+            column-parallel QKV / gate / up, row-parallel o_proj / down, timed in the parity mode (one ncclAllReduce
+            of the f32 partials through the library's own NCCL communicator, whose rank count is reported) and in the
+            fused mode (the row-parallel GEMM writes its partials into the token-slice owners' memory over NVLink;
+            reduce + RMSNorm + all-gather by the owner); the faster mode is the record's figure, both are listed,
+            with the allreduces' time alone and the per-site GEMM rates at the shard shapes.
   lm_head   BASELINE config 5's decode lm head (Q6_K 128256 x 4096, M = 1 and 32), vocab-column sharded over the
             N GPUs (16032 rows per rank at N = 8, ragged last row tiles): whole-job GB/s, max over ranks.
   sustained the config-2 GEMM over >= 2000 back-to-back launches (about half a second) with the SM clocks of that
