@@ -120,6 +120,9 @@ struct KParams {
   int tma_store;        // 1: the output is written with TMA stores through shared memory (tmap_y is valid)
   int aux_tma;          // 1: the epilogue's aux operand is prefetched by TMA (tmap_aux is valid)
   int help;             // 1: the dequant warps help drain the accumulator (drain_share; one chunk per unit)
+  int whole;            // 1: the schedule hands out whole tiles (see Sched)
+  int64_t total_tiles;  // row tiles x chunks (split K) x token tiles of BN
+  int tpr;              // token tiles of BN per row tile
   int nsl;              // > 0: token slices (output token t at ysl[t / slice_rows] + (t % slice_rows) * ldy)
   int64_t slice_rows;
   void* ysl[kMaxSlices];
@@ -160,17 +163,31 @@ struct AuxCfg {
 // The persistent schedule: CTA b owns units [b * total / G, (b + 1) * total / G) of the (row tile, chunk, 16-token
 // unit) space, walked row tile by row tile, at most BN / 16 units per tile. kp is the accumulation chunk under
 // split K (0 otherwise).
+// Whole tiles instead (p.whole, chosen on the host when it needs fewer K loops on the busiest CTA): CTA b owns tiles
+// [b * T / G, (b + 1) * T / G) of the (row tile, chunk, BN-token tile) space. A tile's K loop costs about the same
+// at any token count up to BN (per-stage issue time, measured), so a range that ends inside a row tile pays a second
+// K loop for its last units; with few tiles per CTA (small shards) that doubled the busiest CTAs' time.
 template <int BN>
 struct Sched {
   int64_t u, end;
-  int upr, M, nsplit;
-  __device__ Sched(const KParams& p) : upr(p.upr), M(p.M), nsplit(p.nsplit) {
+  int upr, M, nsplit, whole, tpr;
+  __device__ Sched(const KParams& p) : upr(p.upr), M(p.M), nsplit(p.nsplit), whole(p.whole), tpr(p.tpr) {
     const int64_t G = gridDim.x / p.ncta, b = blockIdx.x / p.ncta;  // a pair shares one range
-    u = b * p.total_units / G;
-    end = (b + 1) * p.total_units / G;
+    const int64_t total = whole ? p.total_tiles : p.total_units;
+    u = b * total / G;
+    end = (b + 1) * total / G;
   }
   __device__ bool next(int& rt, int& kp, int& t0, int& nt) {
     if (u >= end) return false;
+    if (whole) {
+      const int vt = (int)(u / tpr);
+      rt = vt / nsplit;
+      kp = vt - rt * nsplit;
+      t0 = (int)(u % tpr) * BN;
+      nt = min(BN, M - t0);
+      ++u;
+      return true;
+    }
     const int vt = (int)(u / upr);
     rt = vt / nsplit;
     kp = vt - rt * nsplit;
@@ -811,6 +828,26 @@ cudaError_t launch_t(const QGemmArgs& a, cudaStream_t stream) {
   const int64_t rtiles = (a.N + kTileRows * p.ncta - 1) / (kTileRows * p.ncta);
   p.total_units = rtiles * p.nsplit * p.upr;
   const int grid = qgemm_grid(a);
+  // whole tiles when that gives the busiest CTA (pair) fewer K loops than the equal unit ranges
+  p.tpr = (int)((a.M + BN - 1) / BN);
+  p.total_tiles = rtiles * p.nsplit * p.tpr;
+  {
+    const int64_t G = grid / p.ncta, upt = BN / 16;
+    int64_t max_units = 0;
+    for (int64_t b = 0; b < G; ++b) {  // K loops of CTA b under the unit ranges (Sched::next without whole)
+      int64_t u = b * p.total_units / G, end = (b + 1) * p.total_units / G, loops = 0;
+      while (u < end) {
+        const int64_t tu = u % p.upr;
+        int64_t nu = upt < p.upr - tu ? upt : p.upr - tu;
+        if (nu > end - u) nu = end - u;
+        u += nu;
+        ++loops;
+      }
+      if (loops > max_units) max_units = loops;
+    }
+    const int64_t max_whole = (p.total_tiles + G - 1) / G;
+    p.whole = max_whole < max_units ? 1 : 0;
+  }
   auto kern = qgemm_tc_kernel<T, BN, NACC, EPI, OUT_F16, PAIR, SPLIT>;
   const int smem_bytes = S::kAlloc > kMinSmem ? S::kAlloc : kMinSmem;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
