@@ -145,13 +145,17 @@ struct Smem {
   static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-byte alignment of the base
 };
 
+// Tokens the epilogue drains per step: 16 for f16 outputs, 8 for f32, and 8 for the swiglu epilogue (its gate
+// values and silu on 16 tokens per step spilled registers under the 80-register cap of 736 threads).
+__host__ __device__ constexpr int epi_chunk(int epi, bool out_f16) { return out_f16 && epi != kEpiSwiglu ? 16 : 8; }
+
 // The epilogue's aux operand (residual, or the swiglu gate; f32 [M][ldaux]) is prefetched by TMA into a ring of
 // kDepth slots of 128 rows x CH tokens, ahead of the accumulator it is combined with, so the epilogue does not wait
 // one global round trip per CH tokens. The ring takes what shared memory the stages leave (4, 2 or no slots).
 constexpr int kSmemLimit = 227 * 1024;
 template <int T, int XR, int EPI, bool OUT_F16>
 struct AuxCfg {
-  static constexpr int kCH = OUT_F16 ? 16 : 8;
+  static constexpr int kCH = epi_chunk(EPI, OUT_F16);
   static constexpr int kSlot = kCH * 128 * 4;
   static constexpr int kBase = Smem<T, XR, 0>::kAlloc;
   static constexpr int kDepth = (EPI == kEpiStore || EPI == kEpiFfn) ? 0
@@ -526,7 +530,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Accumulator columns are drained CH at a time (CH = 16 f16 / 8 f32 tokens); the final values go to a
     // [CH tokens][128 rows] shared-memory buffer (double-buffered) written out by one TMA store, or, when the
     // output layout does not allow TMA, by direct stores.
-    constexpr int CH = OUT_F16 ? 16 : 8;
+    constexpr int CH = epi_chunk(EPI, OUT_F16);
     constexpr int ES = OUT_F16 ? 2 : 4;
     const int q = warp & 3;
     const int rloc = q * 32 + lane;
@@ -783,7 +787,7 @@ cudaError_t launch_t(const QGemmArgs& a, cudaStream_t stream) {
   if (tma_store) {
     cuuint64_t dims[2] = {(cuuint64_t)a.N, (cuuint64_t)a.M};
     cuuint64_t strides[1] = {(cuuint64_t)(a.ldy * esz)};
-    cuuint32_t box[2] = {(cuuint32_t)kTileRows, (cuuint32_t)(a.y_f16 ? 16 : 8)};
+    cuuint32_t box[2] = {(cuuint32_t)kTileRows, (cuuint32_t)epi_chunk(EPI, OUT_F16)};
     cuuint32_t es[2] = {1, 1};
     if (enc(&my, a.y_f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, a.y, dims, strides,
             box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
