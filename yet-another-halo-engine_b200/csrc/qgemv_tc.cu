@@ -26,8 +26,9 @@
 //                 and hand D1 to the epilogue;
 //   warps 18-21   epilogue: per super-block tcgen05.ld of D1, acc += d_s * D1; per tile acc -= D2, the cluster
 //                 reduction, the kind (plain / resid / swiglu) and the stores.
-// At the start (after griddepcontrol.wait) the decode and epilogue warps form the group sums of this CTA's K range
-// once (Xhi, Xlo in f16, 4 per group: Xhi Xlo Xhi Xlo against the A side's hi hi lo lo) in shared memory.
+// The group sums of this CTA's K range (Xhi, Xlo in f16, 4 per group: Xhi Xlo Xhi Xlo against the A side's hi hi lo
+// lo) are formed once, on the first tile, by the decode warps of each super-block from its activation stage in shared
+// memory (thread = token row x group), so no warp reads the activations from global memory.
 // Work split: the K range is cut into KS equal parts (thread-block clusters of KS = 1, 2 or 4 CTAs, CTA rank = part)
 // and the rows into tiles of RT rows; persistent clusters walk the tiles. The KS partial sums of a tile meet in
 // distributed shared memory: every CTA parks its [M][RT] partial, and CTA r adds the KS partials of its RT / KS rows
@@ -78,8 +79,8 @@ struct TcCfg {
   static constexpr int kExOff = kParOff + kTcNP * 128 * 4;
   static constexpr int kBarOff = kExOff + TP * 128 * 4;
   // wfull/wempty [NSW], xfull/sbempty/afull [NA], dfull/dempty [ND], d2full/d2empty [2], pfull/pempty [NP],
-  // b2ready, exfull, exempty, drain
-  static constexpr int kNumBars = 2 * kNSW + 3 * kNA + 2 * kND + 4 + 2 * kTcNP + 4;
+  // exfull, exempty, drain
+  static constexpr int kNumBars = 2 * kNSW + 3 * kNA + 2 * kND + 4 + 2 * kTcNP + 3;
   static constexpr int kSlotOff = kBarOff + kNumBars * 8;
   static constexpr int kBytes = kSlotOff + 16;
   static constexpr int kAlloc = kBytes + 1024;
@@ -221,8 +222,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint64_t* d2empty = d2full + 2;
   uint64_t* pfull = d2empty + 2;
   uint64_t* pempty = pfull + kTcNP;
-  uint64_t* b2ready = pempty + kTcNP;
-  uint64_t* exfull = b2ready + 1;
+  uint64_t* exfull = pempty + kTcNP;
   uint64_t* exempty = exfull + 1;
   uint64_t* drain = exempty + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kSlotOff);
@@ -260,7 +260,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mbar_init(&pfull[i], 4);
       mbar_init(&pempty[i], 4);
     }
-    mbar_init(b2ready, 20);
     mbar_init(exfull, 4 * ks);
     mbar_init(exempty, 4 * ks);
     mbar_init(drain, 1);
@@ -319,7 +318,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const uint64_t bx0 = sdesc_sw128(smem_u32(smem + C::kXOff));
       const uint64_t bb0 = sdesc_sw128(smem_u32(smem + C::kB2Off));
       uint32_t i = 0, tc = 0;
-      bool ok = true, b2 = false;
+      bool ok = true;
       for (int tile = cid; ok && tile < p.tiles; tile += G, ++tc) {
         const uint32_t r2 = tc & 1;
         if (!mbar_wait(&d2empty[r2], ((tc >> 1) & 1) ^ 1, p.status, kStatusTimeoutEmpty)) { ok = false; break; }
@@ -329,10 +328,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           if (!mbar_wait(&afull[as], (i / NA) & 1, p.status, kStatusTimeoutFull)) { ok = false; break; }
           if (!mbar_wait(&xfull[as], (i / NA) & 1, p.status, kStatusTimeoutFull)) { ok = false; break; }
           if (!mbar_wait(&dempty[ds], ((i / ND) & 1) ^ 1, p.status, kStatusTimeoutEmpty)) { ok = false; break; }
-          if (!b2) {
-            if (!mbar_wait(b2ready, 0, p.status, kStatusTimeoutFull)) { ok = false; break; }
-            b2 = true;
-          }
           tc_fence_after();
           const uint32_t a = tmem + as * kTcACols;
           const uint32_t dt = tmem + C::kD1Col + ds * TP;
@@ -354,37 +349,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mbar_wait(drain, 0, p.status, kStatusTimeoutDrain, false);
     }
   } else if (warp < kTcWarpEpi0 + 4) {
-    // ------------------------------------------------------------------ group sums of this CTA's K range
-    // (decode and epilogue warps together, once): entry 4g + e of super-block j's 32 entries is Xhi, Xlo, Xhi, Xlo.
-    griddep_wait();
-    {
-      const int b = threadIdx.x - kTcWarpDq0 * 32;  // 0..639
-      const int total = sr * p.M * 8;
-      for (int e = b; e < total; e += 640) {
-        const int g = e & 7, t = (e >> 3) % p.M, j = (e >> 3) / p.M;
-        const uint4* src =
-            reinterpret_cast<const uint4*>(p.x + (int64_t)t * p.ldx + (int64_t)(sbx0 + j) * 256 + 32 * g);
-        float s = 0.f;
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const uint4 v = __ldg(src + u);
-          const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            s += h2f_bits(w[k] & 0xFFFFu);
-            s += h2f_bits(w[k] >> 16);
-          }
-        }
-        const __half hi = __float2half_rn(s);
-        const __half lo = __float2half_rn(s - __half2float(hi));
-        const uint32_t pair = (uint32_t)__half_as_ushort(hi) | ((uint32_t)__half_as_ushort(lo) << 16);
-        uint8_t* tile = smem + C::kB2Off + (j >> 1) * C::kB2Tile;
-        *reinterpret_cast<uint2*>(tile + sw128_off(t, 32 * (j & 1) + 4 * g)) = make_uint2(pair, pair);
-      }
-      fence_proxy_async();  // the MMA (async proxy) reads these
-      __syncwarp();
-      if (lane == 0) mbar_arrive(b2ready);
-    }
     if (warp < kTcWarpEpi0) {
       // ---------------------------------------------------------------- decode
       // two groups of 8 warps take alternate super-blocks; in a group, warp (lane quarter q, half h) decodes
@@ -392,6 +356,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const int q = warp & 3, par = (warp - kTcWarpDq0) >> 3, h = ((warp - kTcWarpDq0) >> 2) & 1;
       const int r = q * 32 + lane;
       const uint32_t tl = tmem + ((uint32_t)(q * 32) << 16);
+      const int gt = (((warp - kTcWarpDq0) & 7) * 32 + lane) >> 3, gg = lane & 7;  // group-sum entry: token, group
       uint32_t i = 0;
       bool ok = true;
       for (int tile = cid; ok && tile < p.tiles; tile += G) {
@@ -402,6 +367,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           const uint32_t as = i % NA;
           if (!warp_wait(&wfull[ws], wph, p.status, kStatusTimeoutFull)) { ok = false; break; }
           if (!warp_wait(&sbempty[as], ((i / NA) & 1) ^ 1, p.status, kStatusTimeoutEmpty)) { ok = false; break; }
+          const bool sums = tile == cid;  // the first tile forms the group sums of super-block j
+          if (sums && !warp_wait(&xfull[as], (i / NA) & 1, p.status, kStatusTimeoutFull)) { ok = false; break; }
           tc_fence_after();  // the MMAs that read this A buffer are complete: order the stores after them
           // Every lane decodes and stores (the stores are warp-aligned): rows past the tile read the stage's
           // unused rows, and the epilogue never reads their results.
@@ -409,6 +376,31 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           const float d = q4k_tc_decode_half(smem_u32(smem + ws * kTcWStage) + r * p.pitch + sbw * 144, h, ta, tm);
           __syncwarp();
           if (lane == 0) mbar_arrive(&wempty[ws]);  // this warp's only read of the stage
+          if (sums) {
+            // X of group gg, token row gt: the group's 32 activations are 4 16-byte units of the 128-byte-swizzled
+            // row gt of 64-K chunk gg / 2 (rows past M are zero); written as (Xhi, Xlo, Xhi, Xlo) into the group-sum
+            // tile (async proxy: fenced before the arrive below)
+            if (gt < TP) {
+              const uint32_t xrow = smem_u32(smem + C::kXOff + as * C::kXStage) + (gg >> 1) * (TP * 128) + gt * 128;
+              float part[4];
+#pragma unroll
+              for (int u = 0; u < 4; ++u) {
+                const uint4 v = lds128(xrow + ((((gg & 1) * 4 + u) ^ gt) & 7) * 16);
+                const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+                float a = 0.f;
+#pragma unroll
+                for (int k = 0; k < 4; ++k) a += h2f_bits(w[k] & 0xFFFFu) + h2f_bits(w[k] >> 16);
+                part[u] = a;
+              }
+              const float sx = (part[0] + part[1]) + (part[2] + part[3]);
+              const __half hi = __float2half_rn(sx);
+              const __half lo = __float2half_rn(sx - __half2float(hi));
+              const uint32_t pair = (uint32_t)__half_as_ushort(hi) | ((uint32_t)__half_as_ushort(lo) << 16);
+              uint8_t* b2 = smem + C::kB2Off + (j >> 1) * C::kB2Tile;
+              *reinterpret_cast<uint2*>(b2 + sw128_off(gt, 32 * (j & 1) + 4 * gg)) = make_uint2(pair, pair);
+            }
+            fence_proxy_async();  // the MMA (async proxy) reads these
+          }
           tmem_wait_st();
           tc_fence_before();
           __syncwarp();
@@ -424,6 +416,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
     } else {
       // ---------------------------------------------------------------- epilogue
+      griddep_wait();  // outputs are written (and aux read) only after the preceding kernel has completed
       const int q = warp & 3;
       const int r = q * 32 + lane;
       const int et = threadIdx.x - kTcWarpEpi0 * 32;  // 0..127
