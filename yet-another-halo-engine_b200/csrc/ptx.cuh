@@ -118,6 +118,11 @@ __device__ __forceinline__ float ld_cluster_f32(uint32_t cluster_addr) {
   return v;
 }
 
+// 32-bit store into the shared memory of a CTA of this cluster (address from mapa_shared).
+__device__ __forceinline__ void st_cluster_f32(uint32_t cluster_addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(cluster_addr), "f"(v) : "memory");
+}
+
 __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(

@@ -31,8 +31,8 @@
 // memory (thread = token row x group), so no warp reads the activations from global memory.
 // Work split: the K range is cut into KS equal parts (thread-block clusters of KS = 1, 2 or 4 CTAs, CTA rank = part)
 // and the rows into tiles of RT rows; persistent clusters walk the tiles. The KS partial sums of a tile meet in
-// distributed shared memory: every CTA parks its [M][RT] partial, and CTA r adds the KS partials of its RT / KS rows
-// in rank order (deterministic) and stores them. No global scratch.
+// distributed shared memory: every CTA stores its partial of each row into the shared memory of the CTA that owns
+// the row (RT / KS rows per CTA), which adds the KS partials in rank order (deterministic) and stores them. No global scratch.
 // Launch overlap: programmatic dependent launch as in the other GEMV (weights stream before griddepcontrol.wait;
 // activations are read and outputs written after it).
 // Every mbarrier wait is bounded (ptx.cuh); a wait that runs out records a status code and the CTA leaves its
@@ -477,26 +477,29 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           }
           continue;
         }
-        // cluster reduction: park the partial [M][128], then add the KS partials of this CTA's row slice
+        // cluster reduction: the rows are split in rank order, `per` rows per CTA; every CTA stores its partial sum
+        // of each row into the owner CTA's shared memory (slot [rank][t][row - owner's first row]; remote stores,
+        // so nothing waits on a remote load), and the owner adds the KS slots of its rows in rank order (deterministic)
         if (!warp_wait_cluster(exempty, (tc & 1) ^ 1, p.status, kStatusTimeoutEmpty)) { ok = false; break; }
+        const int per = (p.rt + ks - 1) / ks;
+        if (r < p.rt) {  // owner o = r / per < ks
+          const int o = r / per;
+          const uint32_t dst = mapa_shared(ex_local + (uint32_t)((int)rank * TP * per + r - o * per) * 4, (uint32_t)o);
 #pragma unroll
-        for (int t = 0; t < TP; ++t)
-          if (t < p.M) ex[t * 128 + r] = acc[t];
+          for (int t = 0; t < TP; ++t)
+            if (t < p.M) st_cluster_f32(dst + (uint32_t)(t * per) * 4, acc[t]);
+        }
         __syncwarp();
         if (lane == 0)
           for (int c = 0; c < ks; ++c) mbar_arrive_cluster_release(mapa_shared(smem_u32(exfull), (uint32_t)c));
         if (!warp_wait_cluster(exfull, tc & 1, p.status, kStatusTimeoutFull)) { ok = false; break; }
-        const int per = (p.rt + ks - 1) / ks;
         const int r0 = (int)rank * per, r1 = min(p.rt, r0 + per);
         const int nr = r1 - r0;
-        if (nr > 0) {
-          for (int e = et; e < nr * p.M; e += 128) {
-            const int t = e / nr, rr = r0 + e % nr;
-            const uint32_t off = ex_local + (uint32_t)(t * 128 + rr) * 4;
-            float s = ld_cluster_f32(mapa_shared(off, 0));
-            for (int c = 1; c < ks; ++c) s = s + ld_cluster_f32(mapa_shared(off, (uint32_t)c));
-            if (row0 + rr < p.N) tc_store<EPI, OUT_F16>(p, t, row0 + rr, s);
-          }
+        for (int e = et; e < nr * p.M; e += 128) {
+          const int t = e / nr, rr = e % nr;
+          float s = ex[t * per + rr];
+          for (int c = 1; c < ks; ++c) s = s + ex[(c * TP + t) * per + rr];
+          if (row0 + r0 + rr < p.N) tc_store<EPI, OUT_F16>(p, t, row0 + r0 + rr, s);
         }
         __syncwarp();
         if (lane == 0)
