@@ -13,18 +13,18 @@
 //
 // B200 design. Weight rows are the MMA's M side (128 TMEM lanes; a tile holds RT <= 128 rows), the tokens its N
 // side (16 or 32 columns; rows past M are zero), one 16 x 16 f16 K step per MMA:
-//   warp 22       weight producer: TMA of raw super-blocks, RT rows x SW (1 or 2) super-blocks per stage, rows
+//   warp 18       weight producer: TMA of raw super-blocks, RT rows x SW (1 or 2) super-blocks per stage, rows
 //                 padded to an odd number of 16-byte units (no shared-memory bank conflicts for thread = row);
 //   warp 0        activation producer: per super-block one 3-D TMA copy of its 4 64-K chunks x TP token rows in
 //                 the 128-byte swizzle the MMA's K-major B descriptor expects;
-//   warps 2-17    decode: thread = row = TMEM lane, warp = (lane quarter, 64-K quarter of the super-block). Per
-//                 super-block a thread turns 32 nibble bytes into 32 cells of f16(sc*q) pairs (2 prmt + 4 and +
-//                 4 fma.rn.f16x2 per 8 weights) and its two groups' (hi, lo) min factors, and tcgen05.st's them into
-//                 an A buffer in TMEM;
+//   warps 2-13    decode, groups of 4 warps (one per A buffer) taking super-blocks in turn: thread = row = TMEM lane, warp =
+//                 lane quarter. Per super-block a thread turns 128 nibble bytes into 128 cells of f16(sc*q) pairs
+//                 (2 prmt + 4 and + 4 fma.rn.f16x2 per 8 weights) and its eight groups' (hi, lo) min factors, and
+//                 tcgen05.st's them into an A buffer in TMEM;
 //   warp 1        MMA issuer (one thread): 16 MMAs into a D1 slot (A buffer x activation tile) and 2 into the tile's
 //                 D2 region (min factors x group sums), then commits that free the A buffer, the activation stage
 //                 and hand D1 to the epilogue;
-//   warps 18-21   epilogue: per super-block tcgen05.ld of D1, acc += d_s * D1; per tile acc -= D2, the cluster
+//   warps 14-17   epilogue: per super-block tcgen05.ld of D1, acc += d_s * D1; per tile acc -= D2, the cluster
 //                 reduction, the kind (plain / resid / swiglu) and the stores.
 // The group sums of this CTA's K range (Xhi, Xlo in f16, 4 per group: Xhi Xlo Xhi Xlo against the A side's hi hi lo
 // lo) are formed once, on the first tile, by the decode warps of each super-block from its activation stage in shared
@@ -49,11 +49,11 @@
 namespace yah {
 namespace {
 
-constexpr int kTcThreads = 736;  // 23 warps
+constexpr int kTcThreads = 608;  // 19 warps
 // One MMA issuer. Measured on B200: a thread that issues tcgen05.mma waits ~45 cycles per instruction whatever its
 // size up to N = 64, and ~100 while other warps store to TMEM, so the small-N MMAs of a GEMV are issue-bound;
 // MMAs issued by two warps at once gave wrong results in whole 32-lane quarters, so the issue stays single.
-constexpr int kTcWarpX = 0, kTcWarpMma = 1, kTcWarpDq0 = 2, kTcWarpEpi0 = 18, kTcWarpW = 22;
+constexpr int kTcWarpX = 0, kTcWarpMma = 1, kTcWarpDq0 = 2, kTcWarpEpi0 = 14, kTcWarpW = 18;
 constexpr int kTcACols = 144;         // an A buffer: 128 columns of f16(sc*q) pairs + 16 of min factors
 constexpr int kTcNP = 8;              // per-row d ring (decode -> epilogue)
 constexpr int kTcWPitch2 = 304;       // weight stage row pitch for 2 super-blocks (19 x 16 B: odd)
@@ -241,12 +241,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < NSW; ++i) {
       mbar_init(&wfull[i], 1);
-      mbar_init(&wempty[i], 8 * p.sw);  // the decode warps that read the stage: one group per super-block
+      mbar_init(&wempty[i], 4 * p.sw);  // the decode warps that read the stage: one group per super-block
     }
     for (int i = 0; i < NA; ++i) {
       mbar_init(&xfull[i], 1);
       mbar_init(&sbempty[i], 1);
-      mbar_init(&afull[i], 8);
+      mbar_init(&afull[i], 4);
     }
     for (int i = 0; i < ND; ++i) {
       mbar_init(&dfull[i], 1);
@@ -351,17 +351,19 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   } else if (warp < kTcWarpEpi0 + 4) {
     if (warp < kTcWarpEpi0) {
       // ---------------------------------------------------------------- decode
-      // two groups of 8 warps take alternate super-blocks; in a group, warp (lane quarter q, half h) decodes
-      // groups 4h .. 4h + 3 of its 32 rows
-      const int q = warp & 3, par = (warp - kTcWarpDq0) >> 3, h = ((warp - kTcWarpDq0) >> 2) & 1;
+      // NA groups of 4 warps (3 or 2; the third group idles when NA = 2) take super-blocks in turn, so group g always
+      // fills A buffer g and waits only for its own previous super-block's MMAs; in a group, the warp of lane
+      // quarter q decodes the whole super-block of its 32 rows (both halves). Fewer decode warps leave the MMA
+      // issuer's SM sub-partition less contended.
+      const int q = warp & 3, par = (warp - kTcWarpDq0) >> 2;
       const int r = q * 32 + lane;
       const uint32_t tl = tmem + ((uint32_t)(q * 32) << 16);
-      const int gt = (((warp - kTcWarpDq0) & 7) * 32 + lane) >> 3, gg = lane & 7;  // group-sum entry: token, group
+      const int gt0 = (((warp - kTcWarpDq0) & 3) * 32 + lane) >> 3, gg = lane & 7;  // group-sum entries: token, group
       uint32_t i = 0;
       bool ok = true;
       for (int tile = cid; ok && tile < p.tiles; tile += G) {
         for (int j = 0; j < sr; ++j, ++i) {
-          if ((int)(i & 1) != par) continue;
+          if ((int)(i % NA) != par) continue;
           const uint32_t st = i / p.sw, ws = st % NSW, wph = (st / NSW) & 1;
           const int sbw = (int)(i % p.sw);
           const uint32_t as = i % NA;
@@ -372,15 +374,17 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           tc_fence_after();  // the MMAs that read this A buffer are complete: order the stores after them
           // Every lane decodes and stores (the stores are warp-aligned): rows past the tile read the stage's
           // unused rows, and the epilogue never reads their results.
-          const uint32_t ta = tl + as * kTcACols + 64 * h, tm = tl + as * kTcACols + 128 + 8 * h;
-          const float d = q4k_tc_decode_half(smem_u32(smem + ws * kTcWStage) + r * p.pitch + sbw * 144, h, ta, tm);
+          const uint32_t rb = smem_u32(smem + ws * kTcWStage) + r * p.pitch + sbw * 144;
+          const uint32_t ta = tl + as * kTcACols, tm = tl + as * kTcACols + 128;
+          const float d = q4k_tc_decode_half(rb, 0, ta, tm);
+          q4k_tc_decode_half(rb, 1, ta + 64, tm + 8);
           __syncwarp();
           if (lane == 0) mbar_arrive(&wempty[ws]);  // this warp's only read of the stage
           if (sums) {
             // X of group gg, token row gt: the group's 32 activations are 4 16-byte units of the 128-byte-swizzled
             // row gt of 64-K chunk gg / 2 (rows past M are zero); written as (Xhi, Xlo, Xhi, Xlo) into the group-sum
             // tile (async proxy: fenced before the arrive below)
-            if (gt < TP) {
+            for (int gt = gt0; gt < TP; gt += 16) {
               const uint32_t xrow = smem_u32(smem + C::kXOff + as * C::kXStage) + (gg >> 1) * (TP * 128) + gt * 128;
               float part[4];
 #pragma unroll
@@ -405,7 +409,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&afull[as]);
-          if (h == 0) {  // the row's d for the epilogue
+          {  // the row's d for the epilogue
             const uint32_t ps = i % kTcNP;
             if (!warp_wait(&pempty[ps], ((i / kTcNP) & 1) ^ 1, p.status, kStatusTimeoutEmpty)) { ok = false; break; }
             params[ps * 128 + r] = d;
